@@ -1,0 +1,453 @@
+#!/usr/bin/env python
+"""Benchmark: Hyena FFT-conv fwd+bwd throughput (GElem/s, E = B*C*N) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg1|cfg2|cfg3|cfg0] [--impl b200|reference]
+
+One "step" = forward + backward of the fused Hyena mixer (configs 1-3: short depthwise
+conv, gates, FFT long conv with D-skip) or of the op-level causal conv (config 0) on one
+batch of seeded synthetic input. Inputs are resident in HBM for ``value``; ``e2e`` runs
+the same step through the public API from pinned host buffers (H2D of the inputs and
+D2H of the output and all gradients inside the timed region).
+
+Multi-GPU (torchrun, one rank per GPU): config 1 runs one independent replica per rank
+(weak scaling); config 2 shards the batch and config 3 the channels across ranks
+(strong scaling). The time is the max over ranks of the device-timed region.
+
+``--impl reference`` times the reference's CPU path (the CPU oracle restating
+nvsubquadratic/ops/fftconv.py + hyena_nd.py on torch.fft) on the host cores, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+METRIC = "Hyena FFT-conv fwd+bwd GElem/s (B·C·N) at 1/2/4/8 B200; % of HBM roofline"
+
+CONFIGS = {
+    # name: dict(nd, B, C, S, K, short, gates, dtype, causal, shard)
+    "cfg0": dict(nd=1, B=2, C=64, S=(4096,), K=(4096,), short=0, g1="identity", g2="identity",
+                 dtype=torch.float32, causal=True, shard="replica", op_only=True,
+                 desc="1D causal FFT long conv + D skip, fp32 (reference CPU case)"),
+    "cfg1": dict(nd=2, B=32, C=768, S=(14, 14), K=(14, 14), short=3, g1="identity", g2="identity",
+                 dtype=torch.bfloat16, causal=False, shard="replica",
+                 desc="2D HyenaND ViT-B grid 14x14, SIREN-style 14x14 filter, F=32x32, 3x3 short conv"),
+    "cfg2": dict(nd=2, B=8, C=256, S=(128, 128), K=(128, 128), short=3, g1="identity", g2="identity",
+                 dtype=torch.bfloat16, causal=False, shard="batch",
+                 desc="2D HyenaND 128x128, exp-radial 128x128 filter, F=256x256, batch-sharded"),
+    "cfg3": dict(nd=3, B=2, C=192, S=(64, 64, 64), K=(64, 64, 64), short=3, g1="identity", g2="identity",
+                 dtype=torch.bfloat16, causal=False, shard="channel",
+                 desc="3D HyenaND 64^3, full-extent exp-radial filter, F=128^3, channel-sharded"),
+}
+
+
+# ----------------------------------------------------------------- inputs
+def siren_filter(C: int, K: tuple[int, ...], gen: torch.Generator, hidden: int = 32, omega0: float = 30.0):
+    """Random-init SIREN-style MLP evaluated on a [-1, 1]^d grid of K points: [1, C, *K] fp32.
+    (Filter generation is not part of the hot path; this only makes a realistic filter.)"""
+    nd = len(K)
+    axes = [torch.linspace(-1.0, 1.0, k) for k in K]
+    grid = torch.stack(torch.meshgrid(*axes, indexing="ij"), dim=-1).reshape(-1, nd)
+    W1 = (torch.rand(nd, hidden, generator=gen) * 2 - 1) / nd
+    W2 = (torch.rand(hidden, hidden, generator=gen) * 2 - 1) * math.sqrt(6 / hidden) / omega0
+    W3 = (torch.rand(hidden, C, generator=gen) * 2 - 1) * math.sqrt(6 / hidden) / omega0
+    h = torch.sin(omega0 * grid @ W1)
+    h = torch.sin(omega0 * h @ W2)
+    out = h @ W3
+    return out.t().reshape((1, C) + tuple(K)).contiguous() * 0.1
+
+
+def decay_filter(C: int, K: tuple[int, ...], gen: torch.Generator, causal: bool):
+    """N(0,1) * exp(-beta_c * r): radius from the filter centre (or time for causal 1D)."""
+    nd = len(K)
+    if causal:
+        r = torch.arange(K[0], dtype=torch.float32).view(1, -1)
+        beta = (torch.rand(C, 1, generator=gen) * 4.5 + 0.5) / K[0]
+    else:
+        axes = [torch.arange(k, dtype=torch.float32) - (k - 1) / 2 for k in K]
+        mesh = torch.stack(torch.meshgrid(*axes, indexing="ij"), dim=0)
+        r = mesh.pow(2).sum(0).sqrt().reshape(1, -1)
+        beta = (torch.rand(C, 1, generator=gen) * 4.5 + 0.5) / max(K)
+    f = torch.randn((C, r.shape[1]), generator=gen) * torch.exp(-beta * r)
+    f = f / math.sqrt(r.shape[1])
+    return f.reshape((1, C) + tuple(K))
+
+
+def make_inputs(cfg: dict, B: int, C: int, c_off: int, seed: int = 0):
+    """Seeded synthetic inputs (CPU, generated in the order of the survey's recipe)."""
+    g = torch.Generator().manual_seed(seed)
+    nd, S, K, dt = cfg["nd"], cfg["S"], cfg["K"], cfg["dtype"]
+    if cfg.get("op_only"):
+        x = torch.randn((B, C) + S, generator=g)
+        filt = decay_filter(C, K, g, causal=True)
+        D = torch.randn(C, generator=g)
+        dy = torch.randn((B, C) + S, generator=g)
+        return dict(x=x.to(dt), filt=filt, D=D.to(dt), dy=dy.to(dt))
+    qkv = torch.randn((B,) + S + (3 * C,), generator=g).to(dt)
+    if S == (14, 14):
+        filt = siren_filter(C, K, g)
+    else:
+        filt = decay_filter(C, K, g, causal=cfg["causal"])
+    D = ((torch.rand(C, generator=g) * 2 - 1) / math.sqrt(C)).to(dt)
+    sk = cfg["short"]
+    sw = ((torch.rand((3 * C, 1) + (sk,) * nd, generator=g) * 2 - 1) / math.sqrt(sk ** nd)).to(dt) if sk else None
+    dy = torch.randn((B,) + S + (C,), generator=g).to(dt)
+    return dict(qkv=qkv, filt=filt, D=D, sw=sw, dy=dy)
+
+
+def alg_bytes(cfg: dict, B: int, C: int) -> int:
+    """Minimum HBM bytes of one fwd+bwd (nothing kept between passes but the inputs)."""
+    N = math.prod(cfg["S"])
+    E = B * C * N
+    KK = math.prod(cfg["K"])
+    if cfg.get("op_only"):
+        return 20 * E + 12 * C * KK  # fp32: x, y, dy, x, dx + filter read x2, dfilt write
+    s = torch.finfo(cfg["dtype"]).bits // 8
+    # fwd: read q,k,v, write y; bwd: read dy, q,k,v, write dq,dk,dv; filter read twice + dfilt
+    return (11 * s) * E + 12 * C * KK
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    def __init__(self, index: int):
+        self.index = index
+        self.rows: list[list[str]] = []
+        self._stop = threading.Event()
+        self._proc = None
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self._proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (OSError, FileNotFoundError):
+            self._proc = None
+        return self
+
+    def _read(self):
+        for line in self._proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+
+    def summary(self):
+        rows = [r for r in self.rows if len(r) >= 7 and r[0].isdigit()]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [int(r[0]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": int(rows[0][1]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ----------------------------------------------------------------- CPU reference arm
+def cpu_reference_time(cfg: dict, budget_s: float = 20.0):
+    """Time the reference's CPU path (oracle restatement on torch.fft) on a channel slice
+    of the workload; returns (GElem/s, threads, sample description)."""
+    from oracle.fftconv import fftconv_bhl
+    from oracle.hyena import hyena_forward
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    B, C = cfg["B"], cfg["C"]
+    N = math.prod(cfg["S"])
+    # pick a channel slice that takes ~1 s per fwd+bwd (grown from a tiny probe)
+    c_s = max(1, min(C, 8))
+
+    def one(cs):
+        inp = make_inputs(cfg, B if cfg["nd"] < 3 else min(B, 2), cs, 0, seed=0)
+        t0 = time.perf_counter()
+        if cfg.get("op_only"):
+            x = inp["x"].requires_grad_(True)
+            k = inp["filt"].requires_grad_(True)
+            D = inp["D"].requires_grad_(True)
+            y = fftconv_bhl(x, k, D, causal=True)
+            y.backward(inp["dy"])
+        else:
+            q, k, v = (t.clone().requires_grad_(True) for t in inp["qkv"].chunk(3, dim=-1))
+            f = inp["filt"].requires_grad_(True)
+            D = inp["D"].clone().requires_grad_(True)
+            sw = inp["sw"].clone().requires_grad_(True) if inp["sw"] is not None else None
+            y = hyena_forward(q, k, v, f, D, sw, None, causal=cfg["causal"], gate1=cfg["g1"], gate2=cfg["g2"])
+            y.backward(inp["dy"])
+        return time.perf_counter() - t0
+
+    one(c_s)  # warm-up (first-call allocation / thread-pool start-up)
+    t = one(c_s)
+    while t < 1.0 and c_s < C:
+        c_s = min(C, c_s * 2)
+        t = one(c_s)
+    reps = max(3, min(15, int(budget_s / max(t, 1e-3))))
+    times = [one(c_s) for _ in range(reps)]
+    med = statistics.median(times)
+    Bs = B if cfg["nd"] < 3 else min(B, 2)
+    elems = Bs * c_s * N
+    sample = f"{Bs}x{c_s} of {B}x{C} (batch x channels), full spatial extent; median of {reps} fwd+bwd"
+    return elems / med / 1e9, threads, sample, med
+
+
+# ----------------------------------------------------------------- GPU arm
+def run_gpu(args, cfg, rank, world, device):
+    from nvsubquadratic_b200 import _lib
+    from nvsubquadratic_b200.fftconv import causal_fftconv1d_fp32_bhl
+    from nvsubquadratic_b200.hyena import hyena_fused
+
+    B, C = cfg["B"], cfg["C"]
+    c_off = 0
+    if world > 1 and cfg["shard"] == "batch":
+        assert B % world == 0
+        B //= world
+    elif world > 1 and cfg["shard"] == "channel":
+        assert C % world == 0
+        C //= world
+        c_off = rank * C
+    inp = make_inputs(cfg, B, C, c_off, seed=rank if cfg["shard"] == "replica" else 0)
+    dev_inp = {k: (v.to(device) if v is not None else None) for k, v in inp.items()}
+
+    op_only = cfg.get("op_only", False)
+    if op_only:
+        x = dev_inp["x"].requires_grad_(True)
+        filt = dev_inp["filt"].requires_grad_(True)
+        D = dev_inp["D"].requires_grad_(True)
+        dy = dev_inp["dy"]
+
+        def step():
+            y = causal_fftconv1d_fp32_bhl(x, filt, D)
+            y.backward(dy)
+            return y
+
+        params = [x, filt, D]
+    else:
+        qkv = dev_inp["qkv"].requires_grad_(True)
+        filt = dev_inp["filt"].requires_grad_(True)
+        D = dev_inp["D"].requires_grad_(True)
+        sw = dev_inp["sw"].requires_grad_(True) if dev_inp["sw"] is not None else None
+        dy = dev_inp["dy"]
+
+        def step():
+            q, k, v = qkv.chunk(3, dim=-1)
+            y = hyena_fused(q, k, v, filt, D, sw, None, causal=cfg["causal"], gate1=cfg["g1"], gate2=cfg["g2"])
+            y.backward(dy)
+            return y
+
+        params = [p for p in (qkv, filt, D, sw) if p is not None]
+
+    def zero_grads():
+        for p in params:
+            p.grad = None
+
+    # eager warm-up (also counts kernel launches of one step)
+    for _ in range(max(1, args.warmup)):
+        zero_grads()
+        step()
+    torch.cuda.synchronize()
+    n0 = _lib.launch_count()
+    zero_grads()
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = _lib.launch_count() - n0
+
+    # capture one step in a CUDA graph (the hot loop is launch-bound otherwise)
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            zero_grads()
+            step()
+    torch.cuda.current_stream(device).wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    zero_grads()
+    with torch.cuda.graph(graph):
+        step()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)  # > 126 MB L2
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        for i in range(args.steps):
+            flush.zero_()  # evict L2 between timed steps (outside the events)
+            starts[i].record()
+            graph.replay()
+            ends[i].record()
+        torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    step_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    t = torch.tensor([total_ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    total_ms = t.item()
+
+    # e2e through the public API from pinned host buffers (eager, no graph)
+    e2e_ms, h2d, d2h = e2e_time(cfg, inp, device, op_only, max(3, min(args.steps, 10)))
+    t2 = torch.tensor([e2e_ms], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
+    e2e_ms = t2.item()
+    del graph
+    return dict(total_ms=total_ms, step_ms=step_ms, launches=launches_per_step, clocks=clk.summary(),
+                B=B, C=C, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h)
+
+
+def e2e_time(cfg, inp, device, op_only, steps):
+    from nvsubquadratic_b200.fftconv import causal_fftconv1d_fp32_bhl
+    from nvsubquadratic_b200.hyena import hyena_fused
+
+    host = {k: (v.pin_memory() if v is not None else None) for k, v in inp.items()}
+    outs = {}
+    h2d = d2h = 0
+    times = []
+    for i in range(steps + 2):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        if op_only:
+            x = host["x"].to(device, non_blocking=True).requires_grad_(True)
+            f = host["filt"].to(device, non_blocking=True).requires_grad_(True)
+            D = host["D"].to(device, non_blocking=True).requires_grad_(True)
+            dy = host["dy"].to(device, non_blocking=True)
+            y = causal_fftconv1d_fp32_bhl(x, f, D)
+            y.backward(dy)
+            res = [y, x.grad, f.grad, D.grad]
+            ins = [host["x"], host["filt"], host["D"], host["dy"]]
+        else:
+            qkv = host["qkv"].to(device, non_blocking=True).requires_grad_(True)
+            f = host["filt"].to(device, non_blocking=True).requires_grad_(True)
+            D = host["D"].to(device, non_blocking=True).requires_grad_(True)
+            sw = host["sw"].to(device, non_blocking=True).requires_grad_(True) if host["sw"] is not None else None
+            dy = host["dy"].to(device, non_blocking=True)
+            q, k, v = qkv.chunk(3, dim=-1)
+            y = hyena_fused(q, k, v, f, D, sw, None, causal=cfg["causal"], gate1=cfg["g1"], gate2=cfg["g2"])
+            y.backward(dy)
+            res = [y, qkv.grad, f.grad, D.grad] + ([sw.grad] if sw is not None else [])
+            ins = [host["qkv"], host["filt"], host["D"], host["dy"]] + ([host["sw"]] if sw is not None else [])
+        if not outs:
+            outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        for o, r in zip(outs, res):
+            o.copy_(r, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        if i >= 2:
+            times.append(a.elapsed_time(b))
+        h2d = sum(t.numel() * t.element_size() for t in ins)
+        d2h = sum(r.numel() * r.element_size() for r in res)
+    return sum(times) / len(times), h2d, d2h
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg1", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    cfg = CONFIGS[args.config]
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    B, C = cfg["B"], cfg["C"]
+    N = math.prod(cfg["S"])
+    dtname = {torch.float32: "f32", torch.bfloat16: "bf16"}[cfg["dtype"]]
+    config = {"workload": args.config + ": " + cfg["desc"], "batch": B, "channels": C, "spatial": list(cfg["S"]),
+              "filter": list(cfg["K"]), "sharding": cfg["shard"], "l2": "flushed between timed steps (256 MB write)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        gel, threads, sample, med = cpu_reference_time(cfg)
+        out = {"metric": METRIC, "value": round(gel, 6), "unit": "GElem/s", "n_gpus": args.gpus, "steps": args.steps,
+               "warmup": args.warmup, "ms_per_step": round(med * 1e3, 3), "higher_is_better": True,
+               "scaling": "weak" if cfg["shard"] == "replica" else "strong", "vs_baseline": None, "dtype": dtname,
+               "data": "synthetic", "config": config, "impl": "reference",
+               "cpu_baseline": {"value": round(gel, 6), "unit": "GElem/s", "cores": threads, "kind": "port",
+                                "sample": sample},
+               "e2e": {"value": round(gel, 6), "unit": "GElem/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(out))
+        return
+
+    if world > 1:
+        import datetime
+
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    res = run_gpu(args, cfg, rank, world, device)
+
+    # whole-job throughput: all ranks' elements / max-over-ranks time
+    elems_rank = res["B"] * res["C"] * N
+    elems_job = elems_rank * world
+    t_step = res["total_ms"] / args.steps / 1e3
+    value = elems_job / t_step / 1e9
+    bytes_rank = alg_bytes(cfg, res["B"], res["C"])
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+    except OSError:
+        pass
+    peak = peaks.get("hbm_gbs", 6650.0)
+    achieved = bytes_rank / t_step / 1e9
+    e2e_val = elems_job / (res["e2e_ms"] / 1e3) / 1e9
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": round(value, 4), "unit": "GElem/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_step * 1e3, 4), "higher_is_better": True,
+            "scaling": "weak" if cfg["shard"] == "replica" else "strong", "vs_baseline": None, "dtype": dtname,
+            "data": "synthetic (seeded N(0,1) activations, random-init filters)", "config": config,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "scope": "whole fwd+bwd step (algorithmic bytes per step / step time)",
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+            "e2e": {"value": round(e2e_val, 4), "unit": "GElem/s", "h2d_bytes_per_step": res["h2d"],
+                    "d2h_bytes_per_step": res["d2h"]},
+            "gpu_launches": res["launches"] * args.steps,
+            "clocks": res["clocks"],
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            gel, threads, sample, _ = cpu_reference_time(cfg)
+            out["cpu_baseline"] = {"value": round(gel, 6), "unit": "GElem/s", "cores": threads, "kind": "port",
+                                   "sample": sample}
+        print(json.dumps(out))
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

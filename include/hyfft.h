@@ -1,0 +1,176 @@
+/*
+ * hyfft.h — C ABI of the B200-native Hyena FFT-convolution backend.
+ *
+ * This is the drop-in boundary for nvSubquadratic's long-convolution hot path.
+ * Every entry point takes plain pointers and sizes, enqueues its work on the
+ * caller's CUDA stream, allocates nothing (all scratch comes from the
+ * caller-provided workspace), never throws, and returns an HYFFT_* status.
+ *
+ * Reference interfaces each group replaces (nvSubquadratic, file:line):
+ *
+ *   hyfft_conv_forward / hyfft_conv_backward
+ *     the op contract  fn(x, kernel, shortcut) -> y  and its autograd backward:
+ *       causal_fftconv1d_fp32_bhl   nvsubquadratic/ops/fftconv.py:546-600
+ *       fftconv1d_fp32_bhl          nvsubquadratic/ops/fftconv.py:603-659
+ *       fftconv2d_fp32_bhl          nvsubquadratic/ops/fftconv.py:662-733
+ *       fftconv3d_fp32_bhl          nvsubquadratic/ops/fftconv.py:736-812
+ *       *_fp32_blh / *_w_reshape    nvsubquadratic/ops/fftconv.py:163-538 (layout = BLH)
+ *     and the external-kernel slot the reference binds for fft_backend="subq_ops"
+ *       fftconv2d_bhl / causal_fftconv1d_bhl  nvsubquadratic/ops/fftconv_custom.py:133-160, :307-335
+ *
+ *   hyfft_hyena_forward / hyfft_hyena_backward
+ *     the fused mixer  Hyena.forward(q, k, v)  with identity norms:
+ *       nvsubquadratic/modules/hyena_nd.py:432-583 (short conv :505-516, gate 1 :546,
+ *       global conv :563 -> modules/ckconv_nd.py:1006-1062, gate 2 :570)
+ *
+ *   hyfft_cp_pack / hyfft_cp_unpack
+ *     the local permutations around the context-parallel all-to-all:
+ *       all_to_all_single_fn  nvsubquadratic/parallel/a2a_comms.py:125-285
+ *
+ * Threading: the host calls are reentrant; concurrent calls on different
+ * streams must use different workspaces.
+ */
+#ifndef HYFFT_H_
+#define HYFFT_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define HYFFT_API __attribute__((visibility("default")))
+#else
+#define HYFFT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+#define HYFFT_OK 0
+#define HYFFT_ERR_INVALID 1      /* bad argument (shape, pointer, enum)        */
+#define HYFFT_ERR_UNSUPPORTED 2  /* valid request this backend does not cover  */
+#define HYFFT_ERR_WORKSPACE 3    /* workspace / saved buffer too small          */
+#define HYFFT_ERR_CUDA 4         /* a CUDA launch failed (see hyfft_last_error) */
+
+/* ---------------------------------------------------------------- enums */
+#define HYFFT_F32 0
+#define HYFFT_BF16 1
+#define HYFFT_F16 2
+
+#define HYFFT_LAYOUT_BHL 0 /* [B, H, *S] channels-first */
+#define HYFFT_LAYOUT_BLH 1 /* [B, *S, H] channels-last  */
+
+#define HYFFT_GATE_IDENTITY 0
+#define HYFFT_GATE_SIGMOID 1
+#define HYFFT_GATE_SILU 2
+
+/* ---------------------------------------------------------------- op level */
+typedef struct hyfft_conv_desc {
+  int32_t ndim;         /* spatial rank: 1, 2 or 3                                  */
+  int32_t batch;        /* B                                                        */
+  int32_t channels;     /* H                                                        */
+  int32_t n[3];         /* spatial extents (unused entries ignored)                 */
+  int32_t k[3];         /* kernel extents, k[d] <= 2 * n[d]                         */
+  int32_t kernel_batch; /* 1 (shared kernel) or B (per-sample / FiLM kernels)       */
+  int32_t causal;       /* 1: causal 1D conv (fftconv.py:546); 0: centred "same"    */
+  int32_t dtype;        /* HYFFT_F32 / BF16 / F16: dtype of x, y, shortcut, dx, dy  */
+  int32_t layout;       /* HYFFT_LAYOUT_BHL or HYFFT_LAYOUT_BLH for x, y, dx, dy    */
+} hyfft_conv_desc;
+
+/* Workspace bytes for one forward / one backward call. */
+HYFFT_API int hyfft_conv_workspace_size(const hyfft_conv_desc* d, size_t* fwd_bytes, size_t* bwd_bytes);
+
+/* y = conv(x, kernel) rounded to dtype, then + shortcut * x (if shortcut != NULL).
+ * x, y: contiguous in `layout`; kernel: float32 contiguous [kernel_batch, H, *k]
+ * (BHL) or [kernel_batch, *k, H] (BLH); shortcut: [H] of `dtype` or NULL.          */
+HYFFT_API int hyfft_conv_forward(const hyfft_conv_desc* d, const void* x, const float* kernel,
+                       const void* shortcut, void* y, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Gradients of hyfft_conv_forward for upstream dy: dx (dtype, layout of x),
+ * dkernel (float32, layout of kernel), dshortcut (float32 [H]; NULL when
+ * shortcut is NULL). Any of dx / dkernel / dshortcut may be NULL to skip it.     */
+HYFFT_API int hyfft_conv_backward(const hyfft_conv_desc* d, const void* x, const float* kernel,
+                        const void* shortcut, const void* dy, void* dx, float* dkernel,
+                        float* dshortcut, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- fused mixer */
+typedef struct hyfft_hyena_desc {
+  int32_t ndim;            /* spatial rank 1..3                                       */
+  int32_t batch;           /* B                                                       */
+  int32_t channels;        /* C (q, k, v each have C channels)                        */
+  int32_t n[3];            /* spatial extents                                         */
+  int32_t k[3];            /* long filter extents (filter is float32 [1, C, *k])      */
+  int32_t causal;          /* causal long conv (1D)                                   */
+  int32_t short_k[3];      /* depthwise short conv extents; 0 = no short conv         */
+  int32_t short_causal;    /* 1D causal short conv (left pad short_k - 1)             */
+  int32_t short_bias;      /* short conv has a bias [3C]                              */
+  int32_t gate1;           /* HYFFT_GATE_* applied to k: z = q * gate1(k)             */
+  int32_t gate2;           /* HYFFT_GATE_* applied to v: y = h * gate2(v)             */
+  int32_t dtype;           /* activation dtype of q, k, v, y, dq, dk, dv, dy          */
+  int64_t in_batch_stride; /* element strides of q, k, v (channel stride is 1):       */
+  int64_t in_pos_stride;   /*   e.g. 3C for views into one [B, *S, 3C] projection     */
+  int64_t out_batch_stride;/* element strides of y, dy, dq, dk, dv (channel stride 1) */
+  int64_t out_pos_stride;
+} hyfft_hyena_desc;
+
+/* Workspace bytes for forward / backward, and the bytes of the `saved` buffer the
+ * forward fills for the backward (0 when the backward recomputes everything).   */
+HYFFT_API int hyfft_hyena_workspace_size(const hyfft_hyena_desc* d, size_t* fwd_bytes, size_t* bwd_bytes,
+                               size_t* saved_bytes);
+
+/* y = gate2(v') * (conv(z) + D * z), z = q' * gate1(k'), (q', k', v') = short conv of
+ * (q, k, v). filt: float32 [1, C, *k]; D: float32 [C]; short_w: float32 [3C, *short_k];
+ * short_b: float32 [3C] or NULL. `saved` may be NULL when saved_bytes == 0.        */
+HYFFT_API int hyfft_hyena_forward(const hyfft_hyena_desc* d, const void* q, const void* k, const void* v,
+                        const float* filt, const float* D, const float* short_w,
+                        const float* short_b, void* y, void* saved, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* Gradients for upstream dy. dfilt [1, C, *k], dD [C], dshort_w [3C, *short_k],
+ * dshort_b [3C] are float32 and OVERWRITTEN (not accumulated). `saved` is what the
+ * matching forward wrote.                                                          */
+HYFFT_API int hyfft_hyena_backward(const hyfft_hyena_desc* d, const void* q, const void* k, const void* v,
+                         const float* filt, const float* D, const float* short_w,
+                         const float* short_b, const void* dy, void* dq, void* dk, void* dv,
+                         float* dfilt, float* dD, float* dshort_w, float* dshort_b,
+                         const void* saved, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* ---------------------------------------------------------------- context parallel */
+/* Local permutations around NCCL all_to_all_single for a 1D/2D/3D tensor whose
+ * axis 2 is the sequence (a2a_comms.py:171-282). elem_bytes: 2 or 4.
+ *
+ * hyfft_cp_pack_split_to_full:   src [B, C, l, *rest] (rank-local, zigzag chunks)
+ *                                -> dst [P, B, C/P, l, *rest] (send buffer)
+ * hyfft_cp_unpack_split_to_full: src [P, B, C/P, l, *rest] (received)
+ *                                -> dst [B, C/P, P*l, *rest] natural order
+ *                                (inverse zigzag when zigzag != 0)
+ * hyfft_cp_pack_full_to_split:   src [B, d, L, *rest] -> dst [P, B, d, L/P, *rest]
+ *                                (zigzag chunk order when zigzag != 0)
+ * hyfft_cp_unpack_full_to_split: src [P, B, d, l, *rest] -> dst [B, P*d, l, *rest]
+ * rest = product of trailing extents after the sequence axis (1 for 1D).           */
+HYFFT_API int hyfft_cp_pack_split_to_full(const void* src, void* dst, int64_t B, int64_t C, int64_t l,
+                                int64_t rest, int32_t P, int32_t elem_bytes, void* stream);
+HYFFT_API int hyfft_cp_unpack_split_to_full(const void* src, void* dst, int64_t B, int64_t d, int64_t l,
+                                  int64_t rest, int32_t P, int32_t zigzag, int32_t elem_bytes,
+                                  void* stream);
+HYFFT_API int hyfft_cp_pack_full_to_split(const void* src, void* dst, int64_t B, int64_t d, int64_t L,
+                                int64_t rest, int32_t P, int32_t zigzag, int32_t elem_bytes,
+                                void* stream);
+HYFFT_API int hyfft_cp_unpack_full_to_split(const void* src, void* dst, int64_t B, int64_t d, int64_t l,
+                                  int64_t rest, int32_t P, int32_t elem_bytes, void* stream);
+
+/* ---------------------------------------------------------------- misc */
+/* Message of the most recent error on this thread ("" if none). */
+HYFFT_API const char* hyfft_last_error(void);
+/* Library version string. */
+HYFFT_API const char* hyfft_version(void);
+/* Number of kernels this process has launched through the library so far. */
+HYFFT_API long long hyfft_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* HYFFT_H_ */

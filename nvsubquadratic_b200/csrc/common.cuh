@@ -1,0 +1,67 @@
+// Shared device helpers for the B200 Hyena FFT-conv kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/hyfft.h"
+
+namespace hyfft {
+
+// ---------------------------------------------------------------- complex
+__device__ __forceinline__ float2 cmul(float2 a, float2 b) {
+  return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));
+}
+// a * conj(b)
+__device__ __forceinline__ float2 cmulc(float2 a, float2 b) {
+  return make_float2(fmaf(a.x, b.x, a.y * b.y), fmaf(a.y, b.x, -a.x * b.y));
+}
+__device__ __forceinline__ float2 cadd(float2 a, float2 b) { return make_float2(a.x + b.x, a.y + b.y); }
+__device__ __forceinline__ float2 csub(float2 a, float2 b) { return make_float2(a.x - b.x, a.y - b.y); }
+__device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2(a.x * s, a.y * s); }
+
+// e^{i*pi*x}
+__device__ __forceinline__ float2 expipi(float x) {
+  float s, c;
+  sincospif(x, &s, &c);
+  return make_float2(c, s);
+}
+
+// ---------------------------------------------------------------- dtypes
+template <typename T> struct DT;
+template <> struct DT<float> {
+  static __device__ __forceinline__ float load(const float* p) { return *p; }
+  static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+  static __device__ __forceinline__ float round(float v) { return v; }
+};
+template <> struct DT<__nv_bfloat16> {
+  static __device__ __forceinline__ float load(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+};
+template <> struct DT<__half> {
+  static __device__ __forceinline__ float load(const __half* p) { return __half2float(*p); }
+  static __device__ __forceinline__ void store(__half* p, float v) { *p = __float2half_rn(v); }
+  static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
+};
+
+// ---------------------------------------------------------------- gates
+// 0 identity, 1 sigmoid, 2 silu (the activations Hyena.forward applies at
+// hyena_nd.py:546 and :570).
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ float gate_f(int g, float x) {
+  if (g == HYFFT_GATE_SIGMOID) return sigmoidf_(x);
+  if (g == HYFFT_GATE_SILU) return x * sigmoidf_(x);
+  return x;
+}
+// derivative of the gate
+__device__ __forceinline__ float gate_df(int g, float x) {
+  if (g == HYFFT_GATE_SIGMOID) { float s = sigmoidf_(x); return s * (1.0f - s); }
+  if (g == HYFFT_GATE_SILU) { float s = sigmoidf_(x); return s * (1.0f + x * (1.0f - s)); }
+  return 1.0f;
+}
+
+}  // namespace hyfft

@@ -1,0 +1,895 @@
+// General FFT-conv engine: host-side planning of the pass sequence and the
+// C-ABI entry points for the op contract and the fused Hyena mixer.
+//
+// Spectra live in caller-provided workspace as complex float32 arrays laid
+// out [pair][F_0]...[F_{D-1}][C] (channels innermost). Two real batch items
+// that share a kernel are packed into one complex signal (real part = item p,
+// imaginary part = item p + ceil(B/2)); because the kernel is real its
+// spectrum multiplies both halves independently, so one complex transform
+// carries two convolutions and no Hermitian post-processing is needed.
+//
+// FFT length per axis: the smallest power of two that is >= K and that
+// leaves no wrap-around inside the kept window (>= N + ceil(K/2) - 1 for the
+// centred "same" conv, >= L + K - 1 for causal). The linear result is
+// identical to the reference's F = min(N + (K+1)//2, 2N) / min(L+K, 2L)
+// (nvsubquadratic/ops/fftconv.py:580, :627, :699-702, :773-777); the one case
+// where the reference wraps around (causal with K > L + 1) is remapped by the
+// Python wrapper to an equivalent centred kernel before it reaches here.
+#include <algorithm>
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "fft_pass.cuh"
+#include "hyena_elem.cuh"
+#include "pointwise.cuh"
+
+namespace hyfft {
+
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+std::atomic<long long> g_launches{0};
+
+static int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(HYFFT_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return HYFFT_OK;
+}
+
+#define HY_TRY(expr)              \
+  do {                            \
+    int _rc = (expr);             \
+    if (_rc != HYFFT_OK) return _rc; \
+  } while (0)
+
+static int ilog2(long long v) {
+  int r = 0;
+  while ((1LL << r) < v) ++r;
+  return r;
+}
+static long long next_pow2(long long v) { return v <= 1 ? 1 : (1LL << ilog2(v)); }
+
+// ------------------------------------------------------------------ geometry
+struct Geo {
+  int D = 1;
+  int N[3] = {1, 1, 1};
+  int K[3] = {1, 1, 1};
+  int F[3] = {1, 1, 1};
+  int crop[3] = {0, 0, 0};  // forward output window start per axis
+  bool four = false;        // 1D four-step decomposition F = Fa * Fb
+  int Fa = 1, Fb = 1;
+  long long vol_F = 1;      // prod F
+};
+
+static int make_geo(int nd, const int* n, const int* k, int causal, Geo& g) {
+  if (nd < 1 || nd > 3) return fail(HYFFT_ERR_INVALID, "ndim must be 1..3 (got %d)", nd);
+  if (causal && nd != 1) return fail(HYFFT_ERR_INVALID, "causal convolution is 1D only");
+  g.D = nd;
+  g.vol_F = 1;
+  for (int d = 0; d < nd; ++d) {
+    if (n[d] < 1 || k[d] < 1) return fail(HYFFT_ERR_INVALID, "extents must be positive");
+    if (k[d] > 2 * n[d]) return fail(HYFFT_ERR_INVALID, "kernel extent %d > 2 * input extent %d", k[d], n[d]);
+    g.N[d] = n[d];
+    g.K[d] = k[d];
+    long long need;
+    if (causal) {
+      if (k[d] > n[d] + 1)
+        return fail(HYFFT_ERR_UNSUPPORTED, "causal kernel longer than L+1 wraps around; remap it to a centred kernel first");
+      need = (long long)n[d] + k[d] - 1;
+      g.crop[d] = 0;
+    } else {
+      need = (long long)n[d] + (k[d] + 1) / 2 - 1;
+      g.crop[d] = k[d] / 2;
+    }
+    need = std::max<long long>(need, k[d]);
+    g.F[d] = (int)next_pow2(need);
+    if (g.F[d] > (1 << 24)) return fail(HYFFT_ERR_UNSUPPORTED, "FFT length %d too large", g.F[d]);
+    if (nd > 1 && g.F[d] > kPassPoints) return fail(HYFFT_ERR_UNSUPPORTED, "multi-D axis FFT length %d > %d", g.F[d], kPassPoints);
+    g.vol_F *= g.F[d];
+  }
+  g.four = (nd == 1 && g.F[0] > kPassPoints);
+  if (g.four) {
+    const int lf = ilog2(g.F[0]);
+    g.Fa = 1 << ((lf + 1) / 2);
+    g.Fb = g.F[0] / g.Fa;
+  }
+  return HYFFT_OK;
+}
+
+// A strided real tensor (element strides), viewed as [b][c][s0][s1][s2].
+struct RealView {
+  const void* ptr = nullptr;
+  long long bst = 0, cst = 0, sst[3] = {0, 0, 0};
+};
+
+static RealView real_view(const void* p, int layout, int B, int C, const int* ext, int nd) {
+  RealView v;
+  v.ptr = p;
+  long long vol = 1;
+  for (int d = 0; d < nd; ++d) vol *= ext[d];
+  if (layout == HYFFT_LAYOUT_BHL) {
+    v.bst = (long long)C * vol;
+    v.cst = vol;
+    long long s = 1;
+    for (int d = nd - 1; d >= 0; --d) { v.sst[d] = s; s *= ext[d]; }
+  } else {
+    v.bst = (long long)C * vol;
+    v.cst = 1;
+    long long s = C;
+    for (int d = nd - 1; d >= 0; --d) { v.sst[d] = s; s *= ext[d]; }
+  }
+  (void)B;
+  return v;
+}
+
+static RealView offset_channels(RealView v, int c0, int elem_bytes) {
+  v.ptr = static_cast<const char*>(v.ptr) + (long long)c0 * v.cst * elem_bytes;
+  return v;
+}
+
+static int dtype_bytes(int dt) { return dt == HYFFT_F32 ? 4 : 2; }
+
+// ------------------------------------------------------------------ pass launch
+template <int IM, int OM, typename TI, typename TO>
+static int launch_pass_t(const PassDesc& d, cudaStream_t st) {
+  const long long grid = (d.nlines + d.TL - 1) / d.TL;
+  if (grid <= 0) return HYFFT_OK;
+  if (grid > 0x7fffffffLL) return fail(HYFFT_ERR_UNSUPPORTED, "too many FFT lines");
+  const size_t smem = sizeof(LineInfo) * kPassMaxLines + sizeof(float2) * (size_t)d.TL * (d.F + 1);
+  fft_pass_kernel<IM, OM, TI, TO><<<(unsigned)grid, kPassThreads, smem, st>>>(d);
+  return check_launch("fft_pass_kernel");
+}
+
+template <int IM, int OM>
+static int launch_pass_dt(const PassDesc& d, int tin, int tout, cudaStream_t st) {
+  // only the real side's dtype matters; complex-only passes use float
+  if (IM == IN_REAL) {
+    if (tin == HYFFT_F32) return launch_pass_t<IM, OM, float, float>(d, st);
+    if (tin == HYFFT_BF16) return launch_pass_t<IM, OM, __nv_bfloat16, float>(d, st);
+    return launch_pass_t<IM, OM, __half, float>(d, st);
+  }
+  if (OM != OUT_CPLX) {
+    if (tout == HYFFT_F32) return launch_pass_t<IM, OM, float, float>(d, st);
+    if (tout == HYFFT_BF16) return launch_pass_t<IM, OM, float, __nv_bfloat16>(d, st);
+    return launch_pass_t<IM, OM, float, __half>(d, st);
+  }
+  return launch_pass_t<IM, OM, float, float>(d, st);
+}
+
+static int launch_pass(const PassDesc& d, int im, int om, int tin, int tout, cudaStream_t st) {
+  if (im == IN_REAL && om == OUT_CPLX) return launch_pass_dt<IN_REAL, OUT_CPLX>(d, tin, tout, st);
+  if (im == IN_CPLX && om == OUT_CPLX) return launch_pass_dt<IN_CPLX, OUT_CPLX>(d, tin, tout, st);
+  if (im == IN_CPLX && om == OUT_REAL) return launch_pass_dt<IN_CPLX, OUT_REAL>(d, tin, tout, st);
+  if (im == IN_CPLX && om == OUT_REAL_SKIP) return launch_pass_dt<IN_CPLX, OUT_REAL_SKIP>(d, tin, tout, st);
+  return fail(HYFFT_ERR_INVALID, "unsupported pass mode");
+}
+
+static void base_desc(PassDesc& d, int F, float dir, int P, int C) {
+  memset(&d, 0, sizeof(d));
+  d.F = F;
+  d.logF = ilog2(F);
+  d.dir = dir;
+  d.scale = dir > 0 ? 1.0f / (float)F : 1.0f;
+  d.TL = std::min(kPassMaxLines, std::max(1, kPassPoints / F));
+  d.P = P;
+  d.C = C;
+  d.pos_mul = 1;
+  d.pos_oth = 0;
+  d.oth_ext[0] = d.oth_ext[1] = 1;
+}
+
+static void finish_lines(PassDesc& d) {
+  long long n = (long long)d.P * d.C;
+  for (int a = 0; a < d.n_oth; ++a) n *= d.oth_ext[a];
+  d.nlines = n;
+}
+
+// Spectrum strides for [pair][F_0..F_{D-1}][C].
+struct SpecStrides {
+  long long st[3];
+  long long pst;
+};
+static SpecStrides spec_strides(const Geo& g, int C) {
+  SpecStrides s;
+  long long acc = C;
+  for (int d = g.D - 1; d >= 0; --d) { s.st[d] = acc; acc *= g.F[d]; }
+  s.pst = acc;
+  return s;
+}
+
+struct Pairing {
+  int P;       // number of complex signals per channel
+  int B;       // number of real items
+  int half;    // item p pairs with p + half
+  int packed;
+};
+static Pairing pairing(int B, bool pack) {
+  Pairing pr;
+  pr.B = B;
+  pr.packed = pack ? 1 : 0;
+  pr.half = pack ? (B + 1) / 2 : B;
+  pr.P = pr.half;
+  return pr;
+}
+
+static void set_real_in(PassDesc& d, const RealView& v, const Pairing& pr) {
+  d.rin = v.ptr;
+  d.ri_bst = v.bst;
+  d.ri_cst = v.cst;
+  d.B = pr.B;
+  d.half = pr.half;
+  d.packed = pr.packed;
+}
+static void set_real_out(PassDesc& d, const RealView& v, const Pairing& pr) {
+  d.rout = const_cast<void*>(v.ptr);
+  d.ro_bst = v.bst;
+  d.ro_cst = v.cst;
+  d.B = pr.B;
+  d.half = pr.half;
+  d.packed = pr.packed;
+}
+
+// Forward transform of a real source (extents E, placed at offsets off) into the
+// full spectrum S. Channels [0, C) of the view.
+static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pairing& pr, const int* E,
+                     const int* off, float2* S, cudaStream_t st) {
+  const SpecStrides ss = spec_strides(g, C);
+  if (g.four) {
+    // pass A: along n_a (stride Fb*C in S), lines (p, n_b, c); twiddle e^{-2 pi i k_a n_b / F}
+    PassDesc a;
+    base_desc(a, g.Fa, -1.f, pr.P, C);
+    a.n_oth = 1;
+    a.oth_ext[0] = g.Fb;
+    a.cout = S;
+    a.co_pst = ss.pst;
+    a.co_tst = (long long)g.Fb * C;
+    a.co_ost[0] = C;
+    set_real_in(a, src, pr);
+    a.ri_tst = src.sst[0];
+    a.pos_mul = g.Fb;
+    a.pos_oth = 1;
+    a.in_off = off[0];
+    a.n_in = E[0];
+    a.out_lo = 0;
+    a.n_out = g.Fa;
+    a.tw_logF = ilog2(g.F[0]);
+    a.load_t_fastest = 0;
+    a.store_t_fastest = 0;
+    finish_lines(a);
+    HY_TRY(launch_pass(a, IN_REAL, OUT_CPLX, tdt, HYFFT_F32, st));
+    // pass B: along n_b (stride C), lines (p, k_a, c)
+    PassDesc b;
+    base_desc(b, g.Fb, -1.f, pr.P, C);
+    b.n_oth = 1;
+    b.oth_ext[0] = g.Fa;
+    b.cin = S;
+    b.cout = S;
+    b.ci_pst = b.co_pst = ss.pst;
+    b.ci_tst = b.co_tst = C;
+    b.ci_ost[0] = b.co_ost[0] = (long long)g.Fb * C;
+    b.in_off = 0;
+    b.n_in = g.Fb;
+    b.out_lo = 0;
+    b.n_out = g.Fb;
+    finish_lines(b);
+    return launch_pass(b, IN_CPLX, OUT_CPLX, tdt, HYFFT_F32, st);
+  }
+  const int D = g.D;
+  // last axis from the real source
+  {
+    PassDesc a;
+    base_desc(a, g.F[D - 1], -1.f, pr.P, C);
+    a.n_oth = D - 1;
+    for (int e = 0; e < D - 1; ++e) {
+      a.oth_ext[e] = E[e];
+      a.co_ost[e] = ss.st[e];
+      a.ri_ost[e] = src.sst[e];
+    }
+    a.cout = S;
+    a.co_pst = ss.pst;
+    a.co_tst = ss.st[D - 1];
+    set_real_in(a, src, pr);
+    a.ri_tst = src.sst[D - 1];
+    a.in_off = off[D - 1];
+    a.n_in = E[D - 1];
+    a.out_lo = 0;
+    a.n_out = g.F[D - 1];
+    a.load_t_fastest = (src.sst[D - 1] == 1) ? 1 : 0;
+    a.store_t_fastest = 0;
+    finish_lines(a);
+    HY_TRY(launch_pass(a, IN_REAL, OUT_CPLX, tdt, HYFFT_F32, st));
+  }
+  for (int d = D - 2; d >= 0; --d) {
+    PassDesc a;
+    base_desc(a, g.F[d], -1.f, pr.P, C);
+    a.n_oth = D - 1;
+    int j = 0;
+    for (int e = 0; e < D; ++e) {
+      if (e == d) continue;
+      a.oth_ext[j] = e < d ? E[e] : g.F[e];
+      a.ci_ost[j] = a.co_ost[j] = ss.st[e];
+      ++j;
+    }
+    a.cin = S;
+    a.cout = S;
+    a.ci_pst = a.co_pst = ss.pst;
+    a.ci_tst = a.co_tst = ss.st[d];
+    a.in_off = off[d];
+    a.n_in = E[d];
+    a.out_lo = 0;
+    a.n_out = g.F[d];
+    finish_lines(a);
+    HY_TRY(launch_pass(a, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
+  }
+  return HYFFT_OK;
+}
+
+struct Epilogue {
+  int mode = OUT_REAL;     // OUT_REAL or OUT_REAL_SKIP
+  const void* skip = nullptr;
+  const float* Dv = nullptr;
+};
+
+// Inverse transform of the full spectrum S into a real destination, keeping the
+// window [lo[d], lo[d] + cnt[d]) of every axis.
+static int inv_chain(const Geo& g, int C, float2* S, const RealView& dst, int tdt, const Pairing& pr, const int* lo,
+                     const int* cnt, const Epilogue& ep, cudaStream_t st) {
+  const SpecStrides ss = spec_strides(g, C);
+  if (g.four) {
+    PassDesc b;  // along k_b with twiddle e^{+2 pi i n_b k_a / F}
+    base_desc(b, g.Fb, +1.f, pr.P, C);
+    b.n_oth = 1;
+    b.oth_ext[0] = g.Fa;
+    b.cin = S;
+    b.cout = S;
+    b.ci_pst = b.co_pst = ss.pst;
+    b.ci_tst = b.co_tst = C;
+    b.ci_ost[0] = b.co_ost[0] = (long long)g.Fb * C;
+    b.in_off = 0;
+    b.n_in = g.Fb;
+    b.out_lo = 0;
+    b.n_out = g.Fb;
+    b.tw_logF = ilog2(g.F[0]);
+    finish_lines(b);
+    HY_TRY(launch_pass(b, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
+    PassDesc a;  // along k_a into the real output, position n_a * Fb + n_b
+    base_desc(a, g.Fa, +1.f, pr.P, C);
+    a.n_oth = 1;
+    a.oth_ext[0] = g.Fb;
+    a.cin = S;
+    a.ci_pst = ss.pst;
+    a.ci_tst = (long long)g.Fb * C;
+    a.ci_ost[0] = C;
+    a.in_off = 0;
+    a.n_in = g.Fa;
+    set_real_out(a, dst, pr);
+    a.ro_tst = dst.sst[0];
+    a.pos_mul = g.Fb;
+    a.pos_oth = 1;
+    a.out_lo = lo[0];
+    a.n_out = cnt[0];
+    a.skip = ep.skip;
+    a.Dv = ep.Dv;
+    a.load_t_fastest = 0;
+    a.store_t_fastest = 0;
+    finish_lines(a);
+    return launch_pass(a, IN_CPLX, ep.mode, HYFFT_F32, tdt, st);
+  }
+  const int D = g.D;
+  for (int d = 0; d < D - 1; ++d) {
+    PassDesc a;
+    base_desc(a, g.F[d], +1.f, pr.P, C);
+    a.n_oth = D - 1;
+    int j = 0;
+    for (int e = 0; e < D; ++e) {
+      if (e == d) continue;
+      a.oth_ext[j] = e < d ? cnt[e] : g.F[e];
+      a.ci_ost[j] = a.co_ost[j] = ss.st[e];
+      ++j;
+    }
+    a.cin = S;
+    a.cout = S;
+    a.ci_pst = a.co_pst = ss.pst;
+    a.ci_tst = a.co_tst = ss.st[d];
+    a.in_off = 0;
+    a.n_in = g.F[d];
+    a.out_lo = lo[d];
+    a.n_out = cnt[d];
+    finish_lines(a);
+    HY_TRY(launch_pass(a, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
+  }
+  PassDesc a;
+  base_desc(a, g.F[D - 1], +1.f, pr.P, C);
+  a.n_oth = D - 1;
+  for (int e = 0; e < D - 1; ++e) {
+    a.oth_ext[e] = cnt[e];
+    a.ci_ost[e] = ss.st[e];
+    a.ro_ost[e] = dst.sst[e];
+  }
+  a.cin = S;
+  a.ci_pst = ss.pst;
+  a.ci_tst = ss.st[D - 1];
+  a.in_off = 0;
+  a.n_in = g.F[D - 1];
+  set_real_out(a, dst, pr);
+  a.ro_tst = dst.sst[D - 1];
+  a.out_lo = lo[D - 1];
+  a.n_out = cnt[D - 1];
+  a.skip = ep.skip;
+  a.Dv = ep.Dv;
+  a.load_t_fastest = 0;
+  a.store_t_fastest = (dst.sst[D - 1] == 1) ? 1 : 0;
+  finish_lines(a);
+  return launch_pass(a, IN_CPLX, ep.mode, HYFFT_F32, tdt, st);
+}
+
+static int grid_for(long long n, int threads = 256) {
+  long long g = (n + threads - 1) / threads;
+  return (int)std::max<long long>(1, std::min<long long>(g, 148LL * 16));
+}
+
+// ------------------------------------------------------------------ conv plan
+struct ConvPlan {
+  Geo g;
+  int B = 0, C = 0, kB = 1, dt = HYFFT_F32, layout = HYFFT_LAYOUT_BHL;
+  bool shared = true;
+  Pairing px, pk;
+  int Cc = 0;  // channels per chunk
+  long long spec_x_bytes_per_ch = 0, spec_k_bytes_per_ch = 0;
+};
+
+static size_t ws_budget() {
+  const char* e = getenv("HYFFT_WS_BUDGET_MB");
+  long long mb = e ? atoll(e) : 16384;
+  if (mb < 64) mb = 64;
+  return (size_t)mb << 20;
+}
+
+static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p) {
+  if (!d) return fail(HYFFT_ERR_INVALID, "null descriptor");
+  HY_TRY(make_geo(d->ndim, d->n, d->k, d->causal, p.g));
+  if (d->batch < 1 || d->channels < 1) return fail(HYFFT_ERR_INVALID, "batch and channels must be positive");
+  if (d->kernel_batch != 1 && d->kernel_batch != d->batch)
+    return fail(HYFFT_ERR_INVALID, "kernel_batch must be 1 or batch (%d), got %d", d->batch, d->kernel_batch);
+  if (d->dtype < HYFFT_F32 || d->dtype > HYFFT_F16) return fail(HYFFT_ERR_INVALID, "bad dtype");
+  if (d->layout != HYFFT_LAYOUT_BHL && d->layout != HYFFT_LAYOUT_BLH) return fail(HYFFT_ERR_INVALID, "bad layout");
+  p.B = d->batch;
+  p.C = d->channels;
+  p.kB = d->kernel_batch;
+  p.dt = d->dtype;
+  p.layout = d->layout;
+  p.shared = (p.kB == 1);
+  p.px = pairing(p.B, p.shared);
+  p.pk = pairing(p.kB, false);
+  p.spec_x_bytes_per_ch = (long long)p.px.P * p.g.vol_F * 8;
+  p.spec_k_bytes_per_ch = (long long)p.pk.P * p.g.vol_F * 8;
+  // bwd holds 2 activation spectra + 2 kernel spectra per channel
+  const long long per_ch = 2 * (p.spec_x_bytes_per_ch + p.spec_k_bytes_per_ch);
+  long long cc = (long long)(ws_budget() / (size_t)std::max<long long>(per_ch, 1));
+  p.Cc = (int)std::max<long long>(1, std::min<long long>(cc, p.C));
+  return HYFFT_OK;
+}
+
+static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static void conv_ws_sizes(const ConvPlan& p, size_t& fwd, size_t& bwd) {
+  const size_t sx = align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
+  const size_t sk = align_up((size_t)p.spec_k_bytes_per_ch * p.Cc);
+  const size_t dvec = align_up((size_t)p.C * 4);
+  fwd = sx + sk + dvec;
+  bwd = 2 * sx + 2 * sk + dvec;
+}
+
+template <typename T>
+__global__ void to_float_kernel(const T* __restrict__ s, float* __restrict__ d, int n) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) d[i] = DT<T>::load(s + i);
+}
+
+static int to_float(const void* src, int dt, float* dst, int n, cudaStream_t st) {
+  const int gr = (n + 255) / 256;
+  if (dt == HYFFT_F32) to_float_kernel<float><<<gr, 256, 0, st>>>((const float*)src, dst, n);
+  else if (dt == HYFFT_BF16) to_float_kernel<__nv_bfloat16><<<gr, 256, 0, st>>>((const __nv_bfloat16*)src, dst, n);
+  else to_float_kernel<__half><<<gr, 256, 0, st>>>((const __half*)src, dst, n);
+  return check_launch("to_float_kernel");
+}
+
+// One forward convolution over channels [c0, c0 + Cc) of already-prepared views.
+static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView& xv, const RealView& kv,
+                              const float* Dfull, const RealView& yv, float2* S, float2* Kh, cudaStream_t st) {
+  const int eb = dtype_bytes(p.dt);
+  const RealView xc = offset_channels(xv, c0, eb);
+  const RealView kc = offset_channels(kv, c0, 4);
+  const RealView yc = offset_channels(yv, c0, eb);
+  const int zero[3] = {0, 0, 0};
+  HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+  HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S, st));
+  const long long per_pair = p.g.vol_F * Cc;
+  spec_mul_kernel<<<grid_for(per_pair * p.px.P), 256, 0, st>>>(S, Kh, per_pair, p.px.P, p.shared ? 1 : 0);
+  HY_TRY(check_launch("spec_mul_kernel"));
+  Epilogue ep;
+  if (Dfull) {
+    ep.mode = OUT_REAL_SKIP;
+    ep.skip = xc.ptr;
+    ep.Dv = Dfull + c0;
+  }
+  return inv_chain(p.g, Cc, S, yc, p.dt, p.px, p.g.crop, p.g.N, ep, st);
+}
+
+static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView& xv, const RealView& kv,
+                               const float* Dfull, const RealView& dyv, const RealView& dxv, const RealView& dkv,
+                               float2* S1, float2* S2, float2* Kh, float2* dKh, cudaStream_t st) {
+  const int eb = dtype_bytes(p.dt);
+  const RealView xc = offset_channels(xv, c0, eb);
+  const RealView kc = offset_channels(kv, c0, 4);
+  const RealView dyc = offset_channels(dyv, c0, eb);
+  const int zero[3] = {0, 0, 0};
+  HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+  HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S1, st));
+  HY_TRY(fwd_chain(p.g, Cc, dyc, p.dt, p.px, p.g.N, p.g.crop, S2, st));
+  const long long per_pair = p.g.vol_F * Cc;
+  spec_bwd_kernel<<<grid_for(per_pair), 256, 0, st>>>(S2, S1, Kh, dKh, per_pair, p.px.P, p.shared ? 1 : 0);
+  HY_TRY(check_launch("spec_bwd_kernel"));
+  if (dxv.ptr) {
+    const RealView dxc = offset_channels(dxv, c0, eb);
+    Epilogue ep;
+    if (Dfull) {
+      ep.mode = OUT_REAL_SKIP;
+      ep.skip = dyc.ptr;
+      ep.Dv = Dfull + c0;
+    }
+    HY_TRY(inv_chain(p.g, Cc, S2, dxc, p.dt, p.px, zero, p.g.N, ep, st));
+  }
+  if (dkv.ptr) {
+    const RealView dkc = offset_channels(dkv, c0, 4);
+    Epilogue ep;
+    HY_TRY(inv_chain(p.g, Cc, dKh, dkc, HYFFT_F32, p.pk, zero, p.g.K, ep, st));
+  }
+  return HYFFT_OK;
+}
+
+static int run_dshortcut(int dt, int layout, const void* dy, const void* x, float* out, int B, int C, long long S,
+                         cudaStream_t st) {
+  const int blh = layout == HYFFT_LAYOUT_BLH;
+  const int gr = (C + 31) / 32;
+  if (dt == HYFFT_F32) dshortcut_kernel<float><<<gr, 256, 0, st>>>((const float*)dy, (const float*)x, out, B, C, S, blh);
+  else if (dt == HYFFT_BF16)
+    dshortcut_kernel<__nv_bfloat16><<<gr, 256, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, out, B, C, S, blh);
+  else dshortcut_kernel<__half><<<gr, 256, 0, st>>>((const __half*)dy, (const __half*)x, out, B, C, S, blh);
+  return check_launch("dshortcut_kernel");
+}
+
+}  // namespace hyfft
+
+using namespace hyfft;
+
+// ===================================================================== C ABI
+extern "C" {
+
+const char* hyfft_last_error(void) { return g_last_error.c_str(); }
+const char* hyfft_version(void) { return "hyfft 0.1 (sm_100a)"; }
+long long hyfft_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int hyfft_conv_workspace_size(const hyfft_conv_desc* d, size_t* fwd_bytes, size_t* bwd_bytes) {
+  ConvPlan p;
+  HY_TRY(make_conv_plan(d, p));
+  size_t f, b;
+  conv_ws_sizes(p, f, b);
+  if (fwd_bytes) *fwd_bytes = f;
+  if (bwd_bytes) *bwd_bytes = b;
+  return HYFFT_OK;
+}
+
+int hyfft_conv_forward(const hyfft_conv_desc* d, const void* x, const float* kernel, const void* shortcut, void* y,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  ConvPlan p;
+  HY_TRY(make_conv_plan(d, p));
+  if (!x || !kernel || !y) return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  size_t need, nb;
+  conv_ws_sizes(p, need, nb);
+  if (!workspace || workspace_bytes < need) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, need);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* w = (char*)workspace;
+  float2* S = (float2*)w;
+  w += align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
+  float2* Kh = (float2*)w;
+  w += align_up((size_t)p.spec_k_bytes_per_ch * p.Cc);
+  float* Dv = (float*)w;
+  if (shortcut) HY_TRY(to_float(shortcut, p.dt, Dv, p.C, st));
+  const RealView xv = real_view(x, p.layout, p.B, p.C, p.g.N, p.g.D);
+  const RealView kv = real_view(kernel, p.layout, p.kB, p.C, p.g.K, p.g.D);
+  const RealView yv = real_view(y, p.layout, p.B, p.C, p.g.N, p.g.D);
+  for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
+    const int cc = std::min(p.Cc, p.C - c0);
+    HY_TRY(conv_forward_chunk(p, c0, cc, xv, kv, shortcut ? Dv : nullptr, yv, S, Kh, st));
+  }
+  return HYFFT_OK;
+}
+
+int hyfft_conv_backward(const hyfft_conv_desc* d, const void* x, const float* kernel, const void* shortcut,
+                        const void* dy, void* dx, float* dkernel, float* dshortcut, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  ConvPlan p;
+  HY_TRY(make_conv_plan(d, p));
+  if (!x || !kernel || !dy) return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  size_t nf, need;
+  conv_ws_sizes(p, nf, need);
+  if (!workspace || workspace_bytes < need) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, need);
+  cudaStream_t st = (cudaStream_t)stream;
+  char* w = (char*)workspace;
+  const size_t sx = align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
+  const size_t sk = align_up((size_t)p.spec_k_bytes_per_ch * p.Cc);
+  float2* S1 = (float2*)w;
+  float2* S2 = (float2*)(w + sx);
+  float2* Kh = (float2*)(w + 2 * sx);
+  float2* dKh = (float2*)(w + 2 * sx + sk);
+  float* Dv = (float*)(w + 2 * sx + 2 * sk);
+  if (shortcut) HY_TRY(to_float(shortcut, p.dt, Dv, p.C, st));
+  const RealView xv = real_view(x, p.layout, p.B, p.C, p.g.N, p.g.D);
+  const RealView kv = real_view(kernel, p.layout, p.kB, p.C, p.g.K, p.g.D);
+  const RealView dyv = real_view(dy, p.layout, p.B, p.C, p.g.N, p.g.D);
+  const RealView dxv = real_view(dx, p.layout, p.B, p.C, p.g.N, p.g.D);
+  const RealView dkv = real_view(dkernel, p.layout, p.kB, p.C, p.g.K, p.g.D);
+  for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
+    const int cc = std::min(p.Cc, p.C - c0);
+    HY_TRY(conv_backward_chunk(p, c0, cc, xv, kv, shortcut ? Dv : nullptr, dyv, dxv, dkv, S1, S2, Kh, dKh, st));
+  }
+  if (shortcut && dshortcut) {
+    long long S = 1;
+    for (int i = 0; i < p.g.D; ++i) S *= p.g.N[i];
+    HY_TRY(run_dshortcut(p.dt, p.layout, dy, x, dshortcut, p.B, p.C, S, st));
+  }
+  return HYFFT_OK;
+}
+
+}  // extern "C"
+
+// ===================================================================== Hyena (general path)
+namespace hyfft {
+
+struct HyenaPlan {
+  hyfft_hyena_desc d;
+  ConvPlan cp;          // the long conv on z (channels-last contiguous [B, *S, C])
+  StencilGeom sg;
+  long long Ntot = 1;   // prod n
+  long long E = 0;      // B * Ntot * C
+  int eb = 2;
+};
+
+static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
+  if (!d) return fail(HYFFT_ERR_INVALID, "null descriptor");
+  h.d = *d;
+  hyfft_conv_desc cd;
+  memset(&cd, 0, sizeof(cd));
+  cd.ndim = d->ndim;
+  cd.batch = d->batch;
+  cd.channels = d->channels;
+  for (int i = 0; i < 3; ++i) {
+    cd.n[i] = i < d->ndim ? d->n[i] : 1;
+    cd.k[i] = i < d->ndim ? d->k[i] : 1;
+  }
+  cd.kernel_batch = 1;
+  cd.causal = d->causal;
+  cd.dtype = d->dtype;
+  cd.layout = HYFFT_LAYOUT_BLH;
+  HY_TRY(make_conv_plan(&cd, h.cp));
+  if (d->gate1 < 0 || d->gate1 > 2 || d->gate2 < 0 || d->gate2 > 2) return fail(HYFFT_ERR_INVALID, "bad gate");
+  StencilGeom& g = h.sg;
+  g.nd = d->ndim;
+  g.has_conv = d->short_k[0] > 0 ? 1 : 0;
+  g.has_bias = (g.has_conv && d->short_bias) ? 1 : 0;
+  g.ntaps = 1;
+  h.Ntot = 1;
+  for (int i = 0; i < 3; ++i) {
+    const bool used = i < d->ndim;
+    g.n[i] = used ? d->n[i] : 1;
+    g.k[i] = (used && g.has_conv) ? d->short_k[i] : 1;
+    if (g.k[i] < 1) return fail(HYFFT_ERR_INVALID, "short conv extents must be positive");
+    if (d->short_causal && g.has_conv) {
+      if (d->ndim != 1) return fail(HYFFT_ERR_INVALID, "causal short conv is 1D only");
+      g.off[i] = g.k[i] - 1;
+    } else {
+      g.off[i] = (g.k[i] - 1) / 2;
+    }
+    g.ntaps *= g.k[i];
+    h.Ntot *= g.n[i];
+  }
+  if (g.ntaps > 27) return fail(HYFFT_ERR_UNSUPPORTED, "short conv with more than 27 taps");
+  h.E = (long long)d->batch * h.Ntot * d->channels;
+  h.eb = dtype_bytes(d->dtype);
+  if (d->in_pos_stride < d->channels || d->out_pos_stride < d->channels)
+    return fail(HYFFT_ERR_INVALID, "position strides must be >= channels");
+  return HYFFT_OK;
+}
+
+static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& saved) {
+  size_t cf, cb;
+  conv_ws_sizes(h.cp, cf, cb);
+  const size_t act = align_up((size_t)h.E * h.eb);
+  const size_t f32 = align_up((size_t)h.E * 4);
+  saved = 5 * act;                 // q', k', v', z, h
+  fwd = cf + align_up((size_t)h.d.channels * 4);
+  bwd = cb + 2 * act + 3 * f32 + align_up((size_t)h.d.channels * 4);
+}
+
+template <typename T>
+static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt, const float* D,
+                           const float* sw, const float* sb, T* y, char* saved, char* ws, cudaStream_t st) {
+  const hyfft_hyena_desc& d = h.d;
+  const size_t act = align_up((size_t)h.E * h.eb);
+  T* qs = (T*)(saved);
+  T* ks = (T*)(saved + act);
+  T* vs = (T*)(saved + 2 * act);
+  T* z = (T*)(saved + 3 * act);
+  T* hb = (T*)(saved + 4 * act);
+  hyena_pre_fwd_kernel<T><<<grid_for(h.E), 256, 0, st>>>(q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch,
+                                                         d.channels, sw, sb, d.gate1, qs, ks, vs, z);
+  HY_TRY(check_launch("hyena_pre_fwd_kernel"));
+  // long conv with D-skip: h = round(conv(z)) + round(D * z)
+  const ConvPlan& p = h.cp;
+  size_t cf, cb;
+  conv_ws_sizes(p, cf, cb);
+  float2* S = (float2*)ws;
+  float2* Kh = (float2*)(ws + align_up((size_t)p.spec_x_bytes_per_ch * p.Cc));
+  const RealView zv = real_view(z, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
+  const RealView kv = real_view(filt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
+  const RealView hv = real_view(hb, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
+  for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
+    const int cc = std::min(p.Cc, p.C - c0);
+    HY_TRY(conv_forward_chunk(p, c0, cc, zv, kv, D, hv, S, Kh, st));
+  }
+  hyena_post_fwd_kernel<T><<<grid_for(h.E), 256, 0, st>>>(hb, vs, d.gate2, h.Ntot, d.batch, d.channels, y,
+                                                          d.out_batch_stride, d.out_pos_stride);
+  return check_launch("hyena_post_fwd_kernel");
+}
+
+template <typename T>
+static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt,
+                            const float* D, const float* sw, const T* dy, T* dq, T* dk, T* dv, float* dfilt,
+                            float* dD, float* dsw, float* dsb, const char* saved, char* ws, cudaStream_t st) {
+  const hyfft_hyena_desc& d = h.d;
+  const size_t act = align_up((size_t)h.E * h.eb);
+  const size_t f32 = align_up((size_t)h.E * 4);
+  const T* qs = (const T*)(saved);
+  const T* ks = (const T*)(saved + act);
+  const T* vs = (const T*)(saved + 2 * act);
+  const T* z = (const T*)(saved + 3 * act);
+  const T* hb = (const T*)(saved + 4 * act);
+  const ConvPlan& p = h.cp;
+  size_t cf, cb;
+  conv_ws_sizes(p, cf, cb);
+  char* w = ws + cb;
+  T* dh = (T*)w;
+  w += act;
+  T* dz = (T*)w;
+  w += act;
+  float* dvp = (float*)w;
+  w += f32;
+  float* dqp = (float*)w;
+  w += f32;
+  float* dkp = (float*)w;
+  hyena_bwd_gate2_kernel<T><<<grid_for(h.E), 256, 0, st>>>(dy, d.out_batch_stride, d.out_pos_stride, hb, vs, d.gate2,
+                                                           h.Ntot, d.batch, d.channels, dh, dvp);
+  HY_TRY(check_launch("hyena_bwd_gate2_kernel"));
+  // long conv backward: dz = convT(dh) + D*dh, dfilt, dD
+  {
+    const size_t sx = align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
+    const size_t sk = align_up((size_t)p.spec_k_bytes_per_ch * p.Cc);
+    float2* S1 = (float2*)ws;
+    float2* S2 = (float2*)(ws + sx);
+    float2* Kh = (float2*)(ws + 2 * sx);
+    float2* dKh = (float2*)(ws + 2 * sx + sk);
+    const RealView zv = real_view(z, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
+    const RealView kv = real_view(filt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
+    const RealView dhv = real_view(dh, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
+    const RealView dzv = real_view(dz, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
+    const RealView dkv = real_view(dfilt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
+    for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
+      const int cc = std::min(p.Cc, p.C - c0);
+      HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, Kh, dKh, st));
+    }
+    if (dD) {
+      dshortcut_kernel<T><<<(d.channels + 31) / 32, 256, 0, st>>>(dh, z, dD, d.batch, d.channels, h.Ntot, 1);
+      HY_TRY(check_launch("dshortcut_kernel"));
+    }
+  }
+  hyena_bwd_gate1_kernel<T><<<grid_for(h.E), 256, 0, st>>>(dz, qs, ks, d.gate1, h.E, dqp, dkp);
+  HY_TRY(check_launch("hyena_bwd_gate1_kernel"));
+  hyena_short_dgrad_kernel<T><<<grid_for(h.E), 256, 0, st>>>(dqp, dkp, dvp, h.sg, d.batch, d.channels, sw, dq, dk, dv,
+                                                             d.out_batch_stride, d.out_pos_stride);
+  HY_TRY(check_launch("hyena_short_dgrad_kernel"));
+  if (h.sg.has_conv && dsw) {
+    cudaMemsetAsync(dsw, 0, sizeof(float) * 3 * (size_t)d.channels * h.sg.ntaps, st);
+    if (dsb && h.sg.has_bias) cudaMemsetAsync(dsb, 0, sizeof(float) * 3 * (size_t)d.channels, st);
+    const long long rows = (long long)d.batch * h.Ntot;
+    dim3 grid((3 * d.channels + 31) / 32, (unsigned)std::max<long long>(1, std::min<long long>(rows / 64, 64)));
+    hyena_short_wgrad_kernel<T><<<grid, 256, 0, st>>>(dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg,
+                                                      d.batch, d.channels, dsw, dsb);
+    HY_TRY(check_launch("hyena_short_wgrad_kernel"));
+  }
+  return HYFFT_OK;
+}
+
+}  // namespace hyfft
+
+extern "C" {
+
+int hyfft_hyena_workspace_size(const hyfft_hyena_desc* d, size_t* fwd_bytes, size_t* bwd_bytes, size_t* saved_bytes) {
+  HyenaPlan h;
+  HY_TRY(make_hyena_plan(d, h));
+  size_t f, b, s;
+  hyena_sizes(h, f, b, s);
+  if (fwd_bytes) *fwd_bytes = f;
+  if (bwd_bytes) *bwd_bytes = b;
+  if (saved_bytes) *saved_bytes = s;
+  return HYFFT_OK;
+}
+
+int hyfft_hyena_forward(const hyfft_hyena_desc* d, const void* q, const void* k, const void* v, const float* filt,
+                        const float* D, const float* short_w, const float* short_b, void* y, void* saved,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  HyenaPlan h;
+  HY_TRY(make_hyena_plan(d, h));
+  if (!q || !k || !v || !filt || !D || !y) return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  if (h.sg.has_conv && !short_w) return fail(HYFFT_ERR_INVALID, "short conv weight missing");
+  if (h.sg.has_bias && !short_b) return fail(HYFFT_ERR_INVALID, "short conv bias missing");
+  size_t f, b, s;
+  hyena_sizes(h, f, b, s);
+  if (!workspace || workspace_bytes < f) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, f);
+  if (!saved) return fail(HYFFT_ERR_WORKSPACE, "saved buffer of %zu bytes required", s);
+  cudaStream_t st = (cudaStream_t)stream;
+  if (d->dtype == HYFFT_BF16)
+    return hyena_forward_t<__nv_bfloat16>(h, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+                                          filt, D, short_w, short_b, (__nv_bfloat16*)y, (char*)saved, (char*)workspace, st);
+  if (d->dtype == HYFFT_F16)
+    return hyena_forward_t<__half>(h, (const __half*)q, (const __half*)k, (const __half*)v, filt, D, short_w, short_b,
+                                   (__half*)y, (char*)saved, (char*)workspace, st);
+  return hyena_forward_t<float>(h, (const float*)q, (const float*)k, (const float*)v, filt, D, short_w, short_b,
+                                (float*)y, (char*)saved, (char*)workspace, st);
+}
+
+int hyfft_hyena_backward(const hyfft_hyena_desc* d, const void* q, const void* k, const void* v, const float* filt,
+                         const float* D, const float* short_w, const float* short_b, const void* dy, void* dq, void* dk,
+                         void* dv, float* dfilt, float* dD, float* dshort_w, float* dshort_b, const void* saved,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  (void)short_b;
+  HyenaPlan h;
+  HY_TRY(make_hyena_plan(d, h));
+  if (!q || !k || !v || !filt || !D || !dy || !dq || !dk || !dv || !dfilt)
+    return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  if (h.sg.has_conv && !short_w) return fail(HYFFT_ERR_INVALID, "short conv weight missing");
+  size_t f, b, s;
+  hyena_sizes(h, f, b, s);
+  if (!workspace || workspace_bytes < b) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, b);
+  if (!saved) return fail(HYFFT_ERR_WORKSPACE, "saved buffer required");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (d->dtype == HYFFT_BF16)
+    return hyena_backward_t<__nv_bfloat16>(h, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+                                           filt, D, short_w, (const __nv_bfloat16*)dy, (__nv_bfloat16*)dq,
+                                           (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, dfilt, dD, dshort_w, dshort_b,
+                                           (const char*)saved, (char*)workspace, st);
+  if (d->dtype == HYFFT_F16)
+    return hyena_backward_t<__half>(h, (const __half*)q, (const __half*)k, (const __half*)v, filt, D, short_w,
+                                    (const __half*)dy, (__half*)dq, (__half*)dk, (__half*)dv, dfilt, dD, dshort_w,
+                                    dshort_b, (const char*)saved, (char*)workspace, st);
+  return hyena_backward_t<float>(h, (const float*)q, (const float*)k, (const float*)v, filt, D, short_w,
+                                 (const float*)dy, (float*)dq, (float*)dk, (float*)dv, dfilt, dD, dshort_w, dshort_b,
+                                 (const char*)saved, (char*)workspace, st);
+}
+
+}  // extern "C"

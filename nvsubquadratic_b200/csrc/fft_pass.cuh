@@ -1,0 +1,278 @@
+// Batched, strided, pruned 1D FFT pass over one axis of a multi-dimensional
+// array: the building block of the general (any-shape) FFT-conv engine.
+//
+// One CTA owns a tile of TL "lines" (1D signals along the FFT axis), stages
+// them in shared memory, runs a radix-4/2 Stockham FFT on all of them, and
+// writes them back. Loads and stores use independent thread mappings so that
+// both sides are coalesced: the spectrum buffers keep channels innermost
+// ([pair][axes...][C]), so consecutive lines of a tile are consecutive
+// channels; real activation tensors are read along whichever axis has unit
+// stride.
+//
+// Zero padding (input pruning), cropping (output pruning), the four-step
+// twiddle of long 1D transforms, packing two real batch items into one complex
+// signal (real part = item p, imaginary part = item p + half) and the
+// D-skip / dtype-rounding epilogue of the reference op are fused into the
+// load / store phases.
+#pragma once
+
+#include "common.cuh"
+
+namespace hyfft {
+
+constexpr int kPassThreads = 256;
+constexpr int kPassPoints = 4096;  // max TL * F per CTA (32 KB of float2)
+constexpr int kPassMaxLines = 128;
+
+enum InMode { IN_CPLX = 0, IN_REAL = 1 };
+enum OutMode { OUT_CPLX = 0, OUT_REAL = 1, OUT_REAL_SKIP = 2 };
+
+struct PassDesc {
+  int F, logF;   // FFT length along the line (power of two, <= kPassPoints)
+  float dir;     // -1 forward, +1 inverse
+  float scale;   // applied to every output element (1/F for inverse passes)
+  int TL;        // lines per CTA
+  int P, C;      // pair groups, channels
+  int n_oth;     // number of "other" axes (0..2) iterated per pair/channel
+  int oth_ext[2];
+  long long nlines;  // P * prod(oth_ext) * C
+
+  // complex buffers: element (p, oth, t, c) at p*c_pst + sum oth*c_ost + t*c_tst + c
+  const float2* cin;
+  float2* cout;
+  long long ci_pst, ci_tst, ci_ost[2];
+  long long co_pst, co_tst, co_ost[2];
+
+  // signal ranges: input holds positions [in_off, in_off+n_in); keep outputs
+  // at positions [out_lo, out_lo+n_out). For complex IO the position is the
+  // FFT index t and the buffer index is position - offset. For real IO the
+  // position is t*pos_mul + oth0*pos_oth (four-step) and the real index along
+  // the axis is position - offset.
+  int in_off, n_in, out_lo, n_out;
+  int pos_mul, pos_oth;
+
+  // post-FFT twiddle e^{dir * 2*pi*i * t * oth0 / 2^tw_logF} (four-step); 0 = off
+  int tw_logF;
+
+  // real tensors: element (b, c, pos, oth) at b*bst + c*cst + pos*tst + sum oth*ost
+  const void* rin;
+  long long ri_bst, ri_cst, ri_tst, ri_ost[2];
+  void* rout;
+  long long ro_bst, ro_cst, ro_tst, ro_ost[2];
+  const void* skip;  // same layout as rout (OUT_REAL_SKIP): y = round(round(v) + round(D*skip))
+  const void* Dv;    // [C] float32 skip scale (values of the activation dtype)
+  int B, half, packed;  // pair p -> items p and p+half (if packed and p+half < B)
+
+  int load_t_fastest;   // 1: load mapping walks t fastest (source contiguous along t)
+  int store_t_fastest;  // 1: store mapping walks t fastest
+};
+
+// Radix-4 / radix-2 butterflies (dir = -1 forward, +1 inverse).
+__device__ __forceinline__ void dft4(float2& a0, float2& a1, float2& a2, float2& a3, float dir) {
+  float2 t0 = cadd(a0, a2), t1 = csub(a0, a2), t2 = cadd(a1, a3), t3 = csub(a1, a3);
+  float2 jt3 = make_float2(-dir * t3.y, dir * t3.x);  // (dir * i) * t3
+  a0 = cadd(t0, t2);
+  a2 = csub(t0, t2);
+  a1 = cadd(t1, jt3);
+  a3 = csub(t1, jt3);
+}
+
+// In-place Stockham autosort FFT of TL lines of length F stored at
+// sm[l * ld + t]. All threads of the CTA participate; each stage stages the
+// butterfly inputs in registers between two barriers.
+__device__ void stockham_tile(float2* sm, int TL, int F, int logF, int ld, float dir) {
+  const int tid = threadIdx.x;
+  int Ns = 1, lgNs = 0;
+  int rem = logF;
+  while (rem > 0) {
+    if (rem >= 2) {
+      const int per_line = F >> 2;
+      const int total = TL * per_line;
+      const int lgpl = logF - 2;
+      float2 v[4][4];
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int item = tid + it * kPassThreads;
+        if (item < total) {
+          const int l = item >> lgpl, j = item & (per_line - 1);
+          const int k = j & (Ns - 1);
+          const float2* src = sm + l * ld + j;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            float2 a = src[r * per_line];
+            if (r > 0 && k > 0) {
+              // angle = dir * 2*pi * r*k / (Ns*4)
+              a = cmul(a, expipi(dir * (float)(2 * r * k) / (float)(Ns * 4)));
+            }
+            v[it][r] = a;
+          }
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int item = tid + it * kPassThreads;
+        if (item < total) {
+          const int l = item >> lgpl, j = item & (per_line - 1);
+          const int k = j & (Ns - 1);
+          dft4(v[it][0], v[it][1], v[it][2], v[it][3], dir);
+          float2* dst = sm + l * ld + ((j >> lgNs) << (lgNs + 2)) + k;
+#pragma unroll
+          for (int r = 0; r < 4; ++r) dst[r * Ns] = v[it][r];
+        }
+      }
+      __syncthreads();
+      Ns <<= 2;
+      lgNs += 2;
+      rem -= 2;
+    } else {
+      const int per_line = F >> 1;
+      const int total = TL * per_line;
+      const int lgpl = logF - 1;
+      float2 v[8][2];
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int item = tid + it * kPassThreads;
+        if (item < total) {
+          const int l = item >> lgpl, j = item & (per_line - 1);
+          const int k = j & (Ns - 1);
+          const float2* src = sm + l * ld + j;
+          float2 a0 = src[0], a1 = src[per_line];
+          if (k > 0) a1 = cmul(a1, expipi(dir * (float)(2 * k) / (float)(Ns * 2)));
+          v[it][0] = a0;
+          v[it][1] = a1;
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int item = tid + it * kPassThreads;
+        if (item < total) {
+          const int l = item >> lgpl, j = item & (per_line - 1);
+          const int k = j & (Ns - 1);
+          float2 a0 = v[it][0], a1 = v[it][1];
+          float2* dst = sm + l * ld + ((j >> lgNs) << (lgNs + 1)) + k;
+          dst[0] = cadd(a0, a1);
+          dst[Ns] = csub(a0, a1);
+        }
+      }
+      __syncthreads();
+      Ns <<= 1;
+      lgNs += 1;
+      rem -= 1;
+    }
+  }
+}
+
+struct LineInfo {
+  long long cin_base, cout_base;  // complex buffer base of the line (t = 0)
+  long long r_re_in, r_im_in;     // real input base of the two packed items (-1: none)
+  long long r_re_out, r_im_out;   // real output base
+  int pos0;                       // oth0 * pos_oth
+  int tw_m;                       // twiddle multiplier (oth0)
+  int c;                          // channel
+  int valid;
+};
+
+template <int IN_MODE, int OUT_MODE, typename TI, typename TO>
+__global__ void __launch_bounds__(kPassThreads) fft_pass_kernel(const PassDesc d) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  LineInfo* li = reinterpret_cast<LineInfo*>(smem_raw);
+  float2* sm = reinterpret_cast<float2*>(smem_raw + sizeof(LineInfo) * kPassMaxLines);
+  const int TL = d.TL, F = d.F;
+  const int ld = F + 1;  // pad the line stride to spread shared-memory banks
+  const long long line0 = (long long)blockIdx.x * TL;
+
+  // ---- per-line bookkeeping
+  for (int l = threadIdx.x; l < TL; l += blockDim.x) {
+    LineInfo L;
+    long long lid = line0 + l;
+    L.valid = lid < d.nlines;
+    if (!L.valid) lid = 0;
+    const int c = (int)(lid % d.C);
+    long long rest = lid / d.C;
+    int o[2] = {0, 0};
+    for (int a = d.n_oth - 1; a >= 0; --a) {
+      o[a] = (int)(rest % d.oth_ext[a]);
+      rest /= d.oth_ext[a];
+    }
+    const int p = (int)rest;
+    L.c = c;
+    L.cin_base = (long long)p * d.ci_pst + (long long)o[0] * d.ci_ost[0] + (long long)o[1] * d.ci_ost[1] + c;
+    L.cout_base = (long long)p * d.co_pst + (long long)o[0] * d.co_ost[0] + (long long)o[1] * d.co_ost[1] + c;
+    const int b_im = p + d.half;
+    const bool has_im = d.packed && b_im < d.B;
+    L.r_re_in = (long long)p * d.ri_bst + (long long)c * d.ri_cst + (long long)o[0] * d.ri_ost[0] + (long long)o[1] * d.ri_ost[1];
+    L.r_im_in = has_im ? L.r_re_in + (long long)d.half * d.ri_bst : -1;
+    L.r_re_out = (long long)p * d.ro_bst + (long long)c * d.ro_cst + (long long)o[0] * d.ro_ost[0] + (long long)o[1] * d.ro_ost[1];
+    L.r_im_out = has_im ? L.r_re_out + (long long)d.half * d.ro_bst : -1;
+    L.pos0 = o[0] * d.pos_oth;
+    L.tw_m = o[0];
+    li[l] = L;
+  }
+  __syncthreads();
+
+  // ---- load
+  const int npts = TL * F;
+  for (int e = threadIdx.x; e < npts; e += blockDim.x) {
+    int l, t;
+    if (d.load_t_fastest) { l = e / F; t = e - l * F; }
+    else { t = e / TL; l = e - t * TL; }
+    const LineInfo& L = li[l];
+    float2 val = make_float2(0.f, 0.f);
+    if (L.valid) {
+      if (IN_MODE == IN_CPLX) {
+        const int bi = t - d.in_off;
+        if (bi >= 0 && bi < d.n_in) val = d.cin[L.cin_base + (long long)bi * d.ci_tst];
+      } else {
+        const int pos = t * d.pos_mul + L.pos0 - d.in_off;
+        if (pos >= 0 && pos < d.n_in) {
+          const TI* src = reinterpret_cast<const TI*>(d.rin);
+          const long long off = (long long)pos * d.ri_tst;
+          val.x = DT<TI>::load(src + L.r_re_in + off);
+          if (L.r_im_in >= 0) val.y = DT<TI>::load(src + L.r_im_in + off);
+        }
+      }
+    }
+    sm[l * ld + t] = val;
+  }
+  __syncthreads();
+
+  stockham_tile(sm, TL, F, d.logF, ld, d.dir);
+
+  // ---- store
+  for (int e = threadIdx.x; e < npts; e += blockDim.x) {
+    int l, t;
+    if (d.store_t_fastest) { l = e / F; t = e - l * F; }
+    else { t = e / TL; l = e - t * TL; }
+    const LineInfo& L = li[l];
+    if (!L.valid) continue;
+    float2 val = cscale(sm[l * ld + t], d.scale);
+    if (d.tw_logF > 0 && L.tw_m != 0) {
+      // e^{dir*2*pi*i*t*m/2^tw_logF}; reduce the exponent mod 2^tw_logF first
+      const long long ex = ((long long)t * L.tw_m) & ((1LL << d.tw_logF) - 1);
+      val = cmul(val, expipi(d.dir * 2.0f * (float)((double)ex / (double)(1LL << d.tw_logF))));
+    }
+    if (OUT_MODE == OUT_CPLX) {
+      const int bo = t - d.out_lo;
+      if (bo >= 0 && bo < d.n_out) d.cout[L.cout_base + (long long)bo * d.co_tst] = val;
+    } else {
+      const int pos = t * d.pos_mul + L.pos0 - d.out_lo;
+      if (pos >= 0 && pos < d.n_out) {
+        TO* dst = reinterpret_cast<TO*>(d.rout);
+        const long long off = (long long)pos * d.ro_tst;
+        float re = DT<TO>::round(val.x), im = DT<TO>::round(val.y);
+        if (OUT_MODE == OUT_REAL_SKIP) {
+          const TO* sk = reinterpret_cast<const TO*>(d.skip);
+          const float Dc = reinterpret_cast<const float*>(d.Dv)[L.c];
+          re = re + DT<TO>::round(Dc * DT<TO>::load(sk + L.r_re_out + off));
+          if (L.r_im_out >= 0) im = im + DT<TO>::round(Dc * DT<TO>::load(sk + L.r_im_out + off));
+        }
+        DT<TO>::store(dst + L.r_re_out + off, re);
+        if (L.r_im_out >= 0) DT<TO>::store(dst + L.r_im_out + off, im);
+      }
+    }
+  }
+}
+
+}  // namespace hyfft

@@ -1,0 +1,112 @@
+"""CPU tests of the C-ABI library and the host-side logic (no GPU needed).
+
+* libhyfft.so loads and exports every entry point declared in include/hyfft.h
+* descriptor validation and workspace sizing (pure host code in the library)
+* the Python wrapper's remapping of the one reference case that wraps around
+  (causal kernel with K >= L + 2 at F = 2L), checked with the CPU oracle
+* the product path refuses CPU tensors (no silent fallback)
+"""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from nvsubquadratic_b200 import _lib
+from nvsubquadratic_b200 import fftconv as b2
+from oracle import fftconv as ofc
+from tests.conftest import ROOT, rel_l2
+
+
+def _declared_symbols() -> list[str]:
+    hdr = (Path(ROOT) / "include" / "hyfft.h").read_text()
+    return sorted(set(re.findall(r"HYFFT_API\s+(?:const\s+char\s*\*|int|long\s+long)\s+(hyfft_\w+)\s*\(", hdr)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = _declared_symbols()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), n
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with include/hyfft.h"
+    assert lib.hyfft_version().decode().startswith("hyfft")
+
+
+def _desc(**kw):
+    d = _lib.ConvDesc()
+    d.ndim = kw.get("ndim", 2)
+    d.batch = kw.get("B", 2)
+    d.channels = kw.get("C", 4)
+    n = kw.get("n", (14, 14, 1))
+    k = kw.get("k", (27, 27, 1))
+    for i in range(3):
+        d.n[i] = n[i]
+        d.k[i] = k[i]
+    d.kernel_batch = kw.get("kB", 1)
+    d.causal = kw.get("causal", 0)
+    d.dtype = kw.get("dtype", _lib.BF16)
+    d.layout = kw.get("layout", _lib.LAYOUT_BHL)
+    return d
+
+
+def _sizes(d):
+    f, b = ctypes.c_size_t(), ctypes.c_size_t()
+    rc = _lib.load().hyfft_conv_workspace_size(ctypes.byref(d), ctypes.byref(f), ctypes.byref(b))
+    return rc, f.value, b.value
+
+
+def test_workspace_sizes_vit_grid():
+    # 14x14 grid, 27x27 kernel -> F = 32x32 (>= 14 + 14 - 1 and >= 27), packed pairs: ceil(B/2)
+    rc, f, b = _sizes(_desc(B=32, C=768))
+    assert rc == _lib.HYFFT_OK
+    spec = 16 * 32 * 32 * 768 * 8
+    kspec = 1 * 32 * 32 * 768 * 8
+    assert f >= spec + kspec and b >= 2 * (spec + kspec)
+
+
+def test_descriptor_validation():
+    assert _sizes(_desc(k=(29, 27, 1)))[0] == _lib.HYFFT_ERR_INVALID  # K > 2N
+    assert _sizes(_desc(ndim=2, causal=1))[0] == _lib.HYFFT_ERR_INVALID  # causal is 1D only
+    assert _sizes(_desc(kB=3))[0] == _lib.HYFFT_ERR_INVALID  # kernel batch not in {1, B}
+    assert _sizes(_desc(ndim=4))[0] == _lib.HYFFT_ERR_INVALID
+    assert _sizes(_desc(dtype=7))[0] == _lib.HYFFT_ERR_INVALID
+    rc = _sizes(_desc(ndim=1, n=(16, 1, 1), k=(20, 1, 1), causal=1))[0]
+    assert rc == _lib.HYFFT_ERR_UNSUPPORTED  # wrap-around case is remapped in Python
+    assert b"wraps" in _lib.load().hyfft_last_error()
+    # four-step 1D (F = 2^21) is planned without error
+    assert _sizes(_desc(ndim=1, B=1, C=8, n=(1 << 20, 1, 1), k=(1 << 20, 1, 1), causal=1))[0] == _lib.HYFFT_OK
+
+
+def test_causal_alias_remap_matches_reference_wraparound():
+    g = torch.Generator().manual_seed(3)
+    for L, K in ((16, 29), (16, 32), (9, 12), (5, 10)):
+        x = torch.randn(2, 3, L, generator=g)
+        k = torch.randn(1, 3, K, generator=g)
+        ref = ofc.causal_fftconv1d_bhl(x, k)
+        k2 = b2._causal_alias_kernel(k, L, _lib.LAYOUT_BHL)
+        assert k2.shape[-1] == 2 * L - 1
+        got = ofc.fftconv1d_bhl(x, k2)
+        assert rel_l2(ref, got) < 1e-6
+        # channels-last form of the same remap
+        k2b = b2._causal_alias_kernel(k.movedim(1, -1), L, _lib.LAYOUT_BLH)
+        assert torch.equal(k2b.movedim(-1, 1), k2)
+
+
+def test_product_path_refuses_cpu_tensors():
+    x = torch.randn(2, 4, 16)
+    k = torch.randn(1, 4, 5)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        b2.fftconv1d_fp32_bhl(x, k)
+
+
+def test_reference_asserts_mirrored():
+    x = torch.randn(2, 4, 16, dtype=torch.bfloat16)
+    with pytest.raises(AssertionError, match=r"shortcut\.dtype"):
+        b2.fftconv1d_fp32_bhl(x, torch.randn(1, 4, 5), torch.randn(4))
+    with pytest.raises(AssertionError):
+        b2.fftconv2d_fp32_bhl(torch.randn(2, 4, 8, 8), torch.randn(1, 4, 17, 3))
+    with pytest.raises(AssertionError, match="Leading dimension"):
+        b2.fftconv2d_fp32_bhl(torch.randn(2, 4, 8, 8), torch.randn(3, 4, 3, 3))
