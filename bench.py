@@ -133,9 +133,12 @@ class ClockSampler:
              "clocks_event_reasons.sw_power_cap")
         try:
             self._proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 10 and self._proc.poll() is None:
+                time.sleep(0.02)  # wait for the first sample before the caller starts timing
         except (OSError, FileNotFoundError):
             self._proc = None
         return self
@@ -264,6 +267,12 @@ def run_gpu(args, cfg, rank, world, device):
         zero_grads()
         step()
     torch.cuda.synchronize()
+    if args.profile:
+        for _ in range(args.steps):
+            zero_grads()
+            step()
+        torch.cuda.synchronize()
+        return None
     n0 = _lib.launch_count()
     zero_grads()
     step()
@@ -292,7 +301,19 @@ def run_gpu(args, cfg, rank, world, device):
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
+    # estimate the step time to size an untimed, clock-sampled burn-in of ~0.5 s right before
+    # the timed steps (nvidia-smi samples every 50 ms; a short timed region alone gets 0-1 samples)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    est_ms = max(e0.elapsed_time(e1) / 3, 1e-3)
+    n_burn = int(min(20000, max(10, 500.0 / est_ms)))
     with ClockSampler(device.index if device.index is not None else 0) as clk:
+        for _ in range(n_burn):
+            graph.replay()
         for i in range(args.steps):
             flush.zero_()  # evict L2 between timed steps (outside the events)
             starts[i].record()
@@ -372,6 +393,8 @@ def main():
     ap.add_argument("--config", default="cfg1", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="run warmup + steps eager fwd+bwd steps and exit (for ncu captures)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
@@ -407,6 +430,10 @@ def main():
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
     res = run_gpu(args, cfg, rank, world, device)
+    if res is None:  # --profile
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
 
     # whole-job throughput: all ranks' elements / max-over-ranks time
     elems_rank = res["B"] * res["C"] * N

@@ -21,12 +21,14 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <string>
 
 #include "common.cuh"
 #include "fft_pass.cuh"
 #include "hyena_elem.cuh"
 #include "pointwise.cuh"
+#include "fused2d.h"
 
 namespace hyfft {
 
@@ -669,7 +671,10 @@ struct HyenaPlan {
   long long Ntot = 1;   // prod n
   long long E = 0;      // B * Ntot * C
   int eb = 2;
+  bool fused = false;   // single-pass fused kernels (fused.cu) apply
+  int SK = 0;
 };
+
 
 static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
   if (!d) return fail(HYFFT_ERR_INVALID, "null descriptor");
@@ -714,10 +719,26 @@ static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
   h.eb = dtype_bytes(d->dtype);
   if (d->in_pos_stride < d->channels || d->out_pos_stride < d->channels)
     return fail(HYFFT_ERR_INVALID, "position strides must be >= channels");
+  // fused single-pass path: 2D, "same" 3x3 (or no) short conv, 8-channel vectors
+  const bool sq3 = g.has_conv && g.k[0] == 3 && g.k[1] == 3 && !d->short_causal;
+  h.SK = sq3 ? 3 : 0;
+  if (!getenv("HYFFT_DISABLE_FUSED") && d->ndim == 2 && !d->causal && (sq3 || !g.has_conv) &&
+      (d->dtype == HYFFT_BF16 || d->dtype == HYFFT_F32) && d->channels % 8 == 0 && d->in_pos_stride % 8 == 0 &&
+      d->in_batch_stride % 8 == 0 && d->out_pos_stride % 8 == 0 && d->out_batch_stride % 8 == 0) {
+    h.fused = fused2d_dispatch(FOP_PROBE, d->dtype, h.cp.g.N[0], h.cp.g.N[1], h.cp.g.F[0], h.cp.g.F[1], h.SK,
+                               nullptr, nullptr) == HYFFT_OK;
+  }
   return HYFFT_OK;
 }
 
 static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& saved) {
+  if (h.fused) {
+    const size_t spec = align_up((size_t)h.d.channels * h.cp.g.vol_F * sizeof(float2));
+    saved = spec;  // filter spectrum, reused by the backward
+    fwd = 256;
+    bwd = spec;    // dK spectrum accumulator
+    return;
+  }
   size_t cf, cb;
   conv_ws_sizes(h.cp, cf, cb);
   const size_t act = align_up((size_t)h.E * h.eb);
@@ -825,6 +846,85 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
   return HYFFT_OK;
 }
 
+static bool aligned16(std::initializer_list<const void*> ps) {
+  for (const void* p : ps)
+    if (p && ((uintptr_t)p % 16) != 0) return false;
+  return true;
+}
+
+static void fused_params(const HyenaPlan& h, Fused2DParams& p, const void* q, const void* k, const void* v,
+                         const float* filt, const float* D, const float* sw, const float* sb) {
+  const hyfft_hyena_desc& d = h.d;
+  memset(&p, 0, sizeof(p));
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.in_bst = d.in_batch_stride;
+  p.in_pst = d.in_pos_stride;
+  p.out_bst = d.out_batch_stride;
+  p.out_pst = d.out_pos_stride;
+  p.w = sw;
+  p.bias = h.sg.has_bias ? sb : nullptr;
+  p.D = D;
+  p.filt = filt;
+  p.B = d.batch;
+  p.C = d.channels;
+  p.half = (d.batch + 1) / 2;
+  p.K0 = h.cp.g.K[0];
+  p.K1 = h.cp.g.K[1];
+  p.gate1 = d.gate1;
+  p.gate2 = d.gate2;
+}
+
+static int fused_op(const HyenaPlan& h, int op, const Fused2DParams& p, cudaStream_t st, const char* what) {
+  const Geo& g = h.cp.g;
+  const int rc = fused2d_dispatch(op, h.d.dtype, g.N[0], g.N[1], g.F[0], g.F[1], h.SK, &p, st);
+  if (rc != HYFFT_OK) return fail(rc == HYFFT_ERR_UNSUPPORTED ? rc : HYFFT_ERR_CUDA, "%s launch failed", what);
+  return HYFFT_OK;
+}
+
+static int hyena_fused_forward(const HyenaPlan& h, const void* q, const void* k, const void* v, const float* filt,
+                               const float* D, const float* sw, const float* sb, void* y, void* saved,
+                               cudaStream_t st) {
+  if (!aligned16({q, k, v, y, saved}))
+    return fail(HYFFT_ERR_INVALID, "q, k, v, y and saved must be 16-byte aligned");
+  Fused2DParams p;
+  fused_params(h, p, q, k, v, filt, D, sw, sb);
+  p.y = y;
+  p.Kbr = static_cast<float2*>(saved);
+  HY_TRY(fused_op(h, FOP_KSPEC, p, st, "kspec2d_kernel"));
+  return fused_op(h, FOP_FWD, p, st, "hyena2d_fwd_kernel");
+}
+
+static int hyena_fused_backward(const HyenaPlan& h, const void* q, const void* k, const void* v, const float* filt,
+                                const float* D, const float* sw, const float* sb, const void* dy, void* dq, void* dk,
+                                void* dv, float* dfilt, float* dD, float* dsw, float* dsb, const void* saved,
+                                void* ws, cudaStream_t st) {
+  if (!aligned16({q, k, v, dy, dq, dk, dv, saved, ws}))
+    return fail(HYFFT_ERR_INVALID, "q, k, v, dy, dq, dk, dv, saved and workspace must be 16-byte aligned");
+  if (!dD || (h.sg.has_conv && !dsw) || (h.sg.has_bias && !dsb))
+    return fail(HYFFT_ERR_INVALID, "dD, dshort_w (and dshort_b with a bias) are required");
+  const hyfft_hyena_desc& d = h.d;
+  Fused2DParams p;
+  fused_params(h, p, q, k, v, filt, D, sw, sb);
+  p.dy = dy;
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.Kbr = const_cast<float2*>(static_cast<const float2*>(saved));
+  p.G = static_cast<float2*>(ws);
+  p.dfilt = dfilt;
+  p.dD = dD;
+  p.dw = h.sg.has_conv ? dsw : nullptr;
+  p.db = h.sg.has_bias ? dsb : nullptr;
+  cudaMemsetAsync(p.G, 0, sizeof(float2) * (size_t)d.channels * h.cp.g.vol_F, st);
+  cudaMemsetAsync(dD, 0, sizeof(float) * d.channels, st);
+  if (p.dw) cudaMemsetAsync(p.dw, 0, sizeof(float) * 3 * (size_t)d.channels * h.sg.ntaps, st);
+  if (p.db) cudaMemsetAsync(p.db, 0, sizeof(float) * 3 * (size_t)d.channels, st);
+  HY_TRY(fused_op(h, FOP_BWD, p, st, "hyena2d_bwd_kernel"));
+  return fused_op(h, FOP_DFILT, p, st, "dfilt2d_kernel");
+}
+
 }  // namespace hyfft
 
 extern "C" {
@@ -853,6 +953,7 @@ int hyfft_hyena_forward(const hyfft_hyena_desc* d, const void* q, const void* k,
   if (!workspace || workspace_bytes < f) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, f);
   if (!saved) return fail(HYFFT_ERR_WORKSPACE, "saved buffer of %zu bytes required", s);
   cudaStream_t st = (cudaStream_t)stream;
+  if (h.fused) return hyena_fused_forward(h, q, k, v, filt, D, short_w, short_b, y, saved, st);
   if (d->dtype == HYFFT_BF16)
     return hyena_forward_t<__nv_bfloat16>(h, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
                                           filt, D, short_w, short_b, (__nv_bfloat16*)y, (char*)saved, (char*)workspace, st);
@@ -878,6 +979,9 @@ int hyfft_hyena_backward(const hyfft_hyena_desc* d, const void* q, const void* k
   if (!workspace || workspace_bytes < b) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, b);
   if (!saved) return fail(HYFFT_ERR_WORKSPACE, "saved buffer required");
   cudaStream_t st = (cudaStream_t)stream;
+  if (h.fused)
+    return hyena_fused_backward(h, q, k, v, filt, D, short_w, short_b, dy, dq, dk, dv, dfilt, dD, dshort_w, dshort_b,
+                                saved, workspace, st);
   if (d->dtype == HYFFT_BF16)
     return hyena_backward_t<__nv_bfloat16>(h, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
                                            filt, D, short_w, (const __nv_bfloat16*)dy, (__nv_bfloat16*)dq,

@@ -113,3 +113,43 @@ def test_hyena_vs_oracle_seeded(case):
         if a is None:
             continue
         assert rel_l2(a, b) <= tol, (name, rel_l2(a, b))
+
+
+FUSED_CASES = [
+    # B, C, S, K, short_k, gate1, gate2, dtype, bias
+    (32, 64, (14, 14), (14, 14), 3, "identity", "identity", torch.bfloat16, False),
+    (3, 16, (14, 14), (27, 27), 3, "silu", "sigmoid", torch.bfloat16, True),
+    (5, 8, (16, 16), (31, 31), 0, "sigmoid", "silu", torch.float32, False),
+    (2, 24, (8, 8), (15, 15), 3, "silu", "identity", torch.float32, True),
+]
+
+
+@pytest.mark.parametrize("case", FUSED_CASES, ids=[f"B{c[0]}-C{c[1]}-{c[2]}-{c[7]}" for c in FUSED_CASES])
+def test_fused_path_matches_general_engine(case, monkeypatch):
+    """The single-pass fused kernels and the multi-pass general engine agree."""
+    B, C, S, K, sk, g1, g2, dt, bias = case
+    g = torch.Generator().manual_seed(5)
+    qkv = torch.randn((B,) + S + (3 * C,), generator=g).to(dt)
+    filt = torch.randn((1, C) + K, generator=g) / (torch.tensor(K).prod() ** 0.5)
+    D = torch.randn(C, generator=g).to(dt)
+    sw = ((torch.rand((3 * C, 1, sk, sk), generator=g) * 2 - 1) / sk).to(dt) if sk else None
+    sb = (0.1 * torch.randn(3 * C, generator=g)).to(dt) if (bias and sk) else None
+    dy = torch.randn((B,) + S + (C,), generator=g).to(dt)
+    outs = []
+    for disable in ("", "1"):
+        if disable:
+            monkeypatch.setenv("HYFFT_DISABLE_FUSED", "1")
+        else:
+            monkeypatch.delenv("HYFFT_DISABLE_FUSED", raising=False)
+        qkv_d = qkv.cuda().requires_grad_(True)
+        rest = [t.cuda().requires_grad_(True) if t is not None else None for t in (filt, D, sw, sb)]
+        q, k, v = qkv_d.chunk(3, dim=-1)
+        y = _fused()(q, k, v, *rest, gate1=g1, gate2=g2)
+        y.backward(dy.cuda())
+        torch.cuda.synchronize()
+        outs.append([y, qkv_d.grad] + [t.grad if t is not None else None for t in rest])
+    tol = 2e-2 if dt == torch.bfloat16 else 1e-5
+    for name, a, b in zip(("y", "dqkv", "dfilt", "dD", "dsw", "dsb"), outs[1], outs[0]):
+        if a is None:
+            continue
+        assert rel_l2(a, b) <= tol, (name, rel_l2(a, b))
