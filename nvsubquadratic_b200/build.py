@@ -23,7 +23,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libhyfft.so"
 STAMP = PKG / ".libhyfft.stamp"
 
-SOURCES = ["engine.cu", "cp.cu", "fused.cu"]
+SOURCES = ["engine.cu", "cp.cu", "fused.cu", "toeplitz.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

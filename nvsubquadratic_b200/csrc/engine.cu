@@ -671,7 +671,8 @@ struct HyenaPlan {
   long long Ntot = 1;   // prod n
   long long E = 0;      // B * Ntot * C
   int eb = 2;
-  bool fused = false;   // single-pass fused kernels (fused.cu) apply
+  bool fused = false;   // single-pass fused FFT kernels (fused.cu) apply
+  bool tp = false;      // tensor-core Toeplitz kernels (toeplitz.cu) apply (takes precedence)
   int SK = 0;
 };
 
@@ -727,11 +728,22 @@ static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
       d->in_batch_stride % 8 == 0 && d->out_pos_stride % 8 == 0 && d->out_batch_stride % 8 == 0) {
     h.fused = fused2d_dispatch(FOP_PROBE, d->dtype, h.cp.g.N[0], h.cp.g.N[1], h.cp.g.F[0], h.cp.g.F[1], h.SK,
                                nullptr, nullptr) == HYFFT_OK;
+    // bf16 grids with both sides <= 16: the long conv as a tcgen05 Toeplitz GEMM
+    const int N0 = h.cp.g.N[0], N1 = h.cp.g.N[1], K0 = h.cp.g.K[0], K1 = h.cp.g.K[1];
+    h.tp = !getenv("HYFFT_DISABLE_TP") && d->dtype == HYFFT_BF16 && K0 <= 31 && K1 <= 31 && K0 <= 2 * N0 &&
+           K1 <= 2 * N1 && tp2d_dispatch(TP_PROBE, N0, N1, h.SK, nullptr, nullptr) == HYFFT_OK;
+    if (h.tp) h.fused = false;
   }
   return HYFFT_OK;
 }
 
 static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& saved) {
+  if (h.tp) {  // nothing kept between passes; the workspace holds a status word
+    saved = 0;
+    fwd = 256;
+    bwd = 256;
+    return;
+  }
   if (h.fused) {
     const size_t spec = align_up((size_t)h.d.channels * h.cp.g.vol_F * sizeof(float2));
     saved = spec;  // filter spectrum, reused by the backward
@@ -925,6 +937,48 @@ static int hyena_fused_backward(const HyenaPlan& h, const void* q, const void* k
   return fused_op(h, FOP_DFILT, p, st, "dfilt2d_kernel");
 }
 
+static int hyena_tp_forward(const HyenaPlan& h, const void* q, const void* k, const void* v, const float* filt,
+                            const float* D, const float* sw, const float* sb, void* y, void* ws, cudaStream_t st) {
+  if (!aligned16({q, k, v, y, ws})) return fail(HYFFT_ERR_INVALID, "q, k, v and y must be 16-byte aligned");
+  Fused2DParams p;
+  fused_params(h, p, q, k, v, filt, D, sw, sb);
+  p.y = y;
+  p.status = static_cast<int*>(ws);
+  cudaMemsetAsync(ws, 0, sizeof(int), st);
+  const int rc = tp2d_dispatch(TP_FWD, h.cp.g.N[0], h.cp.g.N[1], h.SK, &p, st);
+  if (rc != HYFFT_OK) return fail(rc, "tp2d_fwd_kernel launch failed");
+  return HYFFT_OK;
+}
+
+static int hyena_tp_backward(const HyenaPlan& h, const void* q, const void* k, const void* v, const float* filt,
+                             const float* D, const float* sw, const float* sb, const void* dy, void* dq, void* dk,
+                             void* dv, float* dfilt, float* dD, float* dsw, float* dsb, void* ws, cudaStream_t st) {
+  if (!aligned16({q, k, v, dy, dq, dk, dv, ws}))
+    return fail(HYFFT_ERR_INVALID, "q, k, v, dy, dq, dk and dv must be 16-byte aligned");
+  if (!dD || (h.sg.has_conv && !dsw) || (h.sg.has_bias && !dsb))
+    return fail(HYFFT_ERR_INVALID, "dD, dshort_w (and dshort_b with a bias) are required");
+  const hyfft_hyena_desc& d = h.d;
+  Fused2DParams p;
+  fused_params(h, p, q, k, v, filt, D, sw, sb);
+  p.dy = dy;
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.dfilt = dfilt;
+  p.dD = dD;
+  p.dw = h.sg.has_conv ? dsw : nullptr;
+  p.db = h.sg.has_bias ? dsb : nullptr;
+  p.status = static_cast<int*>(ws);
+  cudaMemsetAsync(ws, 0, sizeof(int), st);
+  cudaMemsetAsync(dfilt, 0, sizeof(float) * (size_t)d.channels * h.cp.g.K[0] * h.cp.g.K[1], st);
+  cudaMemsetAsync(dD, 0, sizeof(float) * d.channels, st);
+  if (p.dw) cudaMemsetAsync(p.dw, 0, sizeof(float) * 3 * (size_t)d.channels * h.sg.ntaps, st);
+  if (p.db) cudaMemsetAsync(p.db, 0, sizeof(float) * 3 * (size_t)d.channels, st);
+  const int rc = tp2d_dispatch(TP_BWD, h.cp.g.N[0], h.cp.g.N[1], h.SK, &p, st);
+  if (rc != HYFFT_OK) return fail(rc, "tp2d_bwd_kernel launch failed");
+  return HYFFT_OK;
+}
+
 }  // namespace hyfft
 
 extern "C" {
@@ -951,8 +1005,9 @@ int hyfft_hyena_forward(const hyfft_hyena_desc* d, const void* q, const void* k,
   size_t f, b, s;
   hyena_sizes(h, f, b, s);
   if (!workspace || workspace_bytes < f) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, f);
-  if (!saved) return fail(HYFFT_ERR_WORKSPACE, "saved buffer of %zu bytes required", s);
+  if (!saved && s > 0) return fail(HYFFT_ERR_WORKSPACE, "saved buffer of %zu bytes required", s);
   cudaStream_t st = (cudaStream_t)stream;
+  if (h.tp) return hyena_tp_forward(h, q, k, v, filt, D, short_w, short_b, y, workspace, st);
   if (h.fused) return hyena_fused_forward(h, q, k, v, filt, D, short_w, short_b, y, saved, st);
   if (d->dtype == HYFFT_BF16)
     return hyena_forward_t<__nv_bfloat16>(h, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
@@ -977,8 +1032,11 @@ int hyfft_hyena_backward(const hyfft_hyena_desc* d, const void* q, const void* k
   size_t f, b, s;
   hyena_sizes(h, f, b, s);
   if (!workspace || workspace_bytes < b) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, b);
-  if (!saved) return fail(HYFFT_ERR_WORKSPACE, "saved buffer required");
+  if (!saved && s > 0) return fail(HYFFT_ERR_WORKSPACE, "saved buffer required");
   cudaStream_t st = (cudaStream_t)stream;
+  if (h.tp)
+    return hyena_tp_backward(h, q, k, v, filt, D, short_w, short_b, dy, dq, dk, dv, dfilt, dD, dshort_w, dshort_b,
+                             workspace, st);
   if (h.fused)
     return hyena_fused_backward(h, q, k, v, filt, D, short_w, short_b, dy, dq, dk, dv, dfilt, dD, dshort_w, dshort_b,
                                 saved, workspace, st);

@@ -29,7 +29,12 @@ struct Fused2DParams {
   int B, C, half;
   int K0, K1;
   int gate1, gate2;
+  int* status;        // set non-zero by a kernel whose bounded wait timed out (workspace word)
 };
+
+// Tensor-core (tcgen05) Toeplitz path for bf16 grids with both sides <= 16 (toeplitz.cu).
+enum TpOp { TP_FWD = 0, TP_BWD = 1, TP_PROBE = 2 };
+int tp2d_dispatch(int op, int N0, int N1, int SK, const Fused2DParams* p, cudaStream_t st);
 
 // ops of fused2d_dispatch
 enum FusedOp { FOP_KSPEC = 0, FOP_FWD = 1, FOP_BWD = 2, FOP_DFILT = 3, FOP_PROBE = 4 };

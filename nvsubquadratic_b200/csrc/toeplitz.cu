@@ -1,0 +1,671 @@
+// Tensor-core Hyena kernels for small 2D grids (both sides <= 16, bf16 I/O), e.g.
+// the 14x14 ViT token grid: the long convolution runs on tcgen05 as a dense
+// Toeplitz GEMM instead of an FFT.
+//
+// Why: for an N0 x N1 grid the "same" linear convolution with a (<= 2N-1)-tap
+// filter is, per channel, the product of a (N0*N1) x (N0*N1) block-Toeplitz
+// matrix T (blocks T1_d[c_out][c_in] = k[d + K0/2][c_out - c_in + K1/2], d = r_out -
+// r_in) with the images of that channel. At 196 positions that is 77 kFLOP per
+// image on the tensor cores (~2.25 PFLOP/s) versus ~30 kFLOP per image of
+// pruned FFT on the fp32 pipes (~70 TFLOP/s), so the dense form is ~10x cheaper
+// in time and leaves the kernel bound by HBM.
+//
+// Layout tricks:
+//  * Columns are padded to a pitch of 16, so a 128-row M tile covers 8 grid rows
+//    and one K step covers one input row. Every 128x16 A tile of T is then 8
+//    consecutive 16x16 blocks T1_d, T1_{d+1}, ..., so all A tiles are sliding
+//    windows (descriptor start address + 512 B per block) into one buffer of
+//    N0-1+16 blocks per channel (~15 KB), never a materialised N^2 matrix.
+//  * The D-skip is folded into the filter's centre tap (h = conv(z, k + D*delta)),
+//    so the GEMM produces h directly and dD is the centre tap of the filter
+//    gradient.
+//  * z and dh live in one shared-memory layout per row [c/8][img/8][img%8][c%8]
+//    that is a K-major operand (N = images, K = columns) for the convolution GEMMs
+//    and an MN-major operand (M/N = positions, K = images) for the filter-gradient
+//    GEMM G = DH * Z^T.
+//
+// Forward (per CTA: CG channels x NB images): depthwise 3x3 short conv + gate 1
+// from channels-last q, k (16-byte vectors read in place from the projection
+// output) -> z; per channel: Toeplitz blocks -> tcgen05.mma into TMEM; epilogue:
+// gate 2 with v' -> y (channels-last vector stores).
+// Backward: z and dh -> SMEM; per channel H = T z, DZ = T^T dh (TMEM); gate
+// backward -> dq', dk', dv' (SMEM); per channel G = DH Z^T (TMEM, 448 columns),
+// reduced along its Toeplitz diagonals into dK; transposed short conv -> dq, dk,
+// dv; weight / bias gradient reductions.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <atomic>
+
+#include "common.cuh"
+#include "fused2d.h"
+#include "umma.cuh"
+
+namespace hyfft {
+
+extern std::atomic<long long> g_launches;
+
+namespace tp {
+
+using bf16 = __nv_bfloat16;
+
+template <int CG>
+struct VG;
+template <>
+struct VG<8> {
+  static __device__ __forceinline__ void load(const bf16* p, float (&o)[8]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void store(bf16* p, const float (&o)[8]) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+};
+template <>
+struct VG<4> {
+  static __device__ __forceinline__ void load(const bf16* p, float (&o)[4]) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void store(bf16* p, const float (&o)[4]) {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) h[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+    *reinterpret_cast<uint2*>(p) = u;
+  }
+  // shared-memory variants (plain loads)
+  static __device__ __forceinline__ void lds(const bf16* p, float (&o)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+};
+
+__device__ __forceinline__ float rbf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Depthwise SKxSK "same" cross-correlation of CG channels at (n0, n1) of one image,
+// read from global memory (channels-last, position stride pst, channel offset applied).
+template <int N0, int N1, int SK, int CG>
+__device__ __forceinline__ void gstencil(const bf16* img, long long pst, const float* w, const float* bias, int n0,
+                                         int n1, float (&o)[CG]) {
+  if constexpr (SK == 0) {
+    VG<CG>::load(img + (long long)(n0 * N1 + n1) * pst, o);
+  } else {
+    constexpr int OFF = (SK - 1) / 2, NT = SK * SK;
+#pragma unroll
+    for (int c = 0; c < CG; ++c) o[c] = bias ? bias[c] : 0.f;
+#pragma unroll
+    for (int a = 0; a < SK; ++a) {
+      const int i0 = n0 + a - OFF;
+      if (i0 < 0 || i0 >= N0) continue;
+#pragma unroll
+      for (int b = 0; b < SK; ++b) {
+        const int i1 = n1 + b - OFF;
+        if (i1 < 0 || i1 >= N1) continue;
+        float x[CG];
+        VG<CG>::load(img + (long long)(i0 * N1 + i1) * pst, x);
+#pragma unroll
+        for (int c = 0; c < CG; ++c) o[c] = fmaf(w[c * NT + a * SK + b], x[c], o[c]);
+      }
+    }
+  }
+}
+
+template <int N0>
+struct Geo {
+  static constexpr int MT = (N0 + 7) / 8;        // 128-row M tiles (8 grid rows each)
+  static constexpr int NR = 8 * MT;              // grid rows incl. padding rows
+  static constexpr int NBLK = (N0 - 1) + 8 * MT;  // 16x16 Toeplitz blocks per table
+  static constexpr int BLKB = 512;               // bytes per block
+};
+
+// Fill one table of Toeplitz blocks for a channel (all threads). Block b holds, for
+// d = b - (N0 - 1):  forward  T1_d[m = c_out][k = c_in]  = k'[d + K0/2][c_out - c_in + K1/2]
+//                    adjoint  U_d[m = c_in][k = c_out]   = k'[K0/2 - d][c_out - c_in + K1/2]
+// with k' = k + D at the centre tap; stored K-major [m/8][k/8][m%8][k%8] (bf16).
+template <int N0, int N1, bool ADJ>
+__device__ __forceinline__ void gen_blocks(unsigned char* dst, const float* __restrict__ f, int K0, int K1, float Dc) {
+  constexpr int NBLK = Geo<N0>::NBLK;
+  const int ck0 = K0 / 2, ck1 = K1 / 2;
+  for (int it = threadIdx.x; it < NBLK * 32; it += blockDim.x) {
+    const int b = it >> 5, m = (it >> 1) & 15, kc = it & 1;
+    const int d = b - (N0 - 1);
+    const int row = ADJ ? ck0 - d : d + ck0;
+    const bool row_ok = row >= 0 && row < K0 && m < N1;
+    uint32_t pk[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      float v2[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int k = kc * 8 + e + u;
+        const int co = ADJ ? k : m, ci = ADJ ? m : k;
+        const int col = co - ci + ck1;
+        float val = 0.f;
+        if (row_ok && k < N1 && col >= 0 && col < K1) {
+          val = __ldg(f + row * K1 + col);
+          if (row == ck0 && col == ck1) val += Dc;
+        }
+        v2[u] = val;
+      }
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v2[0], v2[1]);
+      pk[e >> 1] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(dst + b * 512 + (m >> 3) * 256 + kc * 128 + (m & 7) * 16) =
+        make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+}
+
+__host__ __device__ constexpr uint32_t tmem_cols_for(int n) {
+  return n <= 32 ? 32u : n <= 64 ? 64u : n <= 128 ? 128u : n <= 256 ? 256u : 512u;
+}
+
+// offset (bytes) of (image, grid position (r, c)) in the z / dh operand layout of a channel
+template <int NB>
+__device__ __forceinline__ int zoff(int img, int r, int c) {
+  return r * (32 * NB) + (c >> 3) * (16 * NB) + (img >> 3) * 128 + (img & 7) * 16 + (c & 7) * 2;
+}
+
+__device__ __forceinline__ void set_status(int* st) {
+  if (st) atomicExch(st, 1);
+}
+
+// ------------------------------------------------------------------ forward
+template <int N0, int N1, int SK, int CG, int NB>
+struct FwdLayout {
+  using G = Geo<N0>;
+  static constexpr int NT = SK > 0 ? SK * SK : 1;
+  static constexpr int RB = 32 * NB;
+  static constexpr size_t z = 0;
+  static constexpr size_t t = z + (size_t)CG * G::NR * RB;
+  static constexpr size_t w = t + 2 * (size_t)G::NBLK * G::BLKB;
+  static constexpr size_t bar = w + ((4 * (3 * CG * NT + 3 * CG) + 15) / 16) * 16;
+  static constexpr size_t total = bar + 32;
+  static constexpr uint32_t tcols = tmem_cols_for(CG * G::MT * NB);
+};
+
+template <int N0, int N1, int SK, int CG, int NB>
+__global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
+  using G = Geo<N0>;
+  using L = FwdLayout<N0, N1, SK, CG, NB>;
+  constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = N0 * N1;
+  constexpr uint32_t IDESC = umma::idesc_bf16(128, NB, 0, 0);
+  static_assert(MT <= 2, "8 warps cover at most two 128-row tiles");
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char* Zt = smem + L::z;
+  unsigned char* Tb = smem + L::t;
+  float* wts = reinterpret_cast<float*>(smem + L::w);
+  float* bsm = wts + 3 * CG * NT;
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + L::bar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + L::bar + 16);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c0 = blockIdx.x * CG, b0 = blockIdx.y * NB;
+
+  if (warp == 0) umma::tmem_alloc(tslot, L::tcols);
+  if (tid == 0) {
+    umma::mbar_init(&mbar[0], 1);
+    umma::mbar_init(&mbar[1], 1);
+    umma::fence_mbar_init();
+  }
+  for (int i = tid; i < 3 * CG * NT; i += blockDim.x) {
+    const int t = i / (CG * NT), r = i % (CG * NT), cc = r / NT, tap = r % NT;
+    wts[i] = SK > 0 ? p.w[((long long)t * p.C + c0 + cc) * NT + tap] : 1.f;
+  }
+  for (int i = tid; i < 3 * CG; i += blockDim.x) bsm[i] = p.bias ? p.bias[(i / CG) * p.C + c0 + i % CG] : 0.f;
+  for (int i = tid; i < CG * NR * RB / 16; i += blockDim.x) reinterpret_cast<uint4*>(Zt)[i] = make_uint4(0, 0, 0, 0);
+  __syncthreads();
+
+  const bf16* q = reinterpret_cast<const bf16*>(p.q) + c0;
+  const bf16* k = reinterpret_cast<const bf16*>(p.k) + c0;
+  const float* bq = p.bias ? bsm : nullptr;
+  const float* bk = p.bias ? bsm + CG : nullptr;
+  const float* bv = p.bias ? bsm + 2 * CG : nullptr;
+  // ---- z = q' * g1(k') into the operand layout
+  for (int it = tid; it < NB * NP; it += blockDim.x) {
+    const int img = it % NB, pos = it / NB, r = pos / N1, c = pos % N1;
+    const int b = b0 + img;
+    if (b >= p.B) continue;
+    const long long ib = (long long)b * p.in_bst;
+    float qv[CG], kv[CG];
+    gstencil<N0, N1, SK, CG>(q + ib, p.in_pst, wts, bq, r, c, qv);
+    gstencil<N0, N1, SK, CG>(k + ib, p.in_pst, wts + CG * NT, bk, r, c, kv);
+    const int off = zoff<NB>(img, r, c);
+#pragma unroll
+    for (int ch = 0; ch < CG; ++ch) {
+      const float z = rbf(rbf(qv[ch]) * rbf(gate_f(p.gate1, rbf(kv[ch]))));
+      *reinterpret_cast<bf16*>(Zt + ch * NR * RB + off) = __float2bfloat16_rn(z);
+    }
+  }
+  umma::fence_async_smem();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+
+  // ---- per channel: Toeplitz blocks + MMAs (double-buffered block tables)
+  bool ok = true;
+  for (int ch = 0; ch < CG; ++ch) {
+    const int buf = ch & 1;
+    if (ch >= 2) ok &= umma::mbar_wait(&mbar[buf], ((ch - 2) >> 1) & 1);
+    unsigned char* tb = Tb + buf * G::NBLK * G::BLKB;
+    const int cg = c0 + ch;
+    gen_blocks<N0, N1, false>(tb, p.filt + (long long)cg * p.K0 * p.K1, p.K0, p.K1, p.D[cg]);
+    umma::fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        for (int ri = 0; ri < N0; ++ri) {
+          const uint64_t da = umma::sdesc(umma::su32(tb + (8 * mt - ri + N0 - 1) * G::BLKB), 128, 256);
+          const uint64_t db = umma::sdesc(umma::su32(Zt + ch * NR * RB + ri * RB), 16 * NB, 128);
+          umma::mma(tmem + (uint32_t)((ch * MT + mt) * NB), da, db, IDESC, ri > 0 ? 1u : 0u);
+        }
+      }
+      umma::commit(&mbar[buf]);
+    }
+  }
+  ok &= umma::mbar_wait(&mbar[(CG - 1) & 1], ((CG - 1) >> 1) & 1);
+  if (!ok && tid == 0) set_status(p.status);
+  umma::fence_after_sync();
+
+  // ---- epilogue: y = round(h) * round(g2(v'))
+  const int mt = warp >> 2, q4 = warp & 3;
+  if (mt < MT) {
+    const int m = q4 * 32 + lane, r = mt * 8 + (m >> 4), c = m & 15;
+    const bool valid = ok && r < N0 && c < N1;
+    const bf16* v = reinterpret_cast<const bf16*>(p.v) + c0;
+    bf16* y = reinterpret_cast<bf16*>(p.y) + c0;
+    const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+#pragma unroll 1
+    for (int i0 = 0; i0 < NB; i0 += 8) {
+      float h[CG][8];
+#pragma unroll
+      for (int ch = 0; ch < CG; ++ch) umma::tmem_ld8(lane_base + (uint32_t)((ch * MT + mt) * NB + i0), h[ch]);
+#pragma unroll 1
+      for (int j = 0; j < 8; ++j) {
+        const int b = b0 + i0 + j;
+        if (!valid || b >= p.B) continue;
+        float vv[CG], out[CG];
+        gstencil<N0, N1, SK, CG>(v + (long long)b * p.in_bst, p.in_pst, wts + 2 * CG * NT, bv, r, c, vv);
+#pragma unroll
+        for (int ch = 0; ch < CG; ++ch) out[ch] = rbf(h[ch][j]) * rbf(gate_f(p.gate2, rbf(vv[ch])));
+        VG<CG>::store(y + (long long)b * p.out_bst + (long long)(r * N1 + c) * p.out_pst, out);
+      }
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, L::tcols);
+}
+
+// ------------------------------------------------------------------ backward
+template <int N0, int N1, int SK, int CG, int NB>
+struct BwdLayout {
+  using G = Geo<N0>;
+  static constexpr int NT = SK > 0 ? SK * SK : 1;
+  static constexpr int RB = 32 * NB;
+  static constexpr int KMAX = 2 * 16 - 1;
+  static constexpr size_t z = 0;
+  static constexpr size_t dh = z + (size_t)CG * G::NR * RB;
+  static constexpr size_t tf = dh + (size_t)CG * G::NR * RB;
+  static constexpr size_t tt = tf + 2 * (size_t)G::NBLK * G::BLKB;
+  static constexpr size_t ds = tt + 2 * (size_t)G::NBLK * G::BLKB;                 // [3][NB][NP][CG] bf16
+  static constexpr size_t dk = ds + ((size_t)3 * NB * N0 * N1 * CG * 2 + 15) / 16 * 16;  // [CG][KMAX*KMAX] f32
+  static constexpr size_t w = dk + (size_t)CG * KMAX * KMAX * 4;
+  static constexpr size_t dw = w + ((4 * (3 * CG * NT + 3 * CG) + 15) / 16) * 16;     // [3][CG][NT+1] f32
+  static constexpr size_t bar = dw + ((4 * 3 * CG * (NT + 1) + 15) / 16) * 16;
+  static constexpr size_t total = bar + 48;
+};
+
+template <int N0, int N1, int SK, int CG, int NB>
+__global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
+  using G = Geo<N0>;
+  using L = BwdLayout<N0, N1, SK, CG, NB>;
+  constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = N0 * N1, KMAX = L::KMAX;
+  constexpr uint32_t IDESC = umma::idesc_bf16(128, NB, 0, 0);
+  constexpr uint32_t IDESC_G = umma::idesc_bf16(128, 16 * N0, 1, 1);
+  constexpr uint32_t TCOLS = 512;
+  static_assert(MT <= 2, "8 warps cover at most two 128-row tiles");
+  static_assert(2 * CG * MT * NB <= 512 && MT * 16 * N0 <= 512, "TMEM budget");
+  static_assert(NB == 16, "the filter-gradient GEMM uses one K step of 16 images");
+  extern __shared__ __align__(1024) unsigned char smem[];
+  unsigned char* Zt = smem + L::z;
+  unsigned char* DHt = smem + L::dh;
+  unsigned char* Tf = smem + L::tf;
+  unsigned char* Tt = smem + L::tt;
+  bf16* ds = reinterpret_cast<bf16*>(smem + L::ds);
+  float* dkacc = reinterpret_cast<float*>(smem + L::dk);
+  float* wts = reinterpret_cast<float*>(smem + L::w);
+  float* bsm = wts + 3 * CG * NT;
+  float* dwacc = reinterpret_cast<float*>(smem + L::dw);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + L::bar);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + L::bar + 32);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c0 = blockIdx.x * CG, b0 = blockIdx.y * NB;
+  const int ck0 = p.K0 / 2, ck1 = p.K1 / 2;
+
+  if (warp == 0) umma::tmem_alloc(tslot, TCOLS);
+  if (tid == 0) {
+    umma::mbar_init(&mbar[0], 1);
+    umma::mbar_init(&mbar[1], 1);
+    umma::mbar_init(&mbar[2], 1);
+    umma::fence_mbar_init();
+  }
+  for (int i = tid; i < 3 * CG * NT; i += blockDim.x) {
+    const int t = i / (CG * NT), r = i % (CG * NT), cc = r / NT, tap = r % NT;
+    wts[i] = SK > 0 ? p.w[((long long)t * p.C + c0 + cc) * NT + tap] : 1.f;
+  }
+  for (int i = tid; i < 3 * CG; i += blockDim.x) bsm[i] = p.bias ? p.bias[(i / CG) * p.C + c0 + i % CG] : 0.f;
+  for (int i = tid; i < 2 * CG * NR * RB / 16; i += blockDim.x) reinterpret_cast<uint4*>(Zt)[i] = make_uint4(0, 0, 0, 0);
+  for (int i = tid; i < CG * KMAX * KMAX; i += blockDim.x) dkacc[i] = 0.f;
+  for (int i = tid; i < 3 * CG * (NT + 1); i += blockDim.x) dwacc[i] = 0.f;
+  __syncthreads();
+
+  const bf16* src[3] = {reinterpret_cast<const bf16*>(p.q) + c0, reinterpret_cast<const bf16*>(p.k) + c0,
+                        reinterpret_cast<const bf16*>(p.v) + c0};
+  const bf16* dyp = reinterpret_cast<const bf16*>(p.dy) + c0;
+  const float* bias3[3] = {p.bias ? bsm : nullptr, p.bias ? bsm + CG : nullptr, p.bias ? bsm + 2 * CG : nullptr};
+
+  // ---- z and dh into the operand layouts
+  for (int it = tid; it < NB * NP; it += blockDim.x) {
+    const int img = it % NB, pos = it / NB, r = pos / N1, c = pos % N1;
+    const int b = b0 + img;
+    if (b >= p.B) continue;
+    const long long ib = (long long)b * p.in_bst;
+    float qv[CG], kv[CG], vv[CG], g[CG];
+    gstencil<N0, N1, SK, CG>(src[0] + ib, p.in_pst, wts, bias3[0], r, c, qv);
+    gstencil<N0, N1, SK, CG>(src[1] + ib, p.in_pst, wts + CG * NT, bias3[1], r, c, kv);
+    gstencil<N0, N1, SK, CG>(src[2] + ib, p.in_pst, wts + 2 * CG * NT, bias3[2], r, c, vv);
+    VG<CG>::load(dyp + (long long)b * p.out_bst + (long long)pos * p.out_pst, g);
+    const int off = zoff<NB>(img, r, c);
+#pragma unroll
+    for (int ch = 0; ch < CG; ++ch) {
+      const float z = rbf(rbf(qv[ch]) * rbf(gate_f(p.gate1, rbf(kv[ch]))));
+      const float dh = rbf(g[ch] * rbf(gate_f(p.gate2, rbf(vv[ch]))));
+      *reinterpret_cast<bf16*>(Zt + ch * NR * RB + off) = __float2bfloat16_rn(z);
+      *reinterpret_cast<bf16*>(DHt + ch * NR * RB + off) = __float2bfloat16_rn(dh);
+    }
+  }
+  umma::fence_async_smem();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tslot;
+  const uint32_t DZ0 = (uint32_t)(CG * MT * NB);
+
+  // ---- per channel: H = T z and DZ = T^T dh
+  bool ok = true;
+  for (int ch = 0; ch < CG; ++ch) {
+    const int buf = ch & 1;
+    if (ch >= 2) ok &= umma::mbar_wait(&mbar[buf], ((ch - 2) >> 1) & 1);
+    unsigned char* tf = Tf + buf * G::NBLK * G::BLKB;
+    unsigned char* tt = Tt + buf * G::NBLK * G::BLKB;
+    const int cg = c0 + ch;
+    const float* fch = p.filt + (long long)cg * p.K0 * p.K1;
+    gen_blocks<N0, N1, false>(tf, fch, p.K0, p.K1, p.D[cg]);
+    gen_blocks<N0, N1, true>(tt, fch, p.K0, p.K1, p.D[cg]);
+    umma::fence_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        for (int s = 0; s < N0; ++s) {
+          const uint32_t blk = (uint32_t)((8 * mt - s + N0 - 1) * G::BLKB);
+          const uint64_t dz = umma::sdesc(umma::su32(Zt + ch * NR * RB + s * RB), 16 * NB, 128);
+          const uint64_t dd = umma::sdesc(umma::su32(DHt + ch * NR * RB + s * RB), 16 * NB, 128);
+          umma::mma(tmem + (uint32_t)((ch * MT + mt) * NB), umma::sdesc(umma::su32(tf) + blk, 128, 256), dz, IDESC,
+                    s > 0 ? 1u : 0u);
+          umma::mma(tmem + DZ0 + (uint32_t)((ch * MT + mt) * NB), umma::sdesc(umma::su32(tt) + blk, 128, 256), dd,
+                    IDESC, s > 0 ? 1u : 0u);
+        }
+      }
+      umma::commit(&mbar[buf]);
+    }
+  }
+  ok &= umma::mbar_wait(&mbar[(CG - 1) & 1], ((CG - 1) >> 1) & 1);
+  umma::fence_after_sync();
+
+  // ---- gate backward: dq' = dz g1(k'), dk' = dz q' g1'(k'), dv' = dy h g2'(v')  -> ds
+  const int mt = warp >> 2, q4 = warp & 3;
+  const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+  if (mt < MT) {
+    const int m = q4 * 32 + lane, r = mt * 8 + (m >> 4), c = m & 15;
+    const bool valid = ok && r < N0 && c < N1;
+    const int pos = r * N1 + c;
+#pragma unroll 1
+    for (int i0 = 0; i0 < NB; i0 += 8) {
+      float hacc[CG][8], dacc[CG][8];
+#pragma unroll
+      for (int ch = 0; ch < CG; ++ch) {
+        umma::tmem_ld8(lane_base + (uint32_t)((ch * MT + mt) * NB + i0), hacc[ch]);
+        umma::tmem_ld8(lane_base + DZ0 + (uint32_t)((ch * MT + mt) * NB + i0), dacc[ch]);
+      }
+#pragma unroll 1
+      for (int j = 0; j < 8; ++j) {
+        const int img = i0 + j, b = b0 + img;
+        if (!valid || b >= p.B) continue;
+        const long long ib = (long long)b * p.in_bst;
+        float qv[CG], kv[CG], vv[CG], g[CG], oq[CG], ok_[CG], ov[CG];
+        gstencil<N0, N1, SK, CG>(src[0] + ib, p.in_pst, wts, bias3[0], r, c, qv);
+        gstencil<N0, N1, SK, CG>(src[1] + ib, p.in_pst, wts + CG * NT, bias3[1], r, c, kv);
+        gstencil<N0, N1, SK, CG>(src[2] + ib, p.in_pst, wts + 2 * CG * NT, bias3[2], r, c, vv);
+        VG<CG>::load(dyp + (long long)b * p.out_bst + (long long)pos * p.out_pst, g);
+#pragma unroll
+        for (int ch = 0; ch < CG; ++ch) {
+          const float qr = rbf(qv[ch]), kr = rbf(kv[ch]), vr = rbf(vv[ch]);
+          const float hv = rbf(hacc[ch][j]);
+          const float dz = rbf(dacc[ch][j]);
+          ov[ch] = g[ch] * hv * gate_df(p.gate2, vr);
+          oq[ch] = dz * rbf(gate_f(p.gate1, kr));
+          ok_[ch] = dz * qr * gate_df(p.gate1, kr);
+        }
+        bf16* dsi = ds + ((long long)img * NP + pos) * CG;
+        VG<CG>::store(dsi, oq);
+        VG<CG>::store(dsi + (long long)NB * NP * CG, ok_);
+        VG<CG>::store(dsi + 2LL * NB * NP * CG, ov);
+      }
+    }
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+
+  // ---- per channel: G = DH Z^T (positions x positions), reduced along Toeplitz diagonals
+  for (int ch = 0; ch < CG; ++ch) {
+    if (tid == 0) {
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        const uint64_t da = umma::sdesc(umma::su32(DHt + ch * NR * RB + t * 8 * RB), 128, 16 * NB);
+        const uint64_t db = umma::sdesc(umma::su32(Zt + ch * NR * RB), 128, 16 * NB);
+        umma::mma(tmem + (uint32_t)(t * 16 * N0), da, db, IDESC_G, 0u);
+      }
+      umma::commit(&mbar[2]);
+    }
+    ok &= umma::mbar_wait(&mbar[2], ch & 1);
+    umma::fence_after_sync();
+    if (mt < MT) {
+      const int m = q4 * 32 + lane, ro = mt * 8 + (m >> 4), co = m & 15;
+      const bool valid = ok && ro < N0 && co < N1;
+      float* acc = dkacc + ch * KMAX * KMAX;
+#pragma unroll 1
+      for (int ri = 0; ri < N0; ++ri) {
+        float gv[16];
+        umma::tmem_ld16(lane_base + (uint32_t)(mt * 16 * N0 + ri * 16), gv);
+        const int a = ro - ri + ck0;
+        if (!valid || a < 0 || a >= p.K0) continue;
+#pragma unroll
+        for (int ci = 0; ci < N1; ++ci) {
+          const int bb = co - ci + ck1;
+          if (bb >= 0 && bb < p.K1) atomicAdd(acc + a * KMAX + bb, gv[ci]);
+        }
+      }
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    umma::fence_after_sync();
+  }
+  if (!ok && tid == 0) set_status(p.status);
+
+  // ---- transposed short conv -> dq, dk, dv; weight / bias gradients
+  bf16* outs[3] = {reinterpret_cast<bf16*>(p.dq) + c0, reinterpret_cast<bf16*>(p.dk) + c0,
+                   reinterpret_cast<bf16*>(p.dv) + c0};
+  constexpr int OFF = SK > 0 ? (SK - 1) / 2 : 0;
+#pragma unroll 1
+  for (int t = 0; t < 3; ++t) {
+    float wacc[CG][NT + 1];
+#pragma unroll
+    for (int ch = 0; ch < CG; ++ch)
+#pragma unroll
+      for (int u = 0; u <= NT; ++u) wacc[ch][u] = 0.f;
+    const bf16* dst_t = ds + (long long)t * NB * NP * CG;
+    const float* wt = wts + t * CG * NT;
+    for (int it = tid; it < NB * NP; it += blockDim.x) {
+      const int img = it % NB, pos = it / NB, r = pos / N1, c = pos % N1;
+      const int b = b0 + img;
+      if (b >= p.B) continue;
+      const bf16* dimg = dst_t + (long long)img * NP * CG;
+      float o[CG];
+      if constexpr (SK == 0) {
+        VG<CG>::lds(dimg + pos * CG, o);
+      } else {
+#pragma unroll
+        for (int ch = 0; ch < CG; ++ch) o[ch] = 0.f;
+#pragma unroll
+        for (int a = 0; a < SK; ++a) {
+          const int i0 = r - a + OFF;
+          if (i0 < 0 || i0 >= N0) continue;
+#pragma unroll
+          for (int bq = 0; bq < SK; ++bq) {
+            const int i1 = c - bq + OFF;
+            if (i1 < 0 || i1 >= N1) continue;
+            float x[CG];
+            VG<CG>::lds(dimg + (i0 * N1 + i1) * CG, x);
+#pragma unroll
+            for (int ch = 0; ch < CG; ++ch) o[ch] = fmaf(wt[ch * NT + a * SK + bq], x[ch], o[ch]);
+          }
+        }
+        // dw[t][ch][tap] += d'(pos) * in(pos + tap - OFF)
+        float d0[CG];
+        VG<CG>::lds(dimg + pos * CG, d0);
+        const bf16* inimg = src[t] + (long long)b * p.in_bst;
+#pragma unroll
+        for (int a = 0; a < SK; ++a) {
+          const int i0 = r + a - OFF;
+          if (i0 < 0 || i0 >= N0) continue;
+#pragma unroll
+          for (int bq = 0; bq < SK; ++bq) {
+            const int i1 = c + bq - OFF;
+            if (i1 < 0 || i1 >= N1) continue;
+            float x[CG];
+            VG<CG>::load(inimg + (long long)(i0 * N1 + i1) * p.in_pst, x);
+#pragma unroll
+            for (int ch = 0; ch < CG; ++ch) wacc[ch][a * SK + bq] = fmaf(d0[ch], x[ch], wacc[ch][a * SK + bq]);
+          }
+        }
+#pragma unroll
+        for (int ch = 0; ch < CG; ++ch) wacc[ch][NT] += d0[ch];
+      }
+      VG<CG>::store(outs[t] + (long long)b * p.out_bst + (long long)pos * p.out_pst, o);
+    }
+    if constexpr (SK > 0) {
+#pragma unroll
+      for (int ch = 0; ch < CG; ++ch)
+#pragma unroll
+        for (int u = 0; u <= NT; ++u) {
+          float s = wacc[ch][u];
+          for (int o2 = 16; o2 > 0; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
+          if (lane == 0) atomicAdd(dwacc + (t * CG + ch) * (NT + 1) + u, s);
+        }
+    }
+  }
+  __syncthreads();
+  if constexpr (SK > 0) {
+    for (int i = tid; i < 3 * CG * (NT + 1); i += blockDim.x) {
+      const int t = i / (CG * (NT + 1)), rr = i % (CG * (NT + 1)), ch = rr / (NT + 1), u = rr % (NT + 1);
+      const long long chg = (long long)t * p.C + c0 + ch;
+      if (u < NT) atomicAdd(p.dw + chg * NT + u, dwacc[i]);
+      else if (p.db) atomicAdd(p.db + chg, dwacc[i]);
+    }
+  }
+  // filter gradient (of k' = k + D*delta): dfilt = dk', dD = dk' at the centre tap
+  for (int i = tid; i < CG * p.K0 * p.K1; i += blockDim.x) {
+    const int ch = i / (p.K0 * p.K1), rr = i % (p.K0 * p.K1), a = rr / p.K1, bb = rr % p.K1;
+    const float v = dkacc[ch * KMAX * KMAX + a * KMAX + bb];
+    atomicAdd(p.dfilt + ((long long)(c0 + ch) * p.K0 + a) * p.K1 + bb, v);
+    if (a == ck0 && bb == ck1) atomicAdd(p.dD + c0 + ch, v);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, TCOLS);
+}
+
+// ------------------------------------------------------------------ dispatch
+constexpr int kFwdCG = 8, kBwdCG = 4, kNB = 16;
+
+template <int N0, int N1, int SK>
+static int tp_run(int op, const Fused2DParams* pp, cudaStream_t st) {
+  using LF = FwdLayout<N0, N1, SK, kFwdCG, kNB>;
+  using LB = BwdLayout<N0, N1, SK, kBwdCG, kNB>;
+  if (op == TP_PROBE) return (LF::total <= 227 * 1024 && LB::total <= 227 * 1024) ? HYFFT_OK : HYFFT_ERR_UNSUPPORTED;
+  const Fused2DParams& p = *pp;
+  if (p.C % kFwdCG != 0) return HYFFT_ERR_UNSUPPORTED;
+  if (p.K0 > 2 * N0 - 1 + 1 || p.K1 > 2 * N1 - 1 + 1 || p.K0 > 31 || p.K1 > 31) return HYFFT_ERR_UNSUPPORTED;
+  if (op == TP_FWD) {
+    auto kern = tp2d_fwd_kernel<N0, N1, SK, kFwdCG, kNB>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LF::total) != cudaSuccess)
+      return HYFFT_ERR_CUDA;
+    dim3 grid(p.C / kFwdCG, (p.B + kNB - 1) / kNB);
+    kern<<<grid, 256, LF::total, st>>>(p);
+  } else {
+    auto kern = tp2d_bwd_kernel<N0, N1, SK, kBwdCG, kNB>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LB::total) != cudaSuccess)
+      return HYFFT_ERR_CUDA;
+    dim3 grid(p.C / kBwdCG, (p.B + kNB - 1) / kNB);
+    kern<<<grid, 256, LB::total, st>>>(p);
+  }
+  if (cudaGetLastError() != cudaSuccess) return HYFFT_ERR_CUDA;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return HYFFT_OK;
+}
+
+}  // namespace tp
+
+#define HYFFT_TP_SHAPES(X) \
+  X(14, 14)                \
+  X(16, 16)                \
+  X(8, 8)
+
+int tp2d_dispatch(int op, int N0, int N1, int SK, const Fused2DParams* p, cudaStream_t st) {
+#define HYFFT_TP_TRY(a, b)                                        \
+  if (N0 == a && N1 == b) {                                       \
+    if (SK == 3) return tp::tp_run<a, b, 3>(op, p, st);           \
+    if (SK == 0) return tp::tp_run<a, b, 0>(op, p, st);           \
+  }
+  HYFFT_TP_SHAPES(HYFFT_TP_TRY)
+#undef HYFFT_TP_TRY
+  return HYFFT_ERR_UNSUPPORTED;
+}
+
+}  // namespace hyfft

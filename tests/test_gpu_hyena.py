@@ -118,6 +118,9 @@ def test_hyena_vs_oracle_seeded(case):
 FUSED_CASES = [
     # B, C, S, K, short_k, gate1, gate2, dtype, bias
     (32, 64, (14, 14), (14, 14), 3, "identity", "identity", torch.bfloat16, False),
+    (17, 32, (14, 14), (28, 28), 0, "sigmoid", "silu", torch.bfloat16, False),
+    (20, 16, (16, 16), (31, 31), 3, "silu", "sigmoid", torch.bfloat16, True),
+    (6, 8, (8, 8), (15, 15), 3, "identity", "sigmoid", torch.bfloat16, False),
     (3, 16, (14, 14), (27, 27), 3, "silu", "sigmoid", torch.bfloat16, True),
     (5, 8, (16, 16), (31, 31), 0, "sigmoid", "silu", torch.float32, False),
     (2, 24, (8, 8), (15, 15), 3, "silu", "identity", torch.float32, True),
@@ -136,11 +139,14 @@ def test_fused_path_matches_general_engine(case, monkeypatch):
     sb = (0.1 * torch.randn(3 * C, generator=g)).to(dt) if (bias and sk) else None
     dy = torch.randn((B,) + S + (C,), generator=g).to(dt)
     outs = []
-    for disable in ("", "1"):
-        if disable:
-            monkeypatch.setenv("HYFFT_DISABLE_FUSED", "1")
-        else:
-            monkeypatch.delenv("HYFFT_DISABLE_FUSED", raising=False)
+    # default path (tensor-core Toeplitz for bf16 grids <= 16x16, else fused FFT), fused FFT only,
+    # general multi-pass engine
+    for env in ({}, {"HYFFT_DISABLE_TP": "1"}, {"HYFFT_DISABLE_FUSED": "1"}):
+        for key in ("HYFFT_DISABLE_TP", "HYFFT_DISABLE_FUSED"):
+            if key in env:
+                monkeypatch.setenv(key, env[key])
+            else:
+                monkeypatch.delenv(key, raising=False)
         qkv_d = qkv.cuda().requires_grad_(True)
         rest = [t.cuda().requires_grad_(True) if t is not None else None for t in (filt, D, sw, sb)]
         q, k, v = qkv_d.chunk(3, dim=-1)
@@ -149,7 +155,8 @@ def test_fused_path_matches_general_engine(case, monkeypatch):
         torch.cuda.synchronize()
         outs.append([y, qkv_d.grad] + [t.grad if t is not None else None for t in rest])
     tol = 2e-2 if dt == torch.bfloat16 else 1e-5
-    for name, a, b in zip(("y", "dqkv", "dfilt", "dD", "dsw", "dsb"), outs[1], outs[0]):
-        if a is None:
-            continue
-        assert rel_l2(a, b) <= tol, (name, rel_l2(a, b))
+    for variant in (0, 1):
+        for name, a, b in zip(("y", "dqkv", "dfilt", "dD", "dsw", "dsb"), outs[2], outs[variant]):
+            if a is None:
+                continue
+            assert rel_l2(a, b) <= tol, (variant, name, rel_l2(a, b))
