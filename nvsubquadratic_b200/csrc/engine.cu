@@ -730,7 +730,9 @@ static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
                                nullptr, nullptr) == HYFFT_OK;
     // bf16 grids with both sides <= 16: the long conv as a tcgen05 Toeplitz GEMM
     const int N0 = h.cp.g.N[0], N1 = h.cp.g.N[1], K0 = h.cp.g.K[0], K1 = h.cp.g.K[1];
-    h.tp = !getenv("HYFFT_DISABLE_TP") && d->dtype == HYFFT_BF16 && K0 <= 31 && K1 <= 31 && K0 <= 2 * N0 &&
+    // (opt-in while its CUDA-core stencil / reduction phases are slower than the fused FFT kernels)
+    h.tp = getenv("HYFFT_USE_TP") && !getenv("HYFFT_DISABLE_TP") && d->dtype == HYFFT_BF16 && K0 <= 31 && K1 <= 31 &&
+           K0 <= 2 * N0 &&
            K1 <= 2 * N1 && tp2d_dispatch(TP_PROBE, N0, N1, h.SK, nullptr, nullptr) == HYFFT_OK;
     if (h.tp) h.fused = false;
   }

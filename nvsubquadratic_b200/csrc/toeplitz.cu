@@ -192,14 +192,100 @@ __device__ __forceinline__ void set_status(int* st) {
   if (st) atomicExch(st, 1);
 }
 
+// ------------------------------------------------------------------ shared-memory helpers
+template <int CG>
+struct VS;
+template <>
+struct VS<4> {
+  using Raw = uint2;
+  static __device__ __forceinline__ void load(const bf16* p, float (&o)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+  }
+  static __device__ __forceinline__ void store(bf16* p, const float (&o)[4]) {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    h[0] = __floats2bfloat162_rn(o[0], o[1]);
+    h[1] = __floats2bfloat162_rn(o[2], o[3]);
+    *reinterpret_cast<uint2*>(p) = u;
+  }
+};
+template <>
+struct VS<8> {
+  using Raw = uint4;
+  static __device__ __forceinline__ void load(const bf16* p, float (&o)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(h[i]);
+      o[2 * i] = f.x;
+      o[2 * i + 1] = f.y;
+    }
+  }
+  static __device__ __forceinline__ void store(bf16* p, const float (&o)[8]) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(o[2 * i], o[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+  }
+};
+
+// Stage CG channels of NT_ tensors x HB images x NP positions (channels-last global, one
+// vector per position) into shared memory [tensor][image][position][CG]; zeros past B.
+template <int NP, int CG, int HB, int NT_>
+__device__ __forceinline__ void stage_tiles(bf16* R, const bf16* const* srcs, const long long* bst,
+                                            const long long* pst, int b_first, int B) {
+  using Raw = typename VS<CG>::Raw;
+  for (int i = threadIdx.x; i < NT_ * HB * NP; i += blockDim.x) {
+    const int t = i / (HB * NP), rem = i - t * (HB * NP), j = rem / NP, pos = rem - j * NP;
+    const int b = b_first + j;
+    Raw v = {};
+    if (b < B) v = __ldg(reinterpret_cast<const Raw*>(srcs[t] + (long long)b * bst[t] + (long long)pos * pst[t]));
+    *reinterpret_cast<Raw*>(R + ((long long)(t * HB + j) * NP + pos) * CG) = v;
+  }
+}
+
+// Depthwise SKxSK "same" cross-correlation of CG channels at (n0, n1) of a staged
+// image tile [NP][CG] (bf16, shared memory). SK == 0: identity.
+template <int N0, int N1, int SK, int CG>
+__device__ __forceinline__ void sstencil(const bf16* tile, const float* w, const float* bias, int n0, int n1,
+                                         float (&o)[CG]) {
+  if constexpr (SK == 0) {
+    VS<CG>::load(tile + (n0 * N1 + n1) * CG, o);
+  } else {
+    constexpr int OFF = (SK - 1) / 2, NT = SK * SK;
+#pragma unroll
+    for (int c = 0; c < CG; ++c) o[c] = bias ? bias[c] : 0.f;
+#pragma unroll
+    for (int a = 0; a < SK; ++a) {
+      const int i0 = n0 + a - OFF;
+      if (i0 < 0 || i0 >= N0) continue;
+#pragma unroll
+      for (int b = 0; b < SK; ++b) {
+        const int i1 = n1 + b - OFF;
+        if (i1 < 0 || i1 >= N1) continue;
+        float x[CG];
+        VS<CG>::load(tile + (i0 * N1 + i1) * CG, x);
+#pragma unroll
+        for (int c = 0; c < CG; ++c) o[c] = fmaf(w[c * NT + a * SK + b], x[c], o[c]);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ forward
 template <int N0, int N1, int SK, int CG, int NB>
 struct FwdLayout {
   using G = Geo<N0>;
   static constexpr int NT = SK > 0 ? SK * SK : 1;
-  static constexpr int RB = 32 * NB;
+  static constexpr int RB = 32 * NB, HB = 8, NP = N0 * N1;
   static constexpr size_t z = 0;
-  static constexpr size_t t = z + (size_t)CG * G::NR * RB;
+  static constexpr size_t r = z + (size_t)CG * G::NR * RB;                     // [3][HB][NP][CG] bf16
+  static constexpr size_t t = r + ((size_t)3 * HB * NP * CG * 2 + 127) / 128 * 128;
   static constexpr size_t w = t + 2 * (size_t)G::NBLK * G::BLKB;
   static constexpr size_t bar = w + ((4 * (3 * CG * NT + 3 * CG) + 15) / 16) * 16;
   static constexpr size_t total = bar + 32;
@@ -210,11 +296,13 @@ template <int N0, int N1, int SK, int CG, int NB>
 __global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
   using G = Geo<N0>;
   using L = FwdLayout<N0, N1, SK, CG, NB>;
-  constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = N0 * N1;
+  constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = L::NP, HB = L::HB;
   constexpr uint32_t IDESC = umma::idesc_bf16(128, NB, 0, 0);
   static_assert(MT <= 2, "8 warps cover at most two 128-row tiles");
+  static_assert(NB % HB == 0 && HB == 8, "images are staged 8 at a time");
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* Zt = smem + L::z;
+  bf16* R = reinterpret_cast<bf16*>(smem + L::r);
   unsigned char* Tb = smem + L::t;
   float* wts = reinterpret_cast<float*>(smem + L::w);
   float* bsm = wts + 3 * CG * NT;
@@ -235,27 +323,31 @@ __global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
   }
   for (int i = tid; i < 3 * CG; i += blockDim.x) bsm[i] = p.bias ? p.bias[(i / CG) * p.C + c0 + i % CG] : 0.f;
   for (int i = tid; i < CG * NR * RB / 16; i += blockDim.x) reinterpret_cast<uint4*>(Zt)[i] = make_uint4(0, 0, 0, 0);
-  __syncthreads();
 
-  const bf16* q = reinterpret_cast<const bf16*>(p.q) + c0;
-  const bf16* k = reinterpret_cast<const bf16*>(p.k) + c0;
+  const bf16* srcs[3] = {reinterpret_cast<const bf16*>(p.q) + c0, reinterpret_cast<const bf16*>(p.k) + c0,
+                         reinterpret_cast<const bf16*>(p.v) + c0};
+  const long long bst[3] = {p.in_bst, p.in_bst, p.in_bst}, pst[3] = {p.in_pst, p.in_pst, p.in_pst};
   const float* bq = p.bias ? bsm : nullptr;
   const float* bk = p.bias ? bsm + CG : nullptr;
   const float* bv = p.bias ? bsm + 2 * CG : nullptr;
-  // ---- z = q' * g1(k') into the operand layout
-  for (int it = tid; it < NB * NP; it += blockDim.x) {
-    const int img = it % NB, pos = it / NB, r = pos / N1, c = pos % N1;
-    const int b = b0 + img;
-    if (b >= p.B) continue;
-    const long long ib = (long long)b * p.in_bst;
-    float qv[CG], kv[CG];
-    gstencil<N0, N1, SK, CG>(q + ib, p.in_pst, wts, bq, r, c, qv);
-    gstencil<N0, N1, SK, CG>(k + ib, p.in_pst, wts + CG * NT, bk, r, c, kv);
-    const int off = zoff<NB>(img, r, c);
+
+  // ---- z = q' * g1(k') into the operand layout, 8 staged images at a time
+  for (int h0 = 0; h0 < NB; h0 += HB) {
+    __syncthreads();
+    stage_tiles<NP, CG, HB, 2>(R, srcs, bst, pst, b0 + h0, p.B);
+    __syncthreads();
+    for (int it = tid; it < HB * NP; it += blockDim.x) {
+      const int j = it / NP, pos = it - j * NP, r = pos / N1, c = pos - r * N1;
+      if (b0 + h0 + j >= p.B) continue;
+      float qv[CG], kv[CG];
+      sstencil<N0, N1, SK, CG>(R + (long long)j * NP * CG, wts, bq, r, c, qv);
+      sstencil<N0, N1, SK, CG>(R + (long long)(HB + j) * NP * CG, wts + CG * NT, bk, r, c, kv);
+      const int off = zoff<NB>(h0 + j, r, c);
 #pragma unroll
-    for (int ch = 0; ch < CG; ++ch) {
-      const float z = rbf(rbf(qv[ch]) * rbf(gate_f(p.gate1, rbf(kv[ch]))));
-      *reinterpret_cast<bf16*>(Zt + ch * NR * RB + off) = __float2bfloat16_rn(z);
+      for (int ch = 0; ch < CG; ++ch) {
+        const float z = rbf(rbf(qv[ch]) * rbf(gate_f(p.gate1, rbf(kv[ch]))));
+        *reinterpret_cast<bf16*>(Zt + ch * NR * RB + off) = __float2bfloat16_rn(z);
+      }
     }
   }
   umma::fence_async_smem();
@@ -286,35 +378,39 @@ __global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
       umma::commit(&mbar[buf]);
     }
   }
-  ok &= umma::mbar_wait(&mbar[(CG - 1) & 1], ((CG - 1) >> 1) & 1);
-  if (!ok && tid == 0) set_status(p.status);
-  umma::fence_after_sync();
 
-  // ---- epilogue: y = round(h) * round(g2(v'))
+  // ---- epilogue: y = round(h) * round(g2(v')), v staged 8 images at a time
   const int mt = warp >> 2, q4 = warp & 3;
-  if (mt < MT) {
-    const int m = q4 * 32 + lane, r = mt * 8 + (m >> 4), c = m & 15;
-    const bool valid = ok && r < N0 && c < N1;
-    const bf16* v = reinterpret_cast<const bf16*>(p.v) + c0;
-    bf16* y = reinterpret_cast<bf16*>(p.y) + c0;
-    const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
-#pragma unroll 1
-    for (int i0 = 0; i0 < NB; i0 += 8) {
+  const int m = q4 * 32 + lane, r = mt * 8 + (m >> 4), c = m & 15;
+  bf16* y = reinterpret_cast<bf16*>(p.y) + c0;
+  const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
+  const bf16* vsrc[1] = {srcs[2]};
+  for (int h0 = 0; h0 < NB; h0 += HB) {
+    __syncthreads();
+    stage_tiles<NP, CG, HB, 1>(R, vsrc, bst, pst, b0 + h0, p.B);
+    if (h0 == 0) ok &= umma::mbar_wait(&mbar[(CG - 1) & 1], ((CG - 1) >> 1) & 1);
+    __syncthreads();
+    umma::fence_after_sync();
+    if (mt < MT) {
+      const bool valid = ok && r < N0 && c < N1;
       float h[CG][8];
 #pragma unroll
-      for (int ch = 0; ch < CG; ++ch) umma::tmem_ld8(lane_base + (uint32_t)((ch * MT + mt) * NB + i0), h[ch]);
-#pragma unroll 1
-      for (int j = 0; j < 8; ++j) {
-        const int b = b0 + i0 + j;
-        if (!valid || b >= p.B) continue;
-        float vv[CG], out[CG];
-        gstencil<N0, N1, SK, CG>(v + (long long)b * p.in_bst, p.in_pst, wts + 2 * CG * NT, bv, r, c, vv);
+      for (int ch = 0; ch < CG; ++ch) umma::tmem_ld8(lane_base + (uint32_t)((ch * MT + mt) * NB + h0), h[ch]);
+      if (valid) {
+#pragma unroll 2
+        for (int j = 0; j < HB; ++j) {
+          const int b = b0 + h0 + j;
+          if (b >= p.B) break;
+          float vv[CG], out[CG];
+          sstencil<N0, N1, SK, CG>(R + (long long)j * NP * CG, wts + 2 * CG * NT, bv, r, c, vv);
 #pragma unroll
-        for (int ch = 0; ch < CG; ++ch) out[ch] = rbf(h[ch][j]) * rbf(gate_f(p.gate2, rbf(vv[ch])));
-        VG<CG>::store(y + (long long)b * p.out_bst + (long long)(r * N1 + c) * p.out_pst, out);
+          for (int ch = 0; ch < CG; ++ch) out[ch] = rbf(h[ch][j]) * rbf(gate_f(p.gate2, rbf(vv[ch])));
+          VG<CG>::store(y + (long long)b * p.out_bst + (long long)(r * N1 + c) * p.out_pst, out);
+        }
       }
     }
   }
+  if (!ok && tid == 0) set_status(p.status);
   umma::fence_before_sync();
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, L::tcols);
@@ -325,16 +421,17 @@ template <int N0, int N1, int SK, int CG, int NB>
 struct BwdLayout {
   using G = Geo<N0>;
   static constexpr int NT = SK > 0 ? SK * SK : 1;
-  static constexpr int RB = 32 * NB;
-  static constexpr int KMAX = 2 * 16 - 1;
+  static constexpr int RB = 32 * NB, HB = 8, NP = N0 * N1;
+  static constexpr int KR = 31, KP = 48;  // dK accumulator rows / padded row pitch (bank spread)
   static constexpr size_t z = 0;
   static constexpr size_t dh = z + (size_t)CG * G::NR * RB;
-  static constexpr size_t tf = dh + (size_t)CG * G::NR * RB;
-  static constexpr size_t tt = tf + 2 * (size_t)G::NBLK * G::BLKB;
-  static constexpr size_t ds = tt + 2 * (size_t)G::NBLK * G::BLKB;                 // [3][NB][NP][CG] bf16
-  static constexpr size_t dk = ds + ((size_t)3 * NB * N0 * N1 * CG * 2 + 15) / 16 * 16;  // [CG][KMAX*KMAX] f32
-  static constexpr size_t w = dk + (size_t)CG * KMAX * KMAX * 4;
-  static constexpr size_t dw = w + ((4 * (3 * CG * NT + 3 * CG) + 15) / 16) * 16;     // [3][CG][NT+1] f32
+  static constexpr size_t rsz = ((size_t)4 * HB * NP * CG * 2 + 127) / 128 * 128;
+  static constexpr size_t tsz = 2 * (size_t)G::NBLK * G::BLKB;  // forward + adjoint tables (aliased with R)
+  static constexpr size_t r = dh + (size_t)CG * G::NR * RB;      // [4][HB][NP][CG] bf16
+  static constexpr size_t ds = r + (rsz > tsz ? rsz : tsz);       // [3][HB][NP][CG] bf16
+  static constexpr size_t dk = ds + ((size_t)3 * HB * NP * CG * 2 + 15) / 16 * 16;
+  static constexpr size_t w = dk + (size_t)CG * KR * KP * 4;
+  static constexpr size_t dw = w + ((4 * (3 * CG * NT + 3 * CG) + 15) / 16) * 16;  // [3][CG][NT+1]
   static constexpr size_t bar = dw + ((4 * 3 * CG * (NT + 1) + 15) / 16) * 16;
   static constexpr size_t total = bar + 48;
 };
@@ -343,7 +440,7 @@ template <int N0, int N1, int SK, int CG, int NB>
 __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   using G = Geo<N0>;
   using L = BwdLayout<N0, N1, SK, CG, NB>;
-  constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = N0 * N1, KMAX = L::KMAX;
+  constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = L::NP, HB = L::HB, KP = L::KP;
   constexpr uint32_t IDESC = umma::idesc_bf16(128, NB, 0, 0);
   constexpr uint32_t IDESC_G = umma::idesc_bf16(128, 16 * N0, 1, 1);
   constexpr uint32_t TCOLS = 512;
@@ -353,8 +450,9 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   extern __shared__ __align__(1024) unsigned char smem[];
   unsigned char* Zt = smem + L::z;
   unsigned char* DHt = smem + L::dh;
-  unsigned char* Tf = smem + L::tf;
-  unsigned char* Tt = smem + L::tt;
+  bf16* R = reinterpret_cast<bf16*>(smem + L::r);
+  unsigned char* Tf = smem + L::r;  // block tables alias the staging area (phase 2 only)
+  unsigned char* Tt = Tf + G::NBLK * G::BLKB;
   bf16* ds = reinterpret_cast<bf16*>(smem + L::ds);
   float* dkacc = reinterpret_cast<float*>(smem + L::dk);
   float* wts = reinterpret_cast<float*>(smem + L::w);
@@ -370,7 +468,6 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   if (tid == 0) {
     umma::mbar_init(&mbar[0], 1);
     umma::mbar_init(&mbar[1], 1);
-    umma::mbar_init(&mbar[2], 1);
     umma::fence_mbar_init();
   }
   for (int i = tid; i < 3 * CG * NT; i += blockDim.x) {
@@ -379,52 +476,50 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   }
   for (int i = tid; i < 3 * CG; i += blockDim.x) bsm[i] = p.bias ? p.bias[(i / CG) * p.C + c0 + i % CG] : 0.f;
   for (int i = tid; i < 2 * CG * NR * RB / 16; i += blockDim.x) reinterpret_cast<uint4*>(Zt)[i] = make_uint4(0, 0, 0, 0);
-  for (int i = tid; i < CG * KMAX * KMAX; i += blockDim.x) dkacc[i] = 0.f;
+  for (int i = tid; i < CG * L::KR * KP; i += blockDim.x) dkacc[i] = 0.f;
   for (int i = tid; i < 3 * CG * (NT + 1); i += blockDim.x) dwacc[i] = 0.f;
-  __syncthreads();
 
-  const bf16* src[3] = {reinterpret_cast<const bf16*>(p.q) + c0, reinterpret_cast<const bf16*>(p.k) + c0,
-                        reinterpret_cast<const bf16*>(p.v) + c0};
-  const bf16* dyp = reinterpret_cast<const bf16*>(p.dy) + c0;
+  const bf16* srcs[4] = {reinterpret_cast<const bf16*>(p.q) + c0, reinterpret_cast<const bf16*>(p.k) + c0,
+                         reinterpret_cast<const bf16*>(p.v) + c0, reinterpret_cast<const bf16*>(p.dy) + c0};
+  const long long bst[4] = {p.in_bst, p.in_bst, p.in_bst, p.out_bst};
+  const long long pst[4] = {p.in_pst, p.in_pst, p.in_pst, p.out_pst};
   const float* bias3[3] = {p.bias ? bsm : nullptr, p.bias ? bsm + CG : nullptr, p.bias ? bsm + 2 * CG : nullptr};
 
-  // ---- z and dh into the operand layouts
-  for (int it = tid; it < NB * NP; it += blockDim.x) {
-    const int img = it % NB, pos = it / NB, r = pos / N1, c = pos % N1;
-    const int b = b0 + img;
-    if (b >= p.B) continue;
-    const long long ib = (long long)b * p.in_bst;
-    float qv[CG], kv[CG], vv[CG], g[CG];
-    gstencil<N0, N1, SK, CG>(src[0] + ib, p.in_pst, wts, bias3[0], r, c, qv);
-    gstencil<N0, N1, SK, CG>(src[1] + ib, p.in_pst, wts + CG * NT, bias3[1], r, c, kv);
-    gstencil<N0, N1, SK, CG>(src[2] + ib, p.in_pst, wts + 2 * CG * NT, bias3[2], r, c, vv);
-    VG<CG>::load(dyp + (long long)b * p.out_bst + (long long)pos * p.out_pst, g);
-    const int off = zoff<NB>(img, r, c);
+  // ---- z and dh into the operand layouts, 8 staged images at a time
+  for (int h0 = 0; h0 < NB; h0 += HB) {
+    __syncthreads();
+    stage_tiles<NP, CG, HB, 4>(R, srcs, bst, pst, b0 + h0, p.B);
+    __syncthreads();
+    for (int it = tid; it < HB * NP; it += blockDim.x) {
+      const int j = it / NP, pos = it - j * NP, r = pos / N1, c = pos - r * N1;
+      if (b0 + h0 + j >= p.B) continue;
+      float qv[CG], kv[CG], vv[CG], g[CG];
+      sstencil<N0, N1, SK, CG>(R + (long long)(0 * HB + j) * NP * CG, wts, bias3[0], r, c, qv);
+      sstencil<N0, N1, SK, CG>(R + (long long)(1 * HB + j) * NP * CG, wts + CG * NT, bias3[1], r, c, kv);
+      sstencil<N0, N1, SK, CG>(R + (long long)(2 * HB + j) * NP * CG, wts + 2 * CG * NT, bias3[2], r, c, vv);
+      VS<CG>::load(R + ((long long)(3 * HB + j) * NP + pos) * CG, g);
+      const int off = zoff<NB>(h0 + j, r, c);
 #pragma unroll
-    for (int ch = 0; ch < CG; ++ch) {
-      const float z = rbf(rbf(qv[ch]) * rbf(gate_f(p.gate1, rbf(kv[ch]))));
-      const float dh = rbf(g[ch] * rbf(gate_f(p.gate2, rbf(vv[ch]))));
-      *reinterpret_cast<bf16*>(Zt + ch * NR * RB + off) = __float2bfloat16_rn(z);
-      *reinterpret_cast<bf16*>(DHt + ch * NR * RB + off) = __float2bfloat16_rn(dh);
+      for (int ch = 0; ch < CG; ++ch) {
+        const float z = rbf(rbf(qv[ch]) * rbf(gate_f(p.gate1, rbf(kv[ch]))));
+        const float dh = rbf(g[ch] * rbf(gate_f(p.gate2, rbf(vv[ch]))));
+        *reinterpret_cast<bf16*>(Zt + ch * NR * RB + off) = __float2bfloat16_rn(z);
+        *reinterpret_cast<bf16*>(DHt + ch * NR * RB + off) = __float2bfloat16_rn(dh);
+      }
     }
   }
-  umma::fence_async_smem();
   __syncthreads();
-  umma::fence_after_sync();
   const uint32_t tmem = *tslot;
   const uint32_t DZ0 = (uint32_t)(CG * MT * NB);
 
-  // ---- per channel: H = T z and DZ = T^T dh
+  // ---- per channel: H = T z and DZ = T^T dh (one pair of block tables, reused per channel)
   bool ok = true;
   for (int ch = 0; ch < CG; ++ch) {
-    const int buf = ch & 1;
-    if (ch >= 2) ok &= umma::mbar_wait(&mbar[buf], ((ch - 2) >> 1) & 1);
-    unsigned char* tf = Tf + buf * G::NBLK * G::BLKB;
-    unsigned char* tt = Tt + buf * G::NBLK * G::BLKB;
+    if (ch >= 1) ok &= umma::mbar_wait(&mbar[0], (ch - 1) & 1);
     const int cg = c0 + ch;
     const float* fch = p.filt + (long long)cg * p.K0 * p.K1;
-    gen_blocks<N0, N1, false>(tf, fch, p.K0, p.K1, p.D[cg]);
-    gen_blocks<N0, N1, true>(tt, fch, p.K0, p.K1, p.D[cg]);
+    gen_blocks<N0, N1, false>(Tf, fch, p.K0, p.K1, p.D[cg]);
+    gen_blocks<N0, N1, true>(Tt, fch, p.K0, p.K1, p.D[cg]);
     umma::fence_async_smem();
     __syncthreads();
     if (tid == 0) {
@@ -435,56 +530,129 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
           const uint32_t blk = (uint32_t)((8 * mt - s + N0 - 1) * G::BLKB);
           const uint64_t dz = umma::sdesc(umma::su32(Zt + ch * NR * RB + s * RB), 16 * NB, 128);
           const uint64_t dd = umma::sdesc(umma::su32(DHt + ch * NR * RB + s * RB), 16 * NB, 128);
-          umma::mma(tmem + (uint32_t)((ch * MT + mt) * NB), umma::sdesc(umma::su32(tf) + blk, 128, 256), dz, IDESC,
+          umma::mma(tmem + (uint32_t)((ch * MT + mt) * NB), umma::sdesc(umma::su32(Tf) + blk, 128, 256), dz, IDESC,
                     s > 0 ? 1u : 0u);
-          umma::mma(tmem + DZ0 + (uint32_t)((ch * MT + mt) * NB), umma::sdesc(umma::su32(tt) + blk, 128, 256), dd,
+          umma::mma(tmem + DZ0 + (uint32_t)((ch * MT + mt) * NB), umma::sdesc(umma::su32(Tt) + blk, 128, 256), dd,
                     IDESC, s > 0 ? 1u : 0u);
         }
       }
-      umma::commit(&mbar[buf]);
+      umma::commit(&mbar[0]);
     }
   }
-  ok &= umma::mbar_wait(&mbar[(CG - 1) & 1], ((CG - 1) >> 1) & 1);
+  ok &= umma::mbar_wait(&mbar[0], (CG - 1) & 1);
   umma::fence_after_sync();
 
-  // ---- gate backward: dq' = dz g1(k'), dk' = dz q' g1'(k'), dv' = dy h g2'(v')  -> ds
+  // ---- gate backward + transposed short conv + weight gradients, 8 staged images at a time
   const int mt = warp >> 2, q4 = warp & 3;
   const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
-  if (mt < MT) {
-    const int m = q4 * 32 + lane, r = mt * 8 + (m >> 4), c = m & 15;
-    const bool valid = ok && r < N0 && c < N1;
-    const int pos = r * N1 + c;
-#pragma unroll 1
-    for (int i0 = 0; i0 < NB; i0 += 8) {
+  bf16* outs[3] = {reinterpret_cast<bf16*>(p.dq) + c0, reinterpret_cast<bf16*>(p.dk) + c0,
+                   reinterpret_cast<bf16*>(p.dv) + c0};
+  constexpr int OFF = SK > 0 ? (SK - 1) / 2 : 0;
+  for (int h0 = 0; h0 < NB; h0 += HB) {
+    __syncthreads();
+    stage_tiles<NP, CG, HB, 4>(R, srcs, bst, pst, b0 + h0, p.B);
+    __syncthreads();
+    umma::fence_after_sync();
+    if (mt < MT) {
+      const int m = q4 * 32 + lane, r = mt * 8 + (m >> 4), c = m & 15;
+      const bool valid = ok && r < N0 && c < N1;
+      const int pos = r * N1 + c;
       float hacc[CG][8], dacc[CG][8];
 #pragma unroll
       for (int ch = 0; ch < CG; ++ch) {
-        umma::tmem_ld8(lane_base + (uint32_t)((ch * MT + mt) * NB + i0), hacc[ch]);
-        umma::tmem_ld8(lane_base + DZ0 + (uint32_t)((ch * MT + mt) * NB + i0), dacc[ch]);
+        umma::tmem_ld8(lane_base + (uint32_t)((ch * MT + mt) * NB + h0), hacc[ch]);
+        umma::tmem_ld8(lane_base + DZ0 + (uint32_t)((ch * MT + mt) * NB + h0), dacc[ch]);
       }
+      if (valid) {
 #pragma unroll 1
-      for (int j = 0; j < 8; ++j) {
-        const int img = i0 + j, b = b0 + img;
-        if (!valid || b >= p.B) continue;
-        const long long ib = (long long)b * p.in_bst;
-        float qv[CG], kv[CG], vv[CG], g[CG], oq[CG], ok_[CG], ov[CG];
-        gstencil<N0, N1, SK, CG>(src[0] + ib, p.in_pst, wts, bias3[0], r, c, qv);
-        gstencil<N0, N1, SK, CG>(src[1] + ib, p.in_pst, wts + CG * NT, bias3[1], r, c, kv);
-        gstencil<N0, N1, SK, CG>(src[2] + ib, p.in_pst, wts + 2 * CG * NT, bias3[2], r, c, vv);
-        VG<CG>::load(dyp + (long long)b * p.out_bst + (long long)pos * p.out_pst, g);
+        for (int j = 0; j < HB; ++j) {
+          if (b0 + h0 + j >= p.B) break;
+          float qv[CG], kv[CG], vv[CG], g[CG], oq[CG], ok_[CG], ov[CG];
+          sstencil<N0, N1, SK, CG>(R + (long long)(0 * HB + j) * NP * CG, wts, bias3[0], r, c, qv);
+          sstencil<N0, N1, SK, CG>(R + (long long)(1 * HB + j) * NP * CG, wts + CG * NT, bias3[1], r, c, kv);
+          sstencil<N0, N1, SK, CG>(R + (long long)(2 * HB + j) * NP * CG, wts + 2 * CG * NT, bias3[2], r, c, vv);
+          VS<CG>::load(R + ((long long)(3 * HB + j) * NP + pos) * CG, g);
 #pragma unroll
-        for (int ch = 0; ch < CG; ++ch) {
-          const float qr = rbf(qv[ch]), kr = rbf(kv[ch]), vr = rbf(vv[ch]);
-          const float hv = rbf(hacc[ch][j]);
-          const float dz = rbf(dacc[ch][j]);
-          ov[ch] = g[ch] * hv * gate_df(p.gate2, vr);
-          oq[ch] = dz * rbf(gate_f(p.gate1, kr));
-          ok_[ch] = dz * qr * gate_df(p.gate1, kr);
+          for (int ch = 0; ch < CG; ++ch) {
+            const float qr = rbf(qv[ch]), kr = rbf(kv[ch]), vr = rbf(vv[ch]);
+            const float hv = rbf(hacc[ch][j]);
+            const float dz = rbf(dacc[ch][j]);
+            ov[ch] = g[ch] * hv * gate_df(p.gate2, vr);
+            oq[ch] = dz * rbf(gate_f(p.gate1, kr));
+            ok_[ch] = dz * qr * gate_df(p.gate1, kr);
+          }
+          bf16* dsi = ds + ((long long)j * NP + pos) * CG;
+          VS<CG>::store(dsi, oq);
+          VS<CG>::store(dsi + (long long)HB * NP * CG, ok_);
+          VS<CG>::store(dsi + 2LL * HB * NP * CG, ov);
         }
-        bf16* dsi = ds + ((long long)img * NP + pos) * CG;
-        VG<CG>::store(dsi, oq);
-        VG<CG>::store(dsi + (long long)NB * NP * CG, ok_);
-        VG<CG>::store(dsi + 2LL * NB * NP * CG, ov);
+      }
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int t = 0; t < 3; ++t) {
+      float wacc[CG][NT + 1];
+#pragma unroll
+      for (int ch = 0; ch < CG; ++ch)
+#pragma unroll
+        for (int u = 0; u <= NT; ++u) wacc[ch][u] = 0.f;
+      const float* wt = wts + t * CG * NT;
+      for (int it = tid; it < HB * NP; it += blockDim.x) {
+        const int j = it / NP, pos = it - j * NP, r = pos / N1, c = pos - r * N1;
+        const int b = b0 + h0 + j;
+        if (b >= p.B) continue;
+        const bf16* dimg = ds + (long long)(t * HB + j) * NP * CG;
+        float o[CG];
+        if constexpr (SK == 0) {
+          VS<CG>::load(dimg + pos * CG, o);
+        } else {
+#pragma unroll
+          for (int ch = 0; ch < CG; ++ch) o[ch] = 0.f;
+#pragma unroll
+          for (int a = 0; a < SK; ++a) {
+            const int i0 = r - a + OFF;
+            if (i0 < 0 || i0 >= N0) continue;
+#pragma unroll
+            for (int bq = 0; bq < SK; ++bq) {
+              const int i1 = c - bq + OFF;
+              if (i1 < 0 || i1 >= N1) continue;
+              float x[CG];
+              VS<CG>::load(dimg + (i0 * N1 + i1) * CG, x);
+#pragma unroll
+              for (int ch = 0; ch < CG; ++ch) o[ch] = fmaf(wt[ch * NT + a * SK + bq], x[ch], o[ch]);
+            }
+          }
+          float d0[CG];
+          VS<CG>::load(dimg + pos * CG, d0);
+          const bf16* inimg = R + (long long)(t * HB + j) * NP * CG;
+#pragma unroll
+          for (int a = 0; a < SK; ++a) {
+            const int i0 = r + a - OFF;
+            if (i0 < 0 || i0 >= N0) continue;
+#pragma unroll
+            for (int bq = 0; bq < SK; ++bq) {
+              const int i1 = c + bq - OFF;
+              if (i1 < 0 || i1 >= N1) continue;
+              float x[CG];
+              VS<CG>::load(inimg + (i0 * N1 + i1) * CG, x);
+#pragma unroll
+              for (int ch = 0; ch < CG; ++ch) wacc[ch][a * SK + bq] = fmaf(d0[ch], x[ch], wacc[ch][a * SK + bq]);
+            }
+          }
+#pragma unroll
+          for (int ch = 0; ch < CG; ++ch) wacc[ch][NT] += d0[ch];
+        }
+        VG<CG>::store(outs[t] + (long long)b * p.out_bst + (long long)pos * p.out_pst, o);
+      }
+      if constexpr (SK > 0) {
+#pragma unroll
+        for (int ch = 0; ch < CG; ++ch)
+#pragma unroll
+          for (int u = 0; u <= NT; ++u) {
+            float s = wacc[ch][u];
+            for (int o2 = 16; o2 > 0; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
+            if (lane == 0) atomicAdd(dwacc + (t * CG + ch) * (NT + 1) + u, s);
+          }
       }
     }
   }
@@ -501,14 +669,14 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
         const uint64_t db = umma::sdesc(umma::su32(Zt + ch * NR * RB), 128, 16 * NB);
         umma::mma(tmem + (uint32_t)(t * 16 * N0), da, db, IDESC_G, 0u);
       }
-      umma::commit(&mbar[2]);
+      umma::commit(&mbar[1]);
     }
-    ok &= umma::mbar_wait(&mbar[2], ch & 1);
+    ok &= umma::mbar_wait(&mbar[1], ch & 1);
     umma::fence_after_sync();
     if (mt < MT) {
       const int m = q4 * 32 + lane, ro = mt * 8 + (m >> 4), co = m & 15;
       const bool valid = ok && ro < N0 && co < N1;
-      float* acc = dkacc + ch * KMAX * KMAX;
+      float* acc = dkacc + ch * L::KR * KP;
 #pragma unroll 1
       for (int ri = 0; ri < N0; ++ri) {
         float gv[16];
@@ -518,7 +686,7 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
 #pragma unroll
         for (int ci = 0; ci < N1; ++ci) {
           const int bb = co - ci + ck1;
-          if (bb >= 0 && bb < p.K1) atomicAdd(acc + a * KMAX + bb, gv[ci]);
+          if (bb >= 0 && bb < p.K1) atomicAdd(acc + a * KP + bb, gv[ci]);
         }
       }
     }
@@ -527,80 +695,6 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
     umma::fence_after_sync();
   }
   if (!ok && tid == 0) set_status(p.status);
-
-  // ---- transposed short conv -> dq, dk, dv; weight / bias gradients
-  bf16* outs[3] = {reinterpret_cast<bf16*>(p.dq) + c0, reinterpret_cast<bf16*>(p.dk) + c0,
-                   reinterpret_cast<bf16*>(p.dv) + c0};
-  constexpr int OFF = SK > 0 ? (SK - 1) / 2 : 0;
-#pragma unroll 1
-  for (int t = 0; t < 3; ++t) {
-    float wacc[CG][NT + 1];
-#pragma unroll
-    for (int ch = 0; ch < CG; ++ch)
-#pragma unroll
-      for (int u = 0; u <= NT; ++u) wacc[ch][u] = 0.f;
-    const bf16* dst_t = ds + (long long)t * NB * NP * CG;
-    const float* wt = wts + t * CG * NT;
-    for (int it = tid; it < NB * NP; it += blockDim.x) {
-      const int img = it % NB, pos = it / NB, r = pos / N1, c = pos % N1;
-      const int b = b0 + img;
-      if (b >= p.B) continue;
-      const bf16* dimg = dst_t + (long long)img * NP * CG;
-      float o[CG];
-      if constexpr (SK == 0) {
-        VG<CG>::lds(dimg + pos * CG, o);
-      } else {
-#pragma unroll
-        for (int ch = 0; ch < CG; ++ch) o[ch] = 0.f;
-#pragma unroll
-        for (int a = 0; a < SK; ++a) {
-          const int i0 = r - a + OFF;
-          if (i0 < 0 || i0 >= N0) continue;
-#pragma unroll
-          for (int bq = 0; bq < SK; ++bq) {
-            const int i1 = c - bq + OFF;
-            if (i1 < 0 || i1 >= N1) continue;
-            float x[CG];
-            VG<CG>::lds(dimg + (i0 * N1 + i1) * CG, x);
-#pragma unroll
-            for (int ch = 0; ch < CG; ++ch) o[ch] = fmaf(wt[ch * NT + a * SK + bq], x[ch], o[ch]);
-          }
-        }
-        // dw[t][ch][tap] += d'(pos) * in(pos + tap - OFF)
-        float d0[CG];
-        VG<CG>::lds(dimg + pos * CG, d0);
-        const bf16* inimg = src[t] + (long long)b * p.in_bst;
-#pragma unroll
-        for (int a = 0; a < SK; ++a) {
-          const int i0 = r + a - OFF;
-          if (i0 < 0 || i0 >= N0) continue;
-#pragma unroll
-          for (int bq = 0; bq < SK; ++bq) {
-            const int i1 = c + bq - OFF;
-            if (i1 < 0 || i1 >= N1) continue;
-            float x[CG];
-            VG<CG>::load(inimg + (long long)(i0 * N1 + i1) * p.in_pst, x);
-#pragma unroll
-            for (int ch = 0; ch < CG; ++ch) wacc[ch][a * SK + bq] = fmaf(d0[ch], x[ch], wacc[ch][a * SK + bq]);
-          }
-        }
-#pragma unroll
-        for (int ch = 0; ch < CG; ++ch) wacc[ch][NT] += d0[ch];
-      }
-      VG<CG>::store(outs[t] + (long long)b * p.out_bst + (long long)pos * p.out_pst, o);
-    }
-    if constexpr (SK > 0) {
-#pragma unroll
-      for (int ch = 0; ch < CG; ++ch)
-#pragma unroll
-        for (int u = 0; u <= NT; ++u) {
-          float s = wacc[ch][u];
-          for (int o2 = 16; o2 > 0; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
-          if (lane == 0) atomicAdd(dwacc + (t * CG + ch) * (NT + 1) + u, s);
-        }
-    }
-  }
-  __syncthreads();
   if constexpr (SK > 0) {
     for (int i = tid; i < 3 * CG * (NT + 1); i += blockDim.x) {
       const int t = i / (CG * (NT + 1)), rr = i % (CG * (NT + 1)), ch = rr / (NT + 1), u = rr % (NT + 1);
@@ -612,7 +706,7 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   // filter gradient (of k' = k + D*delta): dfilt = dk', dD = dk' at the centre tap
   for (int i = tid; i < CG * p.K0 * p.K1; i += blockDim.x) {
     const int ch = i / (p.K0 * p.K1), rr = i % (p.K0 * p.K1), a = rr / p.K1, bb = rr % p.K1;
-    const float v = dkacc[ch * KMAX * KMAX + a * KMAX + bb];
+    const float v = dkacc[ch * L::KR * KP + a * KP + bb];
     atomicAdd(p.dfilt + ((long long)(c0 + ch) * p.K0 + a) * p.K1 + bb, v);
     if (a == ck0 && bb == ck1) atomicAdd(p.dD + c0 + ch, v);
   }
@@ -622,7 +716,7 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
 }
 
 // ------------------------------------------------------------------ dispatch
-constexpr int kFwdCG = 8, kBwdCG = 4, kNB = 16;
+constexpr int kFwdCG = 4, kBwdCG = 4, kNB = 16;
 
 template <int N0, int N1, int SK>
 static int tp_run(int op, const Fused2DParams* pp, cudaStream_t st) {
@@ -630,7 +724,7 @@ static int tp_run(int op, const Fused2DParams* pp, cudaStream_t st) {
   using LB = BwdLayout<N0, N1, SK, kBwdCG, kNB>;
   if (op == TP_PROBE) return (LF::total <= 227 * 1024 && LB::total <= 227 * 1024) ? HYFFT_OK : HYFFT_ERR_UNSUPPORTED;
   const Fused2DParams& p = *pp;
-  if (p.C % kFwdCG != 0) return HYFFT_ERR_UNSUPPORTED;
+  if (p.C % kFwdCG != 0 || p.C % kBwdCG != 0) return HYFFT_ERR_UNSUPPORTED;
   if (p.K0 > 2 * N0 - 1 + 1 || p.K1 > 2 * N1 - 1 + 1 || p.K0 > 31 || p.K1 > 31) return HYFFT_ERR_UNSUPPORTED;
   if (op == TP_FWD) {
     auto kern = tp2d_fwd_kernel<N0, N1, SK, kFwdCG, kNB>;

@@ -139,10 +139,10 @@ def test_fused_path_matches_general_engine(case, monkeypatch):
     sb = (0.1 * torch.randn(3 * C, generator=g)).to(dt) if (bias and sk) else None
     dy = torch.randn((B,) + S + (C,), generator=g).to(dt)
     outs = []
-    # default path (tensor-core Toeplitz for bf16 grids <= 16x16, else fused FFT), fused FFT only,
+    # tensor-core Toeplitz kernels (bf16 grids <= 16x16, opt-in), default fused FFT kernels,
     # general multi-pass engine
-    for env in ({}, {"HYFFT_DISABLE_TP": "1"}, {"HYFFT_DISABLE_FUSED": "1"}):
-        for key in ("HYFFT_DISABLE_TP", "HYFFT_DISABLE_FUSED"):
+    for env in ({"HYFFT_USE_TP": "1"}, {}, {"HYFFT_DISABLE_FUSED": "1"}):
+        for key in ("HYFFT_USE_TP", "HYFFT_DISABLE_FUSED"):
             if key in env:
                 monkeypatch.setenv(key, env[key])
             else:
