@@ -162,6 +162,22 @@ HYFFT_API int hyfft_cp_pack_full_to_split(const void* src, void* dst, int64_t B,
 HYFFT_API int hyfft_cp_unpack_full_to_split(const void* src, void* dst, int64_t B, int64_t d, int64_t l,
                                   int64_t rest, int32_t P, int32_t elem_bytes, void* stream);
 
+/* Channels-last form used by the fused CP mixer: tensors [B, seq, *rest, G, C] with the
+ * sequence split along its first spatial axis (l rows per rank; zigzag chunks r and
+ * 2P-1-r of 2P when zigzag != 0) and G channel groups (G = 3 moves q, k, v of one
+ * [B, seq, *rest, 3C] projection output at once). d = C / P.
+ *   PACK_SEQ_TO_CHAN    [B, l, rest, G, C]     -> send [P, B, l, rest, G, d]
+ *   UNPACK_SEQ_TO_CHAN  recv [P, B, l, rest, G, d] -> [B, P*l, rest, G, d] (natural order)
+ *   PACK_CHAN_TO_SEQ    [B, P*l, rest, G, d]  -> send [P, B, l, rest, G, d]
+ *   UNPACK_CHAN_TO_SEQ  recv [P, B, l, rest, G, d] -> [B, l, rest, G, C]                */
+#define HYFFT_CP_PACK_SEQ_TO_CHAN 0
+#define HYFFT_CP_UNPACK_SEQ_TO_CHAN 1
+#define HYFFT_CP_PACK_CHAN_TO_SEQ 2
+#define HYFFT_CP_UNPACK_CHAN_TO_SEQ 3
+HYFFT_API int hyfft_cp_permute_cl(const void* src, void* dst, int32_t op, int64_t B, int64_t l_rows, int64_t rest,
+                                  int64_t G, int64_t C, int32_t P, int32_t zigzag, int32_t elem_bytes,
+                                  void* stream);
+
 /* ---------------------------------------------------------------- misc */
 /* Message of the most recent error on this thread ("" if none). */
 HYFFT_API const char* hyfft_last_error(void);

@@ -16,13 +16,19 @@ namespace hyfft {
 
 extern std::atomic<long long> g_launches;
 
-enum CpMode { PACK_S2F = 0, UNPACK_S2F = 1, PACK_F2S = 2, UNPACK_F2S = 3 };
+// BHL modes ([B, C, seq, rest]) and channels-last modes ([B, seq*rest, G, C]: positions
+// outer, G channel groups, channels innermost; l, L, h count positions incl. rest).
+enum CpMode {
+  PACK_S2F = 0, UNPACK_S2F = 1, PACK_F2S = 2, UNPACK_F2S = 3,
+  CL_PACK_S2F = 4, CL_UNPACK_S2F = 5, CL_PACK_F2S = 6, CL_UNPACK_F2S = 7
+};
 
 struct CpDesc {
   int mode;
   long long B, C, d, l, L, h, rest;  // h = chunk length (l / 2 with zigzag)
   int P, zigzag;
   long long rows, run;                // rows of `run` contiguous elements
+  long long G;                        // channel groups (channels-last modes)
 };
 
 __device__ __forceinline__ void cp_row(const CpDesc& c, long long row, long long& so, long long& dof) {
@@ -60,10 +66,48 @@ __device__ __forceinline__ void cp_row(const CpDesc& c, long long row, long long
       }
       break;
     }
-    default: {  // UNPACK_F2S: row = (j, b, cc): dst[b, j*d+cc, :] = src[j, b, cc, :]
+    case UNPACK_F2S: {  // row = (j, b, cc): dst[b, j*d+cc, :] = src[j, b, cc, :]
       const long long cc = row % c.d, r = row / c.d, b = r % c.B, j = r / c.B;
       dof = ((b * c.P * c.d + j * c.d + cc) * c.l) * c.rest;
       so = (((j * c.B + b) * c.d + cc) * c.l) * c.rest;
+      break;
+    }
+    case CL_PACK_S2F: {  // row = (j, b, t, g): dst[j,b,t,g,:] = src[b,t,g, j*d : (j+1)*d]
+      const long long g = row % c.G, r1 = row / c.G, t = r1 % c.l, r2 = r1 / c.l, b = r2 % c.B, j = r2 / c.B;
+      so = ((b * c.l + t) * c.G + g) * c.C + j * c.d;
+      dof = (((j * c.B + b) * c.l + t) * c.G + g) * c.d;
+      break;
+    }
+    case CL_UNPACK_S2F: {
+      if (c.zigzag) {  // row = (r, b, half): rank r's chunk r (half 0) / 2P-1-r (half 1) -> natural place
+        const long long half = row & 1, r1 = row >> 1, b = r1 % c.B, r = r1 / c.B;
+        const long long chunk = half ? 2 * c.P - 1 - r : r;
+        so = ((r * c.B + b) * c.l + half * c.h) * c.G * c.d;
+        dof = (b * c.L + chunk * c.h) * c.G * c.d;
+      } else {  // row = (r, b)
+        const long long b = row % c.B, r = row / c.B;
+        so = (r * c.B + b) * c.l * c.G * c.d;
+        dof = (b * c.L + r * c.l) * c.G * c.d;
+      }
+      break;
+    }
+    case CL_PACK_F2S: {
+      if (c.zigzag) {  // row = (j, b, half): rank j gets natural chunks j, 2P-1-j
+        const long long half = row & 1, r1 = row >> 1, b = r1 % c.B, j = r1 / c.B;
+        const long long chunk = half ? 2 * c.P - 1 - j : j;
+        so = (b * c.L + chunk * c.h) * c.G * c.d;
+        dof = ((j * c.B + b) * c.l + half * c.h) * c.G * c.d;
+      } else {
+        const long long b = row % c.B, j = row / c.B;
+        so = (b * c.L + j * c.l) * c.G * c.d;
+        dof = (j * c.B + b) * c.l * c.G * c.d;
+      }
+      break;
+    }
+    default: {  // CL_UNPACK_F2S: row = (r, b, t, g): dst[b,t,g, r*d : (r+1)*d] = src[r,b,t,g,:]
+      const long long g = row % c.G, r1 = row / c.G, t = r1 % c.l, r2 = r1 / c.l, b = r2 % c.B, r = r2 / c.B;
+      so = (((r * c.B + b) * c.l + t) * c.G + g) * c.d;
+      dof = ((b * c.l + t) * c.G + g) * c.C + r * c.d;
       break;
     }
   }
@@ -94,9 +138,14 @@ static int cp_launch(CpDesc c, const void* src, void* dst, int eb, cudaStream_t 
   if (c.rows <= 0 || c.run <= 0) return HYFFT_OK;
   const bool aligned = ((uintptr_t)src % 16 == 0) && ((uintptr_t)dst % 16 == 0);
   // every row offset is a multiple of `run` or of h*rest; require those to be 16-byte multiples
-  const long long unit = c.zigzag && (c.mode == UNPACK_S2F || c.mode == PACK_F2S) ? c.h * c.rest : c.run;
-  const int vec_ok = aligned && ((c.run * eb) % 16 == 0) && ((unit * eb) % 16 == 0) && ((c.l * c.rest * eb) % 16 == 0) &&
-                     ((c.L * c.rest * eb) % 16 == 0);
+  int vec_ok;
+  if (c.mode >= CL_PACK_S2F) {  // every offset is a multiple of d or C elements
+    vec_ok = aligned && ((c.d * eb) % 16 == 0) && ((c.C * eb) % 16 == 0) && ((c.run * eb) % 16 == 0);
+  } else {
+    const long long unit = c.zigzag && (c.mode == UNPACK_S2F || c.mode == PACK_F2S) ? c.h * c.rest : c.run;
+    vec_ok = aligned && ((c.run * eb) % 16 == 0) && ((unit * eb) % 16 == 0) && ((c.l * c.rest * eb) % 16 == 0) &&
+             ((c.L * c.rest * eb) % 16 == 0);
+  }
   long long blocks = (c.rows * 32 + 255) / 256;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
   if (blocks < 1) blocks = 1;
@@ -151,6 +200,34 @@ int hyfft_cp_pack_full_to_split(const void* src, void* dst, int64_t B, int64_t d
   c.zigzag = zigzag ? 1 : 0;
   c.rows = zigzag ? (long long)P * B * d * 2 : (long long)P * B * d;
   c.run = c.h * rest;
+  return cp_launch(c, src, dst, elem_bytes, (cudaStream_t)stream);
+}
+
+int hyfft_cp_permute_cl(const void* src, void* dst, int32_t op, int64_t B, int64_t l_rows, int64_t rest, int64_t G,
+                        int64_t C, int32_t P, int32_t zigzag, int32_t elem_bytes, void* stream) {
+  if (P < 1 || !src || !dst || B < 1 || l_rows < 1 || rest < 1 || G < 1 || C < 1 || C % P != 0)
+    return HYFFT_ERR_INVALID;
+  if (zigzag && (l_rows % 2 != 0)) return HYFFT_ERR_INVALID;
+  CpDesc c{};
+  c.B = B; c.C = C; c.d = C / P; c.G = G; c.P = P; c.zigzag = zigzag ? 1 : 0; c.rest = 1;
+  c.l = l_rows * rest;                        // positions per rank
+  c.L = c.l * P;                              // positions of the full sequence
+  c.h = zigzag ? (l_rows / 2) * rest : c.l;   // positions per zigzag chunk
+  switch (op) {
+    case HYFFT_CP_PACK_SEQ_TO_CHAN: c.mode = CL_PACK_S2F; c.rows = (long long)P * B * c.l * G; c.run = c.d; break;
+    case HYFFT_CP_UNPACK_SEQ_TO_CHAN:
+      c.mode = CL_UNPACK_S2F;
+      c.rows = zigzag ? (long long)P * B * 2 : (long long)P * B;
+      c.run = (zigzag ? c.h : c.l) * G * c.d;
+      break;
+    case HYFFT_CP_PACK_CHAN_TO_SEQ:
+      c.mode = CL_PACK_F2S;
+      c.rows = zigzag ? (long long)P * B * 2 : (long long)P * B;
+      c.run = (zigzag ? c.h : c.l) * G * c.d;
+      break;
+    case HYFFT_CP_UNPACK_CHAN_TO_SEQ: c.mode = CL_UNPACK_F2S; c.rows = (long long)P * B * c.l * G; c.run = c.d; break;
+    default: return HYFFT_ERR_INVALID;
+  }
   return cp_launch(c, src, dst, elem_bytes, (cudaStream_t)stream);
 }
 

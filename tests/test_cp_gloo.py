@@ -1,0 +1,151 @@
+"""Context-parallel redistribution on CPU gloo ranks (world 2 and 4).
+
+Drives the product's collective choreography (``nvsubquadratic_b200.cp``: pack ->
+``all_to_all_single`` -> unpack, autograd duals, zigzag helpers) on CPU processes, with
+the device gather kernels swapped for a plain-torch restatement of the same
+permutations (test-only), and checks the results against the reference's own
+``all_to_all_single_fn`` outputs captured on a real gloo group
+(``tests/golden/cp.pt``, ``tests/golden/make_golden.py``).
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests.conftest import ROOT
+
+
+def cpu_permute(x, op, B, l_rows, rest, G, C, P, zigzag, out):
+    """Plain-torch restatement of the four channels-last permutations of hyfft_cp_permute_cl."""
+    d = C // P
+    h = l_rows // 2
+    if op == 0:  # [B, l, *rest, G, C] -> [P, B, l, *rest, G, d]
+        out.copy_(torch.stack([x[..., j * d:(j + 1) * d] for j in range(P)], dim=0))
+    elif op == 1:  # recv [P, B, l, ...] -> [B, P*l, ...] natural order
+        for r in range(P):
+            if zigzag:
+                out[:, r * h:(r + 1) * h] = x[r][:, :h]
+                c2 = 2 * P - 1 - r
+                out[:, c2 * h:(c2 + 1) * h] = x[r][:, h:]
+            else:
+                out[:, r * l_rows:(r + 1) * l_rows] = x[r]
+    elif op == 2:  # [B, P*l, ...] -> [P, B, l, ...]
+        for j in range(P):
+            if zigzag:
+                c2 = 2 * P - 1 - j
+                out[j] = torch.cat([x[:, j * h:(j + 1) * h], x[:, c2 * h:(c2 + 1) * h]], dim=1)
+            else:
+                out[j] = x[:, j * l_rows:(j + 1) * l_rows]
+    else:  # recv [P, B, l, ..., d] -> [B, l, ..., C]
+        for r in range(P):
+            out[..., r * d:(r + 1) * d] = x[r]
+    return out
+
+
+def _worker(rank, world, port, result_dir):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    from nvsubquadratic_b200 import cp
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cp._permute_impl = cpu_permute
+    golden = torch.load(os.path.join(ROOT, "tests", "golden", "cp.pt"), weights_only=False)[f"world{world}"]
+    group = dist.group.WORLD
+    errors = []
+    for nd in (1, 2, 3):
+        ref = golden[rank][nd]
+        local = cp.zigzag_split_across_group_ranks(ref["full"], group, seq_dim=2)
+        if not torch.equal(local, ref["local"]):
+            errors.append(f"zigzag split nd={nd}")
+        s2f = cp.all_to_all_single_fn(group, "split_to_full", local, True)
+        if not torch.equal(s2f, ref["s2f"]):
+            errors.append(f"split_to_full nd={nd}")
+        s2f_nz = cp.all_to_all_single_fn(group, "split_to_full", local, False)
+        if not torch.equal(s2f_nz, ref["s2f_nozigzag"]):
+            errors.append(f"split_to_full no-zigzag nd={nd}")
+        f2s = cp.all_to_all_single_fn(group, "full_to_split", s2f, True)
+        if not torch.equal(f2s, ref["f2s"]):
+            errors.append(f"full_to_split nd={nd}")
+        gathered = cp.zigzag_gather_from_group_ranks(local, group, seq_dim=2)
+        if not torch.equal(gathered, ref["full"]):
+            errors.append(f"zigzag gather nd={nd}")
+        # autograd dual: d/dx <g, A2A(x)> = A2A^T(g)
+        x = local.clone().requires_grad_(True)
+        y = cp.AllToAllSingleFunction.apply(x, group, "split_to_full", True)
+        g = torch.randn_like(y)
+        (y * g).sum().backward()
+        back = cp.all_to_all_single_fn(group, "full_to_split", g, True)
+        if not torch.equal(x.grad, back):
+            errors.append(f"autograd dual nd={nd}")
+    # channels-last q/k/v path with 3 channel groups: seq->chan->seq round trip
+    torch.manual_seed(rank)
+    x = torch.randn(2, 8, 3, 3, 4 * world)  # [B, l, rest, G, C]
+    y = cp.chan_to_seq(cp.seq_to_chan(x, group), group)
+    if not torch.equal(x, y):
+        errors.append("channels-last round trip")
+    torch.save(errors, os.path.join(result_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_cp_collectives_match_reference(world, tmp_path):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+    for r in range(world):
+        errors = torch.load(tmp_path / f"rank{r}.pt")
+        assert errors == [], (r, errors)
+
+
+def test_rank_failure_is_reported_not_hung(tmp_path):
+    """A rank that raises before the collective must surface as a failure on the host side
+    (process-group timeout), not hang the job (host-side fault injection, gloo, CPU)."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    codes = sorted(p.exitcode for p in procs)
+    assert all(c is not None for c in codes), "a rank hung"
+    assert codes[-1] != 0, "the injected failure was not reported"
+
+
+def _failing_worker(rank, world, port):
+    import datetime
+    import sys
+
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    from nvsubquadratic_b200 import cp
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    cp._permute_impl = cpu_permute
+    if rank == 1:
+        raise SystemExit(3)  # this rank dies before joining the collective
+    x = torch.randn(1, 4, 8)
+    cp.all_to_all_single_fn(dist.group.WORLD, "split_to_full", x, True)  # times out -> raises
