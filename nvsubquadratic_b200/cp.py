@@ -190,11 +190,20 @@ def _channel_block(t: torch.Tensor | None, dim: int, r: int, d: int, groups: int
     return torch.cat([t.narrow(dim, g * C + r * d, d) for g in range(groups)], dim=dim)
 
 
+def _fused_local(*args, **kwargs):
+    from .hyena import hyena_fused
+
+    return hyena_fused(*args, **kwargs)
+
+
+# The single-device mixer run on the local channel block. Swappable so that host-side
+# tests can drive the CP choreography on CPU gloo ranks; the product path is the CUDA one.
+_local_mixer = _fused_local
+
+
 def hyena_context_parallel(module, query, key, value, filt, group, zigzag: bool = True):
     """CP forward of ``HyenaB200``: q, k, v ``[B, l, *rest, C]`` hold this rank's zigzag
     sequence chunks; returns y in the same layout."""
-    from .hyena import hyena_fused
-
     P, r = group.size(), group.rank()
     C = query.shape[-1]
     assert C % P == 0, f"hidden_dim {C} must be divisible by the CP size {P}"
@@ -206,7 +215,7 @@ def hyena_context_parallel(module, query, key, value, filt, group, zigzag: bool 
     D_r = _channel_block(module.shortcut, 0, r, d).to(query.dtype)
     sw_r = _channel_block(module.short_weight, 0, r, d, groups=3, C=C)
     sb_r = _channel_block(module.short_bias, 0, r, d, groups=3, C=C)
-    y_loc = hyena_fused(q, k, v, filt_r, D_r, sw_r, sb_r, causal=module.causal, short_causal=module.short_causal,
-                        gate1=module.gate1, gate2=module.gate2)        # [B, L, *rest, d]
+    y_loc = _local_mixer(q, k, v, filt_r, D_r, sw_r, sb_r, causal=module.causal, short_causal=module.short_causal,
+                         gate1=module.gate1, gate2=module.gate2)       # [B, L, *rest, d]
     y = ChanToSeq.apply(y_loc.unsqueeze(-2), group, zigzag)            # [B, l, *rest, 1, C]
     return y.squeeze(-2)

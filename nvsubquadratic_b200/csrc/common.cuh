@@ -10,6 +10,23 @@
 
 namespace hyfft {
 
+// The library links its own (static) CUDA runtime, whose current device is independent
+// of the caller's: make the device that owns `p` current before launching anything.
+inline int bind_device_of(const void* p) {
+  if (!p) return HYFFT_OK;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return HYFFT_OK;
+  }
+  if (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged) {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != a.device && cudaSetDevice(a.device) != cudaSuccess) return HYFFT_ERR_CUDA;
+  }
+  return HYFFT_OK;
+}
+
 // ---------------------------------------------------------------- complex
 __device__ __forceinline__ float2 cmul(float2 a, float2 b) {
   return make_float2(fmaf(a.x, b.x, -a.y * b.y), fmaf(a.x, b.y, a.y * b.x));

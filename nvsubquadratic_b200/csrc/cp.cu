@@ -11,6 +11,7 @@
 #include <atomic>
 
 #include "../../include/hyfft.h"
+#include "common.cuh"
 
 namespace hyfft {
 
@@ -169,6 +170,7 @@ extern "C" {
 int hyfft_cp_pack_split_to_full(const void* src, void* dst, int64_t B, int64_t C, int64_t l, int64_t rest, int32_t P,
                                 int32_t elem_bytes, void* stream) {
   if (P < 1 || C % P != 0 || !src || !dst) return HYFFT_ERR_INVALID;
+  if (bind_device_of(src) != HYFFT_OK) return HYFFT_ERR_CUDA;
   CpDesc c{};
   c.mode = PACK_S2F;
   c.B = B; c.C = C; c.d = C / P; c.l = l; c.L = l * P; c.h = l; c.rest = rest; c.P = P; c.zigzag = 0;
@@ -181,6 +183,7 @@ int hyfft_cp_unpack_split_to_full(const void* src, void* dst, int64_t B, int64_t
                                   int32_t zigzag, int32_t elem_bytes, void* stream) {
   if (P < 1 || !src || !dst) return HYFFT_ERR_INVALID;
   if (zigzag && (l % 2 != 0)) return HYFFT_ERR_INVALID;
+  if (bind_device_of(src) != HYFFT_OK) return HYFFT_ERR_CUDA;
   CpDesc c{};
   c.mode = UNPACK_S2F;
   c.B = B; c.d = d; c.C = d * P; c.l = l; c.L = l * P; c.h = zigzag ? l / 2 : l; c.rest = rest; c.P = P;
@@ -194,6 +197,7 @@ int hyfft_cp_pack_full_to_split(const void* src, void* dst, int64_t B, int64_t d
                                 int32_t zigzag, int32_t elem_bytes, void* stream) {
   if (P < 1 || !src || !dst) return HYFFT_ERR_INVALID;
   if (zigzag ? (L % (2 * P) != 0) : (L % P != 0)) return HYFFT_ERR_INVALID;
+  if (bind_device_of(src) != HYFFT_OK) return HYFFT_ERR_CUDA;
   CpDesc c{};
   c.mode = PACK_F2S;
   c.B = B; c.d = d; c.C = d * P; c.L = L; c.l = L / P; c.h = zigzag ? L / (2 * P) : L / P; c.rest = rest; c.P = P;
@@ -208,6 +212,7 @@ int hyfft_cp_permute_cl(const void* src, void* dst, int32_t op, int64_t B, int64
   if (P < 1 || !src || !dst || B < 1 || l_rows < 1 || rest < 1 || G < 1 || C < 1 || C % P != 0)
     return HYFFT_ERR_INVALID;
   if (zigzag && (l_rows % 2 != 0)) return HYFFT_ERR_INVALID;
+  if (bind_device_of(src) != HYFFT_OK) return HYFFT_ERR_CUDA;
   CpDesc c{};
   c.B = B; c.C = C; c.d = C / P; c.G = G; c.P = P; c.zigzag = zigzag ? 1 : 0; c.rest = 1;
   c.l = l_rows * rest;                        // positions per rank
@@ -234,6 +239,7 @@ int hyfft_cp_permute_cl(const void* src, void* dst, int32_t op, int64_t B, int64
 int hyfft_cp_unpack_full_to_split(const void* src, void* dst, int64_t B, int64_t d, int64_t l, int64_t rest, int32_t P,
                                   int32_t elem_bytes, void* stream) {
   if (P < 1 || !src || !dst) return HYFFT_ERR_INVALID;
+  if (bind_device_of(src) != HYFFT_OK) return HYFFT_ERR_CUDA;
   CpDesc c{};
   c.mode = UNPACK_F2S;
   c.B = B; c.d = d; c.C = d * P; c.l = l; c.L = l * P; c.h = l; c.rest = rest; c.P = P; c.zigzag = 0;

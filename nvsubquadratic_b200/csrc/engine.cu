@@ -602,6 +602,7 @@ int hyfft_conv_forward(const hyfft_conv_desc* d, const void* x, const float* ker
   ConvPlan p;
   HY_TRY(make_conv_plan(d, p));
   if (!x || !kernel || !y) return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  if (bind_device_of(x) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "cannot make the device of the inputs current");
   size_t need, nb;
   conv_ws_sizes(p, need, nb);
   if (!workspace || workspace_bytes < need) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, need);
@@ -629,6 +630,7 @@ int hyfft_conv_backward(const hyfft_conv_desc* d, const void* x, const float* ke
   ConvPlan p;
   HY_TRY(make_conv_plan(d, p));
   if (!x || !kernel || !dy) return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  if (bind_device_of(x) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "cannot make the device of the inputs current");
   size_t nf, need;
   conv_ws_sizes(p, nf, need);
   if (!workspace || workspace_bytes < need) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, need);
@@ -1002,6 +1004,7 @@ int hyfft_hyena_forward(const hyfft_hyena_desc* d, const void* q, const void* k,
   HyenaPlan h;
   HY_TRY(make_hyena_plan(d, h));
   if (!q || !k || !v || !filt || !D || !y) return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  if (bind_device_of(q) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "cannot make the device of the inputs current");
   if (h.sg.has_conv && !short_w) return fail(HYFFT_ERR_INVALID, "short conv weight missing");
   if (h.sg.has_bias && !short_b) return fail(HYFFT_ERR_INVALID, "short conv bias missing");
   size_t f, b, s;
@@ -1030,6 +1033,7 @@ int hyfft_hyena_backward(const hyfft_hyena_desc* d, const void* q, const void* k
   HY_TRY(make_hyena_plan(d, h));
   if (!q || !k || !v || !filt || !D || !dy || !dq || !dk || !dv || !dfilt)
     return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  if (bind_device_of(q) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "cannot make the device of the inputs current");
   if (h.sg.has_conv && !short_w) return fail(HYFFT_ERR_INVALID, "short conv weight missing");
   size_t f, b, s;
   hyena_sizes(h, f, b, s);

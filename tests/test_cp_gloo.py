@@ -149,3 +149,86 @@ def _failing_worker(rank, world, port):
         raise SystemExit(3)  # this rank dies before joining the collective
     x = torch.randn(1, 4, 8)
     cp.all_to_all_single_fn(dist.group.WORLD, "split_to_full", x, True)  # times out -> raises
+
+
+def _oracle_local(q, k, v, filt, D, sw, sb, *, causal, short_causal, gate1, gate2):
+    from oracle.hyena import hyena_forward
+
+    return hyena_forward(q, k, v, filt, D, sw, sb, causal=causal, short_causal=short_causal, gate1=gate1,
+                         gate2=gate2)
+
+
+CP_MIXER_CASES = [
+    # nd, B, C, S, causal, short_k, gate1, gate2
+    (1, 2, 8, (32,), True, 7, "identity", "identity"),
+    (2, 2, 8, (8, 6), False, 3, "silu", "sigmoid"),
+    (1, 1, 8, (16,), False, 3, "sigmoid", "silu"),
+]
+
+
+def _mixer_worker(rank, world, port, result_dir):
+    import sys
+
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    from nvsubquadratic_b200 import cp
+    from nvsubquadratic_b200.hyena import ExplicitKernel, HyenaB200
+    from oracle.hyena import hyena_forward
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cp._permute_impl = cpu_permute
+    cp._local_mixer = _oracle_local
+    group = dist.group.WORLD
+    out = []
+    for nd, B, C, S, causal, sk, g1, g2 in CP_MIXER_CASES:
+        gen = torch.Generator().manual_seed(7)
+        q, k, v = (torch.randn((B,) + S + (C,), generator=gen, dtype=torch.float64) for _ in range(3))
+        K = S if causal else tuple(2 * s - 1 for s in S)
+        filt = torch.randn((1, C) + K, generator=gen, dtype=torch.float64) / (torch.tensor(K).prod() ** 0.5)
+        dy = torch.randn((B,) + S + (C,), generator=gen, dtype=torch.float64)
+        torch.manual_seed(7)  # identical module parameters on every rank
+        mod = HyenaB200(C, nd, ExplicitKernel(filt), short_kernel_size=sk, gate1=g1, gate2=g2, causal=causal,
+                        dtype=torch.float64)
+        qf, kf, vf = (t.clone().requires_grad_(True) for t in (q, k, v))
+        yf = hyena_forward(qf, kf, vf, mod.kernel_fn.weight, mod.shortcut, mod.short_weight, mod.short_bias,
+                           causal=causal, gate1=g1, gate2=g2)
+        yf.backward(dy)
+        ref = [yf.detach(), qf.grad, kf.grad, vf.grad, mod.kernel_fn.weight.grad.clone(), mod.shortcut.grad.clone(),
+               mod.short_weight.grad.clone()]
+        mod.zero_grad()
+        ql, kl, vl = (cp.zigzag_split_across_group_ranks(t, group, seq_dim=1).requires_grad_(True)
+                      for t in (q, k, v))
+        yl = mod(ql, kl, vl, cp_group=group)
+        yl.backward(cp.zigzag_split_across_group_ranks(dy, group, seq_dim=1))
+        got = [cp.zigzag_gather_from_group_ranks(t, group, seq_dim=1) for t in (yl.detach(), ql.grad, kl.grad, vl.grad)]
+        for p in (mod.kernel_fn.weight, mod.shortcut, mod.short_weight):
+            gsum = p.grad.clone()
+            dist.all_reduce(gsum)  # each rank holds the gradient of its channel block
+            got.append(gsum)
+        out.append([float((a - b).norm() / a.norm()) for a, b in zip(ref, got)])
+    torch.save(out, os.path.join(result_dir, f"rank{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_cp_mixer_choreography_matches_single_device(world, tmp_path):
+    """hyena_context_parallel (zigzag split -> seq->chan all-to-all -> local mixer on the
+    channel block -> chan->seq all-to-all, and the autograd duals) reproduces the
+    single-device mixer and its gradients; the local mixer and the permutations are the
+    CPU restatements here, the CUDA ones are covered by the GPU tests."""
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_mixer_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0, f"rank exited with {p.exitcode}"
+    for r in range(world):
+        errs = torch.load(tmp_path / f"rank{r}.pt")
+        for case, e in zip(CP_MIXER_CASES, errs):
+            assert max(e) < 1e-6, (r, case, e)  # the oracle's FFT runs in float32

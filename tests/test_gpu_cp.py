@@ -99,6 +99,7 @@ def _cp_worker(rank, world, port, case, result_dir):
     K = S if causal else tuple(2 * s - 1 for s in S)
     filt = torch.randn((1, C) + K, generator=gen) / (torch.tensor(K).prod() ** 0.5)
     dy = torch.randn((B,) + S + (C,), generator=gen).to(dt)
+    torch.manual_seed(11)  # identical module parameters on every rank
     mod = HyenaB200(C, nd, ExplicitKernel(filt), short_kernel_size=sk, gate1=g1, gate2=g2, causal=causal,
                     dtype=torch.float32).cuda()
     with torch.no_grad():
