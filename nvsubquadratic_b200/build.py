@@ -15,6 +15,7 @@ import os
 import shutil
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -44,12 +45,21 @@ def _digest() -> str:
     return h.hexdigest()
 
 
+def _object_digest(src: Path, common: list[str]) -> str:
+    """Inputs of one object file: the source, every shared header, the flags."""
+    h = hashlib.sha256()
+    for p in [src] + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted((ROOT / "include").glob("*.h")):
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    h.update(" ".join(common).encode())
+    return h.hexdigest()
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     digest = _digest()
     if not force and LIB.exists() and STAMP.exists() and STAMP.read_text().strip() == digest:
         return LIB
     nvcc = _nvcc()
-    objs = []
     tmp = PKG / "_build"
     tmp.mkdir(exist_ok=True)
     common = [
@@ -58,18 +68,25 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     ]
     if verbose:
         common += ["-Xptxas", "-v"]
-    for src in SOURCES:
+
+    def compile_one(src: str) -> str:
         s = CSRC / src
-        if not s.exists():
-            continue
         o = tmp / (s.stem + ".o")
-        cmd = [nvcc, *common, "-c", str(s), "-o", str(o)]
-        r = subprocess.run(cmd, capture_output=True, text=True)
+        stamp = tmp / (s.stem + ".o.stamp")
+        od = _object_digest(s, common)
+        if not force and o.exists() and stamp.exists() and stamp.read_text().strip() == od:
+            return str(o)
+        r = subprocess.run([nvcc, *common, "-c", str(s), "-o", str(o)], capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"nvcc failed for {src}:\n{r.stdout}\n{r.stderr}")
         if verbose and r.stderr:
             print(r.stderr, file=sys.stderr)
-        objs.append(str(o))
+        stamp.write_text(od)
+        return str(o)
+
+    srcs = [s for s in SOURCES if (CSRC / s).exists()]
+    with ThreadPoolExecutor(max_workers=len(srcs)) as pool:
+        objs = list(pool.map(compile_one, srcs))
     out_tmp = tmp / "libhyfft.so"
     cmd = [nvcc, *ARCH, "-shared", "-cudart", "static", "-o", str(out_tmp), *objs]
     r = subprocess.run(cmd, capture_output=True, text=True)
