@@ -160,3 +160,79 @@ def test_fused_path_matches_general_engine(case, monkeypatch):
             if a is None:
                 continue
             assert rel_l2(a, b) <= tol, (variant, name, rel_l2(a, b))
+
+
+class _Kernel(torch.nn.Module):
+    """Stand-in kernel generator with CKConvND's call shape: grid_lens -> ([1, *(2n-1), C], grid)."""
+
+    def __init__(self, C, nd, n, gen):
+        super().__init__()
+        K = tuple(2 * s - 1 for s in n)
+        self.w = torch.nn.Parameter(torch.randn((1,) + K + (C,), generator=gen) / (torch.tensor(K).prod() ** 0.5))
+
+    def forward(self, grid_lens, conditioning=None):
+        return self.w, None
+
+
+class _RefLikeMixer(torch.nn.Module):
+    """The attributes of a reference Hyena instance the b200 adapter reads."""
+
+    def __init__(self, C, nd, n, short_conv, causal, gate1, gate2, gen):
+        super().__init__()
+        gc = torch.nn.Module()
+        gc.fft_backend, gc.is_causal, gc.mask = "b200", causal, torch.nn.Identity()
+        gc.kernel = _Kernel(C, nd, n, gen)
+        gc.shortcut = torch.nn.Parameter(torch.randn(C, generator=gen))
+        self.global_conv = gc
+        self.short_conv = short_conv
+        self.gate_nonlinear, self.gate_nonlinear_2 = gate1, gate2
+        self.pixelhyena_norm = self.output_norm = torch.nn.Identity()
+        self.q_norm = self.k_norm = None
+
+
+@pytest.mark.parametrize("nd,causal", [(2, False), (1, True)])
+def test_fused_adapter_runs_reference_module_parameters(nd, causal):
+    """backend.FusedHyena on a reference-shaped Hyena instance == the oracle composition
+    with that instance's parameters (kernel generated, causally cropped, channels moved)."""
+    from nvsubquadratic_b200.backend import FusedHyena, ckconv_kernel
+
+    g = torch.Generator().manual_seed(3)
+    C = 16
+    n = (12, 10) if nd == 2 else (256,)
+    conv = (torch.nn.Conv2d(3 * C, 3 * C, 3, padding=1, groups=3 * C) if nd == 2 else
+            torch.nn.Conv1d(3 * C, 3 * C, 4, padding=0, groups=3 * C))
+    if nd == 1:
+        conv.__class__ = type("CausalConv1D", (torch.nn.Conv1d,), {})
+        conv.is_causal = True
+    mixer = _RefLikeMixer(C, nd, n, conv, causal, torch.nn.SiLU(), torch.nn.Sigmoid(), g).cuda()
+    shape = (2,) + n + (C,)
+    q, k, v, dy = (torch.randn(shape, generator=g) for _ in range(4))
+    adapter = FusedHyena(mixer)
+    ins = [t.cuda().requires_grad_(True) for t in (q, k, v)]
+    y = adapter(*ins)
+    y.backward(dy.cuda())
+    filt, D = ckconv_kernel(mixer.global_conv, list(n))
+    ref_ins = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    yr = hyena_forward(*ref_ins, filt.detach().cpu(), D.detach().cpu(), conv.weight.detach().cpu(),
+                       conv.bias.detach().cpu(), causal=causal, short_causal=causal, gate1="silu", gate2="sigmoid")
+    yr.backward(dy)
+    assert rel_l2(yr, y) <= 1e-5
+    for a, b in zip(ref_ins, ins):
+        assert rel_l2(a.grad, b.grad) <= 1e-5
+    assert mixer.global_conv.kernel.w.grad is not None and conv.weight.grad is not None
+
+
+def test_backend_apply_convolution_matches_oracle():
+    from nvsubquadratic_b200 import backend
+    from oracle.fftconv import fftconv_bhl
+
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(2, 8, 16, 12, generator=g)
+    kern_blh = torch.randn(1, 31, 23, 8, generator=g) / 25
+    D = torch.randn(8, generator=g)
+    fns = backend.select_fftconv_fns(2, False)
+    y_bhl = backend.apply_convolution(fns, x.cuda(), kern_blh.cuda(), D.cuda(), True)
+    y_blh = backend.apply_convolution(fns, x.movedim(1, -1).contiguous().cuda(), kern_blh.cuda(), D.cuda(), False)
+    ref = fftconv_bhl(x, kern_blh.movedim(-1, 1).contiguous(), D)
+    assert rel_l2(ref, y_bhl) <= 1e-5
+    assert rel_l2(ref.movedim(1, -1), y_blh) <= 1e-5
