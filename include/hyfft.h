@@ -88,6 +88,32 @@ HYFFT_API int hyfft_conv_forward(const hyfft_conv_desc* d, const void* x, const 
                        const void* shortcut, void* y, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* hyfft_conv_forward without a caller workspace and without allocating anything.
+ * No counterpart in the reference (its op allocates through torch on every call).
+ *
+ * For callers that cannot allocate device memory at call time: an FFI binding with
+ * no device allocator of its own (a ctypes / cgo / JNI caller handing over raw
+ * pointers), a serving loop or pre-planned memory pool that forbids allocator
+ * calls after warm-up, or code that must not grow the device footprint mid-run.
+ * The scratch is one fixed array of HYFFT_CONV_SCRATCH_MAX_BYTES in the library's
+ * device image, one per device; channels are processed in chunks that fit it.
+ *
+ * - The first call on a device looks up that array's address for the device (with
+ *   the device that owns x current); make that first call before any stream
+ *   capture on the device.
+ * - Problems whose single-channel spectra (plus the [H] float shortcut vector) do
+ *   not fit in HYFFT_CONV_SCRATCH_MAX_BYTES are rejected with HYFFT_ERR_WORKSPACE
+ *   before anything is launched; use hyfft_conv_forward with a workspace for them.
+ * - Nothing in the scratch needs to start at zero: every byte a call reads was
+ *   written earlier in the same call.
+ * - All calls on one device share the one array: calls that overlap in time (on
+ *   different streams, or from different host threads) race and corrupt each
+ *   other's results. Serialize them, e.g. issue them on one stream.
+ * Arguments and results are those of hyfft_conv_forward.                         */
+#define HYFFT_CONV_SCRATCH_MAX_BYTES (32u << 20)
+HYFFT_API int hyfft_conv_forward_static_scratch(const hyfft_conv_desc* d, const void* x, const float* kernel,
+                                                const void* shortcut, void* y, void* stream);
+
 /* Gradients of hyfft_conv_forward for upstream dy: dx (dtype, layout of x),
  * dkernel (float32, layout of kernel), dshortcut (float32 [H]; NULL when
  * shortcut is NULL). Any of dx / dkernel / dshortcut may be NULL to skip it.     */

@@ -75,6 +75,7 @@ _i32 = ctypes.c_int32
 SIGNATURES = {
     "hyfft_conv_workspace_size": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_sz), ctypes.POINTER(_sz)],
     "hyfft_conv_forward": [ctypes.POINTER(ConvDesc), _vp, _vp, _vp, _vp, _vp, _sz, _vp],
+    "hyfft_conv_forward_static_scratch": [ctypes.POINTER(ConvDesc), _vp, _vp, _vp, _vp, _vp],
     "hyfft_conv_backward": [ctypes.POINTER(ConvDesc), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _sz, _vp],
     "hyfft_hyena_workspace_size": [ctypes.POINTER(HyenaDesc), ctypes.POINTER(_sz), ctypes.POINTER(_sz),
                                    ctypes.POINTER(_sz)],

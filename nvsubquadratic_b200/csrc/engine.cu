@@ -22,6 +22,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <initializer_list>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -657,6 +658,84 @@ int hyfft_conv_backward(const hyfft_conv_desc* d, const void* x, const float* ke
     long long S = 1;
     for (int i = 0; i < p.g.D; ++i) S *= p.g.N[i];
     HY_TRY(run_dshortcut(p.dt, p.layout, dy, x, dshortcut, p.B, p.C, S, st));
+  }
+  return HYFFT_OK;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------ forward on a fixed device scratch
+// The scratch of hyfft_conv_forward_static_scratch: one array per device, part of the
+// library's device image, so using it allocates nothing. Host code never uses the
+// name as a device address; it asks the runtime for the address once per device.
+static __device__ __align__(256) unsigned char g_conv_scratch[HYFFT_CONV_SCRATCH_MAX_BYTES];
+
+namespace {
+constexpr int kMaxScratchDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxScratchDevices] = {};
+
+// With the target device current: the device address of g_conv_scratch on it, looked
+// up on the first call for that device and cached afterwards.
+int conv_scratch_address(void** out) {
+  int dev = -1;
+  const cudaError_t ge = cudaGetDevice(&dev);
+  if (ge != cudaSuccess) return fail(HYFFT_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(ge));
+  if (dev < 0 || dev >= kMaxScratchDevices)
+    return fail(HYFFT_ERR_UNSUPPORTED, "device ordinal %d beyond the %d the static scratch tracks", dev,
+                kMaxScratchDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_conv_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(HYFFT_ERR_CUDA, "cudaGetSymbolAddress(static scratch) on device %d: %s", dev,
+                  cudaGetErrorString(e));
+    g_scratch_addr[dev] = p;
+  }
+  *out = g_scratch_addr[dev];
+  return HYFFT_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int hyfft_conv_forward_static_scratch(const hyfft_conv_desc* d, const void* x, const float* kernel,
+                                      const void* shortcut, void* y, void* stream) {
+  ConvPlan p;
+  HY_TRY(make_conv_plan(d, p));
+  if (!x || !kernel || !y) return fail(HYFFT_ERR_INVALID, "null tensor pointer");
+  // Chunk the channels so that one chunk's spectra, the float shortcut vector and the
+  // 256-byte alignment padding of the two spectrum buffers fit the scratch.
+  const size_t cap = HYFFT_CONV_SCRATCH_MAX_BYTES;
+  const size_t dvec = align_up((size_t)p.C * 4);
+  const size_t per_ch = (size_t)(p.spec_x_bytes_per_ch + p.spec_k_bytes_per_ch);
+  if (dvec + 512 + per_ch > cap)
+    return fail(HYFFT_ERR_WORKSPACE,
+                "one channel needs %zu bytes of scratch (spectra %zu + shortcut %zu); the static scratch holds %zu "
+                "bytes: use hyfft_conv_forward with a caller workspace",
+                dvec + 512 + per_ch, per_ch, dvec, cap);
+  p.Cc = (int)std::min<size_t>((size_t)p.C, (cap - dvec - 512) / per_ch);
+  size_t need, nb;
+  conv_ws_sizes(p, need, nb);
+  if (need > cap) return fail(HYFFT_ERR_WORKSPACE, "static scratch plan needs %zu > %zu bytes", need, cap);
+  if (bind_device_of(x) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "cannot make the device of the inputs current");
+  void* scratch = nullptr;
+  HY_TRY(conv_scratch_address(&scratch));
+  cudaStream_t st = (cudaStream_t)stream;
+  char* w = (char*)scratch;
+  float2* S = (float2*)w;
+  w += align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
+  float2* Kh = (float2*)w;
+  w += align_up((size_t)p.spec_k_bytes_per_ch * p.Cc);
+  float* Dv = (float*)w;
+  if (shortcut) HY_TRY(to_float(shortcut, p.dt, Dv, p.C, st));
+  const RealView xv = real_view(x, p.layout, p.B, p.C, p.g.N, p.g.D);
+  const RealView kv = real_view(kernel, p.layout, p.kB, p.C, p.g.K, p.g.D);
+  const RealView yv = real_view(y, p.layout, p.B, p.C, p.g.N, p.g.D);
+  for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
+    const int cc = std::min(p.Cc, p.C - c0);
+    HY_TRY(conv_forward_chunk(p, c0, cc, xv, kv, shortcut ? Dv : nullptr, yv, S, Kh, st));
   }
   return HYFFT_OK;
 }
