@@ -212,6 +212,51 @@ def cpu_reference_time(cfg: dict, budget_s: float = 20.0):
     return elems / med / 1e9, threads, sample, med
 
 
+# ----------------------------------------------------------------- per-pass timing
+def pass_bytes(cfg: dict, B: int, C: int) -> dict:
+    """Algorithmic HBM bytes of each library pass (they sum to alg_bytes)."""
+    E = B * C * math.prod(cfg["S"])
+    KK = math.prod(cfg["K"])
+    if cfg.get("op_only"):
+        return {"hyfft_conv_forward": 8 * E + 4 * C * KK, "hyfft_conv_backward": 12 * E + 8 * C * KK}
+    s = torch.finfo(cfg["dtype"]).bits // 8
+    return {"hyfft_hyena_forward": 4 * s * E + 4 * C * KK, "hyfft_hyena_backward": 7 * s * E + 8 * C * KK}
+
+
+def time_passes(step, zero_grads, flush, names, n):
+    """Mean device time of each named C-ABI call over n eager steps, CUDA events recorded
+    on the stream the library launches on (torch's current stream), L2 flushed right
+    before every timed call."""
+    from nvsubquadratic_b200 import _lib
+
+    lib = _lib.load()
+    recs = {nm: [] for nm in names}
+    origs = {nm: getattr(lib, nm) for nm in names}
+
+    def wrap(nm, orig):
+        def timed(*a):
+            flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            rc = orig(*a)
+            e.record()
+            recs[nm].append((s, e))
+            return rc
+        return timed
+
+    try:
+        for nm, orig in origs.items():
+            setattr(lib, nm, wrap(nm, orig))
+        for _ in range(n):
+            zero_grads()
+            step()
+        torch.cuda.synchronize()
+    finally:
+        for nm, orig in origs.items():
+            setattr(lib, nm, orig)
+    return {nm: sum(a.elapsed_time(b) for a, b in r) / len(r) for nm, r in recs.items() if r}
+
+
 # ----------------------------------------------------------------- GPU arm
 def run_gpu(args, cfg, rank, world, device):
     from nvsubquadratic_b200 import _lib
@@ -329,14 +374,22 @@ def run_gpu(args, cfg, rank, world, device):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     total_ms = t.item()
 
+    del graph
+    names = list(pass_bytes(cfg, B, C))
+    pass_ms = time_passes(step, zero_grads, flush, names, max(3, min(args.steps, 10)))
+    for nm in names:
+        t3 = torch.tensor([pass_ms[nm]], device=device)
+        if world > 1:
+            torch.distributed.all_reduce(t3, op=torch.distributed.ReduceOp.MAX)
+        pass_ms[nm] = t3.item()
+
     # e2e through the public API from pinned host buffers (eager, no graph)
     e2e_ms, h2d, d2h = e2e_time(cfg, inp, device, op_only, max(3, min(args.steps, 10)))
     t2 = torch.tensor([e2e_ms], device=device)
     if world > 1:
         torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
     e2e_ms = t2.item()
-    del graph
-    return dict(total_ms=total_ms, step_ms=step_ms, launches=launches_per_step, clocks=clk.summary(),
+    return dict(pass_ms=pass_ms, total_ms=total_ms, step_ms=step_ms, launches=launches_per_step, clocks=clk.summary(),
                 B=B, C=C, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h)
 
 
@@ -448,7 +501,16 @@ def main():
     except OSError:
         pass
     peak = peaks.get("hbm_gbs", 6650.0)
-    achieved = bytes_rank / t_step / 1e9
+    step_achieved = bytes_rank / t_step / 1e9
+    pbytes = pass_bytes(cfg, res["B"], res["C"])
+    dom = max(res["pass_ms"], key=res["pass_ms"].get)
+    achieved = pbytes[dom] / (res["pass_ms"][dom] / 1e3) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            traffic = json.load(f).get(args.config, {}).get(dom)
+    except (OSError, ValueError):
+        pass
     e2e_val = elems_job / (res["e2e_ms"] / 1e3) / 1e9
 
     if rank == 0:
@@ -458,9 +520,15 @@ def main():
             "scaling": "weak" if cfg["shard"] == "replica" else "strong", "vs_baseline": None, "dtype": dtname,
             "data": "synthetic (seeded N(0,1) activations, random-init filters)", "config": config,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
-                         "scope": "whole fwd+bwd step (algorithmic bytes per step / step time)",
-                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "kernel": dom, "pass_ms": {k: round(v, 4) for k, v in res["pass_ms"].items()},
+                         "pass_bytes": pbytes,
+                         "scope": "dominant library pass: its algorithmic bytes / its mean CUDA-event time "
+                                  "(L2 flushed before each timed call); traffic = ncu dram read+write bytes "
+                                  "per call from profiles/ncu_traffic.json",
+                         "step_achieved": round(step_achieved, 1), "step_frac": round(step_achieved / peak, 4),
+                         "peak_source": ("MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks
+                                         else "fallback 6650 GB/s (of fallback)")},
             "e2e": {"value": round(e2e_val, 4), "unit": "GElem/s", "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"]},
             "gpu_launches": res["launches"] * args.steps,

@@ -23,6 +23,7 @@
 #include <cstring>
 #include <initializer_list>
 #include <mutex>
+#include <type_traits>
 #include <string>
 
 #include "common.cuh"
@@ -153,7 +154,12 @@ static int launch_pass_t(const PassDesc& d, cudaStream_t st) {
   const long long grid = (d.nlines + d.TL - 1) / d.TL;
   if (grid <= 0) return HYFFT_OK;
   if (grid > 0x7fffffffLL) return fail(HYFFT_ERR_UNSUPPORTED, "too many FFT lines");
-  const size_t smem = sizeof(LineInfo) * kPassMaxLines + sizeof(float2) * (size_t)d.TL * (d.F + 1);
+  const size_t smem =
+      sizeof(LineInfo) * kPassMaxLines + sizeof(float2) * ((size_t)d.TL * pass_ld(d.F) + (size_t)(d.F / 2));
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(fft_pass_kernel<IM, OM, TI, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+    return fail(HYFFT_ERR_CUDA, "fft_pass_kernel: cannot allow %zu bytes of shared memory", smem);
   fft_pass_kernel<IM, OM, TI, TO><<<(unsigned)grid, kPassThreads, smem, st>>>(d);
   return check_launch("fft_pass_kernel");
 }
@@ -569,7 +575,12 @@ static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView
 static int run_dshortcut(int dt, int layout, const void* dy, const void* x, float* out, int B, int C, long long S,
                          cudaStream_t st) {
   const int blh = layout == HYFFT_LAYOUT_BLH;
-  const int gr = (C + 31) / 32;
+  if (cudaMemsetAsync(out, 0, sizeof(float) * (size_t)C, st) != cudaSuccess) return fail(HYFFT_ERR_CUDA, "memset dshortcut");
+  const dim3 gr = blh ? dim3((unsigned)((C + 31) / 32),
+                             (unsigned)std::max<long long>(1, std::min<long long>(1200 / ((C + 31) / 32) + 1,
+                                                                                  ((long long)B * S + 63) / 64)),
+                             1)
+                      : dim3((unsigned)C, (unsigned)B, 1);
   if (dt == HYFFT_F32) dshortcut_kernel<float><<<gr, 256, 0, st>>>((const float*)dy, (const float*)x, out, B, C, S, blh);
   else if (dt == HYFFT_BF16)
     dshortcut_kernel<__nv_bfloat16><<<gr, 256, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, out, B, C, S, blh);
@@ -843,6 +854,42 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
   bwd = cb + 2 * act + 3 * f32 + align_up((size_t)h.d.channels * 4);
 }
 
+// ---- launch helpers of the elementwise / stencil kernels (hyena_elem.cuh)
+template <int V> using IC = std::integral_constant<int, V>;
+
+// Call f(IC<K0>, IC<K1>, IC<K2>) with the compile-time stencil of g when it is one of the
+// shapes the reference uses, else with the runtime-shaped fallback (-1).
+template <bool PAIR, typename F>
+static void with_stencil(const StencilGeom& g, F&& f) {
+  const int a = g.k[0], b = g.k[1], c = g.k[2];
+  if (!g.has_conv) f(IC<0>{}, IC<0>{}, IC<0>{});
+  else if constexpr (!PAIR) f(IC<-1>{}, IC<-1>{}, IC<-1>{});
+  else if (a == 3 && b == 1 && c == 1) f(IC<3>{}, IC<1>{}, IC<1>{});
+  else if (a == 4 && b == 1 && c == 1) f(IC<4>{}, IC<1>{}, IC<1>{});
+  else if (a == 7 && b == 1 && c == 1) f(IC<7>{}, IC<1>{}, IC<1>{});
+  else if (a == 3 && b == 3 && c == 1) f(IC<3>{}, IC<3>{}, IC<1>{});
+  else if (a == 3 && b == 3 && c == 3) f(IC<3>{}, IC<3>{}, IC<3>{});
+  else f(IC<-1>{}, IC<-1>{}, IC<-1>{});
+}
+
+// Rows of (b, position) per CTA column so that a warp walks about `per_warp` rows.
+static dim3 elem_grid(int C, long long rows, long long per_warp) {
+  const long long gy = std::max<long long>(1, std::min<long long>(65535, (rows + 8 * per_warp - 1) / (8 * per_warp)));
+  return dim3((unsigned)((C + kElemCG - 1) / kElemCG), (unsigned)gy, 1);
+}
+
+// Two-channel vector accesses need an even channel count, even element strides and
+// bases aligned to two elements.
+static bool elem_pairs_ok(const HyenaPlan& h, std::initializer_list<const void*> ps) {
+  const hyfft_hyena_desc& d = h.d;
+  if (d.channels % 2 || d.in_batch_stride % 2 || d.in_pos_stride % 2 || d.out_batch_stride % 2 ||
+      d.out_pos_stride % 2)
+    return false;
+  for (const void* p : ps)
+    if (p && ((uintptr_t)p % (2 * h.eb)) != 0) return false;
+  return true;
+}
+
 template <typename T>
 static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt, const float* D,
                            const float* sw, const float* sb, T* y, char* saved, char* ws, cudaStream_t st) {
@@ -853,8 +900,19 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
   T* vs = (T*)(saved + 2 * act);
   T* z = (T*)(saved + 3 * act);
   T* hb = (T*)(saved + 4 * act);
-  hyena_pre_fwd_kernel<T><<<grid_for(h.E), 256, 0, st>>>(q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch,
-                                                         d.channels, sw, sb, d.gate1, qs, ks, vs, z);
+  const long long rows = (long long)d.batch * h.Ntot;
+  const bool pair = elem_pairs_ok(h, {q, k, v, y});
+  auto pre = [&](auto pr) {
+    constexpr bool P = decltype(pr)::value;
+    with_stencil<P>(h.sg, [&](auto a, auto b, auto c) {
+      hyena_pre_fwd_kernel<T, P, decltype(a)::value, decltype(b)::value, decltype(c)::value>
+          <<<elem_grid(d.channels, rows, 4), kElemThreads, 0, st>>>(q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg,
+                                                                   d.batch, d.channels, sw, sb, d.gate1, qs, ks, vs,
+                                                                   z);
+    });
+  };
+  if (pair) pre(std::true_type{});
+  else pre(std::false_type{});
   HY_TRY(check_launch("hyena_pre_fwd_kernel"));
   // long conv with D-skip: h = round(conv(z)) + round(D * z)
   const ConvPlan& p = h.cp;
@@ -869,8 +927,12 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
     const int cc = std::min(p.Cc, p.C - c0);
     HY_TRY(conv_forward_chunk(p, c0, cc, zv, kv, D, hv, S, Kh, st));
   }
-  hyena_post_fwd_kernel<T><<<grid_for(h.E), 256, 0, st>>>(hb, vs, d.gate2, h.Ntot, d.batch, d.channels, y,
-                                                          d.out_batch_stride, d.out_pos_stride);
+  if (pair)
+    hyena_post_fwd_kernel<T, true><<<elem_grid(d.channels, rows, 8), kElemThreads, 0, st>>>(
+        hb, vs, d.gate2, h.Ntot, d.batch, d.channels, y, d.out_batch_stride, d.out_pos_stride);
+  else
+    hyena_post_fwd_kernel<T, false><<<elem_grid(d.channels, rows, 8), kElemThreads, 0, st>>>(
+        hb, vs, d.gate2, h.Ntot, d.batch, d.channels, y, d.out_batch_stride, d.out_pos_stride);
   return check_launch("hyena_post_fwd_kernel");
 }
 
@@ -899,8 +961,19 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
   float* dqp = (float*)w;
   w += f32;
   float* dkp = (float*)w;
-  hyena_bwd_gate2_kernel<T><<<grid_for(h.E), 256, 0, st>>>(dy, d.out_batch_stride, d.out_pos_stride, hb, vs, d.gate2,
-                                                           h.Ntot, d.batch, d.channels, dh, dvp);
+  const long long rows = (long long)d.batch * h.Ntot;
+  const bool pair = elem_pairs_ok(h, {q, k, v, dy, dq, dk, dv});
+  const dim3 eg = elem_grid(d.channels, rows, 8);
+  // reductions (dD, short-conv weights): about 1200 CTAs in all, one atomic per channel each
+  auto red_rows = [&](int cols) {
+    return std::max<long long>(1, std::min<long long>(65535, 1200 / std::max(1, cols)));
+  };
+  if (pair)
+    hyena_bwd_gate2_kernel<T, true><<<eg, kElemThreads, 0, st>>>(dy, d.out_batch_stride, d.out_pos_stride, hb, vs,
+                                                                 d.gate2, h.Ntot, d.batch, d.channels, dh, dvp);
+  else
+    hyena_bwd_gate2_kernel<T, false><<<eg, kElemThreads, 0, st>>>(dy, d.out_batch_stride, d.out_pos_stride, hb, vs,
+                                                                  d.gate2, h.Ntot, d.batch, d.channels, dh, dvp);
   HY_TRY(check_launch("hyena_bwd_gate2_kernel"));
   // long conv backward: dz = convT(dh) + D*dh, dfilt, dD
   {
@@ -920,22 +993,45 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
       HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, Kh, dKh, st));
     }
     if (dD) {
-      dshortcut_kernel<T><<<(d.channels + 31) / 32, 256, 0, st>>>(dh, z, dD, d.batch, d.channels, h.Ntot, 1);
-      HY_TRY(check_launch("dshortcut_kernel"));
+      if (cudaMemsetAsync(dD, 0, sizeof(float) * (size_t)d.channels, st) != cudaSuccess)
+        return fail(HYFFT_ERR_CUDA, "memset dD");
+      const dim3 rg(eg.x, (unsigned)red_rows((int)eg.x), 1);
+      if (pair) hyena_dskip_kernel<T, true><<<rg, kElemThreads, 0, st>>>(dh, z, rows, d.channels, dD);
+      else hyena_dskip_kernel<T, false><<<rg, kElemThreads, 0, st>>>(dh, z, rows, d.channels, dD);
+      HY_TRY(check_launch("hyena_dskip_kernel"));
     }
   }
-  hyena_bwd_gate1_kernel<T><<<grid_for(h.E), 256, 0, st>>>(dz, qs, ks, d.gate1, h.E, dqp, dkp);
+  if (pair) hyena_bwd_gate1_kernel<T, true><<<eg, kElemThreads, 0, st>>>(dz, qs, ks, d.gate1, rows, d.channels, dqp, dkp);
+  else hyena_bwd_gate1_kernel<T, false><<<eg, kElemThreads, 0, st>>>(dz, qs, ks, d.gate1, rows, d.channels, dqp, dkp);
   HY_TRY(check_launch("hyena_bwd_gate1_kernel"));
-  hyena_short_dgrad_kernel<T><<<grid_for(h.E), 256, 0, st>>>(dqp, dkp, dvp, h.sg, d.batch, d.channels, sw, dq, dk, dv,
-                                                             d.out_batch_stride, d.out_pos_stride);
+  auto dgrad = [&](auto pr) {
+    constexpr bool P = decltype(pr)::value;
+    with_stencil<P>(h.sg, [&](auto a, auto b, auto c) {
+      hyena_short_dgrad_kernel<T, P, decltype(a)::value, decltype(b)::value, decltype(c)::value>
+          <<<elem_grid(d.channels, rows, 4), kElemThreads, 0, st>>>(dqp, dkp, dvp, h.sg, d.batch, d.channels, sw, dq,
+                                                                   dk, dv, d.out_batch_stride, d.out_pos_stride);
+    });
+  };
+  if (pair) dgrad(std::true_type{});
+  else dgrad(std::false_type{});
   HY_TRY(check_launch("hyena_short_dgrad_kernel"));
   if (h.sg.has_conv && dsw) {
-    cudaMemsetAsync(dsw, 0, sizeof(float) * 3 * (size_t)d.channels * h.sg.ntaps, st);
-    if (dsb && h.sg.has_bias) cudaMemsetAsync(dsb, 0, sizeof(float) * 3 * (size_t)d.channels, st);
-    const long long rows = (long long)d.batch * h.Ntot;
-    dim3 grid((3 * d.channels + 31) / 32, (unsigned)std::max<long long>(1, std::min<long long>(rows / 64, 64)));
-    hyena_short_wgrad_kernel<T><<<grid, 256, 0, st>>>(dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg,
-                                                      d.batch, d.channels, dsw, dsb);
+    if (cudaMemsetAsync(dsw, 0, sizeof(float) * 3 * (size_t)d.channels * h.sg.ntaps, st) != cudaSuccess)
+      return fail(HYFFT_ERR_CUDA, "memset dshort_w");
+    if (dsb && h.sg.has_bias && cudaMemsetAsync(dsb, 0, sizeof(float) * 3 * (size_t)d.channels, st) != cudaSuccess)
+      return fail(HYFFT_ERR_CUDA, "memset dshort_b");
+    const unsigned gx = (unsigned)((d.channels + kElemCG - 1) / kElemCG);
+    const dim3 wg(gx, 3, (unsigned)red_rows(3 * (int)gx));
+    auto wgrad = [&](auto pr) {
+      constexpr bool P = decltype(pr)::value;
+      with_stencil<P>(h.sg, [&](auto a, auto b, auto c) {
+        hyena_short_wgrad_kernel<T, P, decltype(a)::value, decltype(b)::value, decltype(c)::value>
+            <<<wg, kElemThreads, 0, st>>>(dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch,
+                                          d.channels, dsw, dsb);
+      });
+    };
+    if (pair) wgrad(std::true_type{});
+    else wgrad(std::false_type{});
     HY_TRY(check_launch("hyena_short_wgrad_kernel"));
   }
   return HYFFT_OK;

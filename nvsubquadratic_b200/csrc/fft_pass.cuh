@@ -77,91 +77,121 @@ __device__ __forceinline__ void dft4(float2& a0, float2& a1, float2& a2, float2&
   a3 = csub(t1, jt3);
 }
 
-// In-place Stockham autosort FFT of TL lines of length F stored at
-// sm[l * ld + t]. All threads of the CTA participate; each stage stages the
-// butterfly inputs in registers between two barriers.
-__device__ void stockham_tile(float2* sm, int TL, int F, int logF, int ld, float dir) {
-  const int tid = threadIdx.x;
-  int Ns = 1, lgNs = 0;
-  int rem = logF;
-  while (rem > 0) {
-    if (rem >= 2) {
-      const int per_line = F >> 2;
-      const int total = TL * per_line;
-      const int lgpl = logF - 2;
-      float2 v[4][4];
+// e^{dir * 2*pi*i * j / F} for 0 <= j < F from a table of the first half turn,
+// tw[j] = (cos(2 pi j / F), sin(2 pi j / F)) for j < F/2.
+__device__ __forceinline__ float2 twiddle(const float2* tw, int j, int half, float dir) {
+  float2 w = tw[j & (half - 1)];
+  if (j >= half) w = make_float2(-w.x, -w.y);
+  return make_float2(w.x, dir * w.y);
+}
+
+// Shared-memory index of point t of a line: one pad slot every 32 points, so the
+// strided writes of a Stockham stage (stride R * Ns) fall into distinct banks.
+__device__ __forceinline__ int padi(int t) { return t + (t >> 5); }
+__host__ __device__ constexpr int pass_ld(int F) { return F + (F >> 5) + 1; }
+
+// 16-point DFT in registers, natural order in, natural order out (two radix-4 layers).
+__device__ __forceinline__ void dft16(float2 (&v)[16], float dir) {
+  constexpr float c1 = 0.92387953251128674f, s1 = 0.38268343236508978f, h = 0.70710678118654752f;
 #pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int item = tid + it * kPassThreads;
-        if (item < total) {
-          const int l = item >> lgpl, j = item & (per_line - 1);
-          const int k = j & (Ns - 1);
-          const float2* src = sm + l * ld + j;
+  for (int n2 = 0; n2 < 4; ++n2) dft4(v[n2], v[n2 + 4], v[n2 + 8], v[n2 + 12], dir);
+  // v[n2 + 4 k1] *= W16^(n2 k1), W16 = e^{dir 2 pi i / 16}
+  const float2 w1 = make_float2(c1, dir * s1), w2 = make_float2(h, dir * h), w3 = make_float2(s1, dir * c1);
+  const float2 w6 = make_float2(-h, dir * h), w9 = make_float2(-c1, -dir * s1);
+  v[5] = cmul(v[5], w1);
+  v[9] = cmul(v[9], w2);
+  v[13] = cmul(v[13], w3);
+  v[6] = cmul(v[6], w2);
+  v[10] = make_float2(-dir * v[10].y, dir * v[10].x);  // * W16^4 = dir * i
+  v[14] = cmul(v[14], w6);
+  v[7] = cmul(v[7], w3);
+  v[11] = cmul(v[11], w6);
+  v[15] = cmul(v[15], w9);
+  float2 o[16];
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
-            float2 a = src[r * per_line];
-            if (r > 0 && k > 0) {
-              // angle = dir * 2*pi * r*k / (Ns*4)
-              a = cmul(a, expipi(dir * (float)(2 * r * k) / (float)(Ns * 4)));
-            }
-            v[it][r] = a;
-          }
-        }
+  for (int k1 = 0; k1 < 4; ++k1) {
+    float2 a0 = v[4 * k1], a1 = v[4 * k1 + 1], a2 = v[4 * k1 + 2], a3 = v[4 * k1 + 3];
+    dft4(a0, a1, a2, a3, dir);
+    o[k1] = a0;
+    o[k1 + 4] = a1;
+    o[k1 + 8] = a2;
+    o[k1 + 12] = a3;
+  }
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v[k] = o[k];
+}
+
+template <int R>
+__device__ __forceinline__ void dftR(float2 (&v)[R], float dir) {
+  if constexpr (R == 16) {
+    dft16(v, dir);
+  } else if constexpr (R == 4) {
+    dft4(v[0], v[1], v[2], v[3], dir);
+  } else {
+    const float2 a = v[0], b = v[1];
+    v[0] = cadd(a, b);
+    v[1] = csub(a, b);
+  }
+}
+
+// One radix-R Stockham stage over TL lines of length F = 2^logF (sub-transform
+// length Ns = 2^lgNs so far). IPT items of R points per thread are held in
+// registers between the two barriers.
+template <int R, int LGR, int IPT>
+__device__ __forceinline__ void stockham_stage(float2* sm, const float2* tw, int TL, int logF, int ld, int lgNs,
+                                               float dir) {
+  const int F = 1 << logF, halfF = F >> 1;
+  const int lgpl = logF - LGR, per_line = 1 << lgpl;
+  const int total = TL << lgpl;
+  const int Ns = 1 << lgNs;
+  float2 v[IPT][R];
+#pragma unroll
+  for (int it = 0; it < IPT; ++it) {
+    const int item = threadIdx.x + it * kPassThreads;
+    if (item < total) {
+      const int l = item >> lgpl, j = item & (per_line - 1);
+      const int k = j & (Ns - 1);
+      const float2* src = sm + l * ld;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        float2 a = src[padi(r * per_line + j)];
+        if (r > 0 && k > 0) a = cmul(a, twiddle(tw, (r * k) << (logF - lgNs - LGR), halfF, dir));
+        v[it][r] = a;
       }
-      __syncthreads();
-#pragma unroll
-      for (int it = 0; it < 4; ++it) {
-        const int item = tid + it * kPassThreads;
-        if (item < total) {
-          const int l = item >> lgpl, j = item & (per_line - 1);
-          const int k = j & (Ns - 1);
-          dft4(v[it][0], v[it][1], v[it][2], v[it][3], dir);
-          float2* dst = sm + l * ld + ((j >> lgNs) << (lgNs + 2)) + k;
-#pragma unroll
-          for (int r = 0; r < 4; ++r) dst[r * Ns] = v[it][r];
-        }
-      }
-      __syncthreads();
-      Ns <<= 2;
-      lgNs += 2;
-      rem -= 2;
-    } else {
-      const int per_line = F >> 1;
-      const int total = TL * per_line;
-      const int lgpl = logF - 1;
-      float2 v[8][2];
-#pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int item = tid + it * kPassThreads;
-        if (item < total) {
-          const int l = item >> lgpl, j = item & (per_line - 1);
-          const int k = j & (Ns - 1);
-          const float2* src = sm + l * ld + j;
-          float2 a0 = src[0], a1 = src[per_line];
-          if (k > 0) a1 = cmul(a1, expipi(dir * (float)(2 * k) / (float)(Ns * 2)));
-          v[it][0] = a0;
-          v[it][1] = a1;
-        }
-      }
-      __syncthreads();
-#pragma unroll
-      for (int it = 0; it < 8; ++it) {
-        const int item = tid + it * kPassThreads;
-        if (item < total) {
-          const int l = item >> lgpl, j = item & (per_line - 1);
-          const int k = j & (Ns - 1);
-          float2 a0 = v[it][0], a1 = v[it][1];
-          float2* dst = sm + l * ld + ((j >> lgNs) << (lgNs + 1)) + k;
-          dst[0] = cadd(a0, a1);
-          dst[Ns] = csub(a0, a1);
-        }
-      }
-      __syncthreads();
-      Ns <<= 1;
-      lgNs += 1;
-      rem -= 1;
     }
   }
+  __syncthreads();
+#pragma unroll
+  for (int it = 0; it < IPT; ++it) {
+    const int item = threadIdx.x + it * kPassThreads;
+    if (item < total) {
+      const int l = item >> lgpl, j = item & (per_line - 1);
+      const int k = j & (Ns - 1);
+      dftR<R>(v[it], dir);
+      float2* dst = sm + l * ld;
+      const int base = ((j >> lgNs) << (lgNs + LGR)) + k;
+#pragma unroll
+      for (int r = 0; r < R; ++r) dst[padi(base + r * Ns)] = v[it][r];
+    }
+  }
+  __syncthreads();
+}
+
+// In-place Stockham autosort FFT of TL lines of length F stored at
+// sm[l * ld + padi(t)] (TL * F <= kPassPoints). All threads of the CTA take part;
+// radix-16 stages while at least four factors of two remain, then radix 4 / 2.
+// Twiddles come from the half-turn table tw (F/2 entries).
+__device__ void stockham_tile(float2* sm, const float2* tw, int TL, int F, int logF, int ld, float dir) {
+  int lgNs = 0;
+  while (logF - lgNs >= 4) {
+    stockham_stage<16, 4, kPassPoints / (16 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
+    lgNs += 4;
+  }
+  if (logF - lgNs >= 2) {
+    stockham_stage<4, 2, kPassPoints / (4 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
+    lgNs += 2;
+  }
+  if (logF - lgNs >= 1) stockham_stage<2, 1, kPassPoints / (2 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
 }
 
 struct LineInfo {
@@ -175,13 +205,20 @@ struct LineInfo {
 };
 
 template <int IN_MODE, int OUT_MODE, typename TI, typename TO>
-__global__ void __launch_bounds__(kPassThreads) fft_pass_kernel(const PassDesc d) {
+__global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDesc d) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   LineInfo* li = reinterpret_cast<LineInfo*>(smem_raw);
   float2* sm = reinterpret_cast<float2*>(smem_raw + sizeof(LineInfo) * kPassMaxLines);
   const int TL = d.TL, F = d.F;
-  const int ld = F + 1;  // pad the line stride to spread shared-memory banks
+  const int ld = pass_ld(F);  // padded line stride (odd, spreads lines over banks)
+  float2* tw = sm + (size_t)TL * ld;
+  const int logF = d.logF, logTL = 31 - __clz(TL);  // TL and F are powers of two
   const long long line0 = (long long)blockIdx.x * TL;
+  for (int j = threadIdx.x; j < (F >> 1); j += blockDim.x) {
+    float sn, cs;
+    sincospif(2.0f * (float)j / (float)F, &sn, &cs);
+    tw[j] = make_float2(cs, sn);
+  }
 
   // ---- per-line bookkeeping
   for (int l = threadIdx.x; l < TL; l += blockDim.x) {
@@ -216,8 +253,8 @@ __global__ void __launch_bounds__(kPassThreads) fft_pass_kernel(const PassDesc d
   const int npts = TL * F;
   for (int e = threadIdx.x; e < npts; e += blockDim.x) {
     int l, t;
-    if (d.load_t_fastest) { l = e / F; t = e - l * F; }
-    else { t = e / TL; l = e - t * TL; }
+    if (d.load_t_fastest) { l = e >> logF; t = e & (F - 1); }
+    else { t = e >> logTL; l = e & (TL - 1); }
     const LineInfo& L = li[l];
     float2 val = make_float2(0.f, 0.f);
     if (L.valid) {
@@ -234,20 +271,20 @@ __global__ void __launch_bounds__(kPassThreads) fft_pass_kernel(const PassDesc d
         }
       }
     }
-    sm[l * ld + t] = val;
+    sm[l * ld + padi(t)] = val;
   }
   __syncthreads();
 
-  stockham_tile(sm, TL, F, d.logF, ld, d.dir);
+  stockham_tile(sm, tw, TL, F, d.logF, ld, d.dir);
 
   // ---- store
   for (int e = threadIdx.x; e < npts; e += blockDim.x) {
     int l, t;
-    if (d.store_t_fastest) { l = e / F; t = e - l * F; }
-    else { t = e / TL; l = e - t * TL; }
+    if (d.store_t_fastest) { l = e >> logF; t = e & (F - 1); }
+    else { t = e >> logTL; l = e & (TL - 1); }
     const LineInfo& L = li[l];
     if (!L.valid) continue;
-    float2 val = cscale(sm[l * ld + t], d.scale);
+    float2 val = cscale(sm[l * ld + padi(t)], d.scale);
     if (d.tw_logF > 0 && L.tw_m != 0) {
       // e^{dir*2*pi*i*t*m/2^tw_logF}; reduce the exponent mod 2^tw_logF first
       const long long ex = ((long long)t * L.tw_m) & ((1LL << d.tw_logF) - 1);

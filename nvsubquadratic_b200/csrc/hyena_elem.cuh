@@ -2,6 +2,14 @@
 // gate 1 (z = q' * g1(k')), gate 2 (y = h * g2(v')) and their backward.
 // Activations are channels-last [B, *S, C] with a per-position element stride,
 // so q, k, v may be strided views into one [B, *S, 3C] projection output.
+//
+// Work split: a CTA owns a group of 64 channels (two per lane: one 2-element vector)
+// and a run of rows (b, position); each warp walks rows, so a warp-wide access is
+// 32 consecutive channel pairs of one position (128 B for bf16). Row -> (b, p0, p1, p2)
+// uses 32-bit division once per row. The stencil extents are template parameters for
+// the shapes the reference uses (1D 3/4/7, 2D 3x3, 3D 3x3x3; K0 = 0 means no short
+// conv, K0 = -1 the runtime-shaped fallback), so the tap loops unroll and the
+// short-conv weights of the CTA's channels sit in shared memory as [tensor][tap][64].
 #pragma once
 
 #include "common.cuh"
@@ -18,226 +26,434 @@ struct StencilGeom {
   int has_bias;
 };
 
-__device__ __forceinline__ void unflatten3(long long pos, const StencilGeom& g, int& p0, int& p1, int& p2) {
-  p2 = (int)(pos % g.n[2]);
-  long long r = pos / g.n[2];
-  p1 = (int)(r % g.n[1]);
-  p0 = (int)(r / g.n[1]);
+constexpr int kElemCG = 64;       // channels per CTA (32 lanes x 2)
+constexpr int kElemThreads = 256;  // 8 warps
+constexpr int kMaxTaps = 27;
+
+// 2-channel vectors of the activation dtype
+template <typename T> struct V2;
+template <> struct V2<float> {
+  static __device__ __forceinline__ float2 load(const float* p) { return *reinterpret_cast<const float2*>(p); }
+  static __device__ __forceinline__ void store(float* p, float2 v) { *reinterpret_cast<float2*>(p) = v; }
+  static __device__ __forceinline__ float2 round(float2 v) { return v; }
+};
+template <> struct V2<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 load(const __nv_bfloat16* p) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+  }
+  static __device__ __forceinline__ void store(__nv_bfloat16* p, float2 v) {
+    *reinterpret_cast<__nv_bfloat162*>(p) = __float22bfloat162_rn(v);
+  }
+  static __device__ __forceinline__ float2 round(float2 v) { return __bfloat1622float2(__float22bfloat162_rn(v)); }
+};
+template <> struct V2<__half> {
+  static __device__ __forceinline__ float2 load(const __half* p) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+  }
+  static __device__ __forceinline__ void store(__half* p, float2 v) {
+    *reinterpret_cast<__half2*>(p) = __float22half2_rn(v);
+  }
+  static __device__ __forceinline__ float2 round(float2 v) { return __half22float2(__float22half2_rn(v)); }
+};
+
+// Geometry of one thread's row.
+struct RowPos {
+  int b, p0, p1, p2;
+  long long pos;  // flat position
+};
+__device__ __forceinline__ RowPos row_pos(long long r, const StencilGeom& g, long long Ntot) {
+  RowPos o;
+  o.b = (int)(r / Ntot);
+  o.pos = r - (long long)o.b * Ntot;
+  if (Ntot < (1LL << 31)) {
+    const unsigned p = (unsigned)o.pos;
+    const unsigned n2 = (unsigned)g.n[2], n1 = (unsigned)g.n[1];
+    const unsigned q2 = p / n2;
+    o.p2 = (int)(p - q2 * n2);
+    const unsigned q1 = q2 / n1;
+    o.p1 = (int)(q2 - q1 * n1);
+    o.p0 = (int)q1;
+  } else {
+    o.p2 = (int)(o.pos % g.n[2]);
+    const long long q2 = o.pos / g.n[2];
+    o.p1 = (int)(q2 % g.n[1]);
+    o.p0 = (int)(q2 / g.n[1]);
+  }
+  return o;
 }
 
-// Depthwise cross-correlation of channel `ch` (of 3C) at position (p0,p1,p2):
-//   out = sum_tap w[ch, tap] * in[pos + tap - off] (+ bias[ch])
-template <typename T>
-__device__ __forceinline__ float short_conv_at(const T* __restrict__ in, long long bbase, long long pstride, int c,
-                                               int ch, int p0, int p1, int p2, const StencilGeom& g,
-                                               const float* __restrict__ w, const float* __restrict__ bias) {
-  if (!g.has_conv) return DT<T>::load(in + bbase + ((long long)(p0 * g.n[1] + p1) * g.n[2] + p2) * pstride + c);
-  float acc = g.has_bias ? bias[ch] : 0.f;
-  const float* wc = w + (long long)ch * g.ntaps;
-  int tap = 0;
-  for (int a = 0; a < g.k[0]; ++a) {
-    const int i0 = p0 + a - g.off[0];
-    for (int b = 0; b < g.k[1]; ++b) {
-      const int i1 = p1 + b - g.off[1];
-      for (int e = 0; e < g.k[2]; ++e, ++tap) {
-        const int i2 = p2 + e - g.off[2];
-        if (i0 < 0 || i0 >= g.n[0] || i1 < 0 || i1 >= g.n[1] || i2 < 0 || i2 >= g.n[2]) continue;
-        const long long pl = ((long long)i0 * g.n[1] + i1) * g.n[2] + i2;
-        acc = fmaf(wc[tap], DT<T>::load(in + bbase + pl * pstride + c), acc);
+// Runtime or compile-time stencil extents.
+template <int K> __device__ __forceinline__ int kext(int rt) { return K > 0 ? K : rt; }
+
+// Visit every in-range tap of a stencil around (p0,p1,p2): f(tap_index, flat_neighbour).
+// SIGN = +1: neighbour = p + tap - off (correlation, forward); -1: p - tap + off (transpose).
+template <int K0, int K1, int K2, int SIGN, typename F>
+__device__ __forceinline__ void for_taps(const StencilGeom& g, const RowPos& rp, F&& f) {
+  if constexpr (K0 > 0 && K1 > 0 && K2 > 0) {
+#pragma unroll
+    for (int a = 0; a < K0; ++a) {
+      const int i0 = rp.p0 + SIGN * (a - g.off[0]);
+      if (i0 < 0 || i0 >= g.n[0]) continue;
+#pragma unroll
+      for (int bq = 0; bq < K1; ++bq) {
+        const int i1 = rp.p1 + SIGN * (bq - g.off[1]);
+        if (i1 < 0 || i1 >= g.n[1]) continue;
+#pragma unroll
+        for (int e = 0; e < K2; ++e) {
+          const int i2 = rp.p2 + SIGN * (e - g.off[2]);
+          if (i2 < 0 || i2 >= g.n[2]) continue;
+          f((a * K1 + bq) * K2 + e, ((long long)i0 * g.n[1] + i1) * g.n[2] + i2);
+        }
+      }
+    }
+  } else {
+    int tap = 0;
+#pragma unroll 1
+    for (int a = 0; a < g.k[0]; ++a) {
+      const int i0 = rp.p0 + SIGN * (a - g.off[0]);
+#pragma unroll 1
+      for (int bq = 0; bq < g.k[1]; ++bq) {
+        const int i1 = rp.p1 + SIGN * (bq - g.off[1]);
+#pragma unroll 1
+        for (int e = 0; e < g.k[2]; ++e, ++tap) {
+          const int i2 = rp.p2 + SIGN * (e - g.off[2]);
+          if (i0 < 0 || i0 >= g.n[0] || i1 < 0 || i1 >= g.n[1] || i2 < 0 || i2 >= g.n[2]) continue;
+          f(tap, ((long long)i0 * g.n[1] + i1) * g.n[2] + i2);
+        }
       }
     }
   }
-  return acc;
+}
+
+// Two consecutive channels: one vector access when PAIR (even channel count, even
+// strides, aligned bases), else two scalar accesses with the second guarded by `two`.
+template <typename T, bool PAIR>
+__device__ __forceinline__ float2 ld2(const T* p, bool two) {
+  if constexpr (PAIR) return V2<T>::load(p);
+  else return make_float2(DT<T>::load(p), two ? DT<T>::load(p + 1) : 0.f);
+}
+template <typename T, bool PAIR>
+__device__ __forceinline__ void st2(T* p, float2 v, bool two) {
+  if constexpr (PAIR) {
+    V2<T>::store(p, v);
+  } else {
+    DT<T>::store(p, v.x);
+    if (two) DT<T>::store(p + 1, v.y);
+  }
+}
+template <bool PAIR>
+__device__ __forceinline__ float2 ld2f(const float* p, bool two) {
+  if constexpr (PAIR) return *reinterpret_cast<const float2*>(p);
+  else return make_float2(p[0], two ? p[1] : 0.f);
+}
+template <bool PAIR>
+__device__ __forceinline__ void st2f(float* p, float2 v, bool two) {
+  if constexpr (PAIR) {
+    *reinterpret_cast<float2*>(p) = v;
+  } else {
+    p[0] = v.x;
+    if (two) p[1] = v.y;
+  }
+}
+
+// Stage the short-conv weights (and biases) of channels [c0, c0 + 64) of q, k and v:
+// sw[(t * ntaps + tap) * 64 + j] = w[(t * C + c0 + j) * ntaps + tap].
+__device__ __forceinline__ void stage_weights(float* sw, float* sb, const float* __restrict__ w,
+                                              const float* __restrict__ bias, int C, int c0, int ntaps,
+                                              bool has_bias) {
+  for (int i = threadIdx.x; i < 3 * ntaps * kElemCG; i += blockDim.x) {
+    const int j = i % kElemCG;
+    const int tt = i / kElemCG;  // t * ntaps + tap
+    const int t = tt / ntaps, tap = tt - t * ntaps;
+    const int c = c0 + j;
+    sw[i] = (w && c < C) ? w[((long long)t * C + c) * ntaps + tap] : 0.f;
+  }
+  for (int i = threadIdx.x; i < 3 * kElemCG; i += blockDim.x) {
+    const int t = i / kElemCG, c = c0 + (i % kElemCG);
+    sb[i] = (has_bias && bias && c < C) ? bias[(long long)t * C + c] : 0.f;
+  }
 }
 
 // Forward prologue: q', k', v' (saved, dtype-rounded) and z = q' * g1(k').
-template <typename T>
-__global__ void hyena_pre_fwd_kernel(const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v,
-                                     long long in_bst, long long in_pst, StencilGeom g, int B, int C,
-                                     const float* __restrict__ w, const float* __restrict__ bias, int gate1,
-                                     T* __restrict__ qs, T* __restrict__ ks, T* __restrict__ vs, T* __restrict__ z) {
+// grid: (ceil(C / 64), row blocks); warp w of CTA y walks rows y * 8 + w + j * (gridDim.y * 8).
+template <typename T, bool PAIR, int K0, int K1, int K2>
+__global__ void __launch_bounds__(kElemThreads) hyena_pre_fwd_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, long long in_bst, long long in_pst,
+    StencilGeom g, int B, int C, const float* __restrict__ w, const float* __restrict__ bias, int gate1,
+    T* __restrict__ qs, T* __restrict__ ks, T* __restrict__ vs, T* __restrict__ z) {
+  __shared__ float sw[3 * kMaxTaps * kElemCG];
+  __shared__ float sb[3 * kElemCG];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * kElemCG;
+  const int c = c0 + 2 * lane;
+  const bool two = c + 1 < C;
+  if constexpr (K0 != 0) {
+    stage_weights(sw, sb, w, bias, C, c0, g.ntaps, g.has_bias);
+    __syncthreads();
+  }
+  if (c >= C) return;
   const long long Ntot = (long long)g.n[0] * g.n[1] * g.n[2];
-  const long long total = (long long)B * Ntot * C;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
-    const long long r = i / C;
-    const long long pos = r % Ntot;
-    const int b = (int)(r / Ntot);
-    int p0, p1, p2;
-    unflatten3(pos, g, p0, p1, p2);
-    const long long bb = (long long)b * in_bst;
-    const float qv = DT<T>::round(short_conv_at(q, bb, in_pst, c, c, p0, p1, p2, g, w, bias));
-    const float kv = DT<T>::round(short_conv_at(k, bb, in_pst, c, C + c, p0, p1, p2, g, w, bias));
-    const float vv = DT<T>::round(short_conv_at(v, bb, in_pst, c, 2 * C + c, p0, p1, p2, g, w, bias));
-    const float zv = qv * DT<T>::round(gate_f(gate1, kv));
-    DT<T>::store(qs + i, qv);
-    DT<T>::store(ks + i, kv);
-    DT<T>::store(vs + i, vv);
-    DT<T>::store(z + i, zv);
+  const long long rows = (long long)B * Ntot;
+  const long long rstride = (long long)gridDim.y * (kElemThreads / 32);
+  for (long long r = (long long)blockIdx.y * (kElemThreads / 32) + warp; r < rows; r += rstride) {
+    const RowPos rp = row_pos(r, g, Ntot);
+    const long long bb = (long long)rp.b * in_bst + c;
+    float2 a[3];
+    if constexpr (K0 == 0) {
+      const long long o = bb + rp.pos * in_pst;
+      a[0] = ld2<T, PAIR>(q + o, two);
+      a[1] = ld2<T, PAIR>(k + o, two);
+      a[2] = ld2<T, PAIR>(v + o, two);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 3; ++t) a[t] = make_float2(sb[t * kElemCG + 2 * lane], sb[t * kElemCG + 2 * lane + 1]);
+      for_taps<K0, K1, K2, 1>(g, rp, [&](int tap, long long pl) {
+        const long long o = bb + pl * in_pst;
+        const float2 xq = ld2<T, PAIR>(q + o, two), xk = ld2<T, PAIR>(k + o, two), xv = ld2<T, PAIR>(v + o, two);
+        const float2 wq = *reinterpret_cast<const float2*>(&sw[(0 * g.ntaps + tap) * kElemCG + 2 * lane]);
+        const float2 wk = *reinterpret_cast<const float2*>(&sw[(1 * g.ntaps + tap) * kElemCG + 2 * lane]);
+        const float2 wv = *reinterpret_cast<const float2*>(&sw[(2 * g.ntaps + tap) * kElemCG + 2 * lane]);
+        a[0].x = fmaf(wq.x, xq.x, a[0].x); a[0].y = fmaf(wq.y, xq.y, a[0].y);
+        a[1].x = fmaf(wk.x, xk.x, a[1].x); a[1].y = fmaf(wk.y, xk.y, a[1].y);
+        a[2].x = fmaf(wv.x, xv.x, a[2].x); a[2].y = fmaf(wv.y, xv.y, a[2].y);
+      });
+    }
+    const float2 qv = V2<T>::round(a[0]), kv = V2<T>::round(a[1]), vv = V2<T>::round(a[2]);
+    const float2 g1 = V2<T>::round(make_float2(gate_f(gate1, kv.x), gate_f(gate1, kv.y)));
+    const long long i = r * C + c;
+    st2<T, PAIR>(qs + i, qv, two);
+    st2<T, PAIR>(ks + i, kv, two);
+    st2<T, PAIR>(vs + i, vv, two);
+    st2<T, PAIR>(z + i, make_float2(qv.x * g1.x, qv.y * g1.y), two);
   }
 }
 
 // Forward epilogue: y = h * g2(v')   (h, v' contiguous [B, N, C]; y strided)
-template <typename T>
-__global__ void hyena_post_fwd_kernel(const T* __restrict__ h, const T* __restrict__ vs, int gate2, long long Ntot,
-                                      int B, int C, T* __restrict__ y, long long out_bst, long long out_pst) {
-  const long long total = (long long)B * Ntot * C;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
-    const long long r = i / C;
-    const long long pos = r % Ntot;
-    const long long b = r / Ntot;
-    const float val = DT<T>::load(h + i) * DT<T>::round(gate_f(gate2, DT<T>::load(vs + i)));
-    DT<T>::store(y + b * out_bst + pos * out_pst + c, val);
+template <typename T, bool PAIR>
+__global__ void __launch_bounds__(kElemThreads) hyena_post_fwd_kernel(
+    const T* __restrict__ h, const T* __restrict__ vs, int gate2, long long Ntot, int B, int C, T* __restrict__ y,
+    long long out_bst, long long out_pst) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * kElemCG + 2 * lane;
+  const bool two = c + 1 < C;
+  if (c >= C) return;
+  const long long rows = (long long)B * Ntot;
+  const long long rstride = (long long)gridDim.y * (kElemThreads / 32);
+  for (long long r = (long long)blockIdx.y * (kElemThreads / 32) + warp; r < rows; r += rstride) {
+    const long long b = r / Ntot, pos = r - b * Ntot;
+    const long long i = r * C + c;
+    const float2 hv = ld2<T, PAIR>(h + i, two), vv = ld2<T, PAIR>(vs + i, two);
+    const float2 g2 = V2<T>::round(make_float2(gate_f(gate2, vv.x), gate_f(gate2, vv.y)));
+    st2<T, PAIR>(y + b * out_bst + pos * out_pst + c, make_float2(hv.x * g2.x, hv.y * g2.y), two);
   }
 }
 
 // Backward through gate 2: dh = dy * g2(v') (dtype), dv' = dy * h * g2'(v') (fp32).
-template <typename T>
-__global__ void hyena_bwd_gate2_kernel(const T* __restrict__ dy, long long out_bst, long long out_pst,
-                                       const T* __restrict__ h, const T* __restrict__ vs, int gate2, long long Ntot,
-                                       int B, int C, T* __restrict__ dh, float* __restrict__ dvp) {
-  const long long total = (long long)B * Ntot * C;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
-    const long long r = i / C;
-    const long long pos = r % Ntot;
-    const long long b = r / Ntot;
-    const float g = DT<T>::load(dy + b * out_bst + pos * out_pst + c);
-    const float vv = DT<T>::load(vs + i);
-    DT<T>::store(dh + i, g * DT<T>::round(gate_f(gate2, vv)));
-    dvp[i] = g * DT<T>::load(h + i) * gate_df(gate2, vv);
+template <typename T, bool PAIR>
+__global__ void __launch_bounds__(kElemThreads) hyena_bwd_gate2_kernel(
+    const T* __restrict__ dy, long long out_bst, long long out_pst, const T* __restrict__ h,
+    const T* __restrict__ vs, int gate2, long long Ntot, int B, int C, T* __restrict__ dh, float* __restrict__ dvp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * kElemCG + 2 * lane;
+  const bool two = c + 1 < C;
+  if (c >= C) return;
+  const long long rows = (long long)B * Ntot;
+  const long long rstride = (long long)gridDim.y * (kElemThreads / 32);
+  for (long long r = (long long)blockIdx.y * (kElemThreads / 32) + warp; r < rows; r += rstride) {
+    const long long b = r / Ntot, pos = r - b * Ntot;
+    const long long i = r * C + c;
+    const float2 gd = ld2<T, PAIR>(dy + b * out_bst + pos * out_pst + c, two);
+    const float2 vv = ld2<T, PAIR>(vs + i, two), hv = ld2<T, PAIR>(h + i, two);
+    const float2 g2 = V2<T>::round(make_float2(gate_f(gate2, vv.x), gate_f(gate2, vv.y)));
+    st2<T, PAIR>(dh + i, make_float2(gd.x * g2.x, gd.y * g2.y), two);
+    st2f<PAIR>(dvp + i, make_float2(gd.x * hv.x * gate_df(gate2, vv.x), gd.y * hv.y * gate_df(gate2, vv.y)), two);
   }
 }
 
-// Backward through gate 1: dq' = dz * g1(k'), dk' = dz * q' * g1'(k') (fp32).
-template <typename T>
-__global__ void hyena_bwd_gate1_kernel(const T* __restrict__ dz, const T* __restrict__ qs, const T* __restrict__ ks,
-                                       int gate1, long long total, float* __restrict__ dqp, float* __restrict__ dkp) {
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const float g = DT<T>::load(dz + i);
-    const float kv = DT<T>::load(ks + i);
-    dqp[i] = g * DT<T>::round(gate_f(gate1, kv));
-    dkp[i] = g * DT<T>::load(qs + i) * gate_df(gate1, kv);
+// Backward through gate 1: dq' = dz * g1(k'), dk' = dz * q' * g1'(k') (fp32); all
+// contiguous [B, N, C], same (row, channel-pair) split as the other kernels.
+template <typename T, bool PAIR>
+__global__ void __launch_bounds__(kElemThreads) hyena_bwd_gate1_kernel(
+    const T* __restrict__ dz, const T* __restrict__ qs, const T* __restrict__ ks, int gate1, long long rows, int C,
+    float* __restrict__ dqp, float* __restrict__ dkp) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * kElemCG + 2 * lane;
+  const bool two = c + 1 < C;
+  if (c >= C) return;
+  const long long rstride = (long long)gridDim.y * (kElemThreads / 32);
+  for (long long r = (long long)blockIdx.y * (kElemThreads / 32) + warp; r < rows; r += rstride) {
+    const long long i = r * C + c;
+    const float2 gd = ld2<T, PAIR>(dz + i, two), kv = ld2<T, PAIR>(ks + i, two), qv = ld2<T, PAIR>(qs + i, two);
+    const float2 g1 = V2<T>::round(make_float2(gate_f(gate1, kv.x), gate_f(gate1, kv.y)));
+    st2f<PAIR>(dqp + i, make_float2(gd.x * g1.x, gd.y * g1.y), two);
+    st2f<PAIR>(dkp + i, make_float2(gd.x * qv.x * gate_df(gate1, kv.x), gd.y * qv.y * gate_df(gate1, kv.y)), two);
   }
 }
 
 // Backward of the depthwise short conv w.r.t. its input (transposed stencil):
 //   din[pos] = sum_tap w[ch, tap] * dout[pos - tap + off]
 // dout: fp32 contiguous [B, N, C] for each of q/k/v (three pointers); din strided.
-template <typename T>
-__global__ void hyena_short_dgrad_kernel(const float* __restrict__ dqp, const float* __restrict__ dkp,
-                                         const float* __restrict__ dvp, StencilGeom g, int B, int C,
-                                         const float* __restrict__ w, T* __restrict__ dq, T* __restrict__ dk,
-                                         T* __restrict__ dv, long long out_bst, long long out_pst) {
+template <typename T, bool PAIR, int K0, int K1, int K2>
+__global__ void __launch_bounds__(kElemThreads) hyena_short_dgrad_kernel(
+    const float* __restrict__ dqp, const float* __restrict__ dkp, const float* __restrict__ dvp, StencilGeom g, int B,
+    int C, const float* __restrict__ w, T* __restrict__ dq, T* __restrict__ dk, T* __restrict__ dv, long long out_bst,
+    long long out_pst) {
+  __shared__ float sw[3 * kMaxTaps * kElemCG];
+  __shared__ float sb[3 * kElemCG];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * kElemCG;
+  const int c = c0 + 2 * lane;
+  const bool two = c + 1 < C;
+  if constexpr (K0 != 0) {
+    stage_weights(sw, sb, w, nullptr, C, c0, g.ntaps, false);
+    __syncthreads();
+  }
+  if (c >= C) return;
   const long long Ntot = (long long)g.n[0] * g.n[1] * g.n[2];
-  const long long total = (long long)B * Ntot * C;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int c = (int)(i % C);
-    const long long r = i / C;
-    const long long pos = r % Ntot;
-    const int b = (int)(r / Ntot);
-    const long long o = (long long)b * out_bst + pos * out_pst + c;
-    if (!g.has_conv) {
-      DT<T>::store(dq + o, dqp[i]);
-      DT<T>::store(dk + o, dkp[i]);
-      DT<T>::store(dv + o, dvp[i]);
-      continue;
+  const long long rows = (long long)B * Ntot;
+  const long long rstride = (long long)gridDim.y * (kElemThreads / 32);
+  for (long long r = (long long)blockIdx.y * (kElemThreads / 32) + warp; r < rows; r += rstride) {
+    const RowPos rp = row_pos(r, g, Ntot);
+    const long long o = (long long)rp.b * out_bst + rp.pos * out_pst + c;
+    float2 a[3] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    if constexpr (K0 == 0) {
+      const long long i = r * C + c;
+      a[0] = ld2f<PAIR>(dqp + i, two);
+      a[1] = ld2f<PAIR>(dkp + i, two);
+      a[2] = ld2f<PAIR>(dvp + i, two);
+    } else {
+      const long long bb = (long long)rp.b * Ntot * C + c;
+      for_taps<K0, K1, K2, -1>(g, rp, [&](int tap, long long pl) {
+        const long long j = bb + pl * C;
+        const float2 xq = ld2f<PAIR>(dqp + j, two), xk = ld2f<PAIR>(dkp + j, two), xv = ld2f<PAIR>(dvp + j, two);
+        const float2 wq = *reinterpret_cast<const float2*>(&sw[(0 * g.ntaps + tap) * kElemCG + 2 * lane]);
+        const float2 wk = *reinterpret_cast<const float2*>(&sw[(1 * g.ntaps + tap) * kElemCG + 2 * lane]);
+        const float2 wv = *reinterpret_cast<const float2*>(&sw[(2 * g.ntaps + tap) * kElemCG + 2 * lane]);
+        a[0].x = fmaf(wq.x, xq.x, a[0].x); a[0].y = fmaf(wq.y, xq.y, a[0].y);
+        a[1].x = fmaf(wk.x, xk.x, a[1].x); a[1].y = fmaf(wk.y, xk.y, a[1].y);
+        a[2].x = fmaf(wv.x, xv.x, a[2].x); a[2].y = fmaf(wv.y, xv.y, a[2].y);
+      });
     }
-    int p0, p1, p2;
-    unflatten3(pos, g, p0, p1, p2);
-    const long long bb = (long long)b * Ntot * C;
-    float aq = 0.f, ak = 0.f, av = 0.f;
-    const float* wq = w + (long long)c * g.ntaps;
-    const float* wk = w + (long long)(C + c) * g.ntaps;
-    const float* wv = w + (long long)(2 * C + c) * g.ntaps;
-    int tap = 0;
-    for (int a = 0; a < g.k[0]; ++a) {
-      const int i0 = p0 - a + g.off[0];
-      for (int bq = 0; bq < g.k[1]; ++bq) {
-        const int i1 = p1 - bq + g.off[1];
-        for (int e = 0; e < g.k[2]; ++e, ++tap) {
-          const int i2 = p2 - e + g.off[2];
-          if (i0 < 0 || i0 >= g.n[0] || i1 < 0 || i1 >= g.n[1] || i2 < 0 || i2 >= g.n[2]) continue;
-          const long long j = bb + (((long long)i0 * g.n[1] + i1) * g.n[2] + i2) * C + c;
-          aq = fmaf(wq[tap], dqp[j], aq);
-          ak = fmaf(wk[tap], dkp[j], ak);
-          av = fmaf(wv[tap], dvp[j], av);
-        }
-      }
-    }
-    DT<T>::store(dq + o, aq);
-    DT<T>::store(dk + o, ak);
-    DT<T>::store(dv + o, av);
+    st2<T, PAIR>(dq + o, a[0], two);
+    st2<T, PAIR>(dk + o, a[1], two);
+    st2<T, PAIR>(dv + o, a[2], two);
   }
 }
 
 // Weight / bias gradient of the short conv:
 //   dw[ch, tap] = sum_{b,pos} dout[b,pos,c] * in[b, pos + tap - off, c],  db[ch] = sum dout
-// grid.x: channel blocks of 32 (over 3C), grid.y: slices of (b, pos); atomics into
-// dw/db (zeroed by the host first).
-template <typename T>
-__global__ void hyena_short_wgrad_kernel(const float* __restrict__ dqp, const float* __restrict__ dkp,
-                                         const float* __restrict__ dvp, const T* __restrict__ q,
-                                         const T* __restrict__ k, const T* __restrict__ v, long long in_bst,
-                                         long long in_pst, StencilGeom g, int B, int C, float* __restrict__ dw,
-                                         float* __restrict__ db) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const int ch = blockIdx.x * 32 + lane;  // channel of the 3C concatenation
-  const bool ok = ch < 3 * C;
-  const int which = ok ? ch / C : 0;
-  const int c = ok ? ch - which * C : 0;
-  const float* dout = which == 0 ? dqp : (which == 1 ? dkp : dvp);
-  const T* in = which == 0 ? q : (which == 1 ? k : v);
+// grid: (ceil(C / 64), 3 tensors, row blocks). Each thread keeps its two channels' taps
+// in registers over its rows (compile-time stencils), the CTA reduces its 8 warps in
+// shared memory, and one atomic per (channel, tap) goes to dw / db (zeroed by the host).
+// The runtime-shaped fallback accumulates straight into shared memory instead.
+template <typename T, bool PAIR, int K0, int K1, int K2>
+__global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_kernel(
+    const float* __restrict__ dqp, const float* __restrict__ dkp, const float* __restrict__ dvp,
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, long long in_bst, long long in_pst,
+    StencilGeom g, int B, int C, float* __restrict__ dw, float* __restrict__ db) {
+  constexpr bool CT = K0 > 0 && K1 > 0 && K2 > 0;
+  constexpr int NT = CT ? K0 * K1 * K2 : 1;
+  constexpr int NW = kElemThreads / 32;
+  __shared__ float red[NW][kElemCG + 1];
+  __shared__ float sacc[CT ? 1 : (kMaxTaps + 1) * kElemCG];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.y;  // 0 q, 1 k, 2 v
+  const int c = blockIdx.x * kElemCG + 2 * lane;
+  const bool ok = c < C;
+  const bool two = c + 1 < C;
+  const float* dout = t == 0 ? dqp : (t == 1 ? dkp : dvp);
+  const T* in = t == 0 ? q : (t == 1 ? k : v);
   const long long Ntot = (long long)g.n[0] * g.n[1] * g.n[2];
   const long long rows = (long long)B * Ntot;
-  float acc[27];
+  if constexpr (!CT) {
+    for (int i = threadIdx.x; i < (kMaxTaps + 1) * kElemCG; i += blockDim.x) sacc[i] = 0.f;
+    __syncthreads();
+  }
+  float2 acc[NT];
 #pragma unroll
-  for (int t = 0; t < 27; ++t) acc[t] = 0.f;
-  float bacc = 0.f;
+  for (int i = 0; i < NT; ++i) acc[i] = make_float2(0.f, 0.f);
+  float2 bacc = make_float2(0.f, 0.f);
   if (ok) {
-    for (long long r = (long long)blockIdx.y * nw + warp; r < rows; r += (long long)gridDim.y * nw) {
-      const long long pos = r % Ntot;
-      const int b = (int)(r / Ntot);
-      int p0, p1, p2;
-      unflatten3(pos, g, p0, p1, p2);
-      const float go = dout[r * C + c];
-      bacc += go;
-      int tap = 0;
-      for (int a = 0; a < g.k[0]; ++a) {
-        const int i0 = p0 + a - g.off[0];
-        for (int bq = 0; bq < g.k[1]; ++bq) {
-          const int i1 = p1 + bq - g.off[1];
-          for (int e = 0; e < g.k[2]; ++e, ++tap) {
-            const int i2 = p2 + e - g.off[2];
-            if (i0 < 0 || i0 >= g.n[0] || i1 < 0 || i1 >= g.n[1] || i2 < 0 || i2 >= g.n[2]) continue;
-            const long long pl = ((long long)i0 * g.n[1] + i1) * g.n[2] + i2;
-            const float xin = DT<T>::load(in + (long long)b * in_bst + pl * in_pst + c);
-#pragma unroll
-            for (int t = 0; t < 27; ++t)
-              if (t == tap) acc[t] = fmaf(go, xin, acc[t]);
-          }
+    // a contiguous run of rows per CTA, so stencil neighbours are mostly L1 hits
+    const long long per = (rows + gridDim.z - 1) / gridDim.z;
+    const long long r0 = (long long)blockIdx.z * per, r1 = min(rows, r0 + per);
+    for (long long r = r0 + warp; r < r1; r += NW) {
+      const RowPos rp = row_pos(r, g, Ntot);
+      const float2 go = ld2f<PAIR>(dout + r * C + c, two);
+      bacc.x += go.x;
+      bacc.y += go.y;
+      const long long bb = (long long)rp.b * in_bst + c;
+      for_taps<K0, K1, K2, 1>(g, rp, [&](int tap, long long pl) {
+        const float2 xin = ld2<T, PAIR>(in + bb + pl * in_pst, two);
+        if constexpr (CT) {
+          acc[tap].x = fmaf(go.x, xin.x, acc[tap].x);
+          acc[tap].y = fmaf(go.y, xin.y, acc[tap].y);
+        } else {
+          atomicAdd(&sacc[tap * kElemCG + 2 * lane], go.x * xin.x);
+          atomicAdd(&sacc[tap * kElemCG + 2 * lane + 1], go.y * xin.y);
         }
-      }
+      });
     }
   }
-  // reduce over warps through shared memory, then one atomic per (ch, tap)
-  __shared__ float red[32][33];
-  for (int t = 0; t < g.ntaps + 1; ++t) {
-    float val = (t < g.ntaps) ? 0.f : bacc;
+  const int ntaps = g.ntaps;
+  for (int tap = 0; tap <= ntaps; ++tap) {
+    float2 val = make_float2(0.f, 0.f);
+    if (tap == ntaps) {
+      val = bacc;
+    } else if constexpr (CT) {
 #pragma unroll
-    for (int u = 0; u < 27; ++u)
-      if (u == t) val = acc[u];
-    if (t == g.ntaps) val = bacc;
-    red[warp][lane] = val;
+      for (int u = 0; u < NT; ++u)
+        if (u == tap) val = acc[u];
+    }
+    red[warp][2 * lane] = val.x;
+    red[warp][2 * lane + 1] = val.y;
     __syncthreads();
-    if (warp == 0 && ok) {
+    if (threadIdx.x < kElemCG) {
+      const int cc = blockIdx.x * kElemCG + threadIdx.x;
       float s = 0.f;
-      for (int j = 0; j < nw; ++j) s += red[j][lane];
-      if (t < g.ntaps) atomicAdd(dw + (long long)ch * g.ntaps + t, s);
-      else if (g.has_bias) atomicAdd(db + ch, s);
+#pragma unroll
+      for (int j = 0; j < NW; ++j) s += red[j][threadIdx.x];
+      if constexpr (!CT) {
+        if (tap < ntaps) s = sacc[tap * kElemCG + threadIdx.x];
+      }
+      if (cc < C) {
+        const long long ch = (long long)t * C + cc;
+        if (tap < ntaps) atomicAdd(dw + ch * ntaps + tap, s);
+        else if (g.has_bias) atomicAdd(db + ch, s);
+      }
     }
     __syncthreads();
+  }
+}
+
+// dD[c] = sum_{b, pos} dh[b, pos, c] * z[b, pos, c] (contiguous [B, N, C]); grid
+// (ceil(C / 64), row blocks), one atomic per channel per CTA (dD zeroed by the host).
+template <typename T, bool PAIR>
+__global__ void __launch_bounds__(kElemThreads) hyena_dskip_kernel(const T* __restrict__ dh, const T* __restrict__ z,
+                                                                    long long rows, int C, float* __restrict__ dD) {
+  constexpr int NW = kElemThreads / 32;
+  __shared__ float red[NW][kElemCG + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = blockIdx.x * kElemCG + 2 * lane;
+  const bool two = c + 1 < C;
+  float2 acc = make_float2(0.f, 0.f);
+  if (c < C) {
+    for (long long r = (long long)blockIdx.y * NW + warp; r < rows; r += (long long)gridDim.y * NW) {
+      const long long i = r * C + c;
+      const float2 a = ld2<T, PAIR>(dh + i, two), b = ld2<T, PAIR>(z + i, two);
+      acc.x = fmaf(a.x, b.x, acc.x);
+      acc.y = fmaf(a.y, b.y, acc.y);
+    }
+  }
+  red[warp][2 * lane] = acc.x;
+  red[warp][2 * lane + 1] = acc.y;
+  __syncthreads();
+  if (threadIdx.x < kElemCG) {
+    const int cc = blockIdx.x * kElemCG + threadIdx.x;
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < NW; ++j) s += red[j][threadIdx.x];
+    if (cc < C) atomicAdd(dD + cc, s);
   }
 }
 

@@ -46,21 +46,22 @@ __global__ void spec_bwd_kernel(float2* __restrict__ Sdy, const float2* __restri
   }
 }
 
-// dD[c] = sum_{b, s} dy[b, c, s] * x[b, c, s] for layout BHL (cst = S) or BLH (cst = 1).
-// One CTA per channel block of 32 channels; threads stride over (b, s).
+// dD[c] = sum_{b, s} dy[b, c, s] * x[b, c, s] for layout BHL (cst = S) or BLH (cst = 1),
+// accumulated with one atomic per channel per CTA into `out` (zeroed by the host).
+// BLH: grid (ceil(C / 32), row blocks), lanes over channels, warps over (b, s) rows.
+// BHL: grid (C, B), the CTA sums one contiguous (b, c) line of S elements.
 template <typename T>
 __global__ void dshortcut_kernel(const T* __restrict__ dy, const T* __restrict__ x, float* __restrict__ out,
                                  int B, int C, long long S, int blh) {
   __shared__ float red[8][33];
-  const int c0 = blockIdx.x * 32;
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;  // 256 threads: 8 warps
-  float acc = 0.f;
   if (blh) {
-    const int c = c0 + lane;
+    const int c = blockIdx.x * 32 + lane;
+    float acc = 0.f;
     if (c < C) {
-      for (long long r = w; r < (long long)B * S; r += 8) {
+      for (long long r = (long long)blockIdx.y * 8 + w; r < (long long)B * S; r += (long long)gridDim.y * 8) {
         const long long i = r * C + c;
-        acc += DT<T>::load(dy + i) * DT<T>::load(x + i);
+        acc = fmaf(DT<T>::load(dy + i), DT<T>::load(x + i), acc);
       }
     }
     red[w][lane] = acc;
@@ -68,20 +69,20 @@ __global__ void dshortcut_kernel(const T* __restrict__ dy, const T* __restrict__
     if (w == 0) {
       float s = 0.f;
       for (int j = 0; j < 8; ++j) s += red[j][lane];
-      if (c < C) out[c] = s;
+      if (c < C) atomicAdd(out + c, s);
     }
   } else {
-    // BHL: each warp sums one channel at a time
-    for (int cc = w; cc < 32; cc += 8) {
-      const int c = c0 + cc;
-      if (c >= C) break;
-      float a = 0.f;
-      for (int b = 0; b < B; ++b) {
-        const long long base = ((long long)b * C + c) * S;
-        for (long long s = lane; s < S; s += 32) a += DT<T>::load(dy + base + s) * DT<T>::load(x + base + s);
-      }
-      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-      if (lane == 0) out[c] = a;
+    const int c = blockIdx.x, b = blockIdx.y;
+    const long long base = ((long long)b * C + c) * S;
+    float a = 0.f;
+    for (long long s = threadIdx.x; s < S; s += blockDim.x) a = fmaf(DT<T>::load(dy + base + s), DT<T>::load(x + base + s), a);
+    for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+    if (lane == 0) red[w][0] = a;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float s = 0.f;
+      for (int j = 0; j < 8; ++j) s += red[j][0];
+      atomicAdd(out + c, s);
     }
   }
 }
