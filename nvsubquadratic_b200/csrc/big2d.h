@@ -1,0 +1,38 @@
+// Parameters and dispatch of the fused large-grid 2D FFT convolution (big2d.cu):
+// 2D, centred ("same") linear convolution with F0 = F1 = 256, N0, N1 <= 128, one
+// filter shared by the batch.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace hyfft {
+
+constexpr int kB2F = 256;             // FFT length per axis
+constexpr int kB2H = kB2F / 2 + 1;    // 129 half-spectrum bins along axis 1
+constexpr int kB2MaxN = 128;          // largest spatial extent
+
+struct Big2DView {  // element (b, c, i0, i1) at b*bst + c*cst + i0*s0 + i1*s1
+  const void* ptr;
+  long long bst, cst, s0, s1;
+};
+
+struct Big2DParams {
+  Big2DView x;        // conv input (x; dy for the adjoint); first input of the dK kernel
+  Big2DView x2;       // second input of the dK kernel (dy)
+  Big2DView y;        // conv output (y; dx for the adjoint)
+  const float* D;     // [C] skip scale or null: out = round(round(conv) + round(D * x))
+  Big2DView filt;     // float32 filter taps (b unused)
+  Big2DView dfilt;    // float32 filter gradient (b unused)
+  float2* Kh;         // [C][129][256] spectrum of the rolled filter (column bins outer)
+  float2* T;          // [C][256][129] row-transform scratch of the filter / its gradient
+  float2* G;          // [C][129][256] filter-gradient spectrum accumulator (zeroed by the host)
+  int B, C, N0, N1, K0, K1;
+  int conj;           // 1: multiply by conj(Kh) (the adjoint, dx = corr(dy, k))
+};
+
+enum Big2DOp { B2_KSPEC = 0, B2_CONV = 1, B2_DK = 2, B2_DFILT = 3 };
+
+// Launch one step (HYFFT_OK, or HYFFT_ERR_CUDA). dtype: HYFFT_F32 / BF16 / F16 of x, x2, y.
+int big2d_dispatch(int op, int dtype, const Big2DParams& p, cudaStream_t st);
+
+}  // namespace hyfft

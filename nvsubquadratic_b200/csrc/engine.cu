@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "fft_pass.cuh"
+#include "big2d.h"
 #include "hyena_elem.cuh"
 #include "pointwise.cuh"
 #include "fused2d.h"
@@ -460,6 +461,7 @@ struct ConvPlan {
   Pairing px, pk;
   int Cc = 0;  // channels per chunk
   long long spec_x_bytes_per_ch = 0, spec_k_bytes_per_ch = 0;
+  bool big2d = false;  // fused large-grid 2D kernels (big2d.cu) instead of the pass chain
 };
 
 static size_t ws_budget() {
@@ -491,12 +493,23 @@ static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p) {
   const long long per_ch = 2 * (p.spec_x_bytes_per_ch + p.spec_k_bytes_per_ch);
   long long cc = (long long)(ws_budget() / (size_t)std::max<long long>(per_ch, 1));
   p.Cc = (int)std::max<long long>(1, std::min<long long>(cc, p.C));
+  p.big2d = p.g.D == 2 && !d->causal && p.g.F[0] == kB2F && p.g.F[1] == kB2F && p.g.N[0] <= kB2MaxN &&
+            p.g.N[1] <= kB2MaxN && p.kB == 1 && !getenv("HYFFT_DISABLE_BIG2D");
   return HYFFT_OK;
 }
 
 static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
 
+// One [C][129][256] complex spectrum of the large-grid 2D kernels.
+static size_t big2d_spec_bytes(const ConvPlan& p) { return align_up((size_t)p.C * kB2H * kB2F * sizeof(float2)); }
+
 static void conv_ws_sizes(const ConvPlan& p, size_t& fwd, size_t& bwd) {
+  if (p.big2d) {  // Kh, T (+ G for the backward), then the float shortcut vector
+    const size_t spec = big2d_spec_bytes(p), dvec = align_up((size_t)p.C * 4);
+    fwd = 2 * spec + dvec;
+    bwd = 3 * spec + dvec;
+    return;
+  }
   const size_t sx = align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
   const size_t sk = align_up((size_t)p.spec_k_bytes_per_ch * p.Cc);
   const size_t dvec = align_up((size_t)p.C * 4);
@@ -588,6 +601,66 @@ static int run_dshortcut(int dt, int layout, const void* dy, const void* x, floa
   return check_launch("dshortcut_kernel");
 }
 
+// ---- large-grid 2D path: workspace = [Kh | T | G], all [C][129][256]-sized
+static Big2DView b2view(const RealView& v) {
+  Big2DView o;
+  o.ptr = v.ptr;
+  o.bst = v.bst;
+  o.cst = v.cst;
+  o.s0 = v.sst[0];
+  o.s1 = v.sst[1];
+  return o;
+}
+
+static void big2d_params(const ConvPlan& p, const RealView& kv, const float* D, char* ws, Big2DParams& b) {
+  memset(&b, 0, sizeof(b));
+  const size_t spec = big2d_spec_bytes(p);
+  b.filt = b2view(kv);
+  b.D = D;
+  b.Kh = (float2*)ws;
+  b.T = (float2*)(ws + spec);
+  b.G = (float2*)(ws + 2 * spec);
+  b.B = p.B;
+  b.C = p.C;
+  b.N0 = p.g.N[0];
+  b.N1 = p.g.N[1];
+  b.K0 = p.g.K[0];
+  b.K1 = p.g.K[1];
+}
+
+static int big2d_forward(const ConvPlan& p, const RealView& xv, const RealView& kv, const float* D, const RealView& yv,
+                         char* ws, cudaStream_t st) {
+  Big2DParams b;
+  big2d_params(p, kv, D, ws, b);
+  b.x = b2view(xv);
+  b.y = b2view(yv);
+  if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
+  if (big2d_dispatch(B2_CONV, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d conv launch failed");
+  return HYFFT_OK;
+}
+
+static int big2d_backward(const ConvPlan& p, const RealView& xv, const RealView& kv, const float* D,
+                          const RealView& dyv, const RealView& dxv, const RealView& dkv, char* ws, cudaStream_t st) {
+  Big2DParams b;
+  big2d_params(p, kv, D, ws, b);
+  if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
+  if (dxv.ptr) {  // dx = corr(dy, k) + D * dy
+    b.x = b2view(dyv);
+    b.y = b2view(dxv);
+    b.conj = 1;
+    if (big2d_dispatch(B2_CONV, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d adjoint launch failed");
+  }
+  if (dkv.ptr) {
+    if (cudaMemsetAsync(b.G, 0, big2d_spec_bytes(p), st) != cudaSuccess) return fail(HYFFT_ERR_CUDA, "memset G");
+    b.x = b2view(xv);
+    b.x2 = b2view(dyv);
+    b.dfilt = b2view(dkv);
+    if (big2d_dispatch(B2_DK, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d dK launch failed");
+    if (big2d_dispatch(B2_DFILT, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d dfilt launch failed");
+  }
+  return HYFFT_OK;
+}
+
 }  // namespace hyfft
 
 using namespace hyfft;
@@ -619,6 +692,13 @@ int hyfft_conv_forward(const hyfft_conv_desc* d, const void* x, const float* ker
   conv_ws_sizes(p, need, nb);
   if (!workspace || workspace_bytes < need) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, need);
   cudaStream_t st = (cudaStream_t)stream;
+  if (p.big2d) {
+    float* Dv = (float*)((char*)workspace + 2 * big2d_spec_bytes(p));
+    if (shortcut) HY_TRY(to_float(shortcut, p.dt, Dv, p.C, st));
+    return big2d_forward(p, real_view(x, p.layout, p.B, p.C, p.g.N, p.g.D),
+                         real_view(kernel, p.layout, p.kB, p.C, p.g.K, p.g.D), shortcut ? Dv : nullptr,
+                         real_view(y, p.layout, p.B, p.C, p.g.N, p.g.D), (char*)workspace, st);
+  }
   char* w = (char*)workspace;
   float2* S = (float2*)w;
   w += align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
@@ -647,6 +727,20 @@ int hyfft_conv_backward(const hyfft_conv_desc* d, const void* x, const float* ke
   conv_ws_sizes(p, nf, need);
   if (!workspace || workspace_bytes < need) return fail(HYFFT_ERR_WORKSPACE, "workspace %zu < %zu bytes", workspace_bytes, need);
   cudaStream_t st = (cudaStream_t)stream;
+  if (p.big2d) {
+    float* Dv = (float*)((char*)workspace + 3 * big2d_spec_bytes(p));
+    if (shortcut) HY_TRY(to_float(shortcut, p.dt, Dv, p.C, st));
+    HY_TRY(big2d_backward(p, real_view(x, p.layout, p.B, p.C, p.g.N, p.g.D),
+                          real_view(kernel, p.layout, p.kB, p.C, p.g.K, p.g.D), shortcut ? Dv : nullptr,
+                          real_view(dy, p.layout, p.B, p.C, p.g.N, p.g.D), real_view(dx, p.layout, p.B, p.C, p.g.N, p.g.D),
+                          real_view(dkernel, p.layout, p.kB, p.C, p.g.K, p.g.D), (char*)workspace, st));
+    if (shortcut && dshortcut) {
+      long long S = 1;
+      for (int i = 0; i < p.g.D; ++i) S *= p.g.N[i];
+      HY_TRY(run_dshortcut(p.dt, p.layout, dy, x, dshortcut, p.B, p.C, S, st));
+    }
+    return HYFFT_OK;
+  }
   char* w = (char*)workspace;
   const size_t sx = align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
   const size_t sk = align_up((size_t)p.spec_k_bytes_per_ch * p.Cc);
@@ -852,6 +946,19 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
   saved = 5 * act;                 // q', k', v', z, h
   fwd = cf + align_up((size_t)h.d.channels * 4);
   bwd = cb + 2 * act + 3 * f32 + align_up((size_t)h.d.channels * 4);
+  if (h.cp.big2d) {  // channel-major copies around the large-grid kernels: z, h | z, dh, dz
+    fwd += 2 * act;
+    bwd += 3 * act;
+  }
+}
+
+// channels-last [B][N][C] <-> channel-major [B][C][N] (contiguous)
+template <typename T>
+static int cl_cm(const T* src, T* dst, int B, long long N, int C, bool to_cm, cudaStream_t st) {
+  const dim3 grid((unsigned)((N + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)B);
+  if (to_cm) cl_cm_transpose_kernel<T, true><<<grid, 256, 0, st>>>(src, dst, N, C);
+  else cl_cm_transpose_kernel<T, false><<<grid, 256, 0, st>>>(src, dst, N, C);
+  return check_launch("cl_cm_transpose_kernel");
 }
 
 // ---- launch helpers of the elementwise / stencil kernels (hyena_elem.cuh)
@@ -923,9 +1030,18 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
   const RealView zv = real_view(z, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
   const RealView kv = real_view(filt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
   const RealView hv = real_view(hb, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
-  for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
-    const int cc = std::min(p.Cc, p.C - c0);
-    HY_TRY(conv_forward_chunk(p, c0, cc, zv, kv, D, hv, S, Kh, st));
+  if (p.big2d) {  // channel-major z and h around the large-grid kernels (unit-stride rows)
+    T* zc = (T*)(ws + cf + align_up((size_t)d.channels * 4));
+    T* hc = (T*)((char*)zc + align_up((size_t)h.E * h.eb));
+    HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
+    HY_TRY(big2d_forward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
+                         real_view(hc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), ws, st));
+    HY_TRY(cl_cm<T>(hc, hb, d.batch, h.Ntot, d.channels, false, st));
+  } else {
+    for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
+      const int cc = std::min(p.Cc, p.C - c0);
+      HY_TRY(conv_forward_chunk(p, c0, cc, zv, kv, D, hv, S, Kh, st));
+    }
   }
   if (pair)
     hyena_post_fwd_kernel<T, true><<<elem_grid(d.channels, rows, 8), kElemThreads, 0, st>>>(
@@ -988,9 +1104,21 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     const RealView dhv = real_view(dh, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
     const RealView dzv = real_view(dz, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
     const RealView dkv = real_view(dfilt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
-    for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
-      const int cc = std::min(p.Cc, p.C - c0);
-      HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, Kh, dKh, st));
+    if (p.big2d) {  // channel-major z, dh, dz around the large-grid kernels
+      T* zc = (T*)(ws + cb + 2 * act + 3 * f32 + align_up((size_t)d.channels * 4));
+      T* dhc = (T*)((char*)zc + act);
+      T* dzc = (T*)((char*)dhc + act);
+      HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
+      HY_TRY(cl_cm<T>(dh, dhc, d.batch, h.Ntot, d.channels, true, st));
+      HY_TRY(big2d_backward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
+                            real_view(dhc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D),
+                            real_view(dzc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), dkv, ws, st));
+      HY_TRY(cl_cm<T>(dzc, dz, d.batch, h.Ntot, d.channels, false, st));
+    } else {
+      for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
+        const int cc = std::min(p.Cc, p.C - c0);
+        HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, Kh, dKh, st));
+      }
     }
     if (dD) {
       if (cudaMemsetAsync(dD, 0, sizeof(float) * (size_t)d.channels, st) != cudaSuccess)

@@ -181,7 +181,7 @@ __device__ __forceinline__ void stockham_stage(float2* sm, const float2* tw, int
 // sm[l * ld + padi(t)] (TL * F <= kPassPoints). All threads of the CTA take part;
 // radix-16 stages while at least four factors of two remain, then radix 4 / 2.
 // Twiddles come from the half-turn table tw (F/2 entries).
-__device__ void stockham_tile(float2* sm, const float2* tw, int TL, int F, int logF, int ld, float dir) {
+static __device__ void stockham_tile(float2* sm, const float2* tw, int TL, int F, int logF, int ld, float dir) {
   int lgNs = 0;
   while (logF - lgNs >= 4) {
     stockham_stage<16, 4, kPassPoints / (16 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);

@@ -63,23 +63,40 @@ struct RowPos {
 };
 __device__ __forceinline__ RowPos row_pos(long long r, const StencilGeom& g, long long Ntot) {
   RowPos o;
-  o.b = (int)(r / Ntot);
-  o.pos = r - (long long)o.b * Ntot;
-  if (Ntot < (1LL << 31)) {
-    const unsigned p = (unsigned)o.pos;
+  if (r < (1LL << 31) && Ntot < (1LL << 31)) {  // 32-bit division: far cheaper than 64-bit
+    const unsigned ur = (unsigned)r, un = (unsigned)Ntot;
+    const unsigned b = ur / un;
+    const unsigned p = ur - b * un;
     const unsigned n2 = (unsigned)g.n[2], n1 = (unsigned)g.n[1];
     const unsigned q2 = p / n2;
-    o.p2 = (int)(p - q2 * n2);
     const unsigned q1 = q2 / n1;
+    o.b = (int)b;
+    o.pos = p;
+    o.p2 = (int)(p - q2 * n2);
     o.p1 = (int)(q2 - q1 * n1);
     o.p0 = (int)q1;
   } else {
+    o.b = (int)(r / Ntot);
+    o.pos = r - (long long)o.b * Ntot;
     o.p2 = (int)(o.pos % g.n[2]);
     const long long q2 = o.pos / g.n[2];
     o.p1 = (int)(q2 % g.n[1]);
     o.p0 = (int)(q2 / g.n[1]);
   }
   return o;
+}
+
+// (b, position) of row r without the stencil coordinates.
+__device__ __forceinline__ void row_bp(long long r, long long Ntot, long long& b, long long& pos) {
+  if (r < (1LL << 31) && Ntot < (1LL << 31)) {
+    const unsigned ur = (unsigned)r, un = (unsigned)Ntot;
+    const unsigned ub = ur / un;
+    b = ub;
+    pos = ur - ub * un;
+  } else {
+    b = r / Ntot;
+    pos = r - b * Ntot;
+  }
 }
 
 // Runtime or compile-time stencil extents.
@@ -240,7 +257,8 @@ __global__ void __launch_bounds__(kElemThreads) hyena_post_fwd_kernel(
   const long long rows = (long long)B * Ntot;
   const long long rstride = (long long)gridDim.y * (kElemThreads / 32);
   for (long long r = (long long)blockIdx.y * (kElemThreads / 32) + warp; r < rows; r += rstride) {
-    const long long b = r / Ntot, pos = r - b * Ntot;
+    long long b, pos;
+    row_bp(r, Ntot, b, pos);
     const long long i = r * C + c;
     const float2 hv = ld2<T, PAIR>(h + i, two), vv = ld2<T, PAIR>(vs + i, two);
     const float2 g2 = V2<T>::round(make_float2(gate_f(gate2, vv.x), gate_f(gate2, vv.y)));
@@ -260,7 +278,8 @@ __global__ void __launch_bounds__(kElemThreads) hyena_bwd_gate2_kernel(
   const long long rows = (long long)B * Ntot;
   const long long rstride = (long long)gridDim.y * (kElemThreads / 32);
   for (long long r = (long long)blockIdx.y * (kElemThreads / 32) + warp; r < rows; r += rstride) {
-    const long long b = r / Ntot, pos = r - b * Ntot;
+    long long b, pos;
+    row_bp(r, Ntot, b, pos);
     const long long i = r * C + c;
     const float2 gd = ld2<T, PAIR>(dy + b * out_bst + pos * out_pst + c, two);
     const float2 vv = ld2<T, PAIR>(vs + i, two), hv = ld2<T, PAIR>(h + i, two);
@@ -454,6 +473,47 @@ __global__ void __launch_bounds__(kElemThreads) hyena_dskip_kernel(const T* __re
 #pragma unroll
     for (int j = 0; j < NW; ++j) s += red[j][threadIdx.x];
     if (cc < C) atomicAdd(dD + cc, s);
+  }
+}
+
+// Layout change between channels-last [B][N][C] and channel-major [B][C][N] (both
+// contiguous) through 32 x 32 shared-memory tiles, so both sides are read and written
+// along their unit stride. TO_CM: channels-last -> channel-major. grid (ceil(N/32),
+// ceil(C/32), B), 256 threads.
+template <typename T, bool TO_CM>
+__global__ void __launch_bounds__(256) cl_cm_transpose_kernel(const T* __restrict__ src, T* __restrict__ dst,
+                                                              long long N, int C) {
+  __shared__ T tile[32][33];
+  const long long n0 = (long long)blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  const long long base = (long long)blockIdx.z * N * C;
+  const T* sp = src + base;
+  T* dp = dst + base;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  if constexpr (TO_CM) {
+    for (int i = ty; i < 32; i += 8) {
+      const long long n = n0 + i;
+      const int c = c0 + tx;
+      if (n < N && c < C) tile[i][tx] = sp[n * C + c];
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+      const int c = c0 + i;
+      const long long n = n0 + tx;
+      if (n < N && c < C) dp[(long long)c * N + n] = tile[tx][i];
+    }
+  } else {
+    for (int i = ty; i < 32; i += 8) {
+      const int c = c0 + i;
+      const long long n = n0 + tx;
+      if (n < N && c < C) tile[i][tx] = sp[(long long)c * N + n];
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+      const long long n = n0 + i;
+      const int c = c0 + tx;
+      if (n < N && c < C) dp[n * C + c] = tile[tx][i];
+    }
   }
 }
 

@@ -75,6 +75,10 @@ SHAPES = [
     (False, (1, 4, 16, 16, 16), (1, 4, 31, 31, 31), torch.float32),
     (False, (3, 2, 10, 12, 9), (1, 2, 7, 23, 9), torch.bfloat16),
     (False, (2, 8, 300), (1, 8, 77), torch.float32),
+    # large-grid 2D kernels (F = 256 x 256, N <= 128)
+    (False, (2, 6, 100, 120), (1, 6, 129, 150), torch.float32),
+    (False, (3, 4, 128, 128), (1, 4, 128, 128), torch.bfloat16),
+    (False, (1, 3, 128, 97), (1, 3, 255, 193), torch.float32),
 ]
 
 
@@ -153,3 +157,25 @@ def test_inputs_not_mutated_and_new_output():
     y = b2.fftconv2d_fp32_bhl(x, k)
     assert torch.equal(x, x0) and torch.equal(k, k0)
     assert y.data_ptr() != x.data_ptr()
+
+
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_large_grid_2d_matches_pass_chain_and_blh(dt, monkeypatch):
+    """The fused large-grid 2D kernels agree with the multi-pass engine, and the
+    channels-last entry agrees with the channels-first one."""
+    b2 = _b2()
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(3, 5, 112, 128, generator=g).to(dt)
+    k = torch.randn(1, 5, 127, 101, generator=g) * 0.05
+    sc = torch.randn(5, generator=g).to(dt)
+    dy = torch.randn(3, 5, 112, 128, generator=g).to(dt)
+    fused = _run(b2.fftconv2d_fp32_bhl, x, k, sc, dy)
+    blh = _run(b2.fftconv2d_fp32_blh, x.permute(0, 2, 3, 1).contiguous(), k.permute(0, 2, 3, 1).contiguous(), sc,
+               dy.permute(0, 2, 3, 1).contiguous())
+    monkeypatch.setenv("HYFFT_DISABLE_BIG2D", "1")
+    chain = _run(b2.fftconv2d_fp32_bhl, x, k, sc, dy)
+    tol = TOL[dt]
+    for a, b, c, name in zip(chain, fused, blh, ("y", "dx", "dk", "dshortcut")):
+        assert rel_l2(a, b) <= tol, (name, rel_l2(a, b))
+        c = c.permute(0, 3, 1, 2) if c.ndim == 4 else c
+        assert rel_l2(b, c) <= tol, (name, "blh", rel_l2(b, c))

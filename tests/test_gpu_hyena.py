@@ -70,6 +70,9 @@ CASES = [
     (1, 1, 8, (8192,), (8192,), 7, True, "sigmoid", "silu", torch.float32, False, False),
     (3, 2, 4, (8, 8, 8), (8, 8, 8), 3, False, "silu", "silu", torch.float32, False, True),
     (2, 3, 8, (12, 10), (23, 19), 0, False, "identity", "sigmoid", torch.float32, False, False),
+    # large-grid 2D kernels (F = 256 x 256)
+    (2, 2, 8, (128, 128), (128, 128), 3, False, "silu", "sigmoid", torch.bfloat16, False, True),
+    (2, 1, 4, (100, 90), (129, 120), 3, False, "identity", "sigmoid", torch.float32, True, False),
 ]
 
 
