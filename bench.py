@@ -50,6 +50,10 @@ CONFIGS = {
     "cfg3": dict(nd=3, B=2, C=192, S=(64, 64, 64), K=(64, 64, 64), short=3, g1="identity", g2="identity",
                  dtype=torch.bfloat16, causal=False, shard="channel",
                  desc="3D HyenaND 64^3, full-extent exp-radial filter, F=128^3, channel-sharded"),
+    "cfg4": dict(nd=1, B=1, C=4096, S=(1 << 20,), K=(1 << 20,), short=7, g1="identity", g2="identity",
+                 dtype=torch.bfloat16, causal=True, shard="cp",
+                 desc="1D causal long-context Hyena, L=2^20, context-parallel (zigzag sequence shards, "
+                      "NCCL all-to-all to channel shards and back), F=2^21, causal short conv k=7"),
 }
 
 
@@ -257,6 +261,114 @@ def time_passes(step, zero_grads, flush, names, n):
     return {nm: sum(a.elapsed_time(b) for a, b in r) / len(r) for nm, r in recs.items() if r}
 
 
+# ----------------------------------------------------------------- context-parallel arm
+def run_cp(args, cfg, rank, world, device):
+    """cfg4: every rank holds its zigzag sequence chunks of q, k, v (one [B, L/P, 3C]
+    projection output) and its channel block of the filter; a step is the CP mixer's
+    forward + backward (two NCCL all-to-alls each way). Eager steps (the collectives stay
+    outside CUDA graphs); inputs are far larger than L2, so no flush is needed."""
+    from types import SimpleNamespace
+
+    from nvsubquadratic_b200 import _lib, cp
+
+    group = torch.distributed.group.WORLD
+    B, C, L = cfg["B"], cfg["C"], cfg["S"][0]
+    P = world
+    assert C % P == 0 and L % (2 * P) == 0
+    d, l = C // P, L // P
+    dt = cfg["dtype"]
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    qkv = torch.randn((B, l, 3 * C), generator=gen, device=device, dtype=dt).requires_grad_(True)
+    dy = torch.randn((B, l, C), generator=gen, device=device, dtype=dt)
+    gc = torch.Generator(device=device).manual_seed(7)  # identical parameters on every rank
+    t = torch.arange(L, device=device, dtype=torch.float32)
+    alpha = (torch.rand(C, generator=gc, device=device) * 4.5 + 0.5) / L
+    filt = torch.randn((1, d, L), generator=gen, device=device) * torch.exp(-alpha[rank * d:(rank + 1) * d, None] * t)
+    filt.requires_grad_(True)
+    del t
+    D = ((torch.rand(C, generator=gc, device=device) * 2 - 1) / math.sqrt(C)).requires_grad_(True)
+    sk = cfg["short"]
+    sw = ((torch.rand((3 * C, 1, sk), generator=gc, device=device) * 2 - 1) / math.sqrt(sk)).requires_grad_(True)
+    mod = SimpleNamespace(shortcut=D, short_weight=sw, short_bias=None, causal=True, short_causal=True,
+                          gate1=cfg["g1"], gate2=cfg["g2"])
+    params = [qkv, filt, D, sw]
+
+    def zero_grads():
+        for p_ in params:
+            p_.grad = None
+
+    def step():
+        q, k, v = qkv.chunk(3, dim=-1)
+        y = cp.hyena_context_parallel(mod, q, k, v, filt, group)
+        y.backward(dy)
+        return y
+
+    for _ in range(args.warmup):
+        zero_grads()
+        step()
+    torch.cuda.synchronize()
+    if args.profile:
+        return None
+    n0 = _lib.launch_count()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device.index if device.index is not None else 0) as clk:
+        for i in range(args.steps):
+            zero_grads()
+            starts[i].record()
+            step()
+            ends[i].record()
+        torch.cuda.synchronize()
+    torch.distributed.barrier()
+    launches = (_lib.launch_count() - n0) // max(1, args.steps)
+    total_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+    tt = torch.tensor([total_ms], device=device)
+    torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+    total_ms = tt.item()
+    # the dominant library pass on the local channel block
+    names = ["hyfft_hyena_forward", "hyfft_hyena_backward"]
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    pass_ms = time_passes(step, zero_grads, flush, names, 1)
+    for nm in names:
+        t3 = torch.tensor([pass_ms[nm]], device=device)
+        torch.distributed.all_reduce(t3, op=torch.distributed.ReduceOp.MAX)
+        pass_ms[nm] = t3.item()
+    # e2e: local inputs from pinned host memory, outputs and gradients back, per step
+    host_qkv = torch.empty(qkv.shape, dtype=qkv.dtype, pin_memory=True)
+    host_qkv.copy_(qkv.detach())
+    host_dy = torch.empty(dy.shape, dtype=dy.dtype, pin_memory=True)
+    host_dy.copy_(dy)
+    outs = None
+    e2e = []
+    for i in range(2):
+        a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.distributed.barrier()
+        a.record()
+        x = host_qkv.to(device, non_blocking=True).requires_grad_(True)
+        g_ = host_dy.to(device, non_blocking=True)
+        filt.grad = None
+        q, k, v = x.chunk(3, dim=-1)
+        y = cp.hyena_context_parallel(mod, q, k, v, filt, group)
+        y.backward(g_)
+        res = [y]  # the step's result; gradients stay on the device for the optimizer
+        if outs is None:
+            outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
+        for o, r in zip(outs, res):
+            o.copy_(r, non_blocking=True)
+        b_.record()
+        torch.cuda.synchronize()
+        e2e.append(a.elapsed_time(b_))
+        del x, g_, y, res, q, k, v
+    te = torch.tensor([min(e2e)], device=device)
+    torch.distributed.all_reduce(te, op=torch.distributed.ReduceOp.MAX)
+    h2d = host_qkv.numel() * host_qkv.element_size() + host_dy.numel() * host_dy.element_size()
+    d2h = sum(o.numel() * o.element_size() for o in outs)
+    return dict(pass_ms=pass_ms, total_ms=total_ms, launches=launches, clocks=clk.summary(), B=B, C=d,
+                e2e_ms=te.item(), h2d=h2d, d2h=d2h)
+
+
 # ----------------------------------------------------------------- GPU arm
 def run_gpu(args, cfg, rank, world, device):
     from nvsubquadratic_b200 import _lib
@@ -461,6 +573,13 @@ def main():
     dtname = {torch.float32: "f32", torch.bfloat16: "bf16"}[cfg["dtype"]]
     config = {"workload": args.config + ": " + cfg["desc"], "batch": B, "channels": C, "spatial": list(cfg["S"]),
               "filter": list(cfg["K"]), "sharding": cfg["shard"], "l2": "flushed between timed steps (256 MB write)"}
+    if cfg["shard"] == "cp":
+        config["l2"] = "inputs (GBs per rank) far larger than L2; no flush"
+        config["parallelism"] = f"cp{world}"
+        # keep the engine's spectrum workspace small next to the 1M-long activations
+        os.environ.setdefault("HYFFT_WS_BUDGET_MB", "4096")
+        # GB-sized activations of varying shapes: avoid caching-allocator fragmentation
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
 
     if args.impl == "reference":
         if rank != 0:
@@ -482,7 +601,13 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    res = run_gpu(args, cfg, rank, world, device)
+    if cfg["shard"] == "cp":
+        if world < 2:
+            raise SystemExit("cfg4 (context parallel, 12.9 GB of q/k/v per copy) runs on 2 or more GPUs "
+                             "(python -m torch.distributed.run ... bench.py --config cfg4 --gpus N)")
+        res = run_cp(args, cfg, rank, world, device)
+    else:
+        res = run_gpu(args, cfg, rank, world, device)
     if res is None:  # --profile
         if world > 1:
             torch.distributed.destroy_process_group()

@@ -211,7 +211,8 @@ def hyena_context_parallel(module, query, key, value, filt, group, zigzag: bool 
     qkv = torch.stack([query, key, value], dim=-2)                     # [B, l, *rest, 3, C]
     loc = SeqToChan.apply(qkv, group, zigzag)                          # [B, L, *rest, 3, d]
     q, k, v = loc.unbind(dim=-2)                                       # channel-last views, pos stride 3d
-    filt_r = _channel_block(filt, 1, r, d)
+    # the full filter [1, C, *K], or this rank's channel block [1, C/P, *K] already
+    filt_r = filt if filt.shape[1] == d and d != C else _channel_block(filt, 1, r, d)
     D_r = _channel_block(module.shortcut, 0, r, d).to(query.dtype)
     sw_r = _channel_block(module.short_weight, 0, r, d, groups=3, C=C)
     sb_r = _channel_block(module.short_bias, 0, r, d, groups=3, C=C)

@@ -114,23 +114,31 @@ __device__ __forceinline__ void cp_row(const CpDesc& c, long long row, long long
   }
 }
 
-// One warp per row; 16-byte vectors when the run and both offsets allow it.
+// Rows are cut into segments of kCpSeg elements (a multiple of 16 bytes) and one warp
+// copies one segment at a time, so a few very long rows (whole zigzag chunks) spread over
+// the grid as well as many short ones; 16-byte vectors when the run and both offsets
+// allow it.
+constexpr long long kCpSeg = 4096;
+
 template <typename E>
 __global__ void cp_copy_kernel(const E* __restrict__ src, E* __restrict__ dst, CpDesc c, int vec_ok) {
   const int lane = threadIdx.x & 31;
   const long long warp = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
   const long long nwarps = ((long long)gridDim.x * blockDim.x) >> 5;
-  for (long long row = warp; row < c.rows; row += nwarps) {
+  const long long nseg = (c.run + kCpSeg - 1) / kCpSeg;
+  for (long long w = warp; w < c.rows * nseg; w += nwarps) {
+    const long long row = w / nseg, sg = w - row * nseg;
     long long so, dof;
     cp_row(c, row, so, dof);
+    const long long e0 = sg * kCpSeg, e1 = min(c.run, e0 + kCpSeg);
     if (vec_ok) {
       constexpr int V = 16 / sizeof(E);
-      const uint4* s4 = reinterpret_cast<const uint4*>(src + so);
-      uint4* d4 = reinterpret_cast<uint4*>(dst + dof);
-      const long long nv = c.run / V;
+      const uint4* s4 = reinterpret_cast<const uint4*>(src + so + e0);
+      uint4* d4 = reinterpret_cast<uint4*>(dst + dof + e0);
+      const long long nv = (e1 - e0) / V;
       for (long long i = lane; i < nv; i += 32) d4[i] = s4[i];
     } else {
-      for (long long i = lane; i < c.run; i += 32) dst[dof + i] = src[so + i];
+      for (long long i = e0 + lane; i < e1; i += 32) dst[dof + i] = src[so + i];
     }
   }
 }
@@ -147,7 +155,8 @@ static int cp_launch(CpDesc c, const void* src, void* dst, int eb, cudaStream_t 
     vec_ok = aligned && ((c.run * eb) % 16 == 0) && ((unit * eb) % 16 == 0) && ((c.l * c.rest * eb) % 16 == 0) &&
              ((c.L * c.rest * eb) % 16 == 0);
   }
-  long long blocks = (c.rows * 32 + 255) / 256;
+  const long long items = c.rows * ((c.run + kCpSeg - 1) / kCpSeg);
+  long long blocks = (items * 32 + 255) / 256;
   if (blocks > 148LL * 32) blocks = 148LL * 32;
   if (blocks < 1) blocks = 1;
   if (eb == 2)

@@ -942,10 +942,9 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
   size_t cf, cb;
   conv_ws_sizes(h.cp, cf, cb);
   const size_t act = align_up((size_t)h.E * h.eb);
-  const size_t f32 = align_up((size_t)h.E * 4);
   saved = 5 * act;                 // q', k', v', z, h
   fwd = cf + align_up((size_t)h.d.channels * 4);
-  bwd = cb + 2 * act + 3 * f32 + align_up((size_t)h.d.channels * 4);
+  bwd = cb + 5 * act + align_up((size_t)h.d.channels * 4);  // dh, dz, dv', dq', dk'
   if (h.cp.big2d) {  // channel-major copies around the large-grid kernels: z, h | z, dh, dz
     fwd += 2 * act;
     bwd += 3 * act;
@@ -1058,8 +1057,7 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
                             float* dD, float* dsw, float* dsb, const char* saved, char* ws, cudaStream_t st) {
   const hyfft_hyena_desc& d = h.d;
   const size_t act = align_up((size_t)h.E * h.eb);
-  const size_t f32 = align_up((size_t)h.E * 4);
-  const T* qs = (const T*)(saved);
+    const T* qs = (const T*)(saved);
   const T* ks = (const T*)(saved + act);
   const T* vs = (const T*)(saved + 2 * act);
   const T* z = (const T*)(saved + 3 * act);
@@ -1072,11 +1070,11 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
   w += act;
   T* dz = (T*)w;
   w += act;
-  float* dvp = (float*)w;
-  w += f32;
-  float* dqp = (float*)w;
-  w += f32;
-  float* dkp = (float*)w;
+  T* dvp = (T*)w;
+  w += act;
+  T* dqp = (T*)w;
+  w += act;
+  T* dkp = (T*)w;
   const long long rows = (long long)d.batch * h.Ntot;
   const bool pair = elem_pairs_ok(h, {q, k, v, dy, dq, dk, dv});
   const dim3 eg = elem_grid(d.channels, rows, 8);
@@ -1105,7 +1103,7 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     const RealView dzv = real_view(dz, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
     const RealView dkv = real_view(dfilt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
     if (p.big2d) {  // channel-major z, dh, dz around the large-grid kernels
-      T* zc = (T*)(ws + cb + 2 * act + 3 * f32 + align_up((size_t)d.channels * 4));
+      T* zc = (T*)(ws + cb + 5 * act + align_up((size_t)d.channels * 4));
       T* dhc = (T*)((char*)zc + act);
       T* dzc = (T*)((char*)dhc + act);
       HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));

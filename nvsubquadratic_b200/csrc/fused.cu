@@ -228,8 +228,9 @@ struct FwdSmem {
   template <int F1>
   static constexpr size_t W() { return al16(sizeof(float2) * kCG * PG * N0 * (F1 + 1)); }
   static constexpr size_t small = al16(sizeof(float) * (3 * kCG * NT + 3 * kCG + kCG));
+  static constexpr size_t zbuf = al16(sizeof(T) * NIMG * NP * kCG);  // z = q' * g1(k'), reused by the epilogue
   template <int F1>
-  static constexpr size_t total() { return stage + W<F1>() + small; }
+  static constexpr size_t total() { return stage + W<F1>() + small + zbuf; }
 };
 
 template <typename T, int N0, int N1, int F0, int F1, int SK, int PG>
@@ -242,6 +243,7 @@ __global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p)
   float* wts = reinterpret_cast<float*>(smem + L::stage + L::template W<F1>());  // [3][8][NT]
   float* bsm = wts + 3 * kCG * NT;                                               // [3][8]
   float* Dsm = bsm + 3 * kCG;                                                    // [8]
+  T* zs = reinterpret_cast<T*>(smem + L::stage + L::template W<F1>() + L::small);  // [NIMG][NP][8]
   const int tid = threadIdx.x;
   const int c0 = blockIdx.x * kCG;
   const int p0 = blockIdx.y * PG;
@@ -284,6 +286,7 @@ __global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p)
       round8<T>(kv);
 #pragma unroll
       for (int c = 0; c < 8; ++c) z[h][c] = DT<T>::round(qv[c] * DT<T>::round(gate_f(p.gate1, kv[c])));
+      V8<T>::store(zs + (s * NP + pos) * kCG, z[h]);
     }
 #pragma unroll
     for (int c = 0; c < 8; ++c) W[((c * PG + ps) * N0 + n0) * LD + n1] = make_float2(z[0][c], z[1][c]);
@@ -340,20 +343,16 @@ __global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p)
     const int pp = p0 + ps;
     const int b = h == 0 ? pp : pp + p.half;
     if (pp >= p.half || b >= p.B) continue;
-    float qv[8], kv[8], vv[8], out[8];
-    stencil8<T, N0, N1, SK>(stage + (0 * NIMG + s) * NP * kCG, wts, has_bias ? bsm : nullptr, n0, n1, qv);
-    stencil8<T, N0, N1, SK>(stage + (1 * NIMG + s) * NP * kCG, wts + kCG * NT, has_bias ? bsm + kCG : nullptr, n0,
-                            n1, kv);
+    float zv[8], vv[8], out[8];
+    V8<T>::load(zs + (s * NP + pos) * kCG, zv);
     stencil8<T, N0, N1, SK>(stage + (2 * NIMG + s) * NP * kCG, wts + 2 * kCG * NT, has_bias ? bsm + 2 * kCG : nullptr,
                             n0, n1, vv);
-    round8<T>(qv);
-    round8<T>(kv);
     round8<T>(vv);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const float2 cv = W[((c * PG + ps) * N0 + n0) * LD + n1];
       const float conv = h == 0 ? cv.x : cv.y;
-      const float z = DT<T>::round(qv[c] * DT<T>::round(gate_f(p.gate1, kv[c])));
+      const float z = zv[c];
       const float hv = DT<T>::round(DT<T>::round(conv) + DT<T>::round(Dsm[c] * z));
       out[c] = hv * DT<T>::round(gate_f(p.gate2, vv[c]));
     }
@@ -369,9 +368,10 @@ struct BwdSmem {
   template <int F1>
   static constexpr size_t W() { return al16(sizeof(float2) * kCG * N0 * (F1 + 1)); }
   static constexpr size_t dgrad = al16(sizeof(T) * 3 * NIMG * NP * kCG);  // dq', dk', dv'
+  static constexpr size_t qkv = al16(sizeof(T) * 3 * NIMG * NP * kCG);    // q', k', v' (short conv outputs)
   static constexpr size_t small = al16(sizeof(float) * (3 * kCG * NT + 3 * kCG + kCG + kCG));
   template <int F1>
-  static constexpr size_t total() { return stage + 2 * W<F1>() + dgrad + small; }
+  static constexpr size_t total() { return stage + 2 * W<F1>() + dgrad + qkv + small; }
 };
 
 template <typename T, int N0, int N1, int F0, int F1, int SK>
@@ -383,7 +383,8 @@ __global__ void __launch_bounds__(256) hyena2d_bwd_kernel(const Fused2DParams p)
   float2* W1 = reinterpret_cast<float2*>(smem + L::stage);                         // z -> h
   float2* W2 = reinterpret_cast<float2*>(smem + L::stage + L::template W<F1>());   // dh -> dz
   T* dgr = reinterpret_cast<T*>(smem + L::stage + 2 * L::template W<F1>());        // [3][2][NP][8]
-  float* wts = reinterpret_cast<float*>(smem + L::stage + 2 * L::template W<F1>() + L::dgrad);
+  T* qkv = reinterpret_cast<T*>(smem + L::stage + 2 * L::template W<F1>() + L::dgrad);  // [3][2][NP][8]
+  float* wts = reinterpret_cast<float*>(smem + L::stage + 2 * L::template W<F1>() + L::dgrad + L::qkv);
   float* bsm = wts + 3 * kCG * NT;
   float* Dsm = bsm + 3 * kCG;
   float* dDsm = Dsm + kCG;
@@ -434,6 +435,9 @@ __global__ void __launch_bounds__(256) hyena2d_bwd_kernel(const Fused2DParams p)
       round8<T>(qv);
       round8<T>(kv);
       round8<T>(vv);
+      V8<T>::store(qkv + ((0 * NIMG + s) * NP + pos) * kCG, qv);
+      V8<T>::store(qkv + ((1 * NIMG + s) * NP + pos) * kCG, kv);
+      V8<T>::store(qkv + ((2 * NIMG + s) * NP + pos) * kCG, vv);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         z[s][c] = DT<T>::round(qv[c] * DT<T>::round(gate_f(p.gate1, kv[c])));
@@ -512,15 +516,10 @@ __global__ void __launch_bounds__(256) hyena2d_bwd_kernel(const Fused2DParams p)
   for (int i = tid; i < NIMG * NP; i += blockDim.x) {
     const int s = i / NP, pos = i % NP, n0 = pos / N1, n1 = pos % N1;
     float qv[8], kv[8], vv[8], g[8], oq[8], ok[8], ov[8];
-    stencil8<T, N0, N1, SK>(stage + (0 * NIMG + s) * NP * kCG, wts, has_bias ? bsm : nullptr, n0, n1, qv);
-    stencil8<T, N0, N1, SK>(stage + (1 * NIMG + s) * NP * kCG, wts + kCG * NT, has_bias ? bsm + kCG : nullptr, n0,
-                            n1, kv);
-    stencil8<T, N0, N1, SK>(stage + (2 * NIMG + s) * NP * kCG, wts + 2 * kCG * NT, has_bias ? bsm + 2 * kCG : nullptr,
-                            n0, n1, vv);
+    V8<T>::load(qkv + ((0 * NIMG + s) * NP + pos) * kCG, qv);
+    V8<T>::load(qkv + ((1 * NIMG + s) * NP + pos) * kCG, kv);
+    V8<T>::load(qkv + ((2 * NIMG + s) * NP + pos) * kCG, vv);
     V8<T>::load(stage + ((3 * NIMG + s) * NP + pos) * kCG, g);
-    round8<T>(qv);
-    round8<T>(kv);
-    round8<T>(vv);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const float2 ch = W1[(c * N0 + n0) * LD + n1];

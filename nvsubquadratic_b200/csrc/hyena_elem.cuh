@@ -266,11 +266,12 @@ __global__ void __launch_bounds__(kElemThreads) hyena_post_fwd_kernel(
   }
 }
 
-// Backward through gate 2: dh = dy * g2(v') (dtype), dv' = dy * h * g2'(v') (fp32).
+// Backward through gate 2: dh = dy * g2(v'), dv' = dy * h * g2'(v') (activation dtype, as
+// autograd produces them).
 template <typename T, bool PAIR>
 __global__ void __launch_bounds__(kElemThreads) hyena_bwd_gate2_kernel(
     const T* __restrict__ dy, long long out_bst, long long out_pst, const T* __restrict__ h,
-    const T* __restrict__ vs, int gate2, long long Ntot, int B, int C, T* __restrict__ dh, float* __restrict__ dvp) {
+    const T* __restrict__ vs, int gate2, long long Ntot, int B, int C, T* __restrict__ dh, T* __restrict__ dvp) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = blockIdx.x * kElemCG + 2 * lane;
   const bool two = c + 1 < C;
@@ -285,16 +286,16 @@ __global__ void __launch_bounds__(kElemThreads) hyena_bwd_gate2_kernel(
     const float2 vv = ld2<T, PAIR>(vs + i, two), hv = ld2<T, PAIR>(h + i, two);
     const float2 g2 = V2<T>::round(make_float2(gate_f(gate2, vv.x), gate_f(gate2, vv.y)));
     st2<T, PAIR>(dh + i, make_float2(gd.x * g2.x, gd.y * g2.y), two);
-    st2f<PAIR>(dvp + i, make_float2(gd.x * hv.x * gate_df(gate2, vv.x), gd.y * hv.y * gate_df(gate2, vv.y)), two);
+    st2<T, PAIR>(dvp + i, make_float2(gd.x * hv.x * gate_df(gate2, vv.x), gd.y * hv.y * gate_df(gate2, vv.y)), two);
   }
 }
 
-// Backward through gate 1: dq' = dz * g1(k'), dk' = dz * q' * g1'(k') (fp32); all
-// contiguous [B, N, C], same (row, channel-pair) split as the other kernels.
+// Backward through gate 1: dq' = dz * g1(k'), dk' = dz * q' * g1'(k') (activation dtype);
+// all contiguous [B, N, C], same (row, channel-pair) split as the other kernels.
 template <typename T, bool PAIR>
 __global__ void __launch_bounds__(kElemThreads) hyena_bwd_gate1_kernel(
     const T* __restrict__ dz, const T* __restrict__ qs, const T* __restrict__ ks, int gate1, long long rows, int C,
-    float* __restrict__ dqp, float* __restrict__ dkp) {
+    T* __restrict__ dqp, T* __restrict__ dkp) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int c = blockIdx.x * kElemCG + 2 * lane;
   const bool two = c + 1 < C;
@@ -304,17 +305,17 @@ __global__ void __launch_bounds__(kElemThreads) hyena_bwd_gate1_kernel(
     const long long i = r * C + c;
     const float2 gd = ld2<T, PAIR>(dz + i, two), kv = ld2<T, PAIR>(ks + i, two), qv = ld2<T, PAIR>(qs + i, two);
     const float2 g1 = V2<T>::round(make_float2(gate_f(gate1, kv.x), gate_f(gate1, kv.y)));
-    st2f<PAIR>(dqp + i, make_float2(gd.x * g1.x, gd.y * g1.y), two);
-    st2f<PAIR>(dkp + i, make_float2(gd.x * qv.x * gate_df(gate1, kv.x), gd.y * qv.y * gate_df(gate1, kv.y)), two);
+    st2<T, PAIR>(dqp + i, make_float2(gd.x * g1.x, gd.y * g1.y), two);
+    st2<T, PAIR>(dkp + i, make_float2(gd.x * qv.x * gate_df(gate1, kv.x), gd.y * qv.y * gate_df(gate1, kv.y)), two);
   }
 }
 
 // Backward of the depthwise short conv w.r.t. its input (transposed stencil):
 //   din[pos] = sum_tap w[ch, tap] * dout[pos - tap + off]
-// dout: fp32 contiguous [B, N, C] for each of q/k/v (three pointers); din strided.
+// dout: contiguous [B, N, C] for each of q/k/v (three pointers); din strided.
 template <typename T, bool PAIR, int K0, int K1, int K2>
 __global__ void __launch_bounds__(kElemThreads) hyena_short_dgrad_kernel(
-    const float* __restrict__ dqp, const float* __restrict__ dkp, const float* __restrict__ dvp, StencilGeom g, int B,
+    const T* __restrict__ dqp, const T* __restrict__ dkp, const T* __restrict__ dvp, StencilGeom g, int B,
     int C, const float* __restrict__ w, T* __restrict__ dq, T* __restrict__ dk, T* __restrict__ dv, long long out_bst,
     long long out_pst) {
   __shared__ float sw[3 * kMaxTaps * kElemCG];
@@ -337,14 +338,14 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_dgrad_kernel(
     float2 a[3] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     if constexpr (K0 == 0) {
       const long long i = r * C + c;
-      a[0] = ld2f<PAIR>(dqp + i, two);
-      a[1] = ld2f<PAIR>(dkp + i, two);
-      a[2] = ld2f<PAIR>(dvp + i, two);
+      a[0] = ld2<T, PAIR>(dqp + i, two);
+      a[1] = ld2<T, PAIR>(dkp + i, two);
+      a[2] = ld2<T, PAIR>(dvp + i, two);
     } else {
       const long long bb = (long long)rp.b * Ntot * C + c;
       for_taps<K0, K1, K2, -1>(g, rp, [&](int tap, long long pl) {
         const long long j = bb + pl * C;
-        const float2 xq = ld2f<PAIR>(dqp + j, two), xk = ld2f<PAIR>(dkp + j, two), xv = ld2f<PAIR>(dvp + j, two);
+        const float2 xq = ld2<T, PAIR>(dqp + j, two), xk = ld2<T, PAIR>(dkp + j, two), xv = ld2<T, PAIR>(dvp + j, two);
         const float2 wq = *reinterpret_cast<const float2*>(&sw[(0 * g.ntaps + tap) * kElemCG + 2 * lane]);
         const float2 wk = *reinterpret_cast<const float2*>(&sw[(1 * g.ntaps + tap) * kElemCG + 2 * lane]);
         const float2 wv = *reinterpret_cast<const float2*>(&sw[(2 * g.ntaps + tap) * kElemCG + 2 * lane]);
@@ -367,7 +368,7 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_dgrad_kernel(
 // The runtime-shaped fallback accumulates straight into shared memory instead.
 template <typename T, bool PAIR, int K0, int K1, int K2>
 __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_kernel(
-    const float* __restrict__ dqp, const float* __restrict__ dkp, const float* __restrict__ dvp,
+    const T* __restrict__ dqp, const T* __restrict__ dkp, const T* __restrict__ dvp,
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, long long in_bst, long long in_pst,
     StencilGeom g, int B, int C, float* __restrict__ dw, float* __restrict__ db) {
   constexpr bool CT = K0 > 0 && K1 > 0 && K2 > 0;
@@ -380,7 +381,7 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_kernel(
   const int c = blockIdx.x * kElemCG + 2 * lane;
   const bool ok = c < C;
   const bool two = c + 1 < C;
-  const float* dout = t == 0 ? dqp : (t == 1 ? dkp : dvp);
+  const T* dout = t == 0 ? dqp : (t == 1 ? dkp : dvp);
   const T* in = t == 0 ? q : (t == 1 ? k : v);
   const long long Ntot = (long long)g.n[0] * g.n[1] * g.n[2];
   const long long rows = (long long)B * Ntot;
@@ -398,7 +399,7 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_kernel(
     const long long r0 = (long long)blockIdx.z * per, r1 = min(rows, r0 + per);
     for (long long r = r0 + warp; r < r1; r += NW) {
       const RowPos rp = row_pos(r, g, Ntot);
-      const float2 go = ld2f<PAIR>(dout + r * C + c, two);
+      const float2 go = ld2<T, PAIR>(dout + r * C + c, two);
       bacc.x += go.x;
       bacc.y += go.y;
       const long long bb = (long long)rp.b * in_bst + c;
