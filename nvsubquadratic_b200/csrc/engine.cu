@@ -1011,10 +1011,23 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
   auto pre = [&](auto pr) {
     constexpr bool P = decltype(pr)::value;
     with_stencil<P>(h.sg, [&](auto a, auto b, auto c) {
-      hyena_pre_fwd_kernel<T, P, decltype(a)::value, decltype(b)::value, decltype(c)::value>
-          <<<elem_grid(d.channels, rows, 4), kElemThreads, 0, st>>>(q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg,
-                                                                   d.batch, d.channels, sw, sb, d.gate1, qs, ks, vs,
-                                                                   z);
+      constexpr int K0 = decltype(a)::value, K1 = decltype(b)::value, K2 = decltype(c)::value;
+      if constexpr (K0 > 0 && K1 > 0 && K2 > 0) {
+        constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
+        constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
+        if (d.ndim == ND) {
+          const long long nl = h.sg.n[ND - 1];
+          const long long items = (long long)d.batch * (h.Ntot / nl) * ((nl + 63) / 64);
+          const dim3 lg((unsigned)((d.channels + kElemCG - 1) / kElemCG),
+                        (unsigned)std::max<long long>(1, std::min<long long>(65535, (items + 7) / 8)), 1);
+          hyena_line_stencil_kernel<T, P, ND, KA, KB, KI, 0><<<lg, kElemThreads, 0, st>>>(
+              q, k, v, d.in_batch_stride, d.in_pos_stride, qs, ks, vs, 0, 0, z, h.sg, d.batch, d.channels, sw, sb,
+              d.gate1);
+          return;
+        }
+      }
+      hyena_pre_fwd_kernel<T, P, K0, K1, K2><<<elem_grid(d.channels, rows, 4), kElemThreads, 0, st>>>(
+          q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch, d.channels, sw, sb, d.gate1, qs, ks, vs, z);
     });
   };
   if (pair) pre(std::true_type{});
@@ -1133,9 +1146,23 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
   auto dgrad = [&](auto pr) {
     constexpr bool P = decltype(pr)::value;
     with_stencil<P>(h.sg, [&](auto a, auto b, auto c) {
-      hyena_short_dgrad_kernel<T, P, decltype(a)::value, decltype(b)::value, decltype(c)::value>
-          <<<elem_grid(d.channels, rows, 4), kElemThreads, 0, st>>>(dqp, dkp, dvp, h.sg, d.batch, d.channels, sw, dq,
-                                                                   dk, dv, d.out_batch_stride, d.out_pos_stride);
+      constexpr int K0 = decltype(a)::value, K1 = decltype(b)::value, K2 = decltype(c)::value;
+      if constexpr (K0 > 0 && K1 > 0 && K2 > 0) {
+        constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
+        constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
+        if (d.ndim == ND) {
+          const long long nl = h.sg.n[ND - 1];
+          const long long items = (long long)d.batch * (h.Ntot / nl) * ((nl + 63) / 64);
+          const dim3 lg((unsigned)((d.channels + kElemCG - 1) / kElemCG),
+                        (unsigned)std::max<long long>(1, std::min<long long>(65535, (items + 7) / 8)), 1);
+          hyena_line_stencil_kernel<T, P, ND, KA, KB, KI, 1><<<lg, kElemThreads, 0, st>>>(
+              dqp, dkp, dvp, 0, 0, dq, dk, dv, d.out_batch_stride, d.out_pos_stride, nullptr, h.sg, d.batch,
+              d.channels, sw, nullptr, 0);
+          return;
+        }
+      }
+      hyena_short_dgrad_kernel<T, P, K0, K1, K2><<<elem_grid(d.channels, rows, 4), kElemThreads, 0, st>>>(
+          dqp, dkp, dvp, h.sg, d.batch, d.channels, sw, dq, dk, dv, d.out_batch_stride, d.out_pos_stride);
     });
   };
   if (pair) dgrad(std::true_type{});
@@ -1147,13 +1174,30 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     if (dsb && h.sg.has_bias && cudaMemsetAsync(dsb, 0, sizeof(float) * 3 * (size_t)d.channels, st) != cudaSuccess)
       return fail(HYFFT_ERR_CUDA, "memset dshort_b");
     const unsigned gx = (unsigned)((d.channels + kElemCG - 1) / kElemCG);
-    const dim3 wg(gx, 3, (unsigned)red_rows(3 * (int)gx));
+    // about 16 rows per warp (at least ~4 waves of CTAs); one atomic per channel and tap per CTA
+    const long long wz = std::max<long long>(1, std::min<long long>(65535, rows / (8 * 16)));
+    const dim3 wg(gx, 3, (unsigned)std::max<long long>(std::min<long long>(wz, std::max<long long>(1, 24000 / (3 * gx))),
+                                                       (long long)red_rows(3 * (int)gx)));
     auto wgrad = [&](auto pr) {
       constexpr bool P = decltype(pr)::value;
       with_stencil<P>(h.sg, [&](auto a, auto b, auto c) {
-        hyena_short_wgrad_kernel<T, P, decltype(a)::value, decltype(b)::value, decltype(c)::value>
-            <<<wg, kElemThreads, 0, st>>>(dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch,
-                                          d.channels, dsw, dsb);
+        constexpr int K0 = decltype(a)::value, K1 = decltype(b)::value, K2 = decltype(c)::value;
+        if constexpr (K0 > 0 && K1 > 0 && K2 > 0) {
+          // sliding-window form: 1D (k,1,1), 2D (k0,k1,1), 3D (k0,k1,k2) along the innermost axis
+          constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
+          constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
+          if (d.ndim == ND) {
+            const long long nl = h.sg.n[ND - 1];
+            const long long items = (long long)d.batch * (h.Ntot / nl) * ((nl + 63) / 64);
+            const long long gz = std::max<long long>(1, std::min<long long>(65535, std::min<long long>(
+                                                             (items + 7) / 8, 4800 / (3 * (long long)gx))));
+            hyena_short_wgrad_line_kernel<T, P, ND, KA, KB, KI><<<dim3(gx, 3, (unsigned)gz), kElemThreads, 0, st>>>(
+                dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch, d.channels, dsw, dsb);
+            return;
+          }
+        }
+        hyena_short_wgrad_kernel<T, P, K0, K1, K2><<<wg, kElemThreads, 0, st>>>(
+            dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch, d.channels, dsw, dsb);
       });
     };
     if (pair) wgrad(std::true_type{});

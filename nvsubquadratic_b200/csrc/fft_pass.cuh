@@ -287,8 +287,9 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
     float2 val = cscale(sm[l * ld + padi(t)], d.scale);
     if (d.tw_logF > 0 && L.tw_m != 0) {
       // e^{dir*2*pi*i*t*m/2^tw_logF}; reduce the exponent mod 2^tw_logF first
+      // ex < 2^tw_logF <= 2^24 is exact in float, and so is the power-of-two scaling
       const long long ex = ((long long)t * L.tw_m) & ((1LL << d.tw_logF) - 1);
-      val = cmul(val, expipi(d.dir * 2.0f * (float)((double)ex / (double)(1LL << d.tw_logF))));
+      val = cmul(val, expipi(d.dir * ldexpf((float)ex, 1 - d.tw_logF)));
     }
     if (OUT_MODE == OUT_CPLX) {
       const int bo = t - d.out_lo;

@@ -397,6 +397,7 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_kernel(
     // a contiguous run of rows per CTA, so stencil neighbours are mostly L1 hits
     const long long per = (rows + gridDim.z - 1) / gridDim.z;
     const long long r0 = (long long)blockIdx.z * per, r1 = min(rows, r0 + per);
+#pragma unroll 4
     for (long long r = r0 + warp; r < r1; r += NW) {
       const RowPos rp = row_pos(r, g, Ntot);
       const float2 go = ld2<T, PAIR>(dout + r * C + c, two);
@@ -443,6 +444,259 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_kernel(
       }
     }
     __syncthreads();
+  }
+}
+
+// Line geometry of the sliding-window stencil kernels: a "line" is one run of positions
+// along the innermost spatial axis (axis ND-1) at fixed batch item and outer coordinates;
+// KA x KB outer stencil rows (axes 0 and 1 of a 3D stencil, axis 0 of a 2D one, none in
+// 1D) and KI taps along the line.
+template <int ND>
+__device__ __forceinline__ int line_len(const StencilGeom& g) { return g.n[ND - 1]; }
+template <int ND>
+__device__ __forceinline__ long long lines_per_item(const StencilGeom& g) {
+  return ND == 3 ? (long long)g.n[0] * g.n[1] : (ND == 2 ? (long long)g.n[0] : 1LL);
+}
+
+// Short-conv weight / bias gradient, sliding-window form for the compile-time stencils:
+// a warp walks SEG consecutive positions of one line for its 64 channels, keeping the
+// KA*KB x KI input window in registers (one new column of KA*KB loads per position
+// instead of all taps). grid (ceil(C/64), 3 tensors, item blocks). Same result layout
+// and reduction as hyena_short_wgrad_kernel.
+template <typename T, bool PAIR, int ND, int KA, int KB, int KI>
+__global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_line_kernel(
+    const T* __restrict__ dqp, const T* __restrict__ dkp, const T* __restrict__ dvp, const T* __restrict__ q,
+    const T* __restrict__ k, const T* __restrict__ v, long long in_bst, long long in_pst, StencilGeom g, int B, int C,
+    float* __restrict__ dw, float* __restrict__ db) {
+  constexpr int NA = KA * KB, NT = NA * KI, NW = kElemThreads / 32, SEG = 64;
+  __shared__ float red[NW][kElemCG + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int t = blockIdx.y;
+  const int c = blockIdx.x * kElemCG + 2 * lane;
+  const bool ok = c < C, two = c + 1 < C;
+  const T* dout = t == 0 ? dqp : (t == 1 ? dkp : dvp);
+  const T* in = t == 0 ? q : (t == 1 ? k : v);
+  const int nl = line_len<ND>(g);
+  const int offI = g.off[ND - 1];
+  const long long Ntot = (long long)g.n[0] * g.n[1] * g.n[2];
+  const int nseg = (nl + SEG - 1) / SEG;
+  const long long lpi = lines_per_item<ND>(g);
+  const long long items = (long long)B * lpi * nseg;
+  float2 acc[NT];
+#pragma unroll
+  for (int i = 0; i < NT; ++i) acc[i] = make_float2(0.f, 0.f);
+  float2 bacc = make_float2(0.f, 0.f);
+  if (ok) {
+    for (long long it = (long long)blockIdx.z * NW + warp; it < items; it += (long long)gridDim.z * NW) {
+      const long long li = it / nseg;
+      const int sg = (int)(it - li * nseg);
+      const int b = (int)(li / lpi);
+      const long long lo = li - (long long)b * lpi;  // outer line index
+      int o0 = 0, o1 = 0;
+      if (ND == 3) { o0 = (int)(lo / g.n[1]); o1 = (int)(lo - (long long)o0 * g.n[1]); }
+      if (ND == 2) o0 = (int)lo;
+      const int pa = sg * SEG, pb = min(nl, pa + SEG);
+      long long rb[NA];
+      bool rok[NA];
+#pragma unroll
+      for (int a = 0; a < KA; ++a) {
+#pragma unroll
+        for (int bq = 0; bq < KB; ++bq) {
+          const int j = a * KB + bq;
+          long long rowpos;  // flat position of (outer neighbour, 0)
+          bool okr = true;
+          if (ND == 3) {
+            const int i0 = o0 + a - g.off[0], i1 = o1 + bq - g.off[1];
+            okr = i0 >= 0 && i0 < g.n[0] && i1 >= 0 && i1 < g.n[1];
+            rowpos = ((long long)i0 * g.n[1] + i1) * g.n[2];
+          } else if (ND == 2) {
+            const int i0 = o0 + a - g.off[0];
+            okr = i0 >= 0 && i0 < g.n[0];
+            rowpos = (long long)i0 * g.n[1];
+          } else {
+            rowpos = 0;
+          }
+          rok[j] = okr;
+          rb[j] = (long long)b * in_bst + c + rowpos * in_pst;
+        }
+      }
+      const long long lb = (long long)b * Ntot + (ND == 3 ? ((long long)o0 * g.n[1] + o1) * g.n[2]
+                                                          : (ND == 2 ? (long long)o0 * g.n[1] : 0LL));
+      float2 w[NA][KI];
+      auto ldin = [&](int j, int pi) -> float2 {
+        if (!rok[j] || pi < 0 || pi >= nl) return make_float2(0.f, 0.f);
+        return ld2<T, PAIR>(in + rb[j] + (long long)pi * in_pst, two);
+      };
+#pragma unroll
+      for (int j = 0; j < NA; ++j) {
+#pragma unroll
+        for (int e = 1; e < KI; ++e) w[j][e] = ldin(j, pa - 1 + e - offI);
+      }
+      for (int p = pa; p < pb; ++p) {
+#pragma unroll
+        for (int j = 0; j < NA; ++j) {
+#pragma unroll
+          for (int e = 0; e + 1 < KI; ++e) w[j][e] = w[j][e + 1];
+          w[j][KI - 1] = ldin(j, p + KI - 1 - offI);
+        }
+        const float2 go = ld2<T, PAIR>(dout + (lb + p) * C + c, two);
+        bacc.x += go.x;
+        bacc.y += go.y;
+#pragma unroll
+        for (int j = 0; j < NA; ++j) {
+#pragma unroll
+          for (int e = 0; e < KI; ++e) {
+            acc[j * KI + e].x = fmaf(go.x, w[j][e].x, acc[j * KI + e].x);
+            acc[j * KI + e].y = fmaf(go.y, w[j][e].y, acc[j * KI + e].y);
+          }
+        }
+      }
+    }
+  }
+  for (int tap = 0; tap <= NT; ++tap) {
+    float2 val = bacc;
+#pragma unroll
+    for (int u = 0; u < NT; ++u)
+      if (u == tap) val = acc[u];
+    red[warp][2 * lane] = val.x;
+    red[warp][2 * lane + 1] = val.y;
+    __syncthreads();
+    if (threadIdx.x < kElemCG) {
+      const int cc = blockIdx.x * kElemCG + threadIdx.x;
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < NW; ++j) sum += red[j][threadIdx.x];
+      if (cc < C) {
+        const long long ch = (long long)t * C + cc;
+        if (tap < NT) atomicAdd(dw + ch * NT + tap, sum);
+        else if (g.has_bias) atomicAdd(db + ch, sum);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Short conv forward (MODE 0: q', k', v' and z = q' * g1(k')) and input gradient
+// (MODE 1: the transposed stencil of dq', dk', dv'), sliding-window form for the
+// compile-time stencils. A warp takes SEG positions of one line for its 64 channels and
+// sweeps q, k, v one after the other with a KA*KB x KI register window of the input
+// (one new column per position); the CTA's weights sit in shared memory.
+// MODE 0: in = q/k/v (strided), out = qs/ks/vs (+ z) contiguous [B, N, C].
+// MODE 1: in = dq'/dk'/dv' contiguous, out = dq/dk/dv strided.
+// grid (ceil(C/64), item blocks).
+template <typename T, bool PAIR, int ND, int KA, int KB, int KI, int MODE>
+__global__ void __launch_bounds__(kElemThreads) hyena_line_stencil_kernel(
+    const T* __restrict__ in0, const T* __restrict__ in1, const T* __restrict__ in2, long long in_bst,
+    long long in_pst, T* __restrict__ out0, T* __restrict__ out1, T* __restrict__ out2, long long out_bst,
+    long long out_pst, T* __restrict__ z, StencilGeom g, int B, int C, const float* __restrict__ w,
+    const float* __restrict__ bias, int gate1) {
+  constexpr int NA = KA * KB, NT = NA * KI, NW = kElemThreads / 32, SEG = 64;
+  __shared__ float sw[3 * NT * kElemCG];
+  __shared__ float sb[3 * kElemCG];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c0 = blockIdx.x * kElemCG;
+  const int c = c0 + 2 * lane;
+  const bool two = c + 1 < C;
+  stage_weights(sw, sb, w, bias, C, c0, NT, MODE == 0 && g.has_bias);
+  __syncthreads();
+  if (c >= C) return;
+  const int nl = line_len<ND>(g);
+  // forward: input position p + e - off; transposed: p - e + off = p + (KI-1-off) - (KI-1-e)
+  const int offI = MODE == 0 ? g.off[ND - 1] : KI - 1 - g.off[ND - 1];
+  const long long Ntot = (long long)g.n[0] * g.n[1] * g.n[2];
+  const int nseg = (nl + SEG - 1) / SEG;
+  const long long lpi = lines_per_item<ND>(g);
+  const long long items = (long long)B * lpi * nseg;
+  const T* ins[3] = {in0, in1, in2};
+  T* outs[3] = {out0, out1, out2};
+  for (long long it = (long long)blockIdx.y * NW + warp; it < items; it += (long long)gridDim.y * NW) {
+    const long long li = it / nseg;
+    const int sg = (int)(it - li * nseg);
+    const int b = (int)(li / lpi);
+    const long long lo = li - (long long)b * lpi;
+    int o0 = 0, o1 = 0;
+    if (ND == 3) { o0 = (int)(lo / g.n[1]); o1 = (int)(lo - (long long)o0 * g.n[1]); }
+    if (ND == 2) o0 = (int)lo;
+    const int pa = sg * SEG, pb = min(nl, pa + SEG);
+    const long long lpos = ND == 3 ? ((long long)o0 * g.n[1] + o1) * g.n[2] : (ND == 2 ? (long long)o0 * g.n[1] : 0LL);
+    // input row bases for the outer stencil rows (j = a * KB + bq), in the input's layout
+    long long rb[NA];
+    bool rok[NA];
+#pragma unroll
+    for (int a = 0; a < KA; ++a) {
+#pragma unroll
+      for (int bq = 0; bq < KB; ++bq) {
+        const int j = a * KB + bq;
+        const int da = MODE == 0 ? a - g.off[0] : g.off[0] - a;
+        const int dbq = MODE == 0 ? bq - g.off[1] : g.off[1] - bq;
+        long long rowpos = 0;
+        bool okr = true;
+        if (ND == 3) {
+          const int i0 = o0 + da, i1 = o1 + dbq;
+          okr = i0 >= 0 && i0 < g.n[0] && i1 >= 0 && i1 < g.n[1];
+          rowpos = ((long long)i0 * g.n[1] + i1) * g.n[2];
+        } else if (ND == 2) {
+          const int i0 = o0 + da;
+          okr = i0 >= 0 && i0 < g.n[0];
+          rowpos = (long long)i0 * g.n[1];
+        }
+        rok[j] = okr;
+        rb[j] = MODE == 0 ? (long long)b * in_bst + c + rowpos * in_pst : ((long long)b * Ntot + rowpos) * C + c;
+      }
+    }
+    const long long ps = MODE == 0 ? in_pst : (long long)C;
+#pragma unroll 1
+    for (int t = 0; t < 3; ++t) {
+      const T* in = ins[t];
+      auto ldin = [&](int j, int pi) -> float2 {
+        if (!rok[j] || pi < 0 || pi >= nl) return make_float2(0.f, 0.f);
+        return ld2<T, PAIR>(in + rb[j] + (long long)pi * ps, two);
+      };
+      // weights of this tensor: tap (j, e) for the forward; (j, KI-1-u) for window slot u in MODE 1
+      float2 wr[NT];
+#pragma unroll
+      for (int j = 0; j < NA; ++j) {
+#pragma unroll
+        for (int u = 0; u < KI; ++u) {
+          const int e = MODE == 0 ? u : KI - 1 - u;
+          wr[j * KI + u] = *reinterpret_cast<const float2*>(&sw[(t * NT + j * KI + e) * kElemCG + 2 * lane]);
+        }
+      }
+      const float2 bs = MODE == 0 ? make_float2(sb[t * kElemCG + 2 * lane], sb[t * kElemCG + 2 * lane + 1])
+                                  : make_float2(0.f, 0.f);
+      float2 win[NA][KI];
+#pragma unroll
+      for (int j = 0; j < NA; ++j) {
+#pragma unroll
+        for (int u = 1; u < KI; ++u) win[j][u] = ldin(j, pa - 1 + u - offI);
+      }
+      for (int p = pa; p < pb; ++p) {
+        float2 acc = bs;
+#pragma unroll
+        for (int j = 0; j < NA; ++j) {
+#pragma unroll
+          for (int u = 0; u + 1 < KI; ++u) win[j][u] = win[j][u + 1];
+          win[j][KI - 1] = ldin(j, p + KI - 1 - offI);
+#pragma unroll
+          for (int u = 0; u < KI; ++u) {
+            acc.x = fmaf(wr[j * KI + u].x, win[j][u].x, acc.x);
+            acc.y = fmaf(wr[j * KI + u].y, win[j][u].y, acc.y);
+          }
+        }
+        if constexpr (MODE == 0) {
+          const long long o = ((long long)b * Ntot + lpos + p) * C + c;
+          const float2 r = V2<T>::round(acc);
+          st2<T, PAIR>(outs[t] + o, r, two);
+          if (t == 1) {  // z = q' * g1(k'); q' was written by this warp in the previous sweep
+            const float2 qv = ld2<T, PAIR>(outs[0] + o, two);
+            const float2 g1 = V2<T>::round(make_float2(gate_f(gate1, r.x), gate_f(gate1, r.y)));
+            st2<T, PAIR>(z + o, make_float2(qv.x * g1.x, qv.y * g1.y), two);
+          }
+        } else {
+          st2<T, PAIR>(outs[t] + (long long)b * out_bst + (lpos + p) * out_pst + c, acc, two);
+        }
+      }
+    }
   }
 }
 
