@@ -85,10 +85,10 @@ __device__ __forceinline__ float2 twiddle(const float2* tw, int j, int half, flo
   return make_float2(w.x, dir * w.y);
 }
 
-// Shared-memory index of point t of a line: one pad slot every 32 points, so the
-// strided writes of a Stockham stage (stride R * Ns) fall into distinct banks.
-__device__ __forceinline__ int padi(int t) { return t + (t >> 5); }
-__host__ __device__ constexpr int pass_ld(int F) { return F + (F >> 5) + 1; }
+// Shared-memory index of point t of a line: one pad slot every 16 points, so the
+// stride-16 writes of a radix-16 Stockham stage fall into distinct banks.
+__device__ __forceinline__ int padi(int t) { return t + (t >> 4); }
+__host__ __device__ constexpr int pass_ld(int F) { return F + (F >> 4) + 1; }
 
 // 16-point DFT in registers, natural order in, natural order out (two radix-4 layers).
 __device__ __forceinline__ void dft16(float2 (&v)[16], float dir) {
@@ -204,10 +204,60 @@ struct LineInfo {
   int valid;
 };
 
+// The per-line bookkeeping lives in shared memory as separate arrays per field, so that
+// threads reading consecutive lines hit consecutive words (no bank conflicts).
+struct LineSoA {
+  long long *cin, *cout, *rri, *rii, *rro, *rio;
+  int *pos0, *twm, *ch, *valid;
+};
+__device__ __forceinline__ LineSoA line_soa(unsigned char* base) {
+  LineSoA s;
+  long long* q = reinterpret_cast<long long*>(base);
+  s.cin = q;
+  s.cout = q + kPassMaxLines;
+  s.rri = q + 2 * kPassMaxLines;
+  s.rii = q + 3 * kPassMaxLines;
+  s.rro = q + 4 * kPassMaxLines;
+  s.rio = q + 5 * kPassMaxLines;
+  int* r = reinterpret_cast<int*>(q + 6 * kPassMaxLines);
+  s.pos0 = r;
+  s.twm = r + kPassMaxLines;
+  s.ch = r + 2 * kPassMaxLines;
+  s.valid = r + 3 * kPassMaxLines;
+  return s;
+}
+__device__ __forceinline__ void put_line(const LineSoA& s, int l, const LineInfo& L) {
+  s.cin[l] = L.cin_base;
+  s.cout[l] = L.cout_base;
+  s.rri[l] = L.r_re_in;
+  s.rii[l] = L.r_im_in;
+  s.rro[l] = L.r_re_out;
+  s.rio[l] = L.r_im_out;
+  s.pos0[l] = L.pos0;
+  s.twm[l] = L.tw_m;
+  s.ch[l] = L.c;
+  s.valid[l] = L.valid;
+}
+__device__ __forceinline__ LineInfo get_line(const LineSoA& s, int l) {
+  LineInfo L;
+  L.cin_base = s.cin[l];
+  L.cout_base = s.cout[l];
+  L.r_re_in = s.rri[l];
+  L.r_im_in = s.rii[l];
+  L.r_re_out = s.rro[l];
+  L.r_im_out = s.rio[l];
+  L.pos0 = s.pos0[l];
+  L.tw_m = s.twm[l];
+  L.c = s.ch[l];
+  L.valid = s.valid[l];
+  return L;
+}
+static_assert(sizeof(LineInfo) * kPassMaxLines >= (6 * 8 + 4 * 4) * kPassMaxLines, "line bookkeeping size");
+
 template <int IN_MODE, int OUT_MODE, typename TI, typename TO>
 __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDesc d) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  LineInfo* li = reinterpret_cast<LineInfo*>(smem_raw);
+  const LineSoA ls = line_soa(smem_raw);
   float2* sm = reinterpret_cast<float2*>(smem_raw + sizeof(LineInfo) * kPassMaxLines);
   const int TL = d.TL, F = d.F;
   const int ld = pass_ld(F);  // padded line stride (odd, spreads lines over banks)
@@ -245,17 +295,18 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
     L.r_im_out = has_im ? L.r_re_out + (long long)d.half * d.ro_bst : -1;
     L.pos0 = o[0] * d.pos_oth;
     L.tw_m = o[0];
-    li[l] = L;
+    put_line(ls, l, L);
   }
   __syncthreads();
 
   // ---- load
   const int npts = TL * F;
+#pragma unroll 4
   for (int e = threadIdx.x; e < npts; e += blockDim.x) {
     int l, t;
     if (d.load_t_fastest) { l = e >> logF; t = e & (F - 1); }
     else { t = e >> logTL; l = e & (TL - 1); }
-    const LineInfo& L = li[l];
+    const LineInfo L = get_line(ls, l);
     float2 val = make_float2(0.f, 0.f);
     if (L.valid) {
       if (IN_MODE == IN_CPLX) {
@@ -278,11 +329,12 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
   stockham_tile(sm, tw, TL, F, d.logF, ld, d.dir);
 
   // ---- store
+#pragma unroll 4
   for (int e = threadIdx.x; e < npts; e += blockDim.x) {
     int l, t;
     if (d.store_t_fastest) { l = e >> logF; t = e & (F - 1); }
     else { t = e >> logTL; l = e & (TL - 1); }
-    const LineInfo& L = li[l];
+    const LineInfo L = get_line(ls, l);
     if (!L.valid) continue;
     float2 val = cscale(sm[l * ld + padi(t)], d.scale);
     if (d.tw_logF > 0 && L.tw_m != 0) {
