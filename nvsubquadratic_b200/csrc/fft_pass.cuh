@@ -306,13 +306,20 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
     int l, t;
     if (d.load_t_fastest) { l = e >> logF; t = e & (F - 1); }
     else { t = e >> logTL; l = e & (TL - 1); }
+    if constexpr (IN_MODE == IN_CPLX) {
+      // asynchronous 8-byte copy straight into shared memory; out-of-range points are
+      // zero-filled by the copy itself (source size 0, the source is not read)
+      const int bi = t - d.in_off;
+      const bool in = ls.valid[l] && bi >= 0 && bi < d.n_in;
+      const float2* g = in ? d.cin + ls.cin[l] + (long long)bi * d.ci_tst : d.cin;
+      const unsigned sa = (unsigned)__cvta_generic_to_shared(sm + l * ld + padi(t));
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(sa), "l"(g), "r"(in ? 8 : 0) : "memory");
+      continue;
+    }
     const LineInfo L = get_line(ls, l);
     float2 val = make_float2(0.f, 0.f);
     if (L.valid) {
-      if (IN_MODE == IN_CPLX) {
-        const int bi = t - d.in_off;
-        if (bi >= 0 && bi < d.n_in) val = d.cin[L.cin_base + (long long)bi * d.ci_tst];
-      } else {
+      {
         const int pos = t * d.pos_mul + L.pos0 - d.in_off;
         if (pos >= 0 && pos < d.n_in) {
           const TI* src = reinterpret_cast<const TI*>(d.rin);
@@ -324,6 +331,7 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
     }
     sm[l * ld + padi(t)] = val;
   }
+  if constexpr (IN_MODE == IN_CPLX) asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
   __syncthreads();
 
   stockham_tile(sm, tw, TL, F, d.logF, ld, d.dir);
