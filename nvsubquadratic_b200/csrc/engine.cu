@@ -156,7 +156,7 @@ static int launch_pass_t(const PassDesc& d, cudaStream_t st) {
   if (grid <= 0) return HYFFT_OK;
   if (grid > 0x7fffffffLL) return fail(HYFFT_ERR_UNSUPPORTED, "too many FFT lines");
   const size_t smem =
-      sizeof(LineInfo) * kPassMaxLines + sizeof(float2) * ((size_t)d.TL * pass_ld(d.F) + (size_t)(d.F / 2));
+      (size_t)kLineBytes + sizeof(float2) * ((size_t)d.TL * pass_ld(d.F) + (size_t)(d.F / 2));
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(fft_pass_kernel<IM, OM, TI, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
           cudaSuccess)
@@ -168,6 +168,11 @@ static int launch_pass_t(const PassDesc& d, cudaStream_t st) {
 template <int IM, int OM>
 static int launch_pass_dt(const PassDesc& d, int tin, int tout, cudaStream_t st) {
   // only the real side's dtype matters; complex-only passes use float
+  if (IM == IN_REAL && OM != OUT_CPLX) {  // fused product pass from a real source to a real output
+    if (tin == HYFFT_F32) return launch_pass_t<IM, OM, float, float>(d, st);
+    if (tin == HYFFT_BF16) return launch_pass_t<IM, OM, __nv_bfloat16, __nv_bfloat16>(d, st);
+    return launch_pass_t<IM, OM, __half, __half>(d, st);
+  }
   if (IM == IN_REAL) {
     if (tin == HYFFT_F32) return launch_pass_t<IM, OM, float, float>(d, st);
     if (tin == HYFFT_BF16) return launch_pass_t<IM, OM, __nv_bfloat16, float>(d, st);
@@ -183,6 +188,8 @@ static int launch_pass_dt(const PassDesc& d, int tin, int tout, cudaStream_t st)
 
 static int launch_pass(const PassDesc& d, int im, int om, int tin, int tout, cudaStream_t st) {
   if (im == IN_REAL && om == OUT_CPLX) return launch_pass_dt<IN_REAL, OUT_CPLX>(d, tin, tout, st);
+  if (im == IN_REAL && om == OUT_REAL) return launch_pass_dt<IN_REAL, OUT_REAL>(d, tin, tout, st);
+  if (im == IN_REAL && om == OUT_REAL_SKIP) return launch_pass_dt<IN_REAL, OUT_REAL_SKIP>(d, tin, tout, st);
   if (im == IN_CPLX && om == OUT_CPLX) return launch_pass_dt<IN_CPLX, OUT_CPLX>(d, tin, tout, st);
   if (im == IN_CPLX && om == OUT_REAL) return launch_pass_dt<IN_CPLX, OUT_REAL>(d, tin, tout, st);
   if (im == IN_CPLX && om == OUT_REAL_SKIP) return launch_pass_dt<IN_CPLX, OUT_REAL_SKIP>(d, tin, tout, st);
@@ -254,10 +261,27 @@ static void set_real_out(PassDesc& d, const RealView& v, const Pairing& pr) {
   d.packed = pr.packed;
 }
 
+// A chain of passes can be recorded instead of launched, so that the last forward pass
+// and the first inverse pass of a convolution can be merged into one product pass.
+struct PassRec {
+  PassDesc d;
+  int im, om, tin, tout;
+};
+struct PassList {
+  PassRec r[4];
+  int n = 0;
+};
+static int emit_pass(PassList* rec, const PassDesc& d, int im, int om, int tin, int tout, cudaStream_t st) {
+  if (!rec) return launch_pass(d, im, om, tin, tout, st);
+  if (rec->n >= 4) return fail(HYFFT_ERR_INVALID, "pass list overflow");
+  rec->r[rec->n++] = PassRec{d, im, om, tin, tout};
+  return HYFFT_OK;
+}
+
 // Forward transform of a real source (extents E, placed at offsets off) into the
 // full spectrum S. Channels [0, C) of the view.
 static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pairing& pr, const int* E,
-                     const int* off, float2* S, cudaStream_t st) {
+                     const int* off, float2* S, cudaStream_t st, PassList* rec = nullptr) {
   const SpecStrides ss = spec_strides(g, C);
   if (g.four) {
     // pass A: along n_a (stride Fb*C in S), lines (p, n_b, c); twiddle e^{-2 pi i k_a n_b / F}
@@ -281,7 +305,7 @@ static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pa
     a.load_t_fastest = 0;
     a.store_t_fastest = 0;
     finish_lines(a);
-    HY_TRY(launch_pass(a, IN_REAL, OUT_CPLX, tdt, HYFFT_F32, st));
+    HY_TRY(emit_pass(rec, a, IN_REAL, OUT_CPLX, tdt, HYFFT_F32, st));
     // pass B: along n_b (stride C), lines (p, k_a, c)
     PassDesc b;
     base_desc(b, g.Fb, -1.f, pr.P, C);
@@ -297,7 +321,7 @@ static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pa
     b.out_lo = 0;
     b.n_out = g.Fb;
     finish_lines(b);
-    return launch_pass(b, IN_CPLX, OUT_CPLX, tdt, HYFFT_F32, st);
+    return emit_pass(rec, b, IN_CPLX, OUT_CPLX, tdt, HYFFT_F32, st);
   }
   const int D = g.D;
   // last axis from the real source
@@ -322,7 +346,7 @@ static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pa
     a.load_t_fastest = (src.sst[D - 1] == 1) ? 1 : 0;
     a.store_t_fastest = 0;
     finish_lines(a);
-    HY_TRY(launch_pass(a, IN_REAL, OUT_CPLX, tdt, HYFFT_F32, st));
+    HY_TRY(emit_pass(rec, a, IN_REAL, OUT_CPLX, tdt, HYFFT_F32, st));
   }
   for (int d = D - 2; d >= 0; --d) {
     PassDesc a;
@@ -344,7 +368,7 @@ static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pa
     a.out_lo = 0;
     a.n_out = g.F[d];
     finish_lines(a);
-    HY_TRY(launch_pass(a, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
+    HY_TRY(emit_pass(rec, a, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
   }
   return HYFFT_OK;
 }
@@ -358,7 +382,7 @@ struct Epilogue {
 // Inverse transform of the full spectrum S into a real destination, keeping the
 // window [lo[d], lo[d] + cnt[d]) of every axis.
 static int inv_chain(const Geo& g, int C, float2* S, const RealView& dst, int tdt, const Pairing& pr, const int* lo,
-                     const int* cnt, const Epilogue& ep, cudaStream_t st) {
+                     const int* cnt, const Epilogue& ep, cudaStream_t st, PassList* rec = nullptr) {
   const SpecStrides ss = spec_strides(g, C);
   if (g.four) {
     PassDesc b;  // along k_b with twiddle e^{+2 pi i n_b k_a / F}
@@ -376,7 +400,7 @@ static int inv_chain(const Geo& g, int C, float2* S, const RealView& dst, int td
     b.n_out = g.Fb;
     b.tw_logF = ilog2(g.F[0]);
     finish_lines(b);
-    HY_TRY(launch_pass(b, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
+    HY_TRY(emit_pass(rec, b, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
     PassDesc a;  // along k_a into the real output, position n_a * Fb + n_b
     base_desc(a, g.Fa, +1.f, pr.P, C);
     a.n_oth = 1;
@@ -398,7 +422,7 @@ static int inv_chain(const Geo& g, int C, float2* S, const RealView& dst, int td
     a.load_t_fastest = 0;
     a.store_t_fastest = 0;
     finish_lines(a);
-    return launch_pass(a, IN_CPLX, ep.mode, HYFFT_F32, tdt, st);
+    return emit_pass(rec, a, IN_CPLX, ep.mode, HYFFT_F32, tdt, st);
   }
   const int D = g.D;
   for (int d = 0; d < D - 1; ++d) {
@@ -421,7 +445,7 @@ static int inv_chain(const Geo& g, int C, float2* S, const RealView& dst, int td
     a.out_lo = lo[d];
     a.n_out = cnt[d];
     finish_lines(a);
-    HY_TRY(launch_pass(a, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
+    HY_TRY(emit_pass(rec, a, IN_CPLX, OUT_CPLX, HYFFT_F32, HYFFT_F32, st));
   }
   PassDesc a;
   base_desc(a, g.F[D - 1], +1.f, pr.P, C);
@@ -445,7 +469,7 @@ static int inv_chain(const Geo& g, int C, float2* S, const RealView& dst, int td
   a.load_t_fastest = 0;
   a.store_t_fastest = (dst.sst[D - 1] == 1) ? 1 : 0;
   finish_lines(a);
-  return launch_pass(a, IN_CPLX, ep.mode, HYFFT_F32, tdt, st);
+  return emit_pass(rec, a, IN_CPLX, ep.mode, HYFFT_F32, tdt, st);
 }
 
 static int grid_for(long long n, int threads = 256) {
@@ -531,6 +555,63 @@ static int to_float(const void* src, int dt, float* dst, int n, cudaStream_t st)
   return check_launch("to_float_kernel");
 }
 
+// Forward transform of x, product with the kernel spectrum Kh (conjugated if conj) and
+// inverse transform into y, with the last forward pass and the first inverse pass (both
+// along the same axis, over the same lines) merged into one product pass, so the full
+// spectrum is neither written by the one nor re-read by the other. Returns
+// HYFFT_ERR_UNSUPPORTED (nothing launched) if the two passes do not line up.
+static int fused_conv_chain(const Geo& g, int Cc, const RealView& xc, int tin, const Pairing& px, const int* E,
+                            const int* off, float2* S, const float2* Kh, bool shared, int conj, const RealView& yc,
+                            int tout, const int* lo, const int* cnt, const Epilogue& ep, cudaStream_t st) {
+  PassList fl, il;
+  HY_TRY(fwd_chain(g, Cc, xc, tin, px, E, off, S, st, &fl));
+  HY_TRY(inv_chain(g, Cc, S, yc, tout, px, lo, cnt, ep, st, &il));
+  if (fl.n < 1 || il.n < 1) return HYFFT_ERR_UNSUPPORTED;
+  const PassRec& f = fl.r[fl.n - 1];
+  const PassRec& v = il.r[0];
+  bool same = f.d.F == v.d.F && f.d.TL == v.d.TL && f.d.n_oth == v.d.n_oth && f.d.nlines == v.d.nlines &&
+              f.d.P == v.d.P && f.d.C == v.d.C;
+  for (int j = 0; j < f.d.n_oth; ++j) same = same && f.d.oth_ext[j] == v.d.oth_ext[j];
+  if (f.im == IN_REAL && v.om != OUT_CPLX) same = same && f.d.pos_mul == v.d.pos_mul && f.d.pos_oth == v.d.pos_oth;
+  if (!same) return HYFFT_ERR_UNSUPPORTED;
+  for (int i = 0; i + 1 < fl.n; ++i) HY_TRY(launch_pass(fl.r[i].d, fl.r[i].im, fl.r[i].om, fl.r[i].tin, fl.r[i].tout, st));
+  PassDesc m = f.d;  // load side of the last forward pass
+  m.cout = v.d.cout;  // store side of the first inverse pass
+  m.co_pst = v.d.co_pst;
+  m.co_tst = v.d.co_tst;
+  m.co_ost[0] = v.d.co_ost[0];
+  m.co_ost[1] = v.d.co_ost[1];
+  m.out_lo = v.d.out_lo;
+  m.n_out = v.d.n_out;
+  m.tw_logF = v.d.tw_logF;
+  m.rout = v.d.rout;
+  m.ro_bst = v.d.ro_bst;
+  m.ro_cst = v.d.ro_cst;
+  m.ro_tst = v.d.ro_tst;
+  m.ro_ost[0] = v.d.ro_ost[0];
+  m.ro_ost[1] = v.d.ro_ost[1];
+  m.skip = v.d.skip;
+  m.Dv = v.d.Dv;
+  m.store_t_fastest = v.d.store_t_fastest;
+  m.scale = v.d.scale;
+  m.mid = conj ? 2 : 1;
+  m.kin = Kh;
+  m.k_shared = shared ? 1 : 0;
+  m.k_pst = spec_strides(g, Cc).pst;
+  if (f.im == IN_CPLX) {
+    m.k_tst = f.d.ci_tst;
+    m.k_ost[0] = f.d.ci_ost[0];
+    m.k_ost[1] = f.d.ci_ost[1];
+  } else {
+    m.k_tst = f.d.co_tst;
+    m.k_ost[0] = f.d.co_ost[0];
+    m.k_ost[1] = f.d.co_ost[1];
+  }
+  HY_TRY(launch_pass(m, f.im, v.om, f.tin, v.tout, st));
+  for (int i = 1; i < il.n; ++i) HY_TRY(launch_pass(il.r[i].d, il.r[i].im, il.r[i].om, il.r[i].tin, il.r[i].tout, st));
+  return HYFFT_OK;
+}
+
 // One forward convolution over channels [c0, c0 + Cc) of already-prepared views.
 static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView& xv, const RealView& kv,
                               const float* Dfull, const RealView& yv, float2* S, float2* Kh, cudaStream_t st) {
@@ -540,16 +621,21 @@ static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView&
   const RealView yc = offset_channels(yv, c0, eb);
   const int zero[3] = {0, 0, 0};
   HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
-  HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S, st));
-  const long long per_pair = p.g.vol_F * Cc;
-  spec_mul_kernel<<<grid_for(per_pair * p.px.P), 256, 0, st>>>(S, Kh, per_pair, p.px.P, p.shared ? 1 : 0);
-  HY_TRY(check_launch("spec_mul_kernel"));
   Epilogue ep;
   if (Dfull) {
     ep.mode = OUT_REAL_SKIP;
     ep.skip = xc.ptr;
     ep.Dv = Dfull + c0;
   }
+  const int rc = getenv("HYFFT_DISABLE_PRODUCT_PASS")
+                     ? HYFFT_ERR_UNSUPPORTED
+                     : fused_conv_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S, Kh, p.shared, 0, yc, p.dt, p.g.crop,
+                                        p.g.N, ep, st);
+  if (rc != HYFFT_ERR_UNSUPPORTED) return rc;
+  HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S, st));
+  const long long per_pair = p.g.vol_F * Cc;
+  spec_mul_kernel<<<grid_for(per_pair * p.px.P), 256, 0, st>>>(S, Kh, per_pair, p.px.P, p.shared ? 1 : 0);
+  HY_TRY(check_launch("spec_mul_kernel"));
   return inv_chain(p.g, Cc, S, yc, p.dt, p.px, p.g.crop, p.g.N, ep, st);
 }
 

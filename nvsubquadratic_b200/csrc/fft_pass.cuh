@@ -57,6 +57,15 @@ struct PassDesc {
   // real tensors: element (b, c, pos, oth) at b*bst + c*cst + pos*tst + sum oth*ost
   const void* rin;
   long long ri_bst, ri_cst, ri_tst, ri_ost[2];
+  // fused product pass (mid != 0): after the forward transform (dir -1) every point t of
+  // a line is multiplied by the kernel spectrum kin[k_base + t * k_tst] (mid == 2: its
+  // conjugate), then transformed back (+1) before the store; k_base = (k_shared ? 0 : p)
+  // * k_pst + sum oth * k_ost + c.
+  int mid;
+  const float2* kin;
+  long long k_pst, k_tst, k_ost[2];
+  int k_shared;
+
   void* rout;
   long long ro_bst, ro_cst, ro_tst, ro_ost[2];
   const void* skip;  // same layout as rout (OUT_REAL_SKIP): y = round(round(v) + round(D*skip))
@@ -207,9 +216,10 @@ struct LineInfo {
 // The per-line bookkeeping lives in shared memory as separate arrays per field, so that
 // threads reading consecutive lines hit consecutive words (no bank conflicts).
 struct LineSoA {
-  long long *cin, *cout, *rri, *rii, *rro, *rio;
+  long long *cin, *cout, *rri, *rii, *rro, *rio, *kb;
   int *pos0, *twm, *ch, *valid;
 };
+constexpr int kLineBytes = (7 * 8 + 4 * 4) * kPassMaxLines;  // shared-memory bytes of the bookkeeping
 __device__ __forceinline__ LineSoA line_soa(unsigned char* base) {
   LineSoA s;
   long long* q = reinterpret_cast<long long*>(base);
@@ -219,7 +229,8 @@ __device__ __forceinline__ LineSoA line_soa(unsigned char* base) {
   s.rii = q + 3 * kPassMaxLines;
   s.rro = q + 4 * kPassMaxLines;
   s.rio = q + 5 * kPassMaxLines;
-  int* r = reinterpret_cast<int*>(q + 6 * kPassMaxLines);
+  s.kb = q + 6 * kPassMaxLines;
+  int* r = reinterpret_cast<int*>(q + 7 * kPassMaxLines);
   s.pos0 = r;
   s.twm = r + kPassMaxLines;
   s.ch = r + 2 * kPassMaxLines;
@@ -252,13 +263,12 @@ __device__ __forceinline__ LineInfo get_line(const LineSoA& s, int l) {
   L.valid = s.valid[l];
   return L;
 }
-static_assert(sizeof(LineInfo) * kPassMaxLines >= (6 * 8 + 4 * 4) * kPassMaxLines, "line bookkeeping size");
 
 template <int IN_MODE, int OUT_MODE, typename TI, typename TO>
 __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDesc d) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const LineSoA ls = line_soa(smem_raw);
-  float2* sm = reinterpret_cast<float2*>(smem_raw + sizeof(LineInfo) * kPassMaxLines);
+  float2* sm = reinterpret_cast<float2*>(smem_raw + kLineBytes);
   const int TL = d.TL, F = d.F;
   const int ld = pass_ld(F);  // padded line stride (odd, spreads lines over banks)
   float2* tw = sm + (size_t)TL * ld;
@@ -295,6 +305,9 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
     L.r_im_out = has_im ? L.r_re_out + (long long)d.half * d.ro_bst : -1;
     L.pos0 = o[0] * d.pos_oth;
     L.tw_m = o[0];
+    if (d.mid)
+      ls.kb[l] = (long long)(d.k_shared ? 0 : p) * d.k_pst + (long long)o[0] * d.k_ost[0] +
+                 (long long)o[1] * d.k_ost[1] + c;
     put_line(ls, l, L);
   }
   __syncthreads();
@@ -336,6 +349,22 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
 
   stockham_tile(sm, tw, TL, F, d.logF, ld, d.dir);
 
+  if (d.mid) {  // product with the kernel spectrum, then the inverse transform
+    const float cj = d.mid == 2 ? -1.f : 1.f;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < npts; e += blockDim.x) {
+      const int t = e >> logTL, l = e & (TL - 1);  // neighbouring lines are neighbouring channels
+      if (!ls.valid[l]) continue;
+      float2 k = __ldg(d.kin + ls.kb[l] + (long long)t * d.k_tst);
+      k.y *= cj;
+      float2* v = sm + l * ld + padi(t);
+      *v = cmul(*v, k);
+    }
+    __syncthreads();
+    stockham_tile(sm, tw, TL, F, d.logF, ld, 1.f);
+  }
+  const float sdir = d.mid ? 1.f : d.dir;  // direction of the store-side twiddle
+
   // ---- store
 #pragma unroll 4
   for (int e = threadIdx.x; e < npts; e += blockDim.x) {
@@ -349,7 +378,7 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
       // e^{dir*2*pi*i*t*m/2^tw_logF}; reduce the exponent mod 2^tw_logF first
       // ex < 2^tw_logF <= 2^24 is exact in float, and so is the power-of-two scaling
       const long long ex = ((long long)t * L.tw_m) & ((1LL << d.tw_logF) - 1);
-      val = cmul(val, expipi(d.dir * ldexpf((float)ex, 1 - d.tw_logF)));
+      val = cmul(val, expipi(sdir * ldexpf((float)ex, 1 - d.tw_logF)));
     }
     if (OUT_MODE == OUT_CPLX) {
       const int bo = t - d.out_lo;

@@ -179,3 +179,27 @@ def test_large_grid_2d_matches_pass_chain_and_blh(dt, monkeypatch):
         assert rel_l2(a, b) <= tol, (name, rel_l2(a, b))
         c = c.permute(0, 3, 1, 2) if c.ndim == 4 else c
         assert rel_l2(b, c) <= tol, (name, "blh", rel_l2(b, c))
+
+
+@pytest.mark.parametrize("causal,xs,ks,dt", [
+    (True, (2, 8, 1000), (1, 8, 1000), torch.float32),       # one pass each way (F <= 4096)
+    (True, (1, 4, 1 << 14), (1, 4, 1 << 14), torch.float32),  # four-step
+    (False, (3, 6, 40, 36), (1, 6, 79, 35), torch.bfloat16),  # 2D
+    (False, (2, 3, 12, 10, 9), (1, 3, 23, 19, 17), torch.float32),  # 3D
+    (False, (3, 4, 300), (3, 4, 77), torch.float32),          # per-sample kernels
+])
+def test_product_pass_matches_unfused_chain(causal, xs, ks, dt, monkeypatch):
+    """The merged forward/product/inverse pass gives the results of the separate passes."""
+    b2 = _b2()
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(xs, generator=g).to(dt)
+    k = torch.randn(ks, generator=g) * 0.05
+    sc = torch.randn(xs[1], generator=g).to(dt)
+    dy = torch.randn(xs, generator=g).to(dt)
+    fn = b2.causal_fftconv1d_fp32_bhl if causal else b2.fftconv_nd
+    fused = _run(fn, x, k, sc, dy)
+    monkeypatch.setenv("HYFFT_DISABLE_PRODUCT_PASS", "1")
+    plain = _run(fn, x, k, sc, dy)
+    tol = TOL[dt]
+    for a, b, name in zip(plain, fused, ("y", "dx", "dk", "dshortcut")):
+        assert rel_l2(a, b) <= tol, (name, rel_l2(a, b))
