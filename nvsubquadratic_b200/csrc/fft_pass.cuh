@@ -130,10 +130,33 @@ __device__ __forceinline__ void dft16(float2 (&v)[16], float dir) {
   for (int k = 0; k < 16; ++k) v[k] = o[k];
 }
 
+// 8-point DFT in registers, natural order in and out (two 4-point DFTs of the even
+// and odd points, combined with W8^k).
+__device__ __forceinline__ void dft8(float2 (&v)[8], float dir) {
+  constexpr float h = 0.70710678118654752f;
+  float2 e0 = v[0], e1 = v[2], e2 = v[4], e3 = v[6];
+  float2 o0 = v[1], o1 = v[3], o2 = v[5], o3 = v[7];
+  dft4(e0, e1, e2, e3, dir);
+  dft4(o0, o1, o2, o3, dir);
+  o1 = cmul(o1, make_float2(h, dir * h));
+  o2 = make_float2(-dir * o2.y, dir * o2.x);
+  o3 = cmul(o3, make_float2(-h, dir * h));
+  v[0] = cadd(e0, o0);
+  v[4] = csub(e0, o0);
+  v[1] = cadd(e1, o1);
+  v[5] = csub(e1, o1);
+  v[2] = cadd(e2, o2);
+  v[6] = csub(e2, o2);
+  v[3] = cadd(e3, o3);
+  v[7] = csub(e3, o3);
+}
+
 template <int R>
 __device__ __forceinline__ void dftR(float2 (&v)[R], float dir) {
   if constexpr (R == 16) {
     dft16(v, dir);
+  } else if constexpr (R == 8) {
+    dft8(v, dir);
   } else if constexpr (R == 4) {
     dft4(v[0], v[1], v[2], v[3], dir);
   } else {
@@ -188,7 +211,7 @@ __device__ __forceinline__ void stockham_stage(float2* sm, const float2* tw, int
 
 // In-place Stockham autosort FFT of TL lines of length F stored at
 // sm[l * ld + padi(t)] (TL * F <= kPassPoints). All threads of the CTA take part;
-// radix-16 stages while at least four factors of two remain, then radix 4 / 2.
+// radix-16 stages while at least four factors of two remain, then one radix 8 / 4 / 2.
 // Twiddles come from the half-turn table tw (F/2 entries).
 static __device__ void stockham_tile(float2* sm, const float2* tw, int TL, int F, int logF, int ld, float dir) {
   int lgNs = 0;
@@ -196,11 +219,11 @@ static __device__ void stockham_tile(float2* sm, const float2* tw, int TL, int F
     stockham_stage<16, 4, kPassPoints / (16 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
     lgNs += 4;
   }
-  if (logF - lgNs >= 2) {
-    stockham_stage<4, 2, kPassPoints / (4 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
-    lgNs += 2;
-  }
-  if (logF - lgNs >= 1) stockham_stage<2, 1, kPassPoints / (2 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
+  // one final stage for the remaining 1..3 factors of two
+  const int rem = logF - lgNs;
+  if (rem == 3) stockham_stage<8, 3, kPassPoints / (8 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
+  else if (rem == 2) stockham_stage<4, 2, kPassPoints / (4 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
+  else if (rem == 1) stockham_stage<2, 1, kPassPoints / (2 * kPassThreads)>(sm, tw, TL, logF, ld, lgNs, dir);
 }
 
 struct LineInfo {
