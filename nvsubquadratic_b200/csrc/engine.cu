@@ -1277,8 +1277,14 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
             const long long items = (long long)d.batch * (h.Ntot / nl) * ((nl + 63) / 64);
             const long long gz = std::max<long long>(1, std::min<long long>(65535, std::min<long long>(
                                                              (items + 7) / 8, 4800 / (3 * (long long)gx))));
-            hyena_short_wgrad_line_kernel<T, P, ND, KA, KB, KI><<<dim3(gx, 3, (unsigned)gz), kElemThreads, 0, st>>>(
-                dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch, d.channels, dsw, dsb);
+            if constexpr (ND == 3)  // one CTA per outer stencil row: 9 taps per thread in registers
+              hyena_short_wgrad_line_kernel<T, P, ND, KA, KB, KI, true>
+                  <<<dim3(gx, 3 * KA, (unsigned)gz), kElemThreads, 0, st>>>(dqp, dkp, dvp, q, k, v, d.in_batch_stride,
+                                                                            d.in_pos_stride, h.sg, d.batch, d.channels,
+                                                                            dsw, dsb);
+            else
+              hyena_short_wgrad_line_kernel<T, P, ND, KA, KB, KI><<<dim3(gx, 3, (unsigned)gz), kElemThreads, 0, st>>>(
+                  dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.batch, d.channels, dsw, dsb);
             return;
           }
         }

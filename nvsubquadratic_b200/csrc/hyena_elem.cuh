@@ -463,15 +463,18 @@ __device__ __forceinline__ long long lines_per_item(const StencilGeom& g) {
 // KA*KB x KI input window in registers (one new column of KA*KB loads per position
 // instead of all taps). grid (ceil(C/64), 3 tensors, item blocks). Same result layout
 // and reduction as hyena_short_wgrad_kernel.
-template <typename T, bool PAIR, int ND, int KA, int KB, int KI>
+template <typename T, bool PAIR, int ND, int KA, int KB, int KI, bool SPLIT = false>
 __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_line_kernel(
     const T* __restrict__ dqp, const T* __restrict__ dkp, const T* __restrict__ dvp, const T* __restrict__ q,
     const T* __restrict__ k, const T* __restrict__ v, long long in_bst, long long in_pst, StencilGeom g, int B, int C,
     float* __restrict__ dw, float* __restrict__ db) {
-  constexpr int NA = KA * KB, NT = NA * KI, NW = kElemThreads / 32, SEG = 64;
+  // SPLIT: this CTA covers only the outer stencil rows a = blockIdx.y / 3 (KB rows), so a
+  // 3D stencil keeps 9 taps per thread in registers instead of 27 (grid.y = 3 * KA)
+  constexpr int NA = (SPLIT ? 1 : KA) * KB, NT = NA * KI, NTG = KA * KB * KI, NW = kElemThreads / 32, SEG = 64;
   __shared__ float red[NW][kElemCG + 1];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int t = blockIdx.y;
+  const int t = SPLIT ? blockIdx.y % 3 : blockIdx.y;
+  const int a0 = SPLIT ? blockIdx.y / 3 : 0;
   const int c = blockIdx.x * kElemCG + 2 * lane;
   const bool ok = c < C, two = c + 1 < C;
   const T* dout = t == 0 ? dqp : (t == 1 ? dkp : dvp);
@@ -499,10 +502,11 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_line_kernel(
       long long rb[NA];
       bool rok[NA];
 #pragma unroll
-      for (int a = 0; a < KA; ++a) {
+      for (int ai = 0; ai < (SPLIT ? 1 : KA); ++ai) {
+        const int a = a0 + ai;
 #pragma unroll
         for (int bq = 0; bq < KB; ++bq) {
-          const int j = a * KB + bq;
+          const int j = ai * KB + bq;
           long long rowpos;  // flat position of (outer neighbour, 0)
           bool okr = true;
           if (ND == 3) {
@@ -568,8 +572,8 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_line_kernel(
       for (int j = 0; j < NW; ++j) sum += red[j][threadIdx.x];
       if (cc < C) {
         const long long ch = (long long)t * C + cc;
-        if (tap < NT) atomicAdd(dw + ch * NT + tap, sum);
-        else if (g.has_bias) atomicAdd(db + ch, sum);
+        if (tap < NT) atomicAdd(dw + ch * NTG + a0 * KB * KI + tap, sum);
+        else if (g.has_bias && a0 == 0) atomicAdd(db + ch, sum);
       }
     }
     __syncthreads();
@@ -585,7 +589,7 @@ __global__ void __launch_bounds__(kElemThreads) hyena_short_wgrad_line_kernel(
 // MODE 1: in = dq'/dk'/dv' contiguous, out = dq/dk/dv strided.
 // grid (ceil(C/64), item blocks).
 template <typename T, bool PAIR, int ND, int KA, int KB, int KI, int MODE>
-__global__ void __launch_bounds__(kElemThreads) hyena_line_stencil_kernel(
+__global__ void __launch_bounds__(kElemThreads, (KA * KB * KI > 9) ? 2 : 3) hyena_line_stencil_kernel(
     const T* __restrict__ in0, const T* __restrict__ in1, const T* __restrict__ in2, long long in_bst,
     long long in_pst, T* __restrict__ out0, T* __restrict__ out1, T* __restrict__ out2, long long out_bst,
     long long out_pst, T* __restrict__ z, StencilGeom g, int B, int C, const float* __restrict__ w,
@@ -652,14 +656,21 @@ __global__ void __launch_bounds__(kElemThreads) hyena_line_stencil_kernel(
         if (!rok[j] || pi < 0 || pi >= nl) return make_float2(0.f, 0.f);
         return ld2<T, PAIR>(in + rb[j] + (long long)pi * ps, two);
       };
-      // weights of this tensor: tap (j, e) for the forward; (j, KI-1-u) for window slot u in MODE 1
-      float2 wr[NT];
+      // weights of this tensor: tap (j, e) for the forward; (j, KI-1-u) for window slot u in
+      // MODE 1. Up to 9 taps they stay in registers; larger (3D) stencils read them from
+      // shared memory at each use, so the window and the weights do not both hold ~54
+      // registers and the kernel keeps two CTAs per SM.
+      constexpr bool WREG = NT <= 9;
+      auto wsm = [&](int j, int u) -> float2 {
+        const int e = MODE == 0 ? u : KI - 1 - u;
+        return *reinterpret_cast<const float2*>(&sw[(t * NT + j * KI + e) * kElemCG + 2 * lane]);
+      };
+      float2 wr[WREG ? NT : 1];
+      if constexpr (WREG) {
 #pragma unroll
-      for (int j = 0; j < NA; ++j) {
+        for (int j = 0; j < NA; ++j) {
 #pragma unroll
-        for (int u = 0; u < KI; ++u) {
-          const int e = MODE == 0 ? u : KI - 1 - u;
-          wr[j * KI + u] = *reinterpret_cast<const float2*>(&sw[(t * NT + j * KI + e) * kElemCG + 2 * lane]);
+          for (int u = 0; u < KI; ++u) wr[j * KI + u] = wsm(j, u);
         }
       }
       const float2 bs = MODE == 0 ? make_float2(sb[t * kElemCG + 2 * lane], sb[t * kElemCG + 2 * lane + 1])
@@ -679,8 +690,11 @@ __global__ void __launch_bounds__(kElemThreads) hyena_line_stencil_kernel(
           win[j][KI - 1] = ldin(j, p + KI - 1 - offI);
 #pragma unroll
           for (int u = 0; u < KI; ++u) {
-            acc.x = fmaf(wr[j * KI + u].x, win[j][u].x, acc.x);
-            acc.y = fmaf(wr[j * KI + u].y, win[j][u].y, acc.y);
+            float2 wv;
+            if constexpr (WREG) wv = wr[j * KI + u];
+            else wv = wsm(j, u);
+            acc.x = fmaf(wv.x, win[j][u].x, acc.x);
+            acc.y = fmaf(wv.y, win[j][u].y, acc.y);
           }
         }
         if constexpr (MODE == 0) {
