@@ -524,7 +524,7 @@ def e2e_time(cfg, inp, device, op_only, steps):
             dy = host["dy"].to(device, non_blocking=True)
             y = causal_fftconv1d_fp32_bhl(x, f, D)
             y.backward(dy)
-            res = [y, x.grad, f.grad, D.grad]
+            res = [y]  # the step's result; the gradients stay on the device for the optimizer
             ins = [host["x"], host["filt"], host["D"], host["dy"]]
         else:
             qkv = host["qkv"].to(device, non_blocking=True).requires_grad_(True)
@@ -535,7 +535,7 @@ def e2e_time(cfg, inp, device, op_only, steps):
             q, k, v = qkv.chunk(3, dim=-1)
             y = hyena_fused(q, k, v, f, D, sw, None, causal=cfg["causal"], gate1=cfg["g1"], gate2=cfg["g2"])
             y.backward(dy)
-            res = [y, qkv.grad, f.grad, D.grad] + ([sw.grad] if sw is not None else [])
+            res = [y]  # the step's result; the gradients stay on the device for the optimizer
             ins = [host["qkv"], host["filt"], host["D"], host["dy"]] + ([host["sw"]] if sw is not None else [])
         if not outs:
             outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
@@ -560,9 +560,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="run warmup + steps eager fwd+bwd steps and exit (for ncu captures)")
+    ap.add_argument("--channels", type=int, default=None,
+                    help="with --profile: run the config's shapes with this many channels (a smaller device "
+                         "footprint for full ncu captures; the kernels and line lengths are the config's own)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     cfg = CONFIGS[args.config]
+    if args.channels is not None:
+        if not args.profile:
+            raise SystemExit("--channels only applies to --profile runs (bench lines use the config as published)")
+        cfg = dict(cfg, C=args.channels)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

@@ -946,7 +946,22 @@ struct HyenaPlan {
   bool fused = false;   // single-pass fused FFT kernels (fused.cu) apply
   bool tp = false;      // tensor-core Toeplitz kernels (toeplitz.cu) apply (takes precedence)
   int SK = 0;
+  int fF[2] = {0, 0};   // FFT sizes of the fused kernels (2^m or 3 * 2^m per axis)
 };
+
+// Smallest FFT length of the fused kernels (2^m or 3 * 2^m, at most 64) for an axis of
+// n points and a k-tap centred filter rolled by its crop offset k/2: the circular
+// convolution equals the linear one on [0, n) when F >= n + k/2 and F >= n + ceil(k/2) - 1,
+// and the filter fits when F >= k.
+static int fused_fft_len(int n, int k) {
+  const int need = std::max(std::max(n + k / 2, n + (k + 1) / 2 - 1), k);
+  int best = 1 << 30;
+  for (int p = 1; p <= 64; p <<= 1) {
+    if (p >= need) best = std::min(best, p);
+    if (3 * p >= need && 3 * p <= 48) best = std::min(best, 3 * p);
+  }
+  return best;
+}
 
 
 static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
@@ -998,8 +1013,20 @@ static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
   if (!getenv("HYFFT_DISABLE_FUSED") && d->ndim == 2 && !d->causal && (sq3 || !g.has_conv) &&
       (d->dtype == HYFFT_BF16 || d->dtype == HYFFT_F32) && d->channels % 8 == 0 && d->in_pos_stride % 8 == 0 &&
       d->in_batch_stride % 8 == 0 && d->out_pos_stride % 8 == 0 && d->out_batch_stride % 8 == 0) {
-    h.fused = fused2d_dispatch(FOP_PROBE, d->dtype, h.cp.g.N[0], h.cp.g.N[1], h.cp.g.F[0], h.cp.g.F[1], h.SK,
-                               nullptr, nullptr) == HYFFT_OK;
+    // the shortest compiled transform first (e.g. 24 = 3 * 8 for a 14-point axis and a 14-tap
+    // filter), else the power-of-two length of the general plan
+    const int f0 = fused_fft_len(h.cp.g.N[0], h.cp.g.K[0]), f1 = fused_fft_len(h.cp.g.N[1], h.cp.g.K[1]);
+    if (!getenv("HYFFT_FUSED_POW2") && fused2d_dispatch(FOP_PROBE, d->dtype, h.cp.g.N[0], h.cp.g.N[1], f0, f1, h.SK,
+                                                        nullptr, nullptr) == HYFFT_OK) {
+      h.fused = true;
+      h.fF[0] = f0;
+      h.fF[1] = f1;
+    } else if (fused2d_dispatch(FOP_PROBE, d->dtype, h.cp.g.N[0], h.cp.g.N[1], h.cp.g.F[0], h.cp.g.F[1], h.SK,
+                                nullptr, nullptr) == HYFFT_OK) {
+      h.fused = true;
+      h.fF[0] = h.cp.g.F[0];
+      h.fF[1] = h.cp.g.F[1];
+    }
     // bf16 grids with both sides <= 16: the long conv as a tcgen05 Toeplitz GEMM
     const int N0 = h.cp.g.N[0], N1 = h.cp.g.N[1], K0 = h.cp.g.K[0], K1 = h.cp.g.K[1];
     // (opt-in while its CUDA-core stencil / reduction phases are slower than the fused FFT kernels)
@@ -1019,7 +1046,7 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
     return;
   }
   if (h.fused) {
-    const size_t spec = align_up((size_t)h.d.channels * h.cp.g.vol_F * sizeof(float2));
+    const size_t spec = align_up((size_t)h.d.channels * h.fF[0] * h.fF[1] * sizeof(float2));
     saved = spec;  // filter spectrum, reused by the backward
     fwd = 256;
     bwd = spec;    // dK spectrum accumulator
@@ -1331,7 +1358,7 @@ static void fused_params(const HyenaPlan& h, Fused2DParams& p, const void* q, co
 
 static int fused_op(const HyenaPlan& h, int op, const Fused2DParams& p, cudaStream_t st, const char* what) {
   const Geo& g = h.cp.g;
-  const int rc = fused2d_dispatch(op, h.d.dtype, g.N[0], g.N[1], g.F[0], g.F[1], h.SK, &p, st);
+  const int rc = fused2d_dispatch(op, h.d.dtype, g.N[0], g.N[1], h.fF[0], h.fF[1], h.SK, &p, st);
   if (rc != HYFFT_OK) return fail(rc == HYFFT_ERR_UNSUPPORTED ? rc : HYFFT_ERR_CUDA, "%s launch failed", what);
   return HYFFT_OK;
 }
@@ -1370,7 +1397,7 @@ static int hyena_fused_backward(const HyenaPlan& h, const void* q, const void* k
   p.dD = dD;
   p.dw = h.sg.has_conv ? dsw : nullptr;
   p.db = h.sg.has_bias ? dsb : nullptr;
-  cudaMemsetAsync(p.G, 0, sizeof(float2) * (size_t)d.channels * h.cp.g.vol_F, st);
+  cudaMemsetAsync(p.G, 0, sizeof(float2) * (size_t)d.channels * h.fF[0] * h.fF[1], st);
   cudaMemsetAsync(dD, 0, sizeof(float) * d.channels, st);
   if (p.dw) cudaMemsetAsync(p.dw, 0, sizeof(float) * 3 * (size_t)d.channels * h.sg.ntaps, st);
   if (p.db) cudaMemsetAsync(p.db, 0, sizeof(float) * 3 * (size_t)d.channels, st);

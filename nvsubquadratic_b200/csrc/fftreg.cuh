@@ -1,4 +1,5 @@
-// Fully unrolled register FFTs (one thread per transform) for short axes.
+// Fully unrolled register FFTs (one thread per transform) for short axes of length
+// 2^m or 3 * 2^m.
 //
 // fft_dif<N, NIN, SIGN>: natural-order input with v[NIN..N) known to be zero,
 //   decimation in frequency; the output is in bit-reversed order.
@@ -116,11 +117,71 @@ struct DifStage {
   }
 };
 
+__host__ __device__ constexpr bool is_pow2(int n) { return n >= 1 && (n & (n - 1)) == 0; }
+__host__ __device__ constexpr int imin(int a, int b) { return a < b ? a : b; }
+
+// 3-point DFT in place, X_k = sum_n x_n exp(SIGN 2 pi i n k / 3); ZB / ZC: b / c known zero.
+template <int SIGN, bool ZB, bool ZC>
+__device__ __forceinline__ void dft3(float2& a, float2& b, float2& c) {
+  constexpr float h = 0.86602540378443864676f;  // sqrt(3) / 2
+  if constexpr (ZB && ZC) {
+    b = a;
+    c = a;
+  } else {
+    const float2 s = ZC ? b : (ZB ? c : make_float2(b.x + c.x, b.y + c.y));        // b + c
+    const float2 d = ZC ? b : (ZB ? make_float2(-c.x, -c.y) : make_float2(b.x - c.x, b.y - c.y));  // b - c
+    const float2 m = make_float2(fmaf(-0.5f, s.x, a.x), fmaf(-0.5f, s.y, a.y));
+    const float2 r = make_float2(-SIGN * h * d.y, SIGN * h * d.x);  // SIGN * (sqrt(3)/2) * i * (b - c)
+    a = make_float2(a.x + s.x, a.y + s.y);
+    b = make_float2(m.x + r.x, m.y + r.y);
+    c = make_float2(m.x - r.x, m.y - r.y);
+  }
+}
+
+// ---------------------------------------------------------------- N = 3 * M (M a power of two)
+// With n = n1 + M n2 and k = 3 k1 + k2: forward = 3-point DFTs over n2, twiddles
+// W_N^(n1 k2), then M-point DIFs over n1 on the contiguous segments v[M k2 .. M k2 + M).
+// The spectrum is left as v[M k2 + j] = X[3 bitrev_M(j) + k2]; the inverse (DIT) below
+// consumes exactly that order and returns natural order.
+template <int M, int NIN, int SIGN, int N1>
+struct Mix3Dif {
+  static __device__ __forceinline__ void run(float2* v) {
+    if constexpr (N1 < M && N1 < NIN) {  // columns n1 >= NIN are all zero and stay zero
+      constexpr bool zb = N1 + M >= NIN, zc = N1 + 2 * M >= NIN;
+      dft3<SIGN, zb, zc>(v[N1], v[N1 + M], v[N1 + 2 * M]);
+      v[N1 + M] = twmul<N1, 3 * M, SIGN>(v[N1 + M]);
+      v[N1 + 2 * M] = twmul<2 * N1, 3 * M, SIGN>(v[N1 + 2 * M]);
+      Mix3Dif<M, NIN, SIGN, N1 + 1>::run(v);
+    }
+  }
+};
+template <int M, int NOUT, int SIGN, int N1>
+struct Mix3Dit {
+  static __device__ __forceinline__ void run(float2* v) {
+    if constexpr (N1 < M && N1 < NOUT) {  // outputs n = n1 + M n2 >= n1: columns n1 >= NOUT are not needed
+      v[N1 + M] = twmul<N1, 3 * M, SIGN>(v[N1 + M]);
+      v[N1 + 2 * M] = twmul<2 * N1, 3 * M, SIGN>(v[N1 + 2 * M]);
+      dft3<SIGN, false, false>(v[N1], v[N1 + M], v[N1 + 2 * M]);
+      Mix3Dit<M, NOUT, SIGN, N1 + 1>::run(v);
+    }
+  }
+};
+
 template <int N, int NIN, int SIGN>
 __device__ __forceinline__ void fft_dif(float2* v) {
-  static_assert(N >= 1 && N <= 64 && (N & (N - 1)) == 0, "N must be a power of two <= 64");
   static_assert(NIN >= 1 && NIN <= N, "bad NIN");
-  DifStage<N, N / 2, ~low_mask(NIN) & low_mask(N), SIGN>::run(v);
+  if constexpr (is_pow2(N)) {
+    static_assert(N <= 64, "N must be <= 64");
+    DifStage<N, N / 2, ~low_mask(NIN) & low_mask(N), SIGN>::run(v);
+  } else {
+    static_assert(N % 3 == 0 && is_pow2(N / 3) && N / 3 <= 32, "N must be 2^m or 3 * 2^m");
+    constexpr int M = N / 3;
+    Mix3Dif<M, NIN, SIGN, 0>::run(v);
+    constexpr int NS = imin(NIN, M);  // segment inputs n1 >= NIN are zero
+    DifStage<M, M / 2, ~low_mask(NS) & low_mask(M), SIGN>::run(v);
+    DifStage<M, M / 2, ~low_mask(NS) & low_mask(M), SIGN>::run(v + M);
+    DifStage<M, M / 2, ~low_mask(NS) & low_mask(M), SIGN>::run(v + 2 * M);
+  }
 }
 
 // ---------------------------------------------------------------- DIT (output pruning)
@@ -172,9 +233,19 @@ struct DitStage {
 
 template <int N, int NOUT, int SIGN>
 __device__ __forceinline__ void fft_dit(float2* v) {
-  static_assert(N >= 1 && N <= 64 && (N & (N - 1)) == 0, "N must be a power of two <= 64");
   static_assert(NOUT >= 1 && NOUT <= N, "bad NOUT");
-  DitStage<N, NOUT, 1, SIGN>::run(v);
+  if constexpr (is_pow2(N)) {
+    static_assert(N <= 64, "N must be <= 64");
+    DitStage<N, NOUT, 1, SIGN>::run(v);
+  } else {
+    static_assert(N % 3 == 0 && is_pow2(N / 3) && N / 3 <= 32, "N must be 2^m or 3 * 2^m");
+    constexpr int M = N / 3;
+    constexpr int NS = imin(NOUT, M);  // segment outputs n1 >= NOUT are not needed
+    DitStage<M, NS, 1, SIGN>::run(v);
+    DitStage<M, NS, 1, SIGN>::run(v + M);
+    DitStage<M, NS, 1, SIGN>::run(v + 2 * M);
+    Mix3Dit<M, NOUT, SIGN, 0>::run(v);
+  }
 }
 
 __host__ __device__ constexpr int bitrev(int i, int n) {

@@ -634,6 +634,8 @@ struct Fused2D {
 
 // Every (grid, FFT size, short-conv size) the fused path is compiled for.
 #define HYFFT_FUSED2D_SHAPES(X) \
+  X(14, 14, 24, 24)             \
+  X(16, 16, 24, 24)             \
   X(14, 14, 32, 32)             \
   X(16, 16, 32, 32)             \
   X(12, 10, 32, 32)             \

@@ -127,6 +127,10 @@ FUSED_CASES = [
     (3, 16, (14, 14), (27, 27), 3, "silu", "sigmoid", torch.bfloat16, True),
     (5, 8, (16, 16), (31, 31), 0, "sigmoid", "silu", torch.float32, False),
     (2, 24, (8, 8), (15, 15), 3, "silu", "identity", torch.float32, True),
+    # 24 = 3 * 8 point transforms (mixed radix) next to their power-of-two fallback
+    (4, 16, (14, 14), (14, 14), 3, "silu", "sigmoid", torch.float32, True),
+    (3, 8, (16, 16), (16, 16), 0, "identity", "silu", torch.float32, False),
+    (5, 8, (14, 14), (13, 13), 3, "sigmoid", "identity", torch.bfloat16, False),
 ]
 
 
@@ -143,9 +147,10 @@ def test_fused_path_matches_general_engine(case, monkeypatch):
     dy = torch.randn((B,) + S + (C,), generator=g).to(dt)
     outs = []
     # tensor-core Toeplitz kernels (bf16 grids <= 16x16, opt-in), default fused FFT kernels,
-    # general multi-pass engine
-    for env in ({"HYFFT_USE_TP": "1"}, {}, {"HYFFT_DISABLE_FUSED": "1"}):
-        for key in ("HYFFT_USE_TP", "HYFFT_DISABLE_FUSED"):
+    # fused kernels on power-of-two transforms only, general multi-pass engine
+    envs = ({"HYFFT_USE_TP": "1"}, {}, {"HYFFT_FUSED_POW2": "1"}, {"HYFFT_DISABLE_FUSED": "1"})
+    for env in envs:
+        for key in ("HYFFT_USE_TP", "HYFFT_FUSED_POW2", "HYFFT_DISABLE_FUSED"):
             if key in env:
                 monkeypatch.setenv(key, env[key])
             else:
@@ -158,8 +163,8 @@ def test_fused_path_matches_general_engine(case, monkeypatch):
         torch.cuda.synchronize()
         outs.append([y, qkv_d.grad] + [t.grad if t is not None else None for t in rest])
     tol = 2e-2 if dt == torch.bfloat16 else 1e-5
-    for variant in (0, 1):
-        for name, a, b in zip(("y", "dqkv", "dfilt", "dD", "dsw", "dsb"), outs[2], outs[variant]):
+    for variant in (0, 1, 2):
+        for name, a, b in zip(("y", "dqkv", "dfilt", "dD", "dsw", "dsb"), outs[3], outs[variant]):
             if a is None:
                 continue
             assert rel_l2(a, b) <= tol, (variant, name, rel_l2(a, b))
