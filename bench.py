@@ -43,7 +43,7 @@ CONFIGS = {
                  desc="1D causal FFT long conv + D skip, fp32 (reference CPU case)"),
     "cfg1": dict(nd=2, B=32, C=768, S=(14, 14), K=(14, 14), short=3, g1="identity", g2="identity",
                  dtype=torch.bfloat16, causal=False, shard="replica",
-                 desc="2D HyenaND ViT-B grid 14x14, SIREN-style 14x14 filter, F=32x32, 3x3 short conv"),
+                 desc="2D HyenaND ViT-B grid 14x14, SIREN-style 14x14 filter, F=24x24 (linear-conv length 21 padded to 3*2^3), 3x3 short conv"),
     "cfg2": dict(nd=2, B=8, C=256, S=(128, 128), K=(128, 128), short=3, g1="identity", g2="identity",
                  dtype=torch.bfloat16, causal=False, shard="batch",
                  desc="2D HyenaND 128x128, exp-radial 128x128 filter, F=256x256, batch-sharded"),

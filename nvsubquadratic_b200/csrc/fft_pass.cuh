@@ -425,4 +425,154 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
   }
 }
 
+// ---------------------------------------------------------------- channel-innermost complex passes
+// Complex -> complex pass over lines whose neighbours are neighbouring channels (the
+// channel index has unit stride in every spectrum buffer), F = R1 * R2 <= 256 and no
+// four-step twiddle: the middle passes of 2D / 3D transforms. Each lane of a warp owns
+// one of 32 consecutive lines, so every global access of a warp is 32 neighbouring
+// complex values. The transform is a two-level decomposition, t = j + R2 r and
+// k = k1 + R1 k2:
+//   X[k1 + R1 k2] = sum_j W_R2^(j k2) W_F^(j k1) sum_r W_R1^(r k1) x[j + R2 r],
+// level one in registers straight from global memory, the transposition through shared
+// memory laid out [point][line] (conflict-free: a warp touches 32 neighbouring words),
+// level two in registers straight to global memory. All reads of global memory happen
+// before the first barrier, so the pass may run in place.
+// MID != 0 (product pass): forward transform, product with the kernel spectrum (MID == 2:
+// its conjugate), inverse transform, mirrored through shared memory a second time.
+// DIR: direction of a plain pass (-1 forward, +1 inverse); MID passes are forward first.
+constexpr int kClWarps = 8;
+
+template <int F>
+__host__ __device__ constexpr int cl_lines_per_cta() { return F >= 128 ? 32 : 32 * (128 / F); }
+
+template <int F>
+__host__ __device__ constexpr size_t cl_smem_bytes() {
+  return sizeof(float2) * ((size_t)F * cl_lines_per_cta<F>() + F) + 3 * sizeof(long long) * cl_lines_per_cta<F>();
+}
+
+template <int R1, int R2, int MID, int DIR>
+__global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassDesc d) {
+  constexpr int F = R1 * R2;
+  constexpr int NL = cl_lines_per_cta<F>();  // lines per CTA
+  constexpr int G = NL / 32;                 // groups of 32 lines
+  constexpr float D1 = MID ? -1.f : (float)DIR;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float2* sm = reinterpret_cast<float2*>(smem_raw);        // [F][NL]
+  float2* tw = sm + F * NL;                                 // [F] e^{-2 pi i m / F}
+  long long* cb_in = reinterpret_cast<long long*>(tw + F);  // [NL] line bases, -1: past the end
+  long long* cb_out = cb_in + NL;
+  long long* kbase = cb_out + NL;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long line0 = (long long)blockIdx.x * NL;
+  for (int m = threadIdx.x; m < F; m += blockDim.x) {
+    float sn, cs;
+    sincospif(2.0f * (float)m / (float)F, &sn, &cs);
+    tw[m] = make_float2(cs, -sn);
+  }
+  for (int l = threadIdx.x; l < NL; l += blockDim.x) {
+    const long long lid = line0 + l;
+    if (lid >= d.nlines) {
+      cb_in[l] = cb_out[l] = kbase[l] = -1;
+      continue;
+    }
+    const int c = (int)(lid % d.C);
+    long long rest = lid / d.C;
+    int o[2] = {0, 0};
+    for (int a = d.n_oth - 1; a >= 0; --a) {
+      o[a] = (int)(rest % d.oth_ext[a]);
+      rest /= d.oth_ext[a];
+    }
+    const long long p = rest;
+    cb_in[l] = p * d.ci_pst + (long long)o[0] * d.ci_ost[0] + (long long)o[1] * d.ci_ost[1] + c;
+    cb_out[l] = p * d.co_pst + (long long)o[0] * d.co_ost[0] + (long long)o[1] * d.co_ost[1] + c;
+    if (MID)
+      kbase[l] = (d.k_shared ? 0 : p) * d.k_pst + (long long)o[0] * d.k_ost[0] + (long long)o[1] * d.k_ost[1] + c;
+  }
+  __syncthreads();
+
+  // level one: R1-point transforms over r of x[j + R2 r], twiddle W_F^(j k1) -> sm[k1 R2 + j]
+  for (int it = warp; it < G * R2; it += kClWarps) {
+    const int g = it / R2, j = it % R2, l = g * 32 + lane;
+    const long long base = cb_in[l];
+    float2 v[R1];
+    const float2* src = d.cin + base + (long long)(j - d.in_off) * d.ci_tst;
+    const long long step = (long long)R2 * d.ci_tst;
+#pragma unroll
+    for (int r = 0; r < R1; ++r) {
+      const int bi = j + R2 * r - d.in_off;
+      v[r] = (base >= 0 && bi >= 0 && bi < d.n_in) ? src[r * step] : make_float2(0.f, 0.f);
+    }
+    dftR<R1>(v, D1);
+#pragma unroll
+    for (int k1 = 0; k1 < R1; ++k1) {
+      float2 a = v[k1];
+      if (k1 > 0 && j > 0) {
+        float2 w = tw[j * k1];
+        if (D1 > 0.f) w.y = -w.y;
+        a = cmul(a, w);
+      }
+      sm[(k1 * R2 + j) * NL + l] = a;
+    }
+  }
+  __syncthreads();
+
+  // level two: R2-point transforms over j -> X[k1 + R1 k2]
+  for (int it = warp; it < G * R1; it += kClWarps) {
+    const int g = it / R1, k1 = it % R1, l = g * 32 + lane;
+    float2 v[R2];
+#pragma unroll
+    for (int j = 0; j < R2; ++j) v[j] = sm[(k1 * R2 + j) * NL + l];
+    dftR<R2>(v, D1);
+    if constexpr (MID) {
+      const long long kb = kbase[l];
+      if (kb >= 0) {
+#pragma unroll
+        for (int k2 = 0; k2 < R2; ++k2) {
+          float2 kv = __ldg(d.kin + kb + (long long)(k1 + R1 * k2) * d.k_tst);
+          if (MID == 2) kv.y = -kv.y;
+          v[k2] = cmul(v[k2], kv);
+        }
+      }
+      dftR<R2>(v, 1.f);  // inverse over k2 -> j, then W_F^(-j k1)
+#pragma unroll
+      for (int j = 0; j < R2; ++j) {
+        float2 a = v[j];
+        if (k1 > 0 && j > 0) {
+          const float2 w = tw[j * k1];
+          a = cmul(a, make_float2(w.x, -w.y));
+        }
+        sm[(k1 * R2 + j) * NL + l] = a;
+      }
+    } else {
+      const long long ob = cb_out[l];
+      if (ob >= 0) {
+#pragma unroll
+        for (int k2 = 0; k2 < R2; ++k2) {
+          const int bo = k1 + R1 * k2 - d.out_lo;
+          if (bo >= 0 && bo < d.n_out) d.cout[ob + (long long)bo * d.co_tst] = cscale(v[k2], d.scale);
+        }
+      }
+    }
+  }
+  if constexpr (MID) {
+    __syncthreads();
+    // inverse level one: R1-point transforms over k1 -> x[j + R2 r]
+    for (int it = warp; it < G * R2; it += kClWarps) {
+      const int g = it / R2, j = it % R2, l = g * 32 + lane;
+      const long long ob = cb_out[l];
+      float2 v[R1];
+#pragma unroll
+      for (int k1 = 0; k1 < R1; ++k1) v[k1] = sm[(k1 * R2 + j) * NL + l];
+      dftR<R1>(v, 1.f);
+      if (ob >= 0) {
+#pragma unroll
+        for (int r = 0; r < R1; ++r) {
+          const int bo = j + R2 * r - d.out_lo;
+          if (bo >= 0 && bo < d.n_out) d.cout[ob + (long long)bo * d.co_tst] = cscale(v[r], d.scale);
+        }
+      }
+    }
+  }
+}
+
 }  // namespace hyfft

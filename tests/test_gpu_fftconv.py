@@ -105,6 +105,14 @@ def test_ops_vs_oracle_seeded(case):
     assert rel_l2(sr.grad, ds) <= tol, rel_l2(sr.grad, ds)
 
 
+@pytest.mark.parametrize("case", [SHAPES[3], SHAPES[1], SHAPES[8]], ids=["2d-64", "1d-four-step", "3d-ragged"])
+def test_generic_pass_kernel_matches_oracle(case, monkeypatch):
+    """With the channel-innermost two-level kernel switched off, the generic strided pass
+    kernel (which keeps the real-I/O and four-step passes) runs the complex middle passes."""
+    monkeypatch.setenv("HYFFT_DISABLE_CL_PASS", "1")
+    test_ops_vs_oracle_seeded(case)
+
+
 def test_per_sample_kernel_and_odd_batch():
     g = torch.Generator().manual_seed(1)
     b2 = _b2()
