@@ -30,6 +30,7 @@
 #include "fft_pass.cuh"
 #include "big2d.h"
 #include "hyena_elem.cuh"
+#include "stencil3d.cuh"
 #include "pointwise.cuh"
 #include "fused2d.h"
 
@@ -1128,6 +1129,48 @@ static void with_stencil(const StencilGeom& g, F&& f) {
   else f(IC<-1>{}, IC<-1>{}, IC<-1>{});
 }
 
+// ------------------------------------------------------------------ 3D plane-marching stencils
+// 3x3x3 short convs of 16-bit channels-last activations run on the plane-marching kernels
+// (stencil3d.cuh) when every 16-byte chunk of 8 channels is aligned.
+template <typename T>
+static bool plane_stencil_ok(const HyenaPlan& h, std::initializer_list<const void*> ps) {
+  const hyfft_hyena_desc& d = h.d;
+  if (sizeof(T) != 2 || d.ndim != 3 || !h.sg.has_conv || h.sg.k[0] != 3 || h.sg.k[1] != 3 || h.sg.k[2] != 3 ||
+      getenv("HYFFT_DISABLE_PLANE_STENCIL"))
+    return false;
+  if (d.channels % 8 || d.in_batch_stride % 8 || d.in_pos_stride % 8) return false;
+  for (const void* p : ps)
+    if (p && ((uintptr_t)p % 16) != 0) return false;
+  return true;
+}
+
+struct PlaneLaunch {
+  dim3 grid;
+  int xchunk;
+};
+// x runs per CTA such that the grid fills about two waves of two CTAs per SM.
+static PlaneLaunch plane_launch(const HyenaPlan& h) {
+  const StencilGeom& g = h.sg;
+  const long long base = (long long)((h.d.channels + kElemCG - 1) / kElemCG) * ((g.n[1] + kS3TY - 1) / kS3TY) *
+                         ((g.n[2] + kS3TZ - 1) / kS3TZ) * h.d.batch;
+  const long long nxc = std::max<long long>(1, std::min<long long>(g.n[0], (4 * 148 + base - 1) / base));
+  PlaneLaunch pl;
+  pl.xchunk = (int)((g.n[0] + nxc - 1) / nxc);
+  const long long chunks = (g.n[0] + pl.xchunk - 1) / pl.xchunk;
+  pl.grid = dim3((unsigned)((h.d.channels + kElemCG - 1) / kElemCG),
+                 (unsigned)(((g.n[1] + kS3TY - 1) / kS3TY) * ((g.n[2] + kS3TZ - 1) / kS3TZ)),
+                 (unsigned)(h.d.batch * chunks));
+  return pl;
+}
+
+template <typename K>
+static int allow_smem(K kernel, size_t bytes, const char* name) {
+  if (bytes > 48 * 1024 &&
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
+    return fail(HYFFT_ERR_CUDA, "%s: cannot allow %zu bytes of shared memory", name, bytes);
+  return HYFFT_OK;
+}
+
 // Rows of (b, position) per CTA column so that a warp walks about `per_warp` rows.
 static dim3 elem_grid(int C, long long rows, long long per_warp) {
   const long long gy = std::max<long long>(1, std::min<long long>(65535, (rows + 8 * per_warp - 1) / (8 * per_warp)));
@@ -1165,6 +1208,18 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
       if constexpr (K0 > 0 && K1 > 0 && K2 > 0) {
         constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
         constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
+        if constexpr (ND == 3 && P && sizeof(T) == 2 && KA == 3 && KB == 3 && KI == 3) {
+          if (plane_stencil_ok<T>(h, {q, k, v})) {
+            const PlaneLaunch pl = plane_launch(h);
+            constexpr size_t sm = s3_smem_bytes<3, 3>();
+            if (allow_smem(hyena_plane_stencil_kernel<T, 3, 3, 3, 0>, sm, "hyena_plane_stencil_kernel") != HYFFT_OK)
+              return;
+            hyena_plane_stencil_kernel<T, 3, 3, 3, 0><<<pl.grid, kElemThreads, sm, st>>>(
+                q, k, v, d.in_batch_stride, d.in_pos_stride, qs, ks, vs, 0, 0, z, h.sg, d.channels, sw, sb, d.gate1,
+                pl.xchunk);
+            return;
+          }
+        }
         if (d.ndim == ND) {
           const long long nl = h.sg.n[ND - 1];
           const long long items = (long long)d.batch * (h.Ntot / nl) * ((nl + 63) / 64);
@@ -1300,6 +1355,18 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
       if constexpr (K0 > 0 && K1 > 0 && K2 > 0) {
         constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
         constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
+        if constexpr (ND == 3 && P && sizeof(T) == 2 && KA == 3 && KB == 3 && KI == 3) {
+          if (plane_stencil_ok<T>(h, {dqp, dkp, dvp}) && d.out_batch_stride % 2 == 0 && d.out_pos_stride % 2 == 0) {
+            const PlaneLaunch pl = plane_launch(h);
+            constexpr size_t sm = s3_smem_bytes<3, 3>();
+            if (allow_smem(hyena_plane_stencil_kernel<T, 3, 3, 3, 1>, sm, "hyena_plane_stencil_kernel") != HYFFT_OK)
+              return;
+            hyena_plane_stencil_kernel<T, 3, 3, 3, 1><<<pl.grid, kElemThreads, sm, st>>>(
+                dqp, dkp, dvp, 0, 0, dq, dk, dv, d.out_batch_stride, d.out_pos_stride, nullptr, h.sg, d.channels, sw,
+                nullptr, 0, pl.xchunk);
+            return;
+          }
+        }
         if (d.ndim == ND) {
           const long long nl = h.sg.n[ND - 1];
           const long long items = (long long)d.batch * (h.Ntot / nl) * ((nl + 63) / 64);
@@ -1336,6 +1403,17 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
           // sliding-window form: 1D (k,1,1), 2D (k0,k1,1), 3D (k0,k1,k2) along the innermost axis
           constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
           constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
+          if constexpr (ND == 3 && P && sizeof(T) == 2 && KA == 3 && KB == 3 && KI == 3) {
+            if (plane_stencil_ok<T>(h, {q, k, v, dqp, dkp, dvp})) {
+              const PlaneLaunch pl = plane_launch(h);
+              constexpr size_t sm = s3_smem_bytes<3, 3>();
+              if (allow_smem(hyena_plane_wgrad_kernel<T, 3, 3, 3>, sm, "hyena_plane_wgrad_kernel") != HYFFT_OK) return;
+              hyena_plane_wgrad_kernel<T, 3, 3, 3><<<pl.grid, kElemThreads, sm, st>>>(
+                  dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.channels, dsw,
+                  h.sg.has_bias ? dsb : nullptr, pl.xchunk);
+              return;
+            }
+          }
           if (d.ndim == ND) {
             const long long nl = h.sg.n[ND - 1];
             const long long items = (long long)d.batch * (h.Ntot / nl) * ((nl + 63) / 64);

@@ -69,6 +69,10 @@ CASES = [
     (1, 2, 16, (1024,), (1024,), 7, True, "identity", "identity", torch.bfloat16, False, True),
     (1, 1, 8, (8192,), (8192,), 7, True, "sigmoid", "silu", torch.float32, False, False),
     (3, 2, 4, (8, 8, 8), (8, 8, 8), 3, False, "silu", "silu", torch.float32, False, True),
+    # 3D 3x3x3 short conv on the plane-marching kernels (16-bit, channels a multiple of 8):
+    # a channel tail block, ragged y / z tiles, bias, strided q/k/v views
+    (3, 2, 72, (9, 13, 37), (9, 13, 37), 3, False, "silu", "sigmoid", torch.bfloat16, True, True),
+    (3, 3, 16, (6, 5, 20), (11, 9, 39), 3, False, "identity", "identity", torch.bfloat16, False, False),
     (2, 3, 8, (12, 10), (23, 19), 0, False, "identity", "sigmoid", torch.float32, False, False),
     # large-grid 2D kernels (F = 256 x 256)
     (2, 2, 8, (128, 128), (128, 128), 3, False, "silu", "sigmoid", torch.bfloat16, False, True),
