@@ -218,6 +218,31 @@ static int launch_cl(const PassDesc& d, cudaStream_t st) {
     default: return launch_cl_f<16, 16>(d, st);
   }
 }
+template <int R1, int R2>
+static int launch_cl_bwd_t(const PassDesc& fx, const PassDesc& fdy, const PassDesc& idx, const PassDesc& idk, int pl,
+                           cudaStream_t st) {
+  constexpr int F = R1 * R2;
+  const long long nl = fx.nlines / pl;
+  const long long grid = (nl + cl_lines_per_cta<F>() - 1) / cl_lines_per_cta<F>();
+  if (grid <= 0) return HYFFT_OK;
+  if (grid > 0x7fffffffLL) return fail(HYFFT_ERR_UNSUPPORTED, "too many FFT lines");
+  constexpr size_t smem = cl_bwd_smem_bytes<R1, R2>();
+  if (smem > 48 * 1024 && cudaFuncSetAttribute(fft_lines_cl_bwd_kernel<R1, R2>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return fail(HYFFT_ERR_CUDA, "fft_lines_cl_bwd_kernel: cannot allow %zu bytes of shared memory", smem);
+  fft_lines_cl_bwd_kernel<R1, R2><<<(unsigned)grid, kClWarps * 32, smem, st>>>(fx, fdy, idx, idk, pl);
+  return check_launch("fft_lines_cl_bwd_kernel");
+}
+static int launch_cl_bwd(const PassDesc& fx, const PassDesc& fdy, const PassDesc& idx, const PassDesc& idk, int pl,
+                         cudaStream_t st) {
+  switch (fx.F) {
+    case 32: return launch_cl_bwd_t<8, 4>(fx, fdy, idx, idk, pl, st);
+    case 64: return launch_cl_bwd_t<16, 4>(fx, fdy, idx, idk, pl, st);
+    case 128: return launch_cl_bwd_t<16, 8>(fx, fdy, idx, idk, pl, st);
+    default: return launch_cl_bwd_t<16, 16>(fx, fdy, idx, idk, pl, st);
+  }
+}
+
 static bool cl_pass_applies(const PassDesc& d, int im, int om) {
   return im == IN_CPLX && om == OUT_CPLX && d.tw_logF == 0 && (d.F == 32 || d.F == 64 || d.F == 128 || d.F == 256) &&
          !getenv("HYFFT_DISABLE_CL_PASS");
@@ -677,6 +702,50 @@ static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView&
   return inv_chain(p.g, Cc, S, yc, p.dt, p.px, p.g.crop, p.g.N, ep, st);
 }
 
+// Backward with the last forward passes of x and dy, the spectral products and the first
+// inverse passes of dx and dK merged into one backward product pass (complex passes of
+// 32..256 points along the first axis, 2D / 3D). Returns HYFFT_ERR_UNSUPPORTED (nothing
+// launched) when the passes do not line up.
+static int fused_bwd_chain(const ConvPlan& p, int Cc, const RealView& xc, const RealView& dyc, const RealView& dxc,
+                           const RealView& dkc, const Epilogue& ep, float2* S1, float2* S2, const float2* Kh,
+                           float2* dKh, cudaStream_t st) {
+  const int zero[3] = {0, 0, 0};
+  if (getenv("HYFFT_DISABLE_BWD_PASS") || p.g.four || p.g.D < 2) return HYFFT_ERR_UNSUPPORTED;
+  PassList fx, fy, ix, ik;
+  HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S1, st, &fx));
+  HY_TRY(fwd_chain(p.g, Cc, dyc, p.dt, p.px, p.g.N, p.g.crop, S2, st, &fy));
+  HY_TRY(inv_chain(p.g, Cc, S2, dxc, p.dt, p.px, zero, p.g.N, ep, st, &ix));
+  Epilogue none;
+  HY_TRY(inv_chain(p.g, Cc, dKh, dkc, HYFFT_F32, p.pk, zero, p.g.K, none, st, &ik));
+  if (fx.n < 2 || fy.n < 2 || ix.n < 2 || ik.n < 2) return HYFFT_ERR_UNSUPPORTED;
+  PassDesc a = fx.r[fx.n - 1].d;
+  const PassDesc& b = fy.r[fy.n - 1].d;
+  const PassDesc& c = ix.r[0].d;
+  const PassDesc& k = ik.r[0].d;
+  const bool cplx = fx.r[fx.n - 1].im == IN_CPLX && fy.r[fy.n - 1].im == IN_CPLX && ix.r[0].om == OUT_CPLX &&
+                    ik.r[0].om == OUT_CPLX;
+  bool same = cplx && a.F == b.F && a.F == c.F && a.F == k.F && a.n_oth == c.n_oth && a.n_oth == k.n_oth &&
+              a.nlines == b.nlines && a.nlines == c.nlines && a.tw_logF == 0 && c.tw_logF == 0 &&
+              (a.F == 32 || a.F == 64 || a.F == 128 || a.F == 256);
+  for (int j = 0; j < a.n_oth; ++j)
+    same = same && a.oth_ext[j] == b.oth_ext[j] && a.oth_ext[j] == c.oth_ext[j] && a.oth_ext[j] == k.oth_ext[j];
+  if (!same) return HYFFT_ERR_UNSUPPORTED;
+  // Kh shares S's per-axis strides (the same [pair][F...][C] layout)
+  a.kin = Kh;
+  a.k_shared = p.shared ? 1 : 0;
+  a.k_pst = spec_strides(p.g, Cc).pst;
+  a.k_tst = a.ci_tst;
+  a.k_ost[0] = a.ci_ost[0];
+  a.k_ost[1] = a.ci_ost[1];
+  const int pl = p.shared ? p.px.P : 1;
+  for (int i = 0; i + 1 < fx.n; ++i) HY_TRY(launch_pass(fx.r[i].d, fx.r[i].im, fx.r[i].om, fx.r[i].tin, fx.r[i].tout, st));
+  for (int i = 0; i + 1 < fy.n; ++i) HY_TRY(launch_pass(fy.r[i].d, fy.r[i].im, fy.r[i].om, fy.r[i].tin, fy.r[i].tout, st));
+  HY_TRY(launch_cl_bwd(a, b, c, k, pl, st));
+  for (int i = 1; i < ix.n; ++i) HY_TRY(launch_pass(ix.r[i].d, ix.r[i].im, ix.r[i].om, ix.r[i].tin, ix.r[i].tout, st));
+  for (int i = 1; i < ik.n; ++i) HY_TRY(launch_pass(ik.r[i].d, ik.r[i].im, ik.r[i].om, ik.r[i].tin, ik.r[i].tout, st));
+  return HYFFT_OK;
+}
+
 static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView& xv, const RealView& kv,
                                const float* Dfull, const RealView& dyv, const RealView& dxv, const RealView& dkv,
                                float2* S1, float2* S2, float2* Kh, float2* dKh, cudaStream_t st) {
@@ -686,6 +755,17 @@ static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView
   const RealView dyc = offset_channels(dyv, c0, eb);
   const int zero[3] = {0, 0, 0};
   HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+  if (dxv.ptr && dkv.ptr) {
+    Epilogue ep;
+    if (Dfull) {
+      ep.mode = OUT_REAL_SKIP;
+      ep.skip = dyc.ptr;
+      ep.Dv = Dfull + c0;
+    }
+    const int rc = fused_bwd_chain(p, Cc, xc, dyc, offset_channels(dxv, c0, eb), offset_channels(dkv, c0, 4), ep, S1,
+                                   S2, Kh, dKh, st);
+    if (rc != HYFFT_ERR_UNSUPPORTED) return rc;
+  }
   HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S1, st));
   HY_TRY(fwd_chain(p.g, Cc, dyc, p.dt, p.px, p.g.N, p.g.crop, S2, st));
   const long long per_pair = p.g.vol_F * Cc;

@@ -575,4 +575,165 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
   }
 }
 
+// Backward product pass on the same two-level channel-innermost structure: for every
+// line along the last forward axis it transforms the partial spectra of x (fx) and dy
+// (fdy), forms DX = DY * conj(Kh) and DK = DY * conj(X) point by point, and inverse
+// transforms both, storing DX into the dx chain's buffer (idx: crop of the first inverse
+// pass) and DK into the kernel-gradient buffer (idk). With a kernel shared by the batch
+// (pl = number of pairs > 1) the CTA loops over the pairs of its lines and adds the
+// per-pair DK lines (the inverse transform is linear). With packed pairs the real part
+// of the inverse of DY * conj(X) is the sum of both items' correlations.
+// Kh: fx.kin with fx.k_* strides (k_shared: one kernel for all pairs).
+template <int R1, int R2>
+__host__ __device__ constexpr size_t cl_bwd_smem_bytes() {
+  return sizeof(float2) * (2 * (size_t)R1 * R2 * cl_lines_per_cta<R1 * R2>() + R1 * R2) +
+         5 * sizeof(long long) * cl_lines_per_cta<R1 * R2>();
+}
+
+template <int R1, int R2>
+__global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_bwd_kernel(const PassDesc fx, const PassDesc fdy,
+                                                                         const PassDesc idx, const PassDesc idk,
+                                                                         int pl) {
+  constexpr int F = R1 * R2;
+  constexpr int NL = cl_lines_per_cta<F>();
+  constexpr int G = NL / 32;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float2* sa = reinterpret_cast<float2*>(smem_raw);  // [F][NL]: X, then DK
+  float2* sb = sa + F * NL;                           // [F][NL]: DY, then DX
+  float2* tw = sb + F * NL;                           // [F] e^{-2 pi i m / F}
+  long long* bx = reinterpret_cast<long long*>(tw + F);
+  long long* bdy = bx + NL;
+  long long* bdx = bdy + NL;
+  long long* bdk = bdx + NL;
+  long long* bkh = bdk + NL;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const long long nl = fx.nlines / pl;
+  const long long line0 = (long long)blockIdx.x * NL;
+  for (int m = threadIdx.x; m < F; m += blockDim.x) {
+    float sn, cs;
+    sincospif(2.0f * (float)m / (float)F, &sn, &cs);
+    tw[m] = make_float2(cs, -sn);
+  }
+  for (int l = threadIdx.x; l < NL; l += blockDim.x) {
+    const long long lid = line0 + l;
+    if (lid >= nl) {
+      bx[l] = -1;
+      continue;
+    }
+    const int c = (int)(lid % fx.C);
+    long long rest = lid / fx.C;
+    int o[2] = {0, 0};
+    for (int a = fx.n_oth - 1; a >= 0; --a) {
+      o[a] = (int)(rest % fx.oth_ext[a]);
+      rest /= fx.oth_ext[a];
+    }
+    const long long p = rest;  // 0 when the CTA loops over the pairs
+    const long long ks = fx.k_shared ? 0 : p;
+    bx[l] = p * fx.ci_pst + (long long)o[0] * fx.ci_ost[0] + (long long)o[1] * fx.ci_ost[1] + c;
+    bdy[l] = p * fdy.ci_pst + (long long)o[0] * fdy.ci_ost[0] + (long long)o[1] * fdy.ci_ost[1] + c;
+    bdx[l] = p * idx.co_pst + (long long)o[0] * idx.co_ost[0] + (long long)o[1] * idx.co_ost[1] + c;
+    bdk[l] = ks * idk.co_pst + (long long)o[0] * idk.co_ost[0] + (long long)o[1] * idk.co_ost[1] + c;
+    bkh[l] = ks * fx.k_pst + (long long)o[0] * fx.k_ost[0] + (long long)o[1] * fx.k_ost[1] + c;
+  }
+  __syncthreads();
+
+#pragma unroll 1
+  for (int pp = 0; pp < pl; ++pp) {
+    // forward level one of X and DY
+    for (int it = warp; it < G * R2; it += kClWarps) {
+      const int g = it / R2, j = it % R2, l = g * 32 + lane;
+      const bool ok = bx[l] >= 0;
+      float2 u[R1], v[R1];
+      const float2* sx = fx.cin + (ok ? bx[l] : 0) + pp * fx.ci_pst + (long long)(j - fx.in_off) * fx.ci_tst;
+      const float2* sy = fdy.cin + (ok ? bdy[l] : 0) + pp * fdy.ci_pst + (long long)(j - fdy.in_off) * fdy.ci_tst;
+      const long long stx = (long long)R2 * fx.ci_tst, sty = (long long)R2 * fdy.ci_tst;
+#pragma unroll
+      for (int r = 0; r < R1; ++r) {
+        const int bix = j + R2 * r - fx.in_off, biy = j + R2 * r - fdy.in_off;
+        u[r] = (ok && bix >= 0 && bix < fx.n_in) ? sx[r * stx] : make_float2(0.f, 0.f);
+        v[r] = (ok && biy >= 0 && biy < fdy.n_in) ? sy[r * sty] : make_float2(0.f, 0.f);
+      }
+      dftR<R1>(u, -1.f);
+      dftR<R1>(v, -1.f);
+#pragma unroll
+      for (int k1 = 0; k1 < R1; ++k1) {
+        float2 a = u[k1], b = v[k1];
+        if (k1 > 0 && j > 0) {
+          const float2 w = tw[j * k1];
+          a = cmul(a, w);
+          b = cmul(b, w);
+        }
+        sa[(k1 * R2 + j) * NL + l] = a;
+        sb[(k1 * R2 + j) * NL + l] = b;
+      }
+    }
+    __syncthreads();
+    // level two, products, inverse level two
+    for (int it = warp; it < G * R1; it += kClWarps) {
+      const int g = it / R1, k1 = it % R1, l = g * 32 + lane;
+      float2 u[R2], v[R2];
+#pragma unroll
+      for (int j = 0; j < R2; ++j) {
+        u[j] = sa[(k1 * R2 + j) * NL + l];
+        v[j] = sb[(k1 * R2 + j) * NL + l];
+      }
+      dftR<R2>(u, -1.f);
+      dftR<R2>(v, -1.f);
+      const long long kb = bkh[l];
+      if (bx[l] >= 0) {
+#pragma unroll
+        for (int k2 = 0; k2 < R2; ++k2) {
+          const float2 kv = __ldg(fx.kin + kb + (long long)(k1 + R1 * k2) * fx.k_tst);
+          const float2 dk = cmulc(v[k2], u[k2]);  // DY * conj(X)
+          v[k2] = cmulc(v[k2], kv);               // DY * conj(Kh)
+          u[k2] = dk;
+        }
+      }
+      dftR<R2>(u, 1.f);
+      dftR<R2>(v, 1.f);
+#pragma unroll
+      for (int j = 0; j < R2; ++j) {
+        float2 a = u[j], b = v[j];
+        if (k1 > 0 && j > 0) {
+          const float2 w = tw[j * k1];
+          const float2 wc = make_float2(w.x, -w.y);
+          a = cmul(a, wc);
+          b = cmul(b, wc);
+        }
+        sa[(k1 * R2 + j) * NL + l] = a;
+        sb[(k1 * R2 + j) * NL + l] = b;
+      }
+    }
+    __syncthreads();
+    // inverse level one; DX into the dx chain, DK (accumulated over the pairs) into dKh
+    for (int it = warp; it < G * R2; it += kClWarps) {
+      const int g = it / R2, j = it % R2, l = g * 32 + lane;
+      if (bx[l] < 0) continue;
+      float2 u[R1], v[R1];
+#pragma unroll
+      for (int k1 = 0; k1 < R1; ++k1) {
+        u[k1] = sa[(k1 * R2 + j) * NL + l];
+        v[k1] = sb[(k1 * R2 + j) * NL + l];
+      }
+      dftR<R1>(u, 1.f);
+      dftR<R1>(v, 1.f);
+      float2* ox = idx.cout + bdx[l] + pp * idx.co_pst;
+      float2* ok = idk.cout + bdk[l];
+#pragma unroll
+      for (int r = 0; r < R1; ++r) {
+        const int t = j + R2 * r;
+        const int bo = t - idx.out_lo;
+        if (bo >= 0 && bo < idx.n_out) ox[(long long)bo * idx.co_tst] = cscale(v[r], idx.scale);
+        const int bk = t - idk.out_lo;
+        if (bk >= 0 && bk < idk.n_out) {
+          float2* q = ok + (long long)bk * idk.co_tst;
+          const float2 val = cscale(u[r], idk.scale);
+          *q = pp == 0 ? val : cadd(*q, val);
+        }
+      }
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace hyfft

@@ -113,6 +113,14 @@ def test_generic_pass_kernel_matches_oracle(case, monkeypatch):
     test_ops_vs_oracle_seeded(case)
 
 
+@pytest.mark.parametrize("case", [SHAPES[3], SHAPES[7]], ids=["2d-64", "3d-16"])
+def test_unfused_backward_matches_oracle(case, monkeypatch):
+    """The backward as separate passes plus the elementwise spectral kernel (the path taken
+    when the merged backward product pass does not apply)."""
+    monkeypatch.setenv("HYFFT_DISABLE_BWD_PASS", "1")
+    test_ops_vs_oracle_seeded(case)
+
+
 def test_per_sample_kernel_and_odd_batch():
     g = torch.Generator().manual_seed(1)
     b2 = _b2()
