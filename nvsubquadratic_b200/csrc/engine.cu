@@ -187,37 +187,60 @@ static int launch_pass_dt(const PassDesc& d, int tin, int tout, cudaStream_t st)
   return launch_pass_t<IM, OM, float, float>(d, st);
 }
 
-// Complex -> complex passes with F = 32 .. 256 and no four-step twiddle run on the
-// channel-innermost two-level kernel (fft_lines_cl_kernel).
-template <int R1, int R2, int MID, int DIR>
+// Passes with F = 32 .. 256, no four-step twiddle and channel-innermost lines (complex
+// spectra, channels-last activations) run on the two-level kernel (fft_lines_cl_kernel).
+template <int R1, int R2, int MID, int DIR, int IM, int OM, typename TI, typename TO>
 static int launch_cl_t(const PassDesc& d, cudaStream_t st) {
   constexpr int F = R1 * R2;
   const long long grid = (d.nlines + cl_lines_per_cta<F>() - 1) / cl_lines_per_cta<F>();
   if (grid <= 0) return HYFFT_OK;
   if (grid > 0x7fffffffLL) return fail(HYFFT_ERR_UNSUPPORTED, "too many FFT lines");
   constexpr size_t smem = cl_smem_bytes<F>();
+  auto kern = fft_lines_cl_kernel<R1, R2, MID, DIR, IM, OM, TI, TO>;
   if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(fft_lines_cl_kernel<R1, R2, MID, DIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return fail(HYFFT_ERR_CUDA, "fft_lines_cl_kernel: cannot allow %zu bytes of shared memory", smem);
-  fft_lines_cl_kernel<R1, R2, MID, DIR><<<(unsigned)grid, kClWarps * 32, smem, st>>>(d);
+  kern<<<(unsigned)grid, kClWarps * 32, smem, st>>>(d);
   return check_launch("fft_lines_cl_kernel");
 }
 template <int R1, int R2>
-static int launch_cl_f(const PassDesc& d, cudaStream_t st) {
-  if (d.mid == 1) return launch_cl_t<R1, R2, 1, -1>(d, st);
-  if (d.mid == 2) return launch_cl_t<R1, R2, 2, -1>(d, st);
-  if (d.dir < 0) return launch_cl_t<R1, R2, 0, -1>(d, st);
-  return launch_cl_t<R1, R2, 0, 1>(d, st);
+static int launch_cl_f(const PassDesc& d, int im, int om, int tin, int tout, cudaStream_t st) {
+  using bf = __nv_bfloat16;
+  if (im == IN_CPLX && om == OUT_CPLX) {
+    if (d.mid == 1) return launch_cl_t<R1, R2, 1, -1, IN_CPLX, OUT_CPLX, float, float>(d, st);
+    if (d.mid == 2) return launch_cl_t<R1, R2, 2, -1, IN_CPLX, OUT_CPLX, float, float>(d, st);
+    if (d.dir < 0) return launch_cl_t<R1, R2, 0, -1, IN_CPLX, OUT_CPLX, float, float>(d, st);
+    return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_CPLX, float, float>(d, st);
+  }
+  if (im == IN_REAL) {  // forward transform of an activation
+    if (tin == HYFFT_BF16) return launch_cl_t<R1, R2, 0, -1, IN_REAL, OUT_CPLX, bf, float>(d, st);
+    return launch_cl_t<R1, R2, 0, -1, IN_REAL, OUT_CPLX, float, float>(d, st);
+  }
+  if (om == OUT_REAL) {  // inverse transform into an activation
+    if (tout == HYFFT_BF16) return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL, float, bf>(d, st);
+    return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL, float, float>(d, st);
+  }
+  if (tout == HYFFT_BF16) return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL_SKIP, float, bf>(d, st);
+  return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL_SKIP, float, float>(d, st);
 }
-static int launch_cl(const PassDesc& d, cudaStream_t st) {
+static int launch_cl(const PassDesc& d, int im, int om, int tin, int tout, cudaStream_t st) {
   switch (d.F) {
-    case 32: return launch_cl_f<8, 4>(d, st);
-    case 64: return launch_cl_f<16, 4>(d, st);
-    case 128: return launch_cl_f<16, 8>(d, st);
-    default: return launch_cl_f<16, 16>(d, st);
+    case 32: return launch_cl_f<8, 4>(d, im, om, tin, tout, st);
+    case 64: return launch_cl_f<16, 4>(d, im, om, tin, tout, st);
+    case 128: return launch_cl_f<16, 8>(d, im, om, tin, tout, st);
+    default: return launch_cl_f<16, 16>(d, im, om, tin, tout, st);
   }
 }
+static bool cl_pass_applies(const PassDesc& d, int im, int om, int tin, int tout) {
+  if (d.tw_logF != 0 || !(d.F == 32 || d.F == 64 || d.F == 128 || d.F == 256) || getenv("HYFFT_DISABLE_CL_PASS"))
+    return false;
+  if (im == IN_CPLX && om == OUT_CPLX) return true;
+  if (d.mid || d.pos_mul != 1 || d.pos_oth != 0 || getenv("HYFFT_DISABLE_CL_REAL")) return false;
+  if (im == IN_REAL)  // channels-last source: neighbouring lines are neighbouring channels
+    return om == OUT_CPLX && d.dir < 0 && d.ri_cst == 1 && (tin == HYFFT_F32 || tin == HYFFT_BF16);
+  return im == IN_CPLX && d.dir > 0 && d.ro_cst == 1 && (tout == HYFFT_F32 || tout == HYFFT_BF16);
+}
+
 template <int R1, int R2>
 static int launch_cl_bwd_t(const PassDesc& fx, const PassDesc& fdy, const PassDesc& idx, const PassDesc& idk, int pl,
                            cudaStream_t st) {
@@ -243,13 +266,8 @@ static int launch_cl_bwd(const PassDesc& fx, const PassDesc& fdy, const PassDesc
   }
 }
 
-static bool cl_pass_applies(const PassDesc& d, int im, int om) {
-  return im == IN_CPLX && om == OUT_CPLX && d.tw_logF == 0 && (d.F == 32 || d.F == 64 || d.F == 128 || d.F == 256) &&
-         !getenv("HYFFT_DISABLE_CL_PASS");
-}
-
 static int launch_pass(const PassDesc& d, int im, int om, int tin, int tout, cudaStream_t st) {
-  if (cl_pass_applies(d, im, om)) return launch_cl(d, st);
+  if (cl_pass_applies(d, im, om, tin, tout)) return launch_cl(d, im, om, tin, tout, st);
   if (im == IN_REAL && om == OUT_CPLX) return launch_pass_dt<IN_REAL, OUT_CPLX>(d, tin, tout, st);
   if (im == IN_REAL && om == OUT_REAL) return launch_pass_dt<IN_REAL, OUT_REAL>(d, tin, tout, st);
   if (im == IN_REAL && om == OUT_REAL_SKIP) return launch_pass_dt<IN_REAL, OUT_REAL_SKIP>(d, tin, tout, st);

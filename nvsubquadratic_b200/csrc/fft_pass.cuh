@@ -425,12 +425,13 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
   }
 }
 
-// ---------------------------------------------------------------- channel-innermost complex passes
-// Complex -> complex pass over lines whose neighbours are neighbouring channels (the
-// channel index has unit stride in every spectrum buffer), F = R1 * R2 <= 256 and no
-// four-step twiddle: the middle passes of 2D / 3D transforms. Each lane of a warp owns
-// one of 32 consecutive lines, so every global access of a warp is 32 neighbouring
-// complex values. The transform is a two-level decomposition, t = j + R2 r and
+// ---------------------------------------------------------------- channel-innermost passes
+// Pass over lines whose neighbours are neighbouring channels (the channel index has unit
+// stride in every spectrum buffer, and in channels-last activations), F = R1 * R2 <= 256
+// and no four-step twiddle: the middle passes of 2D / 3D transforms, and the first /
+// last pass of a transform from / into a channels-last activation. Each lane of a warp
+// owns one of 32 consecutive lines, so every global access of a warp covers 32
+// neighbouring channels. The transform is a two-level decomposition, t = j + R2 r and
 // k = k1 + R1 k2:
 //   X[k1 + R1 k2] = sum_j W_R2^(j k2) W_F^(j k1) sum_r W_R1^(r k1) x[j + R2 r],
 // level one in registers straight from global memory, the transposition through shared
@@ -440,6 +441,9 @@ __global__ void __launch_bounds__(kPassThreads, 3) fft_pass_kernel(const PassDes
 // MID != 0 (product pass): forward transform, product with the kernel spectrum (MID == 2:
 // its conjugate), inverse transform, mirrored through shared memory a second time.
 // DIR: direction of a plain pass (-1 forward, +1 inverse); MID passes are forward first.
+// IM / OM: complex or real (packed pair: real part item p, imaginary part item p + half)
+// input / output with the same semantics as fft_pass_kernel (OUT_REAL_SKIP adds the
+// dtype-rounded D-skip term).
 constexpr int kClWarps = 8;
 
 template <int F>
@@ -447,10 +451,11 @@ __host__ __device__ constexpr int cl_lines_per_cta() { return F >= 128 ? 32 : 32
 
 template <int F>
 __host__ __device__ constexpr size_t cl_smem_bytes() {
-  return sizeof(float2) * ((size_t)F * cl_lines_per_cta<F>() + F) + 3 * sizeof(long long) * cl_lines_per_cta<F>();
+  return sizeof(float2) * ((size_t)F * cl_lines_per_cta<F>() + F) + 6 * sizeof(long long) * cl_lines_per_cta<F>() +
+         sizeof(int) * cl_lines_per_cta<F>();
 }
 
-template <int R1, int R2, int MID, int DIR>
+template <int R1, int R2, int MID, int DIR, int IM, int OM, typename TI, typename TO>
 __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassDesc d) {
   constexpr int F = R1 * R2;
   constexpr int NL = cl_lines_per_cta<F>();  // lines per CTA
@@ -460,8 +465,12 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
   float2* sm = reinterpret_cast<float2*>(smem_raw);        // [F][NL]
   float2* tw = sm + F * NL;                                 // [F] e^{-2 pi i m / F}
   long long* cb_in = reinterpret_cast<long long*>(tw + F);  // [NL] line bases, -1: past the end
-  long long* cb_out = cb_in + NL;
+  long long* cb_out = cb_in + NL;                           // complex output / real output (item p)
   long long* kbase = cb_out + NL;
+  long long* im_in = kbase + NL;    // real input of item p + half (-1: none)
+  long long* im_out = im_in + NL;   // real output of item p + half (-1: none)
+  long long* pad = im_out + NL;
+  int* chan = reinterpret_cast<int*>(pad + NL);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long line0 = (long long)blockIdx.x * NL;
   for (int m = threadIdx.x; m < F; m += blockDim.x) {
@@ -472,7 +481,7 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
   for (int l = threadIdx.x; l < NL; l += blockDim.x) {
     const long long lid = line0 + l;
     if (lid >= d.nlines) {
-      cb_in[l] = cb_out[l] = kbase[l] = -1;
+      cb_in[l] = -1;
       continue;
     }
     const int c = (int)(lid % d.C);
@@ -483,24 +492,71 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
       rest /= d.oth_ext[a];
     }
     const long long p = rest;
-    cb_in[l] = p * d.ci_pst + (long long)o[0] * d.ci_ost[0] + (long long)o[1] * d.ci_ost[1] + c;
-    cb_out[l] = p * d.co_pst + (long long)o[0] * d.co_ost[0] + (long long)o[1] * d.co_ost[1] + c;
+    const bool has_im = d.packed && p + d.half < d.B;
+    chan[l] = c;
+    if (IM == IN_CPLX) {
+      cb_in[l] = p * d.ci_pst + (long long)o[0] * d.ci_ost[0] + (long long)o[1] * d.ci_ost[1] + c;
+    } else {
+      cb_in[l] = p * d.ri_bst + (long long)c * d.ri_cst + (long long)o[0] * d.ri_ost[0] + (long long)o[1] * d.ri_ost[1];
+      im_in[l] = has_im ? cb_in[l] + (long long)d.half * d.ri_bst : -1;
+    }
+    if (OM == OUT_CPLX) {
+      cb_out[l] = p * d.co_pst + (long long)o[0] * d.co_ost[0] + (long long)o[1] * d.co_ost[1] + c;
+    } else {
+      cb_out[l] = p * d.ro_bst + (long long)c * d.ro_cst + (long long)o[0] * d.ro_ost[0] + (long long)o[1] * d.ro_ost[1];
+      im_out[l] = has_im ? cb_out[l] + (long long)d.half * d.ro_bst : -1;
+    }
     if (MID)
       kbase[l] = (d.k_shared ? 0 : p) * d.k_pst + (long long)o[0] * d.k_ost[0] + (long long)o[1] * d.k_ost[1] + c;
   }
   __syncthreads();
+
+  // store of point t of line l (value before scaling)
+  auto store = [&](int l, int t, float2 v) {
+    const int bo = t - d.out_lo;
+    if (bo < 0 || bo >= d.n_out) return;
+    const float2 val = cscale(v, d.scale);
+    if constexpr (OM == OUT_CPLX) {
+      d.cout[cb_out[l] + (long long)bo * d.co_tst] = val;
+    } else {
+      TO* dst = reinterpret_cast<TO*>(d.rout);
+      const long long off = (long long)bo * d.ro_tst;
+      const long long ri = im_out[l];
+      float re = DT<TO>::round(val.x), im = DT<TO>::round(val.y);
+      if constexpr (OM == OUT_REAL_SKIP) {
+        const TO* sk = reinterpret_cast<const TO*>(d.skip);
+        const float Dc = reinterpret_cast<const float*>(d.Dv)[chan[l]];
+        re = re + DT<TO>::round(Dc * DT<TO>::load(sk + cb_out[l] + off));
+        if (ri >= 0) im = im + DT<TO>::round(Dc * DT<TO>::load(sk + ri + off));
+      }
+      DT<TO>::store(dst + cb_out[l] + off, re);
+      if (ri >= 0) DT<TO>::store(dst + ri + off, im);
+    }
+  };
 
   // level one: R1-point transforms over r of x[j + R2 r], twiddle W_F^(j k1) -> sm[k1 R2 + j]
   for (int it = warp; it < G * R2; it += kClWarps) {
     const int g = it / R2, j = it % R2, l = g * 32 + lane;
     const long long base = cb_in[l];
     float2 v[R1];
-    const float2* src = d.cin + base + (long long)(j - d.in_off) * d.ci_tst;
-    const long long step = (long long)R2 * d.ci_tst;
+    if constexpr (IM == IN_CPLX) {
+      const float2* src = d.cin + base + (long long)(j - d.in_off) * d.ci_tst;
+      const long long step = (long long)R2 * d.ci_tst;
 #pragma unroll
-    for (int r = 0; r < R1; ++r) {
-      const int bi = j + R2 * r - d.in_off;
-      v[r] = (base >= 0 && bi >= 0 && bi < d.n_in) ? src[r * step] : make_float2(0.f, 0.f);
+      for (int r = 0; r < R1; ++r) {
+        const int bi = j + R2 * r - d.in_off;
+        v[r] = (base >= 0 && bi >= 0 && bi < d.n_in) ? src[r * step] : make_float2(0.f, 0.f);
+      }
+    } else {
+      const TI* src = reinterpret_cast<const TI*>(d.rin);
+      const long long ri = base >= 0 ? im_in[l] : -1;
+#pragma unroll
+      for (int r = 0; r < R1; ++r) {
+        const int bi = j + R2 * r - d.in_off;
+        const bool ok = base >= 0 && bi >= 0 && bi < d.n_in;
+        const long long off = (long long)bi * d.ri_tst;
+        v[r] = make_float2(ok ? DT<TI>::load(src + base + off) : 0.f, (ok && ri >= 0) ? DT<TI>::load(src + ri + off) : 0.f);
+      }
     }
     dftR<R1>(v, D1);
 #pragma unroll
@@ -524,8 +580,8 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
     for (int j = 0; j < R2; ++j) v[j] = sm[(k1 * R2 + j) * NL + l];
     dftR<R2>(v, D1);
     if constexpr (MID) {
-      const long long kb = kbase[l];
-      if (kb >= 0) {
+      if (cb_in[l] >= 0) {
+        const long long kb = kbase[l];
 #pragma unroll
         for (int k2 = 0; k2 < R2; ++k2) {
           float2 kv = __ldg(d.kin + kb + (long long)(k1 + R1 * k2) * d.k_tst);
@@ -544,13 +600,9 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
         sm[(k1 * R2 + j) * NL + l] = a;
       }
     } else {
-      const long long ob = cb_out[l];
-      if (ob >= 0) {
+      if (cb_in[l] >= 0) {
 #pragma unroll
-        for (int k2 = 0; k2 < R2; ++k2) {
-          const int bo = k1 + R1 * k2 - d.out_lo;
-          if (bo >= 0 && bo < d.n_out) d.cout[ob + (long long)bo * d.co_tst] = cscale(v[k2], d.scale);
-        }
+        for (int k2 = 0; k2 < R2; ++k2) store(l, k1 + R1 * k2, v[k2]);
       }
     }
   }
@@ -559,17 +611,13 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
     // inverse level one: R1-point transforms over k1 -> x[j + R2 r]
     for (int it = warp; it < G * R2; it += kClWarps) {
       const int g = it / R2, j = it % R2, l = g * 32 + lane;
-      const long long ob = cb_out[l];
       float2 v[R1];
 #pragma unroll
       for (int k1 = 0; k1 < R1; ++k1) v[k1] = sm[(k1 * R2 + j) * NL + l];
       dftR<R1>(v, 1.f);
-      if (ob >= 0) {
+      if (cb_in[l] >= 0) {
 #pragma unroll
-        for (int r = 0; r < R1; ++r) {
-          const int bo = j + R2 * r - d.out_lo;
-          if (bo >= 0 && bo < d.n_out) d.cout[ob + (long long)bo * d.co_tst] = cscale(v[r], d.scale);
-        }
+        for (int r = 0; r < R1; ++r) store(l, j + R2 * r, v[r]);
       }
     }
   }
