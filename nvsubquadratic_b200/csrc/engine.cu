@@ -766,13 +766,14 @@ static int fused_bwd_chain(const ConvPlan& p, int Cc, const RealView& xc, const 
 
 static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView& xv, const RealView& kv,
                                const float* Dfull, const RealView& dyv, const RealView& dxv, const RealView& dkv,
-                               float2* S1, float2* S2, float2* Kh, float2* dKh, cudaStream_t st) {
+                               float2* S1, float2* S2, float2* Kh, float2* dKh, cudaStream_t st,
+                               bool kh_ready = false) {
   const int eb = dtype_bytes(p.dt);
   const RealView xc = offset_channels(xv, c0, eb);
   const RealView kc = offset_channels(kv, c0, 4);
   const RealView dyc = offset_channels(dyv, c0, eb);
   const int zero[3] = {0, 0, 0};
-  HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+  if (!kh_ready) HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
   if (dxv.ptr && dkv.ptr) {
     Epilogue ep;
     if (Dfull) {
@@ -1083,6 +1084,8 @@ struct HyenaPlan {
   bool tp = false;      // tensor-core Toeplitz kernels (toeplitz.cu) apply (takes precedence)
   int SK = 0;
   int fF[2] = {0, 0};   // FFT sizes of the fused kernels (2^m or 3 * 2^m per axis)
+  bool cache_kh = false;  // general engine, one channel chunk: the forward keeps the filter
+                          // spectrum in the saved state and the backward reuses it
 };
 
 // Smallest FFT length of the fused kernels (2^m or 3 * 2^m, at most 64) for an axis of
@@ -1171,6 +1174,7 @@ static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
            K1 <= 2 * N1 && tp2d_dispatch(TP_PROBE, N0, N1, h.SK, nullptr, nullptr) == HYFFT_OK;
     if (h.tp) h.fused = false;
   }
+  h.cache_kh = !h.fused && !h.tp && !h.cp.big2d && h.cp.Cc == h.cp.C && !getenv("HYFFT_NO_KH_CACHE");
   return HYFFT_OK;
 }
 
@@ -1192,6 +1196,7 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
   conv_ws_sizes(h.cp, cf, cb);
   const size_t act = align_up((size_t)h.E * h.eb);
   saved = 5 * act;                 // q', k', v', z, h
+  if (h.cache_kh) saved += align_up((size_t)h.cp.spec_k_bytes_per_ch * h.cp.C);  // filter spectrum
   fwd = cf + align_up((size_t)h.d.channels * 4);
   bwd = cb + 5 * act + align_up((size_t)h.d.channels * 4);  // dh, dz, dv', dq', dk'
   if (h.cp.big2d) {  // channel-major copies around the large-grid kernels: z, h | z, dh, dz
@@ -1341,7 +1346,7 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
   size_t cf, cb;
   conv_ws_sizes(p, cf, cb);
   float2* S = (float2*)ws;
-  float2* Kh = (float2*)(ws + align_up((size_t)p.spec_x_bytes_per_ch * p.Cc));
+  float2* Kh = h.cache_kh ? (float2*)(saved + 5 * act) : (float2*)(ws + align_up((size_t)p.spec_x_bytes_per_ch * p.Cc));
   const RealView zv = real_view(z, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
   const RealView kv = real_view(filt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
   const RealView hv = real_view(hb, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
@@ -1411,7 +1416,7 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     const size_t sk = align_up((size_t)p.spec_k_bytes_per_ch * p.Cc);
     float2* S1 = (float2*)ws;
     float2* S2 = (float2*)(ws + sx);
-    float2* Kh = (float2*)(ws + 2 * sx);
+    float2* Kh = h.cache_kh ? (float2*)const_cast<char*>(saved + 5 * act) : (float2*)(ws + 2 * sx);
     float2* dKh = (float2*)(ws + 2 * sx + sk);
     const RealView zv = real_view(z, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
     const RealView kv = real_view(filt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
@@ -1431,7 +1436,7 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     } else {
       for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
         const int cc = std::min(p.Cc, p.C - c0);
-        HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, Kh, dKh, st));
+        HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, Kh, dKh, st, h.cache_kh));
       }
     }
     if (dD) {
