@@ -135,9 +135,10 @@ typedef struct hyfft_hyena_desc {
   int32_t gate1;           /* HYFFT_GATE_* applied to k: z = q * gate1(k)             */
   int32_t gate2;           /* HYFFT_GATE_* applied to v: y = h * gate2(v)             */
   int32_t dtype;           /* activation dtype of q, k, v, y, dq, dk, dv, dy          */
-  int64_t in_batch_stride; /* element strides of q, k, v (channel stride is 1):       */
-  int64_t in_pos_stride;   /*   e.g. 3C for views into one [B, *S, 3C] projection     */
-  int64_t out_batch_stride;/* element strides of y, dy, dq, dk, dv (channel stride 1) */
+  int64_t in_batch_stride; /* element strides of q, k, v and of their gradients       */
+  int64_t in_pos_stride;   /*   dq, dk, dv (channel stride is 1): e.g. 3C for views    */
+                           /*   into one [B, *S, 3C] projection and its gradient       */
+  int64_t out_batch_stride;/* element strides of y and dy (channel stride 1)          */
   int64_t out_pos_stride;
 } hyfft_hyena_desc;
 
@@ -154,9 +155,10 @@ HYFFT_API int hyfft_hyena_forward(const hyfft_hyena_desc* d, const void* q, cons
                         const float* short_b, void* y, void* saved, void* workspace,
                         size_t workspace_bytes, void* stream);
 
-/* Gradients for upstream dy. dfilt [1, C, *k], dD [C], dshort_w [3C, *short_k],
- * dshort_b [3C] are float32 and OVERWRITTEN (not accumulated). `saved` is what the
- * matching forward wrote.                                                          */
+/* Gradients for upstream dy (read with the out strides). dq, dk, dv are written with
+ * the in strides, so the gradient of a packed [B, *S, 3C] projection is one buffer.
+ * dfilt [1, C, *k], dD [C], dshort_w [3C, *short_k], dshort_b [3C] are float32 and
+ * OVERWRITTEN (not accumulated). `saved` is what the matching forward wrote.       */
 HYFFT_API int hyfft_hyena_backward(const hyfft_hyena_desc* d, const void* q, const void* k, const void* v,
                          const float* filt, const float* D, const float* short_w,
                          const float* short_b, const void* dy, void* dq, void* dk, void* dv,

@@ -1459,13 +1459,13 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
         constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
         constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
         if constexpr (ND == 3 && P && sizeof(T) == 2 && KA == 3 && KB == 3 && KI == 3) {
-          if (plane_stencil_ok<T>(h, {dqp, dkp, dvp}) && d.out_batch_stride % 2 == 0 && d.out_pos_stride % 2 == 0) {
+          if (plane_stencil_ok<T>(h, {dqp, dkp, dvp, dq, dk, dv})) {
             const PlaneLaunch pl = plane_launch(h);
             constexpr size_t sm = s3_smem_bytes<3, 3>();
             if (allow_smem(hyena_plane_stencil_kernel<T, 3, 3, 3, 1>, sm, "hyena_plane_stencil_kernel") != HYFFT_OK)
               return;
             hyena_plane_stencil_kernel<T, 3, 3, 3, 1><<<pl.grid, kElemThreads, sm, st>>>(
-                dqp, dkp, dvp, 0, 0, dq, dk, dv, d.out_batch_stride, d.out_pos_stride, nullptr, h.sg, d.channels, sw,
+                dqp, dkp, dvp, 0, 0, dq, dk, dv, d.in_batch_stride, d.in_pos_stride, nullptr, h.sg, d.channels, sw,
                 nullptr, 0, pl.xchunk);
             return;
           }
@@ -1476,13 +1476,13 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
           const dim3 lg((unsigned)((d.channels + kElemCG - 1) / kElemCG),
                         (unsigned)std::max<long long>(1, std::min<long long>(65535, (items + 7) / 8)), 1);
           hyena_line_stencil_kernel<T, P, ND, KA, KB, KI, 1><<<lg, kElemThreads, 0, st>>>(
-              dqp, dkp, dvp, 0, 0, dq, dk, dv, d.out_batch_stride, d.out_pos_stride, nullptr, h.sg, d.batch,
+              dqp, dkp, dvp, 0, 0, dq, dk, dv, d.in_batch_stride, d.in_pos_stride, nullptr, h.sg, d.batch,
               d.channels, sw, nullptr, 0);
           return;
         }
       }
       hyena_short_dgrad_kernel<T, P, K0, K1, K2><<<elem_grid(d.channels, rows, 4), kElemThreads, 0, st>>>(
-          dqp, dkp, dvp, h.sg, d.batch, d.channels, sw, dq, dk, dv, d.out_batch_stride, d.out_pos_stride);
+          dqp, dkp, dvp, h.sg, d.batch, d.channels, sw, dq, dk, dv, d.in_batch_stride, d.in_pos_stride);
     });
   };
   if (pair) dgrad(std::true_type{});

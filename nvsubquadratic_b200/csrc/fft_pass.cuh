@@ -639,7 +639,7 @@ __host__ __device__ constexpr size_t cl_bwd_smem_bytes() {
 }
 
 template <int R1, int R2>
-__global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_bwd_kernel(const PassDesc fx, const PassDesc fdy,
+__global__ void __launch_bounds__(kClWarps * 32, 3) fft_lines_cl_bwd_kernel(const PassDesc fx, const PassDesc fdy,
                                                                          const PassDesc idx, const PassDesc idk,
                                                                          int pl) {
   constexpr int F = R1 * R2;
@@ -687,32 +687,27 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_bwd_kernel(const P
 
 #pragma unroll 1
   for (int pp = 0; pp < pl; ++pp) {
-    // forward level one of X and DY
-    for (int it = warp; it < G * R2; it += kClWarps) {
-      const int g = it / R2, j = it % R2, l = g * 32 + lane;
+    // forward level one of X (into sa) and DY (into sb), one signal at a time
+    for (int it = warp; it < 2 * G * R2; it += kClWarps) {
+      const int sig = it / (G * R2), ir = it % (G * R2);
+      const int g = ir / R2, j = ir % R2, l = g * 32 + lane;
       const bool ok = bx[l] >= 0;
-      float2 u[R1], v[R1];
-      const float2* sx = fx.cin + (ok ? bx[l] : 0) + pp * fx.ci_pst + (long long)(j - fx.in_off) * fx.ci_tst;
-      const float2* sy = fdy.cin + (ok ? bdy[l] : 0) + pp * fdy.ci_pst + (long long)(j - fdy.in_off) * fdy.ci_tst;
-      const long long stx = (long long)R2 * fx.ci_tst, sty = (long long)R2 * fdy.ci_tst;
+      const PassDesc& f = sig ? fdy : fx;
+      float2 u[R1];
+      const float2* sx = f.cin + (ok ? (sig ? bdy[l] : bx[l]) : 0) + pp * f.ci_pst + (long long)(j - f.in_off) * f.ci_tst;
+      const long long stx = (long long)R2 * f.ci_tst;
 #pragma unroll
       for (int r = 0; r < R1; ++r) {
-        const int bix = j + R2 * r - fx.in_off, biy = j + R2 * r - fdy.in_off;
-        u[r] = (ok && bix >= 0 && bix < fx.n_in) ? sx[r * stx] : make_float2(0.f, 0.f);
-        v[r] = (ok && biy >= 0 && biy < fdy.n_in) ? sy[r * sty] : make_float2(0.f, 0.f);
+        const int bix = j + R2 * r - f.in_off;
+        u[r] = (ok && bix >= 0 && bix < f.n_in) ? sx[r * stx] : make_float2(0.f, 0.f);
       }
       dftR<R1>(u, -1.f);
-      dftR<R1>(v, -1.f);
+      float2* dst = sig ? sb : sa;
 #pragma unroll
       for (int k1 = 0; k1 < R1; ++k1) {
-        float2 a = u[k1], b = v[k1];
-        if (k1 > 0 && j > 0) {
-          const float2 w = tw[j * k1];
-          a = cmul(a, w);
-          b = cmul(b, w);
-        }
-        sa[(k1 * R2 + j) * NL + l] = a;
-        sb[(k1 * R2 + j) * NL + l] = b;
+        float2 a = u[k1];
+        if (k1 > 0 && j > 0) a = cmul(a, tw[j * k1]);
+        dst[(k1 * R2 + j) * NL + l] = a;
       }
     }
     __syncthreads();
@@ -754,29 +749,32 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_bwd_kernel(const P
     }
     __syncthreads();
     // inverse level one; DX into the dx chain, DK (accumulated over the pairs) into dKh
-    for (int it = warp; it < G * R2; it += kClWarps) {
-      const int g = it / R2, j = it % R2, l = g * 32 + lane;
+    for (int it = warp; it < 2 * G * R2; it += kClWarps) {
+      const int sig = it / (G * R2), ir = it % (G * R2);
+      const int g = ir / R2, j = ir % R2, l = g * 32 + lane;
       if (bx[l] < 0) continue;
-      float2 u[R1], v[R1];
+      float2 u[R1];
+      const float2* src = sig ? sb : sa;
 #pragma unroll
-      for (int k1 = 0; k1 < R1; ++k1) {
-        u[k1] = sa[(k1 * R2 + j) * NL + l];
-        v[k1] = sb[(k1 * R2 + j) * NL + l];
-      }
+      for (int k1 = 0; k1 < R1; ++k1) u[k1] = src[(k1 * R2 + j) * NL + l];
       dftR<R1>(u, 1.f);
-      dftR<R1>(v, 1.f);
-      float2* ox = idx.cout + bdx[l] + pp * idx.co_pst;
-      float2* ok = idk.cout + bdk[l];
+      if (sig) {
+        float2* ox = idx.cout + bdx[l] + pp * idx.co_pst;
 #pragma unroll
-      for (int r = 0; r < R1; ++r) {
-        const int t = j + R2 * r;
-        const int bo = t - idx.out_lo;
-        if (bo >= 0 && bo < idx.n_out) ox[(long long)bo * idx.co_tst] = cscale(v[r], idx.scale);
-        const int bk = t - idk.out_lo;
-        if (bk >= 0 && bk < idk.n_out) {
-          float2* q = ok + (long long)bk * idk.co_tst;
-          const float2 val = cscale(u[r], idk.scale);
-          *q = pp == 0 ? val : cadd(*q, val);
+        for (int r = 0; r < R1; ++r) {
+          const int bo = j + R2 * r - idx.out_lo;
+          if (bo >= 0 && bo < idx.n_out) ox[(long long)bo * idx.co_tst] = cscale(u[r], idx.scale);
+        }
+      } else {
+        float2* ok = idk.cout + bdk[l];
+#pragma unroll
+        for (int r = 0; r < R1; ++r) {
+          const int bk = j + R2 * r - idk.out_lo;
+          if (bk >= 0 && bk < idk.n_out) {
+            float2* q = ok + (long long)bk * idk.co_tst;
+            const float2 val = cscale(u[r], idk.scale);
+            *q = pp == 0 ? val : cadd(*q, val);
+          }
         }
       }
     }

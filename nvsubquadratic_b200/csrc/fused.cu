@@ -558,7 +558,7 @@ __global__ void __launch_bounds__(256) hyena2d_bwd_kernel(const Fused2DParams p)
     if (b >= p.B) continue;
     float o[8];
     stencil8_t<N0, N1, SK, T>(dgr + (t * NIMG + s) * NP * kCG, wts + t * kCG * NT, n0, n1, o);
-    V8<T>::store(outs[t] + (long long)b * p.out_bst + (long long)pos * p.out_pst + c0, o);
+    V8<T>::store(outs[t] + (long long)b * p.in_bst + (long long)pos * p.in_pst + c0, o);  // dq, dk, dv mirror q, k, v
   }
   // short conv weight / bias gradients: one thread per (tensor, channel, tap)
   if constexpr (SK > 0) {

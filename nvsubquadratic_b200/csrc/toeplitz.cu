@@ -642,7 +642,7 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
 #pragma unroll
           for (int ch = 0; ch < CG; ++ch) wacc[ch][NT] += d0[ch];
         }
-        VG<CG>::store(outs[t] + (long long)b * p.out_bst + (long long)pos * p.out_pst, o);
+        VG<CG>::store(outs[t] + (long long)b * p.in_bst + (long long)pos * p.in_pst, o);  // dq, dk, dv mirror q, k, v
       }
       if constexpr (SK > 0) {
 #pragma unroll

@@ -20,6 +20,7 @@ Forward and backward are ``libhyfft.so`` calls on the current CUDA stream.
 from __future__ import annotations
 
 import ctypes
+import math
 from typing import Callable
 
 import torch
@@ -86,16 +87,60 @@ def _sizes(desc) -> tuple[int, int, int]:
     return f.value, b.value, s.value
 
 
+def _packed_views(q, k, v) -> bool:
+    """True if q, k, v are the three channel chunks of one contiguous [B, *S, 3C] tensor."""
+    C = q.shape[-1]
+    if not (q.shape == k.shape == v.shape) or q.dtype != k.dtype or q.dtype != v.dtype:
+        return False
+    es = q.element_size()
+    if k.data_ptr() != q.data_ptr() + C * es or v.data_ptr() != q.data_ptr() + 2 * C * es:
+        return False
+    want, acc = [1], 3 * C  # strides of a contiguous [B, *S, 3C] tensor
+    for n in reversed(q.shape[:-1]):
+        want.append(acc)
+        acc *= n
+    want = tuple(reversed(want))
+    return all(all(n == 1 or st == w for n, st, w in zip(t.shape, t.stride(), want)) for t in (q, k, v))
+
+
+def _packed_base(q, k, v):
+    """The [B, *S, 3C] tensor whose channel chunks q, k, v are (a view of their common base
+    over the same memory), or None. Autograd on it hands the fused backward's one gradient
+    buffer straight to the projection, without re-assembling three chunk gradients."""
+    base = q._base
+    if base is None or k._base is not base or v._base is not base or not _packed_views(q, k, v):
+        return None
+    shape = tuple(q.shape[:-1]) + (3 * q.shape[-1],)
+    if not base.is_contiguous() or base.data_ptr() != q.data_ptr() or base.numel() != math.prod(shape):
+        return None
+    return base if tuple(base.shape) == shape else base.view(shape)
+
+
+def _chunks(qkv):
+    C = qkv.shape[-1] // 3
+    return qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
+
+
 class _HyenaFunction(torch.autograd.Function):
+    """Fused Hyena on q, k, v (PACKED False) or on their packed [B, *S, 3C] projection
+    (PACKED True: one input, one gradient)."""
+
     @staticmethod
-    def forward(ctx, q, k, v, filt, D, short_w, short_b, cfg):
+    def forward(ctx, packed, *args):
+        if packed:
+            qkv, filt, D, short_w, short_b, cfg = args
+            q, k, v = _chunks(qkv)
+        else:
+            q, k, v, filt, D, short_w, short_b, cfg = args
         causal, short_k, short_causal, g1, g2 = cfg
         dev = _lib.require_cuda(q, k, v, filt, D, short_w, short_b)
         lib = _lib.load()
         strides = _pos_strides(q)
-        if strides is None or _pos_strides(k) != strides or _pos_strides(v) != strides:
+        if strides is None or _pos_strides(k) != strides or _pos_strides(v) != strides or (
+                strides != _pos_strides(q.contiguous()) and not _packed_views(q, k, v)):
             q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
             strides = _pos_strides(q)
+        ctx.packed = packed
         B, C = q.shape[0], q.shape[-1]
         spatial = tuple(q.shape[1:-1])
         kshape = tuple(filt.shape[2:])
@@ -132,9 +177,13 @@ class _HyenaFunction(torch.autograd.Function):
         _, wb, _ = _sizes(desc)
         ws = _lib.workspace(wb, dev)
         shape = q.shape
-        dq = torch.empty(shape, dtype=q.dtype, device=dev)
-        dk = torch.empty(shape, dtype=q.dtype, device=dev)
-        dv = torch.empty(shape, dtype=q.dtype, device=dev)
+        # dq, dk, dv are written with q's strides: one packed buffer for packed views
+        if q.is_contiguous():
+            dq, dk, dv = (torch.empty(shape, dtype=q.dtype, device=dev) for _ in range(3))
+            dqkv = None
+        else:
+            dqkv = torch.empty(tuple(shape[:-1]) + (3 * C,), dtype=q.dtype, device=dev)
+            dq, dk, dv = _chunks(dqkv)
         dfilt = torch.empty_like(filt32)
         dD = torch.empty_like(D32)
         dsw = torch.empty_like(sw32) if sw32 is not None else None
@@ -152,7 +201,11 @@ class _HyenaFunction(torch.autograd.Function):
             dsw = dsw.reshape(ctx.sw_shape).to(swdt)
         if dsb is not None:
             dsb = dsb.to(sbdt)
-        return dq, dk, dv, dfilt, dD, dsw, dsb, None
+        if ctx.packed:
+            if dqkv is None:
+                dqkv = torch.cat((dq, dk, dv), dim=-1)
+            return None, dqkv, dfilt, dD, dsw, dsb, None
+        return None, dq, dk, dv, dfilt, dD, dsw, dsb, None
 
 
 def hyena_fused(q, k, v, filt, D, short_w=None, short_b=None, *, causal=False, short_causal=None,
@@ -181,8 +234,11 @@ def hyena_fused(q, k, v, filt, D, short_w=None, short_b=None, *, causal=False, s
         L, K = q.shape[1], filt.shape[2]
         assert nd == 1, "causal Hyena is 1D only"
         assert K <= L + 1, "causal filter longer than L+1 is not supported by the fused path"
-    return _HyenaFunction.apply(q, k, v, filt, D, short_w, short_b,
-                                (bool(causal), short_k, bool(short_causal), g1, g2))
+    cfg = (bool(causal), short_k, bool(short_causal), g1, g2)
+    base = _packed_base(q, k, v) if torch.is_grad_enabled() else None
+    if base is not None:
+        return _HyenaFunction.apply(True, base, filt, D, short_w, short_b, cfg)
+    return _HyenaFunction.apply(False, q, k, v, filt, D, short_w, short_b, cfg)
 
 
 class ExplicitKernel(torch.nn.Module):

@@ -110,3 +110,23 @@ def test_reference_asserts_mirrored():
         b2.fftconv2d_fp32_bhl(torch.randn(2, 4, 8, 8), torch.randn(1, 4, 17, 3))
     with pytest.raises(AssertionError, match="Leading dimension"):
         b2.fftconv2d_fp32_bhl(torch.randn(2, 4, 8, 8), torch.randn(3, 4, 3, 3))
+
+
+def test_packed_projection_detection():
+    """hyena_fused runs on the packed [B, *S, 3C] projection (one gradient buffer) exactly
+    when q, k, v are its three channel chunks, including through a reshape of the base."""
+    from nvsubquadratic_b200.hyena import _packed_base, _packed_views
+
+    qkv = torch.randn(2, 5, 6, 9, requires_grad=True)
+    q, k, v = qkv.chunk(3, dim=-1)
+    assert _packed_views(q, k, v) and _packed_base(q, k, v) is qkv
+    assert not _packed_views(k, q, v)  # wrong order
+    flat = torch.randn(2, 30, 9, requires_grad=True) * 2
+    q, k, v = flat.view(2, 5, 6, 9).chunk(3, dim=-1)
+    base = _packed_base(q, k, v)
+    assert base is not None and tuple(base.shape) == (2, 5, 6, 9) and base.data_ptr() == flat.data_ptr()
+    sep = [torch.randn(2, 5, 6, 3) for _ in range(3)]
+    assert not _packed_views(*sep) and _packed_base(*sep) is None
+    wide = torch.randn(2, 5, 6, 12)  # chunks of a 4C tensor are not a packed projection
+    q, k, v = wide[..., :3], wide[..., 3:6], wide[..., 6:9]
+    assert not _packed_views(q, k, v)
