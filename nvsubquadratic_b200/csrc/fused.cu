@@ -375,7 +375,7 @@ struct BwdSmem {
 };
 
 template <typename T, int N0, int N1, int F0, int F1, int SK>
-__global__ void __launch_bounds__(256) hyena2d_bwd_kernel(const Fused2DParams p) {
+__global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams p) {
   using L = BwdSmem<T, N0, N1, SK>;
   constexpr int NP = L::NP, NIMG = 2, NT = L::NT, LD = F1 + 1, NPAIR = kCG;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -611,7 +611,8 @@ struct Fused2D {
   static int fwd(const Fused2DParams& p, cudaStream_t st) {
     auto kern = hyena2d_fwd_kernel<T, N0, N1, F0, F1, SK, PG>;
     const size_t sm = fwd_smem();
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
       return HYFFT_ERR_CUDA;
     dim3 grid(p.C / kCG, (p.half + PG - 1) / PG);
     kern<<<grid, 256, sm, st>>>(p);
@@ -620,7 +621,8 @@ struct Fused2D {
   static int bwd(const Fused2DParams& p, cudaStream_t st) {
     auto kern = hyena2d_bwd_kernel<T, N0, N1, F0, F1, SK>;
     const size_t sm = bwd_smem();
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
       return HYFFT_ERR_CUDA;
     dim3 grid(p.C / kCG, p.half);
     kern<<<grid, 256, sm, st>>>(p);
