@@ -496,13 +496,13 @@ def run_gpu(args, cfg, rank, world, device):
         pass_ms[nm] = t3.item()
 
     # e2e through the public API from pinned host buffers (eager, no graph)
-    e2e_ms, h2d, d2h = e2e_time(cfg, inp, device, op_only, max(3, min(args.steps, 10)))
+    e2e_ms, h2d, d2h, copy_ms = e2e_time(cfg, inp, device, op_only, max(3, min(args.steps, 10)))
     t2 = torch.tensor([e2e_ms], device=device)
     if world > 1:
         torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
     e2e_ms = t2.item()
     return dict(pass_ms=pass_ms, total_ms=total_ms, step_ms=step_ms, launches=launches_per_step, clocks=clk.summary(),
-                B=B, C=C, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h)
+                B=B, C=C, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h, copy_ms=copy_ms)
 
 
 def e2e_time(cfg, inp, device, op_only, steps):
@@ -510,6 +510,17 @@ def e2e_time(cfg, inp, device, op_only, steps):
     from nvsubquadratic_b200.hyena import hyena_fused
 
     host = {k: (v.pin_memory() if v is not None else None) for k, v in inp.items()}
+    # the host->device copies alone (same pinned buffers), to separate link time from the rest
+    copy_times = []
+    for _ in range(5):
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        _tmp = [t.to(device, non_blocking=True) for t in host.values() if t is not None]
+        b.record()
+        torch.cuda.synchronize()
+        copy_times.append(a.elapsed_time(b))
+        del _tmp
     outs = {}
     h2d = d2h = 0
     times = []
@@ -548,7 +559,7 @@ def e2e_time(cfg, inp, device, op_only, steps):
         h2d = sum(t.numel() * t.element_size() for t in ins)
         d2h = sum(r.numel() * r.element_size() for r in res)
     # median step: one host-side stall (allocator, scheduler) must not stand for the path
-    return statistics.median(times), h2d, d2h
+    return statistics.median(times), h2d, d2h, statistics.median(copy_times[1:])
 
 
 def main():
@@ -663,7 +674,9 @@ def main():
                          "peak_source": ("MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks
                                          else "fallback 6650 GB/s (of fallback)")},
             "e2e": {"value": round(e2e_val, 4), "unit": "GElem/s", "h2d_bytes_per_step": res["h2d"],
-                    "d2h_bytes_per_step": res["d2h"]},
+                    "d2h_bytes_per_step": res["d2h"], "ms_per_step": round(res["e2e_ms"], 4),
+                    "h2d_copy_ms": round(res["copy_ms"], 4) if res.get("copy_ms") is not None else None,
+                    "stat": "median step (eager, through hyena_fused / the op API)"},
             "gpu_launches": res["launches"] * args.steps,
             "clocks": res["clocks"],
         }

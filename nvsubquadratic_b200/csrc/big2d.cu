@@ -458,12 +458,10 @@ static_assert(kConvSmem <= 227 * 1024 && kDkSmem <= 227 * 1024, "shared memory p
 template <typename T>
 int run_t(int op, const Big2DParams& p, cudaStream_t st) {
   if (op == B2_CONV) {
-    if (cudaFuncSetAttribute(b2_conv<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kConvSmem) != cudaSuccess)
-      return HYFFT_ERR_CUDA;
+    if (!kernel_smem_once((const void*)b2_conv<T>, kConvSmem)) return HYFFT_ERR_CUDA;
     b2_conv<T><<<p.x.cst == 1 ? dim3(p.C, p.B) : dim3(p.B, p.C), kBigThreads, kConvSmem, st>>>(p);
   } else {
-    if (cudaFuncSetAttribute(b2_dk<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kDkSmem) != cudaSuccess)
-      return HYFFT_ERR_CUDA;
+    if (!kernel_smem_once((const void*)b2_dk<T>, kDkSmem)) return HYFFT_ERR_CUDA;
     b2_dk<T><<<dim3(p.C, p.B), kBigThreads, kDkSmem, st>>>(p);
   }
   g_launches.fetch_add(1, std::memory_order_relaxed);

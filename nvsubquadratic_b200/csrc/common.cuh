@@ -6,6 +6,10 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "../../include/hyfft.h"
 
 namespace hyfft {
@@ -25,6 +29,24 @@ inline int bind_device_of(const void* p) {
     if (cur != a.device && cudaSetDevice(a.device) != cudaSuccess) return HYFFT_ERR_CUDA;
   }
   return HYFFT_OK;
+}
+
+// Raise a kernel's dynamic shared-memory limit (and, with max_carveout, ask for the
+// largest shared-memory carveout) once per kernel and device: the attribute calls are
+// driver round trips that would otherwise sit on every launch.
+inline bool kernel_smem_once(const void* fn, size_t bytes, bool max_carveout = false) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find({fn, dev});
+  if (it != done.end() && it->second >= bytes) return true;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess) return false;
+  if (max_carveout && cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    return false;
+  done[{fn, dev}] = bytes;
+  return true;
 }
 
 // ---------------------------------------------------------------- complex

@@ -158,9 +158,7 @@ static int launch_pass_t(const PassDesc& d, cudaStream_t st) {
   if (grid > 0x7fffffffLL) return fail(HYFFT_ERR_UNSUPPORTED, "too many FFT lines");
   const size_t smem =
       (size_t)kLineBytes + sizeof(float2) * ((size_t)d.TL * pass_ld(d.F) + (size_t)(d.F / 2));
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(fft_pass_kernel<IM, OM, TI, TO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-          cudaSuccess)
+  if (smem > 48 * 1024 && !kernel_smem_once((const void*)fft_pass_kernel<IM, OM, TI, TO>, smem))
     return fail(HYFFT_ERR_CUDA, "fft_pass_kernel: cannot allow %zu bytes of shared memory", smem);
   fft_pass_kernel<IM, OM, TI, TO><<<(unsigned)grid, kPassThreads, smem, st>>>(d);
   return check_launch("fft_pass_kernel");
@@ -189,16 +187,15 @@ static int launch_pass_dt(const PassDesc& d, int tin, int tout, cudaStream_t st)
 
 // Passes with F = 32 .. 256, no four-step twiddle and channel-innermost lines (complex
 // spectra, channels-last activations) run on the two-level kernel (fft_lines_cl_kernel).
-template <int R1, int R2, int MID, int DIR, int IM, int OM, typename TI, typename TO>
+template <int R1, int R2, int MID, int DIR, int IM, int OM, typename TI, typename TO, bool TMAJ = false>
 static int launch_cl_t(const PassDesc& d, cudaStream_t st) {
   constexpr int F = R1 * R2;
   const long long grid = (d.nlines + cl_lines_per_cta<F>() - 1) / cl_lines_per_cta<F>();
   if (grid <= 0) return HYFFT_OK;
   if (grid > 0x7fffffffLL) return fail(HYFFT_ERR_UNSUPPORTED, "too many FFT lines");
   constexpr size_t smem = cl_smem_bytes<F>();
-  auto kern = fft_lines_cl_kernel<R1, R2, MID, DIR, IM, OM, TI, TO>;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  auto kern = fft_lines_cl_kernel<R1, R2, MID, DIR, IM, OM, TI, TO, TMAJ>;
+  if (smem > 48 * 1024 && !kernel_smem_once((const void*)kern, smem))
     return fail(HYFFT_ERR_CUDA, "fft_lines_cl_kernel: cannot allow %zu bytes of shared memory", smem);
   kern<<<(unsigned)grid, kClWarps * 32, smem, st>>>(d);
   return check_launch("fft_lines_cl_kernel");
@@ -212,9 +209,21 @@ static int launch_cl_f(const PassDesc& d, int im, int om, int tin, int tout, cud
     if (d.dir < 0) return launch_cl_t<R1, R2, 0, -1, IN_CPLX, OUT_CPLX, float, float>(d, st);
     return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_CPLX, float, float>(d, st);
   }
-  if (im == IN_REAL) {  // forward transform of an activation
+  if (im == IN_REAL) {  // forward transform of an activation or filter
+    if (d.ri_cst != 1) {  // channel-major source: lines staged t-fastest
+      if (tin == HYFFT_BF16) return launch_cl_t<R1, R2, 0, -1, IN_REAL, OUT_CPLX, bf, float, true>(d, st);
+      return launch_cl_t<R1, R2, 0, -1, IN_REAL, OUT_CPLX, float, float, true>(d, st);
+    }
     if (tin == HYFFT_BF16) return launch_cl_t<R1, R2, 0, -1, IN_REAL, OUT_CPLX, bf, float>(d, st);
     return launch_cl_t<R1, R2, 0, -1, IN_REAL, OUT_CPLX, float, float>(d, st);
+  }
+  if (d.ro_cst != 1) {  // channel-major destination: lines stored t-fastest
+    if (om == OUT_REAL) {
+      if (tout == HYFFT_BF16) return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL, float, bf, true>(d, st);
+      return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL, float, float, true>(d, st);
+    }
+    if (tout == HYFFT_BF16) return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL_SKIP, float, bf, true>(d, st);
+    return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL_SKIP, float, float, true>(d, st);
   }
   if (om == OUT_REAL) {  // inverse transform into an activation
     if (tout == HYFFT_BF16) return launch_cl_t<R1, R2, 0, 1, IN_CPLX, OUT_REAL, float, bf>(d, st);
@@ -236,9 +245,13 @@ static bool cl_pass_applies(const PassDesc& d, int im, int om, int tin, int tout
     return false;
   if (im == IN_CPLX && om == OUT_CPLX) return true;
   if (d.mid || d.pos_mul != 1 || d.pos_oth != 0 || getenv("HYFFT_DISABLE_CL_REAL")) return false;
-  if (im == IN_REAL)  // channels-last source: neighbouring lines are neighbouring channels
-    return om == OUT_CPLX && d.dir < 0 && d.ri_cst == 1 && (tin == HYFFT_F32 || tin == HYFFT_BF16);
-  return im == IN_CPLX && d.dir > 0 && d.ro_cst == 1 && (tout == HYFFT_F32 || tout == HYFFT_BF16);
+  // real side: channels-last (neighbouring lines are neighbouring channels) or channel-major
+  // with unit stride along the line (staged t-fastest through shared memory)
+  if (im == IN_REAL)
+    return om == OUT_CPLX && d.dir < 0 && (d.ri_cst == 1 || (d.ri_tst == 1 && !getenv("HYFFT_DISABLE_CL_TMAJ"))) &&
+           (tin == HYFFT_F32 || tin == HYFFT_BF16);
+  return im == IN_CPLX && d.dir > 0 && (d.ro_cst == 1 || (d.ro_tst == 1 && !getenv("HYFFT_DISABLE_CL_TMAJ"))) &&
+         (tout == HYFFT_F32 || tout == HYFFT_BF16);
 }
 
 template <int R1, int R2>
@@ -250,8 +263,7 @@ static int launch_cl_bwd_t(const PassDesc& fx, const PassDesc& fdy, const PassDe
   if (grid <= 0) return HYFFT_OK;
   if (grid > 0x7fffffffLL) return fail(HYFFT_ERR_UNSUPPORTED, "too many FFT lines");
   constexpr size_t smem = cl_bwd_smem_bytes<R1, R2>();
-  if (smem > 48 * 1024 && cudaFuncSetAttribute(fft_lines_cl_bwd_kernel<R1, R2>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+  if (smem > 48 * 1024 && !kernel_smem_once((const void*)fft_lines_cl_bwd_kernel<R1, R2>, smem))
     return fail(HYFFT_ERR_CUDA, "fft_lines_cl_bwd_kernel: cannot allow %zu bytes of shared memory", smem);
   fft_lines_cl_bwd_kernel<R1, R2><<<(unsigned)grid, kClWarps * 32, smem, st>>>(fx, fdy, idx, idk, pl);
   return check_launch("fft_lines_cl_bwd_kernel");
@@ -1238,9 +1250,9 @@ static void with_stencil(const StencilGeom& g, F&& f) {
 template <typename T>
 static bool plane_stencil_ok(const HyenaPlan& h, std::initializer_list<const void*> ps) {
   const hyfft_hyena_desc& d = h.d;
-  if (sizeof(T) != 2 || d.ndim != 3 || !h.sg.has_conv || h.sg.k[0] != 3 || h.sg.k[1] != 3 || h.sg.k[2] != 3 ||
-      getenv("HYFFT_DISABLE_PLANE_STENCIL"))
-    return false;
+  const bool s3 = d.ndim == 3 && h.sg.k[0] == 3 && h.sg.k[1] == 3 && h.sg.k[2] == 3;
+  const bool s2 = d.ndim == 2 && h.sg.k[0] == 3 && h.sg.k[1] == 3;
+  if (sizeof(T) != 2 || !h.sg.has_conv || !(s3 || s2) || getenv("HYFFT_DISABLE_PLANE_STENCIL")) return false;
   if (d.channels % 8 || d.in_batch_stride % 8 || d.in_pos_stride % 8) return false;
   for (const void* p : ps)
     if (p && ((uintptr_t)p % 16) != 0) return false;
@@ -1250,10 +1262,23 @@ static bool plane_stencil_ok(const HyenaPlan& h, std::initializer_list<const voi
 struct PlaneLaunch {
   dim3 grid;
   int xchunk;
+  StencilGeom g;  // 3D geometry of the kernels (a 2D grid is one x plane)
 };
 // x runs per CTA such that the grid fills about two waves of two CTAs per SM.
 static PlaneLaunch plane_launch(const HyenaPlan& h) {
-  const StencilGeom& g = h.sg;
+  StencilGeom g = h.sg;
+  if (h.d.ndim == 2) {
+    g.nd = 3;
+    g.n[2] = g.n[1];
+    g.n[1] = g.n[0];
+    g.n[0] = 1;
+    g.k[2] = g.k[1];
+    g.k[1] = g.k[0];
+    g.k[0] = 1;
+    g.off[2] = g.off[1];
+    g.off[1] = g.off[0];
+    g.off[0] = 0;
+  }
   const long long base = (long long)((h.d.channels + kElemCG - 1) / kElemCG) * ((g.n[1] + kS3TY - 1) / kS3TY) *
                          ((g.n[2] + kS3TZ - 1) / kS3TZ) * h.d.batch;
   const long long nxc = std::max<long long>(1, std::min<long long>(g.n[0], (4 * 148 + base - 1) / base));
@@ -1263,15 +1288,8 @@ static PlaneLaunch plane_launch(const HyenaPlan& h) {
   pl.grid = dim3((unsigned)((h.d.channels + kElemCG - 1) / kElemCG),
                  (unsigned)(((g.n[1] + kS3TY - 1) / kS3TY) * ((g.n[2] + kS3TZ - 1) / kS3TZ)),
                  (unsigned)(h.d.batch * chunks));
+  pl.g = g;
   return pl;
-}
-
-template <typename K>
-static int allow_smem(K kernel, size_t bytes, const char* name) {
-  if (bytes > 48 * 1024 &&
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) != cudaSuccess)
-    return fail(HYFFT_ERR_CUDA, "%s: cannot allow %zu bytes of shared memory", name, bytes);
-  return HYFFT_OK;
 }
 
 // Rows of (b, position) per CTA column so that a warp walks about `per_warp` rows.
@@ -1311,14 +1329,15 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
       if constexpr (K0 > 0 && K1 > 0 && K2 > 0) {
         constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
         constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
-        if constexpr (ND == 3 && P && sizeof(T) == 2 && KA == 3 && KB == 3 && KI == 3) {
-          if (plane_stencil_ok<T>(h, {q, k, v})) {
+        if constexpr ((ND == 3 || ND == 2) && P && sizeof(T) == 2 && KA == 3 && KI == 3 && (ND == 2 || KB == 3)) {
+          constexpr int PX = ND == 3 ? 3 : 1;
+          constexpr size_t sm = s3_smem_bytes<PX, 3, 3>();
+          // (the line kernels below take over if the shared-memory size cannot be granted)
+          if (plane_stencil_ok<T>(h, {q, k, v}) &&
+              kernel_smem_once((const void*)hyena_plane_stencil_kernel<T, PX, 3, 3, 0>, sm)) {
             const PlaneLaunch pl = plane_launch(h);
-            constexpr size_t sm = s3_smem_bytes<3, 3>();
-            if (allow_smem(hyena_plane_stencil_kernel<T, 3, 3, 3, 0>, sm, "hyena_plane_stencil_kernel") != HYFFT_OK)
-              return;
-            hyena_plane_stencil_kernel<T, 3, 3, 3, 0><<<pl.grid, kElemThreads, sm, st>>>(
-                q, k, v, d.in_batch_stride, d.in_pos_stride, qs, ks, vs, 0, 0, z, h.sg, d.channels, sw, sb, d.gate1,
+            hyena_plane_stencil_kernel<T, PX, 3, 3, 0><<<pl.grid, kElemThreads, sm, st>>>(
+                q, k, v, d.in_batch_stride, d.in_pos_stride, qs, ks, vs, 0, 0, z, pl.g, d.channels, sw, sb, d.gate1,
                 pl.xchunk);
             return;
           }
@@ -1458,14 +1477,14 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
       if constexpr (K0 > 0 && K1 > 0 && K2 > 0) {
         constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
         constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
-        if constexpr (ND == 3 && P && sizeof(T) == 2 && KA == 3 && KB == 3 && KI == 3) {
-          if (plane_stencil_ok<T>(h, {dqp, dkp, dvp, dq, dk, dv})) {
+        if constexpr ((ND == 3 || ND == 2) && P && sizeof(T) == 2 && KA == 3 && KI == 3 && (ND == 2 || KB == 3)) {
+          constexpr int PX = ND == 3 ? 3 : 1;
+          constexpr size_t sm = s3_smem_bytes<PX, 3, 3>();
+          if (plane_stencil_ok<T>(h, {dqp, dkp, dvp, dq, dk, dv}) &&
+              kernel_smem_once((const void*)hyena_plane_stencil_kernel<T, PX, 3, 3, 1>, sm)) {
             const PlaneLaunch pl = plane_launch(h);
-            constexpr size_t sm = s3_smem_bytes<3, 3>();
-            if (allow_smem(hyena_plane_stencil_kernel<T, 3, 3, 3, 1>, sm, "hyena_plane_stencil_kernel") != HYFFT_OK)
-              return;
-            hyena_plane_stencil_kernel<T, 3, 3, 3, 1><<<pl.grid, kElemThreads, sm, st>>>(
-                dqp, dkp, dvp, 0, 0, dq, dk, dv, d.in_batch_stride, d.in_pos_stride, nullptr, h.sg, d.channels, sw,
+            hyena_plane_stencil_kernel<T, PX, 3, 3, 1><<<pl.grid, kElemThreads, sm, st>>>(
+                dqp, dkp, dvp, 0, 0, dq, dk, dv, d.in_batch_stride, d.in_pos_stride, nullptr, pl.g, d.channels, sw,
                 nullptr, 0, pl.xchunk);
             return;
           }
@@ -1506,13 +1525,14 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
           // sliding-window form: 1D (k,1,1), 2D (k0,k1,1), 3D (k0,k1,k2) along the innermost axis
           constexpr int ND = K2 > 1 ? 3 : (K1 > 1 ? 2 : 1);
           constexpr int KA = ND == 1 ? 1 : K0, KB = ND == 3 ? K1 : 1, KI = ND == 3 ? K2 : (ND == 2 ? K1 : K0);
-          if constexpr (ND == 3 && P && sizeof(T) == 2 && KA == 3 && KB == 3 && KI == 3) {
-            if (plane_stencil_ok<T>(h, {q, k, v, dqp, dkp, dvp})) {
+          if constexpr ((ND == 3 || ND == 2) && P && sizeof(T) == 2 && KA == 3 && KI == 3 && (ND == 2 || KB == 3)) {
+            constexpr int PX = ND == 3 ? 3 : 1;
+            constexpr size_t sm = s3_wgrad_smem_bytes<PX, 3, 3>();
+            if (plane_stencil_ok<T>(h, {q, k, v, dqp, dkp, dvp}) &&
+                kernel_smem_once((const void*)hyena_plane_wgrad_kernel<T, PX, 3, 3>, sm)) {
               const PlaneLaunch pl = plane_launch(h);
-              constexpr size_t sm = s3_smem_bytes<3, 3>();
-              if (allow_smem(hyena_plane_wgrad_kernel<T, 3, 3, 3>, sm, "hyena_plane_wgrad_kernel") != HYFFT_OK) return;
-              hyena_plane_wgrad_kernel<T, 3, 3, 3><<<pl.grid, kElemThreads, sm, st>>>(
-                  dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, h.sg, d.channels, dsw,
+              hyena_plane_wgrad_kernel<T, PX, 3, 3><<<pl.grid, kElemThreads, sm, st>>>(
+                  dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, pl.g, d.channels, dsw,
                   h.sg.has_bias ? dsb : nullptr, pl.xchunk);
               return;
             }

@@ -449,21 +449,28 @@ constexpr int kClWarps = 8;
 template <int F>
 __host__ __device__ constexpr int cl_lines_per_cta() { return F >= 128 ? 32 : 32 * (128 / F); }
 
+// shared-memory pitch of one point across the CTA's lines (odd: the staged t-major
+// transposes of TMAJ passes stay conflict-light)
+template <int F>
+__host__ __device__ constexpr int cl_pitch() { return cl_lines_per_cta<F>() + 1; }
+
 template <int F>
 __host__ __device__ constexpr size_t cl_smem_bytes() {
-  return sizeof(float2) * ((size_t)F * cl_lines_per_cta<F>() + F) + 6 * sizeof(long long) * cl_lines_per_cta<F>() +
+  return sizeof(float2) * ((size_t)F * cl_pitch<F>() + F) + 6 * sizeof(long long) * cl_lines_per_cta<F>() +
          sizeof(int) * cl_lines_per_cta<F>();
 }
 
-template <int R1, int R2, int MID, int DIR, int IM, int OM, typename TI, typename TO>
+template <int R1, int R2, int MID, int DIR, int IM, int OM, typename TI, typename TO, bool TMAJ = false>
 __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassDesc d) {
   constexpr int F = R1 * R2;
   constexpr int NL = cl_lines_per_cta<F>();  // lines per CTA
+  constexpr int NP = cl_pitch<F>();          // shared-memory pitch of one point
   constexpr int G = NL / 32;                 // groups of 32 lines
   constexpr float D1 = MID ? -1.f : (float)DIR;
+  static_assert(!TMAJ || (!MID && (IM == IN_REAL) != (OM != OUT_CPLX)), "t-major staging: one real side");
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  float2* sm = reinterpret_cast<float2*>(smem_raw);        // [F][NL]
-  float2* tw = sm + F * NL;                                 // [F] e^{-2 pi i m / F}
+  float2* sm = reinterpret_cast<float2*>(smem_raw);        // [F][NP]
+  float2* tw = sm + F * NP;                                 // [F] e^{-2 pi i m / F}
   long long* cb_in = reinterpret_cast<long long*>(tw + F);  // [NL] line bases, -1: past the end
   long long* cb_out = cb_in + NL;                           // complex output / real output (item p)
   long long* kbase = cb_out + NL;
@@ -534,12 +541,34 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
     }
   };
 
+  if constexpr (TMAJ && IM == IN_REAL) {
+    // t-major source (unit stride along the line, lines far apart): stage every line
+    // t-fastest into sm[t][line] first, zeros outside the input window
+    const TI* src = reinterpret_cast<const TI*>(d.rin);
+    for (int e = threadIdx.x; e < NL * F; e += blockDim.x) {
+      const int l = e / F, t = e - l * F;
+      const long long base = cb_in[l];
+      const int bi = t - d.in_off;
+      float2 v = make_float2(0.f, 0.f);
+      if (base >= 0 && bi >= 0 && bi < d.n_in) {
+        const long long off = (long long)bi * d.ri_tst;
+        v.x = DT<TI>::load(src + base + off);
+        if (im_in[l] >= 0) v.y = DT<TI>::load(src + im_in[l] + off);
+      }
+      sm[t * NP + l] = v;
+    }
+    __syncthreads();
+  }
   // level one: R1-point transforms over r of x[j + R2 r], twiddle W_F^(j k1) -> sm[k1 R2 + j]
+  // (a TMAJ item reads its points {j + R2 r} from shared memory and writes the same set)
   for (int it = warp; it < G * R2; it += kClWarps) {
     const int g = it / R2, j = it % R2, l = g * 32 + lane;
     const long long base = cb_in[l];
     float2 v[R1];
-    if constexpr (IM == IN_CPLX) {
+    if constexpr (TMAJ && IM == IN_REAL) {
+#pragma unroll
+      for (int r = 0; r < R1; ++r) v[r] = sm[(j + R2 * r) * NP + l];
+    } else if constexpr (IM == IN_CPLX) {
       const float2* src = d.cin + base + (long long)(j - d.in_off) * d.ci_tst;
       const long long step = (long long)R2 * d.ci_tst;
 #pragma unroll
@@ -567,17 +596,49 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
         if (D1 > 0.f) w.y = -w.y;
         a = cmul(a, w);
       }
-      sm[(k1 * R2 + j) * NL + l] = a;
+      sm[(k1 * R2 + j) * NP + l] = a;
     }
   }
   __syncthreads();
 
+  if constexpr (TMAJ && OM != OUT_CPLX) {
+    // t-major destination: all level-two items in registers, then natural order into
+    // shared memory, then every line stored t-fastest
+    constexpr int ITEMS = (G * R1 + kClWarps - 1) / kClWarps;
+    float2 res[ITEMS][R2];
+#pragma unroll
+    for (int ii = 0; ii < ITEMS; ++ii) {
+      const int it = warp + ii * kClWarps;
+      if (it < G * R1) {
+        const int g = it / R1, k1 = it % R1, l = g * 32 + lane;
+#pragma unroll
+        for (int j = 0; j < R2; ++j) res[ii][j] = sm[(k1 * R2 + j) * NP + l];
+        dftR<R2>(res[ii], D1);
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int ii = 0; ii < ITEMS; ++ii) {
+      const int it = warp + ii * kClWarps;
+      if (it < G * R1) {
+        const int g = it / R1, k1 = it % R1, l = g * 32 + lane;
+#pragma unroll
+        for (int k2 = 0; k2 < R2; ++k2) sm[(k1 + R1 * k2) * NP + l] = res[ii][k2];
+      }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < NL * d.n_out; e += blockDim.x) {
+      const int l = e / d.n_out, t = d.out_lo + (e - l * d.n_out);
+      if (cb_in[l] >= 0 && t < F) store(l, t, sm[t * NP + l]);
+    }
+    return;
+  }
   // level two: R2-point transforms over j -> X[k1 + R1 k2]
   for (int it = warp; it < G * R1; it += kClWarps) {
     const int g = it / R1, k1 = it % R1, l = g * 32 + lane;
     float2 v[R2];
 #pragma unroll
-    for (int j = 0; j < R2; ++j) v[j] = sm[(k1 * R2 + j) * NL + l];
+    for (int j = 0; j < R2; ++j) v[j] = sm[(k1 * R2 + j) * NP + l];
     dftR<R2>(v, D1);
     if constexpr (MID) {
       if (cb_in[l] >= 0) {
@@ -597,7 +658,7 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
           const float2 w = tw[j * k1];
           a = cmul(a, make_float2(w.x, -w.y));
         }
-        sm[(k1 * R2 + j) * NL + l] = a;
+        sm[(k1 * R2 + j) * NP + l] = a;
       }
     } else {
       if (cb_in[l] >= 0) {
@@ -613,7 +674,7 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
       const int g = it / R2, j = it % R2, l = g * 32 + lane;
       float2 v[R1];
 #pragma unroll
-      for (int k1 = 0; k1 < R1; ++k1) v[k1] = sm[(k1 * R2 + j) * NL + l];
+      for (int k1 = 0; k1 < R1; ++k1) v[k1] = sm[(k1 * R2 + j) * NP + l];
       dftR<R1>(v, 1.f);
       if (cb_in[l] >= 0) {
 #pragma unroll

@@ -369,7 +369,7 @@ struct BwdSmem {
   static constexpr size_t W() { return al16(sizeof(float2) * kCG * N0 * (F1 + 1)); }
   static constexpr size_t dgrad = al16(sizeof(T) * 3 * NIMG * NP * kCG);  // dq', dk', dv'
   static constexpr size_t qkv = al16(sizeof(T) * 3 * NIMG * NP * kCG);    // q', k', v' (short conv outputs)
-  static constexpr size_t small = al16(sizeof(float) * (3 * kCG * NT + 3 * kCG + kCG + kCG));
+  static constexpr size_t small = al16(sizeof(float) * (3 * kCG * NT + 3 * kCG + kCG + kCG + 3 * kCG * (NT + 1)));
   template <int F1>
   static constexpr size_t total() { return stage + 2 * W<F1>() + dgrad + qkv + small; }
 };
@@ -388,9 +388,11 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
   float* bsm = wts + 3 * kCG * NT;
   float* Dsm = bsm + 3 * kCG;
   float* dDsm = Dsm + kCG;
+  float* dwsm = dDsm + kCG;  // [3][8][NT + 1] short-conv weight (and bias) gradient of this CTA
   const int tid = threadIdx.x;
   const int c0 = blockIdx.x * kCG;
   const int pp = blockIdx.y;  // pair index: items pp and pp + half
+  for (int i = tid; i < 3 * kCG * (NT + 1); i += blockDim.x) dwsm[i] = 0.f;
 
   for (int i = tid; i < 3 * kCG * NT; i += blockDim.x) {
     const int t = i / (kCG * NT), r = i % (kCG * NT), cc = r / NT, tap = r % NT;
@@ -560,35 +562,49 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
     stencil8_t<N0, N1, SK, T>(dgr + (t * NIMG + s) * NP * kCG, wts + t * kCG * NT, n0, n1, o);
     V8<T>::store(outs[t] + (long long)b * p.in_bst + (long long)pos * p.in_pst + c0, o);  // dq, dk, dv mirror q, k, v
   }
-  // short conv weight / bias gradients: one thread per (tensor, channel, tap)
+  // short conv weight / bias gradients: one task per (tensor, image, output row, channel)
+  // slides a SK x SK window of the input along the row, accumulates all taps (and the
+  // bias) in registers and adds them into the CTA's shared accumulator
   if constexpr (SK > 0) {
     constexpr int OFF = (SK - 1) / 2;
+    for (int i = tid; i < 3 * NIMG * N0 * kCG; i += blockDim.x) {
+      const int cc = i % kCG, n0 = (i / kCG) % N0, s = (i / (kCG * N0)) % NIMG, t = i / (kCG * N0 * NIMG);
+      const T* go = dgr + (t * NIMG + s) * NP * kCG + cc;
+      const T* in = stage + (t * NIMG + s) * NP * kCG + cc;
+      float acc[NT + 1];
+#pragma unroll
+      for (int j = 0; j <= NT; ++j) acc[j] = 0.f;
+      float win[SK][SK];  // win[a][e] = in[n0 + a - OFF][n1 + e - OFF]
+      auto ld = [&](int r, int c) -> float {
+        return (r >= 0 && r < N0 && c >= 0 && c < N1) ? DT<T>::load(in + (r * N1 + c) * kCG) : 0.f;
+      };
+#pragma unroll
+      for (int a = 0; a < SK; ++a)
+#pragma unroll
+        for (int e = 1; e < SK; ++e) win[a][e] = ld(n0 + a - OFF, e - 1 - OFF);
+#pragma unroll 2
+      for (int n1 = 0; n1 < N1; ++n1) {
+#pragma unroll
+        for (int a = 0; a < SK; ++a) {
+#pragma unroll
+          for (int e = 0; e + 1 < SK; ++e) win[a][e] = win[a][e + 1];
+          win[a][SK - 1] = ld(n0 + a - OFF, n1 + SK - 1 - OFF);
+        }
+        const float g = DT<T>::load(go + (n0 * N1 + n1) * kCG);
+#pragma unroll
+        for (int a = 0; a < SK; ++a)
+#pragma unroll
+          for (int e = 0; e < SK; ++e) acc[a * SK + e] = fmaf(g, win[a][e], acc[a * SK + e]);
+        acc[NT] += g;
+      }
+#pragma unroll
+      for (int j = 0; j <= NT; ++j) atomicAdd(dwsm + (t * kCG + cc) * (NT + 1) + j, acc[j]);
+    }
+    __syncthreads();
     for (int i = tid; i < 3 * kCG * (NT + 1); i += blockDim.x) {
       const int t = i / (kCG * (NT + 1)), r = i % (kCG * (NT + 1)), cc = r / (NT + 1), tap = r % (NT + 1);
-      float acc = 0.f;
-      if (tap < NT) {
-        const int a = tap / SK - OFF, bq = tap % SK - OFF;
-        for (int s = 0; s < NIMG; ++s) {
-          const T* go = dgr + (t * NIMG + s) * NP * kCG + cc;
-          const T* in = stage + (t * NIMG + s) * NP * kCG + cc;
-          for (int n0 = 0; n0 < N0; ++n0) {
-            const int i0 = n0 + a;
-            if (i0 < 0 || i0 >= N0) continue;
-            for (int n1 = 0; n1 < N1; ++n1) {
-              const int i1 = n1 + bq;
-              if (i1 < 0 || i1 >= N1) continue;
-              acc = fmaf(DT<T>::load(go + (n0 * N1 + n1) * kCG), DT<T>::load(in + (i0 * N1 + i1) * kCG), acc);
-            }
-          }
-        }
-        atomicAdd(p.dw + ((long long)t * p.C + c0 + cc) * NT + tap, acc);
-      } else if (p.db) {
-        for (int s = 0; s < NIMG; ++s) {
-          const T* go = dgr + (t * NIMG + s) * NP * kCG + cc;
-          for (int q = 0; q < NP; ++q) acc += DT<T>::load(go + q * kCG);
-        }
-        atomicAdd(p.db + (long long)t * p.C + c0 + cc, acc);
-      }
+      if (tap < NT) atomicAdd(p.dw + ((long long)t * p.C + c0 + cc) * NT + tap, dwsm[i]);
+      else if (p.db) atomicAdd(p.db + (long long)t * p.C + c0 + cc, dwsm[i]);
     }
   }
 }
@@ -611,9 +627,7 @@ struct Fused2D {
   static int fwd(const Fused2DParams& p, cudaStream_t st) {
     auto kern = hyena2d_fwd_kernel<T, N0, N1, F0, F1, SK, PG>;
     const size_t sm = fwd_smem();
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess ||
-        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
-      return HYFFT_ERR_CUDA;
+    if (!kernel_smem_once((const void*)kern, sm, true)) return HYFFT_ERR_CUDA;
     dim3 grid(p.C / kCG, (p.half + PG - 1) / PG);
     kern<<<grid, 256, sm, st>>>(p);
     return cudaGetLastError() == cudaSuccess ? HYFFT_OK : HYFFT_ERR_CUDA;
@@ -621,9 +635,7 @@ struct Fused2D {
   static int bwd(const Fused2DParams& p, cudaStream_t st) {
     auto kern = hyena2d_bwd_kernel<T, N0, N1, F0, F1, SK>;
     const size_t sm = bwd_smem();
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess ||
-        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
-      return HYFFT_ERR_CUDA;
+    if (!kernel_smem_once((const void*)kern, sm, true)) return HYFFT_ERR_CUDA;
     dim3 grid(p.C / kCG, p.half);
     kern<<<grid, 256, sm, st>>>(p);
     return cudaGetLastError() == cudaSuccess ? HYFFT_OK : HYFFT_ERR_CUDA;

@@ -30,9 +30,21 @@ template <int KY, int KZ>
 __host__ __device__ constexpr int s3_plane_positions() {
   return (kS3TY + KY - 1) * (kS3TZ + KZ - 1);
 }
-template <int KY, int KZ>
+// ring depth: four planes for a 3D stencil, one for a 2D stencil run as one x plane
+template <int KX>
+__host__ __device__ constexpr int s3_ring() {
+  return KX == 1 ? 1 : kS3Buf;
+}
+template <int KX, int KY, int KZ>
 __host__ __device__ constexpr size_t s3_smem_bytes() {
-  return (size_t)kS3Buf * s3_plane_positions<KY, KZ>() * kElemCG * 2;  // 16-bit elements
+  return (size_t)s3_ring<KX>() * s3_plane_positions<KY, KZ>() * kElemCG * 2;  // 16-bit elements
+}
+// the weight-gradient kernel reuses its ring for the CTA reduction [8 warps][taps + 1][64]
+template <int KX, int KY, int KZ>
+__host__ __device__ constexpr size_t s3_wgrad_smem_bytes() {
+  return s3_smem_bytes<KX, KY, KZ>() > (size_t)8 * (KX * KY * KZ + 1) * kElemCG * 4
+             ? s3_smem_bytes<KX, KY, KZ>()
+             : (size_t)8 * (KX * KY * KZ + 1) * kElemCG * 4;
 }
 
 struct S3Tile {
@@ -77,6 +89,7 @@ __device__ __forceinline__ float2 s3_ld(const T* p) {
   return V2<T>::load(p);
 }
 
+// A 2D stencil runs as KX = 1 over a single x plane (n[0] = 1): one ring slot, no prefetch.
 // Forward stencil (MODE 0) or its transpose (MODE 1) over q, k, v in turn.
 // MODE 0: in = q/k/v (batch stride in_bst, position stride in_pst), out = q'/k'/v'
 //   contiguous [B, N, C] (dtype-rounded) and z = q' * g1(k').
@@ -84,12 +97,12 @@ __device__ __forceinline__ float2 s3_ld(const T* p) {
 //   out[p] = sum_tap w[tap] in[p - tap + off], a forward stencil with flipped taps and
 //   left padding k - 1 - off.
 template <typename T, int KX, int KY, int KZ, int MODE>
-__global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_stencil_kernel(
+__global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_stencil_kernel(
     const T* __restrict__ in0, const T* __restrict__ in1, const T* __restrict__ in2, long long in_bst,
     long long in_pst, T* __restrict__ out0, T* __restrict__ out1, T* __restrict__ out2, long long out_bst,
     long long out_pst, T* __restrict__ z, StencilGeom g, int C, const float* __restrict__ w,
     const float* __restrict__ bias, int gate1, int xchunk) {
-  constexpr int NT = KX * KY * KZ, ZW = kS3TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ>();
+  constexpr int NT = KX * KY * KZ, ZW = kS3TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ>(), NB = s3_ring<KX>();
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
   const S3Tile t = s3_tile(g, xchunk);
@@ -130,7 +143,7 @@ __global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_stencil_kernel(
 #pragma unroll 1
     for (int a = 0; a < KX; ++a) {
       const int xin = t.xa - ox + a;
-      s3_load_plane<T, KY, KZ>(ring + ((xin + kS3Buf * 64) % kS3Buf) * NPOS * kElemCG, src, bs, ps, g, t, C, xin, oy,
+      s3_load_plane<T, KY, KZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, bs, ps, g, t, C, xin, oy,
                                oz);
     }
 #pragma unroll 1
@@ -138,7 +151,7 @@ __global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_stencil_kernel(
       const bool pre = x + 1 < t.xb;
       if (pre) {
         const int xin = x - ox + KX;
-        s3_load_plane<T, KY, KZ>(ring + ((xin + kS3Buf * 64) % kS3Buf) * NPOS * kElemCG, src, bs, ps, g, t, C, xin,
+        s3_load_plane<T, KY, KZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, bs, ps, g, t, C, xin,
                                  oy, oz);
         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
       } else {
@@ -153,7 +166,7 @@ __global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_stencil_kernel(
           for (int i = 0; i < kS3ZU; ++i) acc[i] = bs2;
 #pragma unroll
           for (int a = 0; a < KX; ++a) {
-            const T* sl = ring + ((x - ox + a + kS3Buf * 64) % kS3Buf) * NPOS * kElemCG;
+            const T* sl = ring + ((x - ox + a + 256) % NB) * NPOS * kElemCG;
 #pragma unroll
             for (int bq = 0; bq < KY; ++bq) {
               const T* row = sl + ((yl + bq) * ZW + zw + zb) * kElemCG + 2 * lane;
@@ -202,14 +215,12 @@ __global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_stencil_kernel(
 // Per-thread accumulators for all taps, a shared-memory reduction over the CTA's warps,
 // one atomic per channel and tap per CTA (dw, db zeroed by the host).
 template <typename T, int KX, int KY, int KZ>
-__global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_wgrad_kernel(
+__global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_wgrad_kernel(
     const T* __restrict__ d0, const T* __restrict__ d1, const T* __restrict__ d2, const T* __restrict__ in0,
     const T* __restrict__ in1, const T* __restrict__ in2, long long in_bst, long long in_pst, StencilGeom g, int C,
     float* __restrict__ dw, float* __restrict__ db, int xchunk) {
-  constexpr int NT = KX * KY * KZ, ZW = kS3TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ>();
+  constexpr int NT = KX * KY * KZ, ZW = kS3TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ>(), NB = s3_ring<KX>();
   constexpr int NW = kElemThreads / 32;
-  static_assert((size_t)NW * (NT + 1) * kElemCG * sizeof(float) <= s3_smem_bytes<KY, KZ>(),
-                "the reduction reuses the plane ring");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
   float* red = reinterpret_cast<float*>(smem_raw);  // [NW][NT + 1][64] after the march
@@ -235,7 +246,7 @@ __global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_wgrad_kernel(
 #pragma unroll 1
     for (int a = 0; a < KX; ++a) {
       const int xin = t.xa - ox + a;
-      s3_load_plane<T, KY, KZ>(ring + ((xin + kS3Buf * 64) % kS3Buf) * NPOS * kElemCG, src, in_bst, in_pst, g, t, C,
+      s3_load_plane<T, KY, KZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, in_bst, in_pst, g, t, C,
                                xin, oy, oz);
     }
 #pragma unroll 1
@@ -243,7 +254,7 @@ __global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_wgrad_kernel(
       const bool pre = x + 1 < t.xb;
       if (pre) {
         const int xin = x - ox + KX;
-        s3_load_plane<T, KY, KZ>(ring + ((xin + kS3Buf * 64) % kS3Buf) * NPOS * kElemCG, src, in_bst, in_pst, g, t,
+        s3_load_plane<T, KY, KZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, in_bst, in_pst, g, t,
                                  C, xin, oy, oz);
         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
       } else {
@@ -264,7 +275,7 @@ __global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_wgrad_kernel(
           }
 #pragma unroll
           for (int a = 0; a < KX; ++a) {
-            const T* sl = ring + ((x - ox + a + kS3Buf * 64) % kS3Buf) * NPOS * kElemCG;
+            const T* sl = ring + ((x - ox + a + 256) % NB) * NPOS * kElemCG;
 #pragma unroll
             for (int bq = 0; bq < KY; ++bq) {
               const T* row = sl + ((yl + bq) * ZW + zw + zb) * kElemCG + 2 * lane;

@@ -728,14 +728,12 @@ static int tp_run(int op, const Fused2DParams* pp, cudaStream_t st) {
   if (p.K0 > 2 * N0 - 1 + 1 || p.K1 > 2 * N1 - 1 + 1 || p.K0 > 31 || p.K1 > 31) return HYFFT_ERR_UNSUPPORTED;
   if (op == TP_FWD) {
     auto kern = tp2d_fwd_kernel<N0, N1, SK, kFwdCG, kNB>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LF::total) != cudaSuccess)
-      return HYFFT_ERR_CUDA;
+    if (!kernel_smem_once((const void*)kern, LF::total)) return HYFFT_ERR_CUDA;
     dim3 grid(p.C / kFwdCG, (p.B + kNB - 1) / kNB);
     kern<<<grid, 256, LF::total, st>>>(p);
   } else {
     auto kern = tp2d_bwd_kernel<N0, N1, SK, kBwdCG, kNB>;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)LB::total) != cudaSuccess)
-      return HYFFT_ERR_CUDA;
+    if (!kernel_smem_once((const void*)kern, LB::total)) return HYFFT_ERR_CUDA;
     dim3 grid(p.C / kBwdCG, (p.B + kNB - 1) / kNB);
     kern<<<grid, 256, LB::total, st>>>(p);
   }

@@ -21,6 +21,7 @@ from __future__ import annotations
 
 import ctypes
 import math
+import os
 from typing import Callable
 
 import torch
@@ -87,6 +88,24 @@ def _sizes(desc) -> tuple[int, int, int]:
     return f.value, b.value, s.value
 
 
+_PLANS: dict = {}
+
+
+def _plan(*args):
+    """(descriptor, (fwd, bwd, saved) workspace bytes) for one problem, built once per
+    shape (and per setting of the library's HYFFT_* switches, which pick its kernels):
+    the per-step host cost of a call is then a dictionary lookup."""
+    key = args + tuple(sorted((k, v) for k, v in os.environ.items() if k.startswith("HYFFT_")))
+    hit = _PLANS.get(key)
+    if hit is None:
+        desc = _hyena_desc(*args)
+        hit = (desc, _sizes(desc))
+        if len(_PLANS) >= 256:
+            _PLANS.clear()
+        _PLANS[key] = hit
+    return hit
+
+
 def _packed_views(q, k, v) -> bool:
     """True if q, k, v are the three channel chunks of one contiguous [B, *S, 3C] tensor."""
     C = q.shape[-1]
@@ -135,9 +154,12 @@ class _HyenaFunction(torch.autograd.Function):
         causal, short_k, short_causal, g1, g2 = cfg
         dev = _lib.require_cuda(q, k, v, filt, D, short_w, short_b)
         lib = _lib.load()
+        # q, k, v are used in place when contiguous or the three chunks of one packed
+        # projection (their gradients then share that layout); anything else is copied
         strides = _pos_strides(q)
+        dense = (math.prod(q.shape[1:]), q.shape[-1])
         if strides is None or _pos_strides(k) != strides or _pos_strides(v) != strides or (
-                strides != _pos_strides(q.contiguous()) and not _packed_views(q, k, v)):
+                strides != dense and not _packed_views(q, k, v)):
             q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
             strides = _pos_strides(q)
         ctx.packed = packed
@@ -150,9 +172,9 @@ class _HyenaFunction(torch.autograd.Function):
         D32 = D.detach().to(torch.float32).contiguous()
         sw32 = short_w.detach().to(torch.float32).reshape(3 * C, -1).contiguous() if short_w is not None else None
         sb32 = short_b.detach().to(torch.float32).contiguous() if short_b is not None else None
-        desc = _hyena_desc(B, C, spatial, kshape, causal, short_k, short_causal, short_b is not None, g1, g2,
-                           q.dtype, strides, out_strides)
-        wf, _, sv = _sizes(desc)
+        desc, (wf, wb, sv) = _plan(B, C, spatial, kshape, causal, short_k, short_causal, short_b is not None, g1,
+                                   g2, q.dtype, strides, out_strides)
+        ctx.wb = wb
         ws = _lib.workspace(wf, dev)
         saved = _lib.workspace(sv, dev)
         rc = lib.hyfft_hyena_forward(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), filt32.data_ptr(),
@@ -174,7 +196,7 @@ class _HyenaFunction(torch.autograd.Function):
         desc = ctx.desc
         B, C = q.shape[0], q.shape[-1]
         dyc = dy.to(q.dtype).contiguous()
-        _, wb, _ = _sizes(desc)
+        wb = ctx.wb
         ws = _lib.workspace(wb, dev)
         shape = q.shape
         # dq, dk, dv are written with q's strides: one packed buffer for packed views

@@ -73,6 +73,8 @@ CASES = [
     # a channel tail block, ragged y / z tiles, bias, strided q/k/v views
     (3, 2, 72, (9, 13, 37), (9, 13, 37), 3, False, "silu", "sigmoid", torch.bfloat16, True, True),
     (3, 3, 16, (6, 5, 20), (11, 9, 39), 3, False, "identity", "identity", torch.bfloat16, False, False),
+    # 2D 3x3 short conv on the same kernels as one x plane (ragged y / z tiles, channel tail)
+    (2, 3, 72, (37, 45), (37, 45), 3, False, "sigmoid", "silu", torch.bfloat16, True, True),
     (2, 3, 8, (12, 10), (23, 19), 0, False, "identity", "sigmoid", torch.float32, False, False),
     # large-grid 2D kernels (F = 256 x 256)
     (2, 2, 8, (128, 128), (128, 128), 3, False, "silu", "sigmoid", torch.bfloat16, False, True),
