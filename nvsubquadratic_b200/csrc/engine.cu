@@ -1199,7 +1199,7 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
   }
   if (h.fused) {
     const size_t spec = align_up((size_t)h.d.channels * h.fF[0] * h.fF[1] * sizeof(float2));
-    saved = spec;  // filter spectrum, reused by the backward
+    saved = spec + 3 * align_up((size_t)h.E * h.eb);  // filter spectrum and q', k', v', reused by the backward
     fwd = 256;
     bwd = spec;    // dK spectrum accumulator
     return;
@@ -1594,6 +1594,16 @@ static void fused_params(const HyenaPlan& h, Fused2DParams& p, const void* q, co
   p.gate2 = d.gate2;
 }
 
+// q', k', v' of the fused path sit after the filter spectrum in the saved state
+static void fused_saved_acts(const HyenaPlan& h, Fused2DParams& p, const void* saved) {
+  char* base = const_cast<char*>(static_cast<const char*>(saved)) +
+               align_up((size_t)h.d.channels * h.fF[0] * h.fF[1] * sizeof(float2));
+  const size_t act = align_up((size_t)h.E * h.eb);
+  p.qs = base;
+  p.ks = base + act;
+  p.vs = base + 2 * act;
+}
+
 static int fused_op(const HyenaPlan& h, int op, const Fused2DParams& p, cudaStream_t st, const char* what) {
   const Geo& g = h.cp.g;
   const int rc = fused2d_dispatch(op, h.d.dtype, g.N[0], g.N[1], h.fF[0], h.fF[1], h.SK, &p, st);
@@ -1610,6 +1620,7 @@ static int hyena_fused_forward(const HyenaPlan& h, const void* q, const void* k,
   fused_params(h, p, q, k, v, filt, D, sw, sb);
   p.y = y;
   p.Kbr = static_cast<float2*>(saved);
+  fused_saved_acts(h, p, saved);
   HY_TRY(fused_op(h, FOP_KSPEC, p, st, "kspec2d_kernel"));
   return fused_op(h, FOP_FWD, p, st, "hyena2d_fwd_kernel");
 }
@@ -1630,6 +1641,7 @@ static int hyena_fused_backward(const HyenaPlan& h, const void* q, const void* k
   p.dk = dk;
   p.dv = dv;
   p.Kbr = const_cast<float2*>(static_cast<const float2*>(saved));
+  fused_saved_acts(h, p, saved);
   p.G = static_cast<float2*>(ws);
   p.dfilt = dfilt;
   p.dD = dD;

@@ -284,6 +284,14 @@ __global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p)
                               n0, n1, kv);
       round8<T>(qv);
       round8<T>(kv);
+      if (p.qs) {  // keep q', k' for the backward
+        const int pp = p0 + ps, b = h == 0 ? pp : pp + p.half;
+        if (pp < p.half && b < p.B) {
+          const long long o = ((long long)b * NP + pos) * p.C + c0;
+          V8<T>::store(reinterpret_cast<T*>(p.qs) + o, qv);
+          V8<T>::store(reinterpret_cast<T*>(p.ks) + o, kv);
+        }
+      }
 #pragma unroll
       for (int c = 0; c < 8; ++c) z[h][c] = DT<T>::round(qv[c] * DT<T>::round(gate_f(p.gate1, kv[c])));
       V8<T>::store(zs + (s * NP + pos) * kCG, z[h]);
@@ -348,6 +356,7 @@ __global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p)
     stencil8<T, N0, N1, SK>(stage + (2 * NIMG + s) * NP * kCG, wts + 2 * kCG * NT, has_bias ? bsm + 2 * kCG : nullptr,
                             n0, n1, vv);
     round8<T>(vv);
+    if (p.vs) V8<T>::store(reinterpret_cast<T*>(p.vs) + ((long long)b * NP + pos) * p.C + c0, vv);
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
       const float2 cv = W[((c * PG + ps) * N0 + n0) * LD + n1];
@@ -418,6 +427,20 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
     else
       V8<T>::zero(dst);
   }
+  const bool kept = p.qs != nullptr;  // q', k', v' saved by the forward
+  if (kept) {
+    const T* sv[3] = {reinterpret_cast<const T*>(p.qs), reinterpret_cast<const T*>(p.ks),
+                      reinterpret_cast<const T*>(p.vs)};
+    for (int i = tid; i < 3 * NIMG * NP; i += blockDim.x) {
+      const int t = i / (NIMG * NP), r = i % (NIMG * NP), s = r / NP, pos = r % NP;
+      const int b = s == 0 ? pp : pp + p.half;
+      T* dst = qkv + ((t * NIMG + s) * NP + pos) * kCG;
+      if (b < p.B)
+        V8<T>::copy(dst, sv[t] + ((long long)b * NP + pos) * p.C + c0);
+      else
+        V8<T>::zero(dst);
+    }
+  }
   __syncthreads();
 
   const bool has_bias = p.bias != nullptr;
@@ -428,18 +451,24 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
 #pragma unroll
     for (int s = 0; s < 2; ++s) {
       float qv[8], kv[8], vv[8], g[8];
-      stencil8<T, N0, N1, SK>(stage + (0 * NIMG + s) * NP * kCG, wts, has_bias ? bsm : nullptr, n0, n1, qv);
-      stencil8<T, N0, N1, SK>(stage + (1 * NIMG + s) * NP * kCG, wts + kCG * NT, has_bias ? bsm + kCG : nullptr,
-                              n0, n1, kv);
-      stencil8<T, N0, N1, SK>(stage + (2 * NIMG + s) * NP * kCG, wts + 2 * kCG * NT,
-                              has_bias ? bsm + 2 * kCG : nullptr, n0, n1, vv);
+      if (kept) {
+        V8<T>::load(qkv + ((0 * NIMG + s) * NP + pos) * kCG, qv);
+        V8<T>::load(qkv + ((1 * NIMG + s) * NP + pos) * kCG, kv);
+        V8<T>::load(qkv + ((2 * NIMG + s) * NP + pos) * kCG, vv);
+      } else {
+        stencil8<T, N0, N1, SK>(stage + (0 * NIMG + s) * NP * kCG, wts, has_bias ? bsm : nullptr, n0, n1, qv);
+        stencil8<T, N0, N1, SK>(stage + (1 * NIMG + s) * NP * kCG, wts + kCG * NT, has_bias ? bsm + kCG : nullptr,
+                                n0, n1, kv);
+        stencil8<T, N0, N1, SK>(stage + (2 * NIMG + s) * NP * kCG, wts + 2 * kCG * NT,
+                                has_bias ? bsm + 2 * kCG : nullptr, n0, n1, vv);
+        round8<T>(qv);
+        round8<T>(kv);
+        round8<T>(vv);
+        V8<T>::store(qkv + ((0 * NIMG + s) * NP + pos) * kCG, qv);
+        V8<T>::store(qkv + ((1 * NIMG + s) * NP + pos) * kCG, kv);
+        V8<T>::store(qkv + ((2 * NIMG + s) * NP + pos) * kCG, vv);
+      }
       V8<T>::load(stage + ((3 * NIMG + s) * NP + pos) * kCG, g);
-      round8<T>(qv);
-      round8<T>(kv);
-      round8<T>(vv);
-      V8<T>::store(qkv + ((0 * NIMG + s) * NP + pos) * kCG, qv);
-      V8<T>::store(qkv + ((1 * NIMG + s) * NP + pos) * kCG, kv);
-      V8<T>::store(qkv + ((2 * NIMG + s) * NP + pos) * kCG, vv);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         z[s][c] = DT<T>::round(qv[c] * DT<T>::round(gate_f(p.gate1, kv[c])));
@@ -616,7 +645,7 @@ struct Shape2D {
 
 template <typename T, int N0, int N1, int F0, int F1, int SK>
 struct Fused2D {
-  static constexpr int PG = 2;
+  static constexpr int PG = 1;
   static size_t fwd_smem() { return FwdSmem<T, N0, N1, SK, PG>::template total<F1>(); }
   static size_t bwd_smem() { return BwdSmem<T, N0, N1, SK>::template total<F1>(); }
 

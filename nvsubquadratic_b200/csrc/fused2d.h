@@ -30,6 +30,9 @@ struct Fused2DParams {
   int K0, K1;
   int gate1, gate2;
   int* status;        // set non-zero by a kernel whose bounded wait timed out (workspace word)
+  void* qs;           // short-conv outputs q', k', v' [B][N0*N1][C] (activation dtype): written by
+  void* ks;           //   the FFT forward and read back by its backward instead of recomputing
+  void* vs;           //   the three stencils; null: not kept
 };
 
 // Tensor-core (tcgen05) Toeplitz path for bf16 grids with both sides <= 16 (toeplitz.cu).
