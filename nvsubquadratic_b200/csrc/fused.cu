@@ -91,8 +91,15 @@ __device__ __forceinline__ void round8(float (&o)[8]) {
   for (int i = 0; i < 8; ++i) o[i] = DT<T>::round(o[i]);
 }
 
+// weight of channel c at tap j from a tap-major [taps][8] table, read as two 16-byte vectors
+__device__ __forceinline__ float wtap8(const float* w, int j, int c) {
+  const float4 v = reinterpret_cast<const float4*>(w + j * 8)[c >> 2];
+  const int r = c & 3;
+  return r == 0 ? v.x : (r == 1 ? v.y : (r == 2 ? v.z : v.w));
+}
+
 // Depthwise SKxSK cross-correlation ("same" padding) of 8 channels of one image tile
-// [N0*N1][8] at (n0, n1); w: [8][SK*SK], bias: [8] or null. SK == 0: identity.
+// [N0*N1][8] at (n0, n1); w: [SK*SK][8] (16-byte aligned), bias: [8] or null. SK == 0: identity.
 template <typename T, int N0, int N1, int SK>
 __device__ __forceinline__ void stencil8(const T* tile, const float* w, const float* bias, int n0, int n1,
                                          float (&o)[8]) {
@@ -113,7 +120,7 @@ __device__ __forceinline__ void stencil8(const T* tile, const float* w, const fl
         float x[8];
         V8<T>::load(tile + (i0 * N1 + i1) * kCG, x);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) o[c] = fmaf(w[c * NT + a * SK + b], x[c], o[c]);
+        for (int c = 0; c < 8; ++c) o[c] = fmaf(wtap8(w, a * SK + b, c), x[c], o[c]);
       }
     }
   }
@@ -140,7 +147,7 @@ __device__ __forceinline__ void stencil8_t(const S* tile, const float* w, int n0
         float x[8];
         V8<S>::load(tile + (i0 * N1 + i1) * kCG, x);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) o[c] = fmaf(w[c * NT + a * SK + b], x[c], o[c]);
+        for (int c = 0; c < 8; ++c) o[c] = fmaf(wtap8(w, a * SK + b, c), x[c], o[c]);
       }
     }
   }
@@ -240,7 +247,7 @@ __global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p)
   extern __shared__ __align__(16) unsigned char smem[];
   T* stage = reinterpret_cast<T*>(smem);                                       // [3][NIMG][NP][8]
   float2* W = reinterpret_cast<float2*>(smem + L::stage);                       // [NPAIR][N0][LD]
-  float* wts = reinterpret_cast<float*>(smem + L::stage + L::template W<F1>());  // [3][8][NT]
+  float* wts = reinterpret_cast<float*>(smem + L::stage + L::template W<F1>());  // [3][NT][8]
   float* bsm = wts + 3 * kCG * NT;                                               // [3][8]
   float* Dsm = bsm + 3 * kCG;                                                    // [8]
   T* zs = reinterpret_cast<T*>(smem + L::stage + L::template W<F1>() + L::small);  // [NIMG][NP][8]
@@ -248,8 +255,8 @@ __global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p)
   const int c0 = blockIdx.x * kCG;
   const int p0 = blockIdx.y * PG;
 
-  for (int i = tid; i < 3 * kCG * NT; i += blockDim.x) {
-    const int t = i / (kCG * NT), r = i % (kCG * NT), cc = r / NT, tap = r % NT;
+  for (int i = tid; i < 3 * kCG * NT; i += blockDim.x) {  // tap-major: the 8 channels of a tap are one vector
+    const int t = i / (kCG * NT), r = i % (kCG * NT), tap = r / kCG, cc = r % kCG;
     wts[i] = SK > 0 ? p.w[((long long)t * p.C + c0 + cc) * NT + tap] : 1.f;
   }
   for (int i = tid; i < 3 * kCG; i += blockDim.x) {
@@ -403,8 +410,8 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
   const int pp = blockIdx.y;  // pair index: items pp and pp + half
   for (int i = tid; i < 3 * kCG * (NT + 1); i += blockDim.x) dwsm[i] = 0.f;
 
-  for (int i = tid; i < 3 * kCG * NT; i += blockDim.x) {
-    const int t = i / (kCG * NT), r = i % (kCG * NT), cc = r / NT, tap = r % NT;
+  for (int i = tid; i < 3 * kCG * NT; i += blockDim.x) {  // tap-major: the 8 channels of a tap are one vector
+    const int t = i / (kCG * NT), r = i % (kCG * NT), tap = r / kCG, cc = r % kCG;
     wts[i] = SK > 0 ? p.w[((long long)t * p.C + c0 + cc) * NT + tap] : 1.f;
   }
   for (int i = tid; i < 3 * kCG; i += blockDim.x) {
