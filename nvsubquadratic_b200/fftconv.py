@@ -25,6 +25,7 @@ CPU tensor raises ``RuntimeError``.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -70,6 +71,25 @@ def _workspace_sizes(desc: _lib.ConvDesc) -> tuple[int, int]:
     return f.value, b.value
 
 
+_PLANS: dict = {}
+# the library's switches that change the conv plan (and so its workspace sizes)
+_PLAN_SWITCHES = ("HYFFT_WS_BUDGET_MB", "HYFFT_DISABLE_BIG2D")
+
+
+def _plan(*args):
+    """(descriptor, (forward, backward) workspace bytes) for one problem, built once per
+    shape: the per-call host cost is then a dictionary lookup."""
+    key = args + tuple(os.environ.get(k) for k in _PLAN_SWITCHES)
+    hit = _PLANS.get(key)
+    if hit is None:
+        desc = _conv_desc(*args)
+        hit = (desc, _workspace_sizes(desc))
+        if len(_PLANS) >= 256:
+            _PLANS.clear()
+        _PLANS[key] = hit
+    return hit
+
+
 class _FFTConvFunction(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, kernel, shortcut, causal, layout):
@@ -88,8 +108,8 @@ class _FFTConvFunction(torch.autograd.Function):
         xc = x.contiguous()
         kf = kernel.detach().to(torch.float32).contiguous()
         sc = shortcut.detach().contiguous() if shortcut is not None else None
-        desc = _conv_desc(B, H, spatial, kshape, kB, causal, x.dtype, layout)
-        wf, _ = _workspace_sizes(desc)
+        desc, (wf, wb) = _plan(B, H, spatial, kshape, kB, causal, x.dtype, layout)
+        ctx.wb = wb
         ws = _lib.workspace(wf, dev)
         y = torch.empty_like(xc)
         rc = lib.hyfft_conv_forward(ctypes.byref(desc), xc.data_ptr(), kf.data_ptr(), _lib.ptr(sc), y.data_ptr(),
@@ -109,8 +129,7 @@ class _FFTConvFunction(torch.autograd.Function):
         dev = xc.device
         lib = _lib.load()
         desc = ctx.desc
-        _, wb = _workspace_sizes(desc)
-        ws = _lib.workspace(wb, dev)
+        ws = _lib.workspace(ctx.wb, dev)
         dyc = dy.to(xc.dtype).contiguous()
         need_x, need_k, need_s = ctx.needs_input_grad[0], ctx.needs_input_grad[1], ctx.needs_input_grad[2]
         dx = torch.empty_like(xc) if need_x else None
