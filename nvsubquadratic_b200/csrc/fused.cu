@@ -91,6 +91,18 @@ __device__ __forceinline__ void round8(float (&o)[8]) {
   for (int i = 0; i < 8; ++i) o[i] = DT<T>::round(o[i]);
 }
 
+// two neighbouring channels of one position (4- or 8-byte aligned)
+template <typename T>
+__device__ __forceinline__ float2 ld2ch(const T* p);
+template <>
+__device__ __forceinline__ float2 ld2ch<__nv_bfloat16>(const __nv_bfloat16* p) {
+  return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(p));
+}
+template <>
+__device__ __forceinline__ float2 ld2ch<float>(const float* p) {
+  return *reinterpret_cast<const float2*>(p);
+}
+
 // weight of channel c at tap j from a tap-major [taps][8] table, read as two 16-byte vectors
 __device__ __forceinline__ float wtap8(const float* w, int j, int c) {
   const float4 v = reinterpret_cast<const float4*>(w + j * 8)[c >> 2];
@@ -106,7 +118,7 @@ __device__ __forceinline__ void stencil8(const T* tile, const float* w, const fl
   if constexpr (SK == 0) {
     V8<T>::load(tile + (n0 * N1 + n1) * kCG, o);
   } else {
-    constexpr int OFF = (SK - 1) / 2, NT = SK * SK;
+    constexpr int OFF = (SK - 1) / 2;
 #pragma unroll
     for (int c = 0; c < 8; ++c) o[c] = bias ? bias[c] : 0.f;
 #pragma unroll
@@ -126,28 +138,43 @@ __device__ __forceinline__ void stencil8(const T* tile, const float* w, const fl
   }
 }
 
-// Transposed stencil: din[n] = sum_tap w[tap] * dout[n - tap + OFF] over a float tile [N0*N1][8].
+// Transposed stencil at the two neighbouring outputs (n0, n1) and (n0, n1 + 1) of one row:
+// they share SK of their SK + 1 input columns, so each input vector is loaded once.
+// o1 is left zero when n1 + 1 == N1.
 template <int N0, int N1, int SK, typename S>
-__device__ __forceinline__ void stencil8_t(const S* tile, const float* w, int n0, int n1, float (&o)[8]) {
+__device__ __forceinline__ void stencil8_t2(const S* tile, const float* w, int n0, int n1, float (&o0)[8],
+                                            float (&o1)[8]) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) o0[c] = o1[c] = 0.f;
+  const bool two = n1 + 1 < N1;
   if constexpr (SK == 0) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) o[c] = (float)tile[(n0 * N1 + n1) * kCG + c];
+    V8<S>::load(tile + (n0 * N1 + n1) * kCG, o0);
+    if (two) V8<S>::load(tile + (n0 * N1 + n1 + 1) * kCG, o1);
   } else {
-    constexpr int OFF = (SK - 1) / 2, NT = SK * SK;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) o[c] = 0.f;
+    constexpr int OFF = (SK - 1) / 2;
 #pragma unroll
     for (int a = 0; a < SK; ++a) {
       const int i0 = n0 - a + OFF;
       if (i0 < 0 || i0 >= N0) continue;
+      float x[SK + 1][8];  // input columns n1 + OFF - SK + 1 + m, m = 0..SK
+#pragma unroll
+      for (int m = 0; m <= SK; ++m) {
+        const int i1 = n1 + OFF - SK + 1 + m;
+        if (i1 >= 0 && i1 < N1) {
+          V8<S>::load(tile + (i0 * N1 + i1) * kCG, x[m]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) x[m][c] = 0.f;
+        }
+      }
 #pragma unroll
       for (int b = 0; b < SK; ++b) {
-        const int i1 = n1 - b + OFF;
-        if (i1 < 0 || i1 >= N1) continue;
-        float x[8];
-        V8<S>::load(tile + (i0 * N1 + i1) * kCG, x);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) o[c] = fmaf(wtap8(w, a * SK + b, c), x[c], o[c]);
+        for (int c = 0; c < 8; ++c) {
+          const float wv = wtap8(w, a * SK + b, c);
+          o0[c] = fmaf(wv, x[SK - 1 - b][c], o0[c]);
+          o1[c] = fmaf(wv, x[SK - b][c], o1[c]);
+        }
       }
     }
   }
@@ -369,7 +396,7 @@ __global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p)
       const float2 cv = W[((c * PG + ps) * N0 + n0) * LD + n1];
       const float conv = h == 0 ? cv.x : cv.y;
       const float z = zv[c];
-      const float hv = DT<T>::round(DT<T>::round(conv) + DT<T>::round(Dsm[c] * z));
+      const float hv = DT<T>::round(DT<T>::round(conv) + DT<T>::round(wtap8(Dsm, 0, c) * z));
       out[c] = hv * DT<T>::round(gate_f(p.gate2, vv[c]));
     }
     V8<T>::store(yout + (long long)b * p.out_bst + (long long)pos * p.out_pst + c0, out);
@@ -567,10 +594,10 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
       const float g1k = DT<T>::round(gate_f(p.gate1, kv[c]));
       const float z = DT<T>::round(qv[c] * g1k);
       const float g2v = DT<T>::round(gate_f(p.gate2, vv[c]));
-      const float hv = DT<T>::round(DT<T>::round(conv_h) + DT<T>::round(Dsm[c] * z));
+      const float hv = DT<T>::round(DT<T>::round(conv_h) + DT<T>::round(wtap8(Dsm, 0, c) * z));
       const float dh = DT<T>::round(g[c] * g2v);
       ov[c] = g[c] * hv * gate_df(p.gate2, vv[c]);
-      const float dz = DT<T>::round(DT<T>::round(conv_d) + DT<T>::round(Dsm[c] * dh));
+      const float dz = DT<T>::round(DT<T>::round(conv_d) + DT<T>::round(wtap8(Dsm, 0, c) * dh));
       oq[c] = dz * g1k;
       ok[c] = dz * qv[c] * gate_df(p.gate1, kv[c]);
       dDp[c] = fmaf(dh, z, dDp[c]);
@@ -590,13 +617,17 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
 
   // short conv input gradients (transposed stencil) -> dq, dk, dv (channels-last)
   T* outs[3] = {reinterpret_cast<T*>(p.dq), reinterpret_cast<T*>(p.dk), reinterpret_cast<T*>(p.dv)};
-  for (int i = tid; i < 3 * NIMG * NP; i += blockDim.x) {
-    const int t = i / (NIMG * NP), r = i % (NIMG * NP), s = r / NP, pos = r % NP, n0 = pos / N1, n1 = pos % N1;
+  constexpr int NH = (N1 + 1) / 2;  // output pairs per row
+  for (int i = tid; i < 3 * NIMG * N0 * NH; i += blockDim.x) {
+    const int t = i / (NIMG * N0 * NH), r = i % (NIMG * N0 * NH), s = r / (N0 * NH), rr = r % (N0 * NH);
+    const int n0 = rr / NH, n1 = (rr % NH) * 2, pos = n0 * N1 + n1;
     const int b = s == 0 ? pp : pp + p.half;
     if (b >= p.B) continue;
-    float o[8];
-    stencil8_t<N0, N1, SK, T>(dgr + (t * NIMG + s) * NP * kCG, wts + t * kCG * NT, n0, n1, o);
-    V8<T>::store(outs[t] + (long long)b * p.in_bst + (long long)pos * p.in_pst + c0, o);  // dq, dk, dv mirror q, k, v
+    float o0[8], o1[8];
+    stencil8_t2<N0, N1, SK, T>(dgr + (t * NIMG + s) * NP * kCG, wts + t * kCG * NT, n0, n1, o0, o1);
+    T* dst = outs[t] + (long long)b * p.in_bst + (long long)pos * p.in_pst + c0;  // dq, dk, dv mirror q, k, v
+    V8<T>::store(dst, o0);
+    if (n1 + 1 < N1) V8<T>::store(dst + p.in_pst, o1);
   }
   // short conv weight / bias gradients: one task per (tensor, image, output row, channel)
   // slides a SK x SK window of the input along the row, accumulates all taps (and the
@@ -633,8 +664,22 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
           for (int e = 0; e < SK; ++e) acc[a * SK + e] = fmaf(g, win[a][e], acc[a * SK + e]);
         acc[NT] += g;
       }
+      if constexpr ((N0 % 2) == 0) {
+        // the task count is a multiple of 32 and a warp never spans two tensors: lanes l, l + 8,
+        // l + 16, l + 24 hold the same (tensor, channel), so sum them before one atomic per value
 #pragma unroll
-      for (int j = 0; j <= NT; ++j) atomicAdd(dwsm + (t * kCG + cc) * (NT + 1) + j, acc[j]);
+        for (int j = 0; j <= NT; ++j) {
+          acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 8);
+          acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], 16);
+        }
+        if ((tid & 31) < 8) {
+#pragma unroll
+          for (int j = 0; j <= NT; ++j) atomicAdd(dwsm + (t * kCG + cc) * (NT + 1) + j, acc[j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j <= NT; ++j) atomicAdd(dwsm + (t * kCG + cc) * (NT + 1) + j, acc[j]);
+      }
     }
     __syncthreads();
     for (int i = tid; i < 3 * kCG * (NT + 1); i += blockDim.x) {
