@@ -268,7 +268,7 @@ struct FwdSmem {
 };
 
 template <typename T, int N0, int N1, int F0, int F1, int SK, int PG>
-__global__ void __launch_bounds__(256) hyena2d_fwd_kernel(const Fused2DParams p) {
+__global__ void __launch_bounds__(256, (F0 <= 24 && F1 <= 24) ? 4 : 1) hyena2d_fwd_kernel(const Fused2DParams p) {
   using L = FwdSmem<T, N0, N1, SK, PG>;
   constexpr int NP = L::NP, NIMG = L::NIMG, NT = L::NT, LD = F1 + 1, NPAIR = kCG * PG;
   extern __shared__ __align__(16) unsigned char smem[];
