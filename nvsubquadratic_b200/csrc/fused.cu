@@ -91,6 +91,24 @@ __device__ __forceinline__ void round8(float (&o)[8]) {
   for (int i = 0; i < 8; ++i) o[i] = DT<T>::round(o[i]);
 }
 
+// Copy of one position's 8 channels (16 bytes for 16-bit types, 32 for float) from global
+// to shared memory, left in flight (cp.async, L2 only); !valid writes zeros and reads
+// nothing. All copies of a load phase are issued before one wait, so their latencies
+// overlap instead of adding up.
+template <typename T>
+__device__ __forceinline__ void cp_v8(T* sdst, const T* gsrc, bool valid) {
+  constexpr int kChunks = (int)(8 * sizeof(T)) / 16;
+#pragma unroll
+  for (int h = 0; h < kChunks; ++h) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(reinterpret_cast<char*>(sdst) + 16 * h);
+    const char* g = reinterpret_cast<const char*>(gsrc) + (valid ? 16 * h : 0);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(g), "r"(valid ? 16 : 0) : "memory");
+  }
+}
+__device__ __forceinline__ void cp_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
 // two neighbouring channels of one position (4- or 8-byte aligned)
 template <typename T>
 __device__ __forceinline__ float2 ld2ch(const T* p);
@@ -297,11 +315,10 @@ __global__ void __launch_bounds__(256, (F0 <= 24 && F1 <= 24) ? 4 : 1) hyena2d_f
     const int pp = p0 + (s % PG);
     const int b = s < PG ? pp : pp + p.half;
     T* dst = stage + ((t * NIMG + s) * NP + pos) * kCG;
-    if (pp < p.half && b < p.B)
-      V8<T>::copy(dst, src[t] + (long long)b * p.in_bst + (long long)pos * p.in_pst + c0);
-    else
-      V8<T>::zero(dst);
+    const bool ok = pp < p.half && b < p.B;
+    cp_v8<T>(dst, ok ? src[t] + (long long)b * p.in_bst + (long long)pos * p.in_pst + c0 : src[t], ok);
   }
+  cp_wait_all();
   __syncthreads();
 
   const bool has_bias = p.bias != nullptr;
@@ -456,10 +473,7 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
     const int b = s == 0 ? pp : pp + p.half;
     T* dst = stage + ((t * NIMG + s) * NP + pos) * kCG;
     const long long bst = t == 3 ? p.out_bst : p.in_bst, pst = t == 3 ? p.out_pst : p.in_pst;
-    if (b < p.B)
-      V8<T>::copy(dst, src[t] + (long long)b * bst + (long long)pos * pst + c0);
-    else
-      V8<T>::zero(dst);
+    cp_v8<T>(dst, b < p.B ? src[t] + (long long)b * bst + (long long)pos * pst + c0 : src[t], b < p.B);
   }
   const bool kept = p.qs != nullptr;  // q', k', v' saved by the forward
   if (kept) {
@@ -469,12 +483,10 @@ __global__ void __launch_bounds__(256, 2) hyena2d_bwd_kernel(const Fused2DParams
       const int t = i / (NIMG * NP), r = i % (NIMG * NP), s = r / NP, pos = r % NP;
       const int b = s == 0 ? pp : pp + p.half;
       T* dst = qkv + ((t * NIMG + s) * NP + pos) * kCG;
-      if (b < p.B)
-        V8<T>::copy(dst, sv[t] + ((long long)b * NP + pos) * p.C + c0);
-      else
-        V8<T>::zero(dst);
+      cp_v8<T>(dst, b < p.B ? sv[t] + ((long long)b * NP + pos) * p.C + c0 : sv[t], b < p.B);
     }
   }
+  cp_wait_all();
   __syncthreads();
 
   const bool has_bias = p.bias != nullptr;
