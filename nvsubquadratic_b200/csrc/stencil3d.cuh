@@ -164,6 +164,17 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
           float2 acc[kS3ZU];
 #pragma unroll
           for (int i = 0; i < kS3ZU; ++i) acc[i] = bs2;
+          // z = q' * g1(k') needs q' of these positions (written by this thread in the q sweep):
+          // load it before the stencil so the load latency hides behind the taps
+          float2 qpre[kS3ZU];
+          if (MODE == 0 && ti == 1) {
+#pragma unroll
+            for (int i = 0; i < kS3ZU; ++i) {
+              const int gz = t.z0 + zw + zb + i;
+              const long long o = ((long long)t.b * N + ((long long)x * g.n[1] + gy) * g.n[2] + gz) * C + c;
+              qpre[i] = gz < g.n[2] ? V2<T>::load(outs[0] + o) : make_float2(0.f, 0.f);
+            }
+          }
 #pragma unroll
           for (int a = 0; a < KX; ++a) {
             const T* sl = ring + ((x - ox + a + 256) % NB) * NPOS * kElemCG;
@@ -192,8 +203,8 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
               const long long o = ((long long)t.b * N + pos) * C + c;
               const float2 r = V2<T>::round(acc[i]);
               V2<T>::store(outs[ti] + o, r);
-              if (ti == 1) {  // z = q' * g1(k'); q' at this position was written by this thread
-                const float2 qv = V2<T>::load(outs[0] + o);
+              if (ti == 1) {  // z = q' * g1(k')
+                const float2 qv = qpre[i];
                 const float2 g1 = V2<T>::round(make_float2(gate_f(gate1, r.x), gate_f(gate1, r.y)));
                 V2<T>::store(z + o, make_float2(qv.x * g1.x, qv.y * g1.y));
               }
@@ -262,17 +273,28 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_wgr
       }
       __syncthreads();
       if (cok && gy < g.n[1]) {
+        // dout of the next step is loaded one step ahead, behind the current step's taps
+        auto ld_dout = [&](int zb, float2 (&dv)[kS3ZU]) {
+#pragma unroll
+          for (int i = 0; i < kS3ZU; ++i) {
+            const int gz = t.z0 + zw + zb + i;
+            const long long pos = ((long long)x * g.n[1] + gy) * g.n[2] + gz;
+            dv[i] = (zb < kS3TZ / 2 && gz < g.n[2]) ? V2<T>::load(dsrc + ((long long)t.b * N + pos) * C + c)
+                                                    : make_float2(0.f, 0.f);
+          }
+        };
+        float2 dnext[kS3ZU];
+        ld_dout(0, dnext);
 #pragma unroll 1
         for (int zb = 0; zb < kS3TZ / 2; zb += kS3ZU) {
           float2 dv[kS3ZU];
 #pragma unroll
           for (int i = 0; i < kS3ZU; ++i) {
-            const int gz = t.z0 + zw + zb + i;
-            const long long pos = ((long long)x * g.n[1] + gy) * g.n[2] + gz;
-            dv[i] = gz < g.n[2] ? V2<T>::load(dsrc + ((long long)t.b * N + pos) * C + c) : make_float2(0.f, 0.f);
+            dv[i] = dnext[i];
             accb.x += dv[i].x;
             accb.y += dv[i].y;
           }
+          ld_dout(zb + kS3ZU, dnext);
 #pragma unroll
           for (int a = 0; a < KX; ++a) {
             const T* sl = ring + ((x - ox + a + 256) % NB) * NPOS * kElemCG;
