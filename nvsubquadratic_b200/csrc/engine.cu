@@ -314,10 +314,13 @@ struct SpecStrides {
   long long st[3];
   long long pst;
 };
-static SpecStrides spec_strides(const Geo& g, int C) {
+static SpecStrides spec_strides(const Geo& g, int C, bool half = false) {
   SpecStrides s;
   long long acc = C;
-  for (int d = g.D - 1; d >= 0; --d) { s.st[d] = acc; acc *= g.F[d]; }
+  for (int d = g.D - 1; d >= 0; --d) {
+    s.st[d] = acc;
+    acc *= (half && d == g.D - 1) ? g.F[d] / 2 + 1 : g.F[d];
+  }
   s.pst = acc;
   return s;
 }
@@ -373,9 +376,11 @@ static int emit_pass(PassList* rec, const PassDesc& d, int im, int om, int tin, 
 
 // Forward transform of a real source (extents E, placed at offsets off) into the
 // full spectrum S. Channels [0, C) of the view.
+// half (a real filter, D >= 2): keep only bins [0, F/2] of the last axis (Hermitian symmetry).
 static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pairing& pr, const int* E,
-                     const int* off, float2* S, cudaStream_t st, PassList* rec = nullptr) {
-  const SpecStrides ss = spec_strides(g, C);
+                     const int* off, float2* S, cudaStream_t st, PassList* rec = nullptr, bool half = false) {
+  const SpecStrides ss = spec_strides(g, C, half);
+  const int FL = half ? g.F[g.D - 1] / 2 + 1 : g.F[g.D - 1];  // stored bins of the last axis
   if (g.four) {
     // pass A: along n_a (stride Fb*C in S), lines (p, n_b, c); twiddle e^{-2 pi i k_a n_b / F}
     PassDesc a;
@@ -435,7 +440,7 @@ static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pa
     a.in_off = off[D - 1];
     a.n_in = E[D - 1];
     a.out_lo = 0;
-    a.n_out = g.F[D - 1];
+    a.n_out = FL;
     a.load_t_fastest = (src.sst[D - 1] == 1) ? 1 : 0;
     a.store_t_fastest = 0;
     finish_lines(a);
@@ -448,7 +453,7 @@ static int fwd_chain(const Geo& g, int C, const RealView& src, int tdt, const Pa
     int j = 0;
     for (int e = 0; e < D; ++e) {
       if (e == d) continue;
-      a.oth_ext[j] = e < d ? E[e] : g.F[e];
+      a.oth_ext[j] = e < d ? E[e] : (e == D - 1 ? FL : g.F[e]);
       a.ci_ost[j] = a.co_ost[j] = ss.st[e];
       ++j;
     }
@@ -579,6 +584,8 @@ struct ConvPlan {
   int Cc = 0;  // channels per chunk
   long long spec_x_bytes_per_ch = 0, spec_k_bytes_per_ch = 0;
   bool big2d = false;  // fused large-grid 2D kernels (big2d.cu) instead of the pass chain
+  bool khalf = false;  // the filter spectrum keeps bins [0, F/2] of the last axis only (product passes
+                       // of 2D / 3D convolutions read the other half mirrored and conjugated)
 };
 
 static size_t ws_budget() {
@@ -612,6 +619,10 @@ static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p) {
   p.Cc = (int)std::max<long long>(1, std::min<long long>(cc, p.C));
   p.big2d = p.g.D == 2 && !d->causal && p.g.F[0] == kB2F && p.g.F[1] == kB2F && p.g.N[0] <= kB2MaxN &&
             p.g.N[1] <= kB2MaxN && p.kB == 1 && !getenv("HYFFT_DISABLE_BIG2D");
+  const int F0 = p.g.F[0];
+  p.khalf = p.g.D >= 2 && !p.g.four && !p.big2d && (F0 == 32 || F0 == 64 || F0 == 128 || F0 == 256) &&
+            p.g.F[p.g.D - 1] % 2 == 0 && !getenv("HYFFT_DISABLE_CL_PASS") && !getenv("HYFFT_DISABLE_PRODUCT_PASS") &&
+            !getenv("HYFFT_FULL_KSPEC");
   return HYFFT_OK;
 }
 
@@ -655,7 +666,8 @@ static int to_float(const void* src, int dt, float* dst, int n, cudaStream_t st)
 // HYFFT_ERR_UNSUPPORTED (nothing launched) if the two passes do not line up.
 static int fused_conv_chain(const Geo& g, int Cc, const RealView& xc, int tin, const Pairing& px, const int* E,
                             const int* off, float2* S, const float2* Kh, bool shared, int conj, const RealView& yc,
-                            int tout, const int* lo, const int* cnt, const Epilogue& ep, cudaStream_t st) {
+                            int tout, const int* lo, const int* cnt, const Epilogue& ep, cudaStream_t st,
+                            bool khalf = false) {
   PassList fl, il;
   HY_TRY(fwd_chain(g, Cc, xc, tin, px, E, off, S, st, &fl));
   HY_TRY(inv_chain(g, Cc, S, yc, tout, px, lo, cnt, ep, st, &il));
@@ -690,8 +702,14 @@ static int fused_conv_chain(const Geo& g, int Cc, const RealView& xc, int tin, c
   m.mid = conj ? 2 : 1;
   m.kin = Kh;
   m.k_shared = shared ? 1 : 0;
-  m.k_pst = spec_strides(g, Cc).pst;
-  if (f.im == IN_CPLX) {
+  m.k_pst = spec_strides(g, Cc, khalf).pst;
+  if (f.im == IN_CPLX && khalf) {  // 2D / 3D lines along axis 0; the other axes 1 .. D-1 in order
+    const SpecStrides ks = spec_strides(g, Cc, true);
+    m.k_tst = ks.st[0];
+    m.k_ost[0] = g.D > 1 ? ks.st[1] : 0;
+    m.k_ost[1] = g.D > 2 ? ks.st[2] : 0;
+    m.k_half = 1;
+  } else if (f.im == IN_CPLX) {  // the filter spectrum has the signal spectrum's layout
     m.k_tst = f.d.ci_tst;
     m.k_ost[0] = f.d.ci_ost[0];
     m.k_ost[1] = f.d.ci_ost[1];
@@ -713,7 +731,7 @@ static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView&
   const RealView kc = offset_channels(kv, c0, 4);
   const RealView yc = offset_channels(yv, c0, eb);
   const int zero[3] = {0, 0, 0};
-  HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+  HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st, nullptr, p.khalf));
   Epilogue ep;
   if (Dfull) {
     ep.mode = OUT_REAL_SKIP;
@@ -723,8 +741,10 @@ static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView&
   const int rc = getenv("HYFFT_DISABLE_PRODUCT_PASS")
                      ? HYFFT_ERR_UNSUPPORTED
                      : fused_conv_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S, Kh, p.shared, 0, yc, p.dt, p.g.crop,
-                                        p.g.N, ep, st);
+                                        p.g.N, ep, st, p.khalf);
   if (rc != HYFFT_ERR_UNSUPPORTED) return rc;
+  // the elementwise product below reads the full filter spectrum
+  if (p.khalf) HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
   HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S, st));
   const long long per_pair = p.g.vol_F * Cc;
   spec_mul_kernel<<<grid_for(per_pair * p.px.P), 256, 0, st>>>(S, Kh, per_pair, p.px.P, p.shared ? 1 : 0);
@@ -763,10 +783,14 @@ static int fused_bwd_chain(const ConvPlan& p, int Cc, const RealView& xc, const 
   // Kh shares S's per-axis strides (the same [pair][F...][C] layout)
   a.kin = Kh;
   a.k_shared = p.shared ? 1 : 0;
-  a.k_pst = spec_strides(p.g, Cc).pst;
-  a.k_tst = a.ci_tst;
-  a.k_ost[0] = a.ci_ost[0];
-  a.k_ost[1] = a.ci_ost[1];
+  {
+    const SpecStrides ks = spec_strides(p.g, Cc, p.khalf);
+    a.k_pst = ks.pst;
+    a.k_tst = ks.st[0];
+    a.k_ost[0] = p.g.D > 1 ? ks.st[1] : 0;
+    a.k_ost[1] = p.g.D > 2 ? ks.st[2] : 0;
+    a.k_half = p.khalf ? 1 : 0;
+  }
   const int pl = p.shared ? p.px.P : 1;
   for (int i = 0; i + 1 < fx.n; ++i) HY_TRY(launch_pass(fx.r[i].d, fx.r[i].im, fx.r[i].om, fx.r[i].tin, fx.r[i].tout, st));
   for (int i = 0; i + 1 < fy.n; ++i) HY_TRY(launch_pass(fy.r[i].d, fy.r[i].im, fy.r[i].om, fy.r[i].tin, fy.r[i].tout, st));
@@ -785,7 +809,7 @@ static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView
   const RealView kc = offset_channels(kv, c0, 4);
   const RealView dyc = offset_channels(dyv, c0, eb);
   const int zero[3] = {0, 0, 0};
-  if (!kh_ready) HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+  if (!kh_ready) HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st, nullptr, p.khalf));
   if (dxv.ptr && dkv.ptr) {
     Epilogue ep;
     if (Dfull) {
@@ -797,6 +821,8 @@ static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView
                                    S2, Kh, dKh, st);
     if (rc != HYFFT_ERR_UNSUPPORTED) return rc;
   }
+  // the elementwise backward below reads the full filter spectrum
+  if (p.khalf) HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
   HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S1, st));
   HY_TRY(fwd_chain(p.g, Cc, dyc, p.dt, p.px, p.g.N, p.g.crop, S2, st));
   const long long per_pair = p.g.vol_F * Cc;

@@ -65,6 +65,10 @@ struct PassDesc {
   const float2* kin;
   long long k_pst, k_tst, k_ost[2];
   int k_shared;
+  // k_half: kin holds only bins [0, ext/2] of the last "other" axis (the spectrum of a real
+  // filter); a line whose last-axis bin is above ext/2 reads the conjugate of the mirrored
+  // line (every other-axis index and the point index t negated modulo their extents)
+  int k_half;
 
   void* rout;
   long long ro_bst, ro_cst, ro_tst, ro_ost[2];
@@ -513,8 +517,14 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
       cb_out[l] = p * d.ro_bst + (long long)c * d.ro_cst + (long long)o[0] * d.ro_ost[0] + (long long)o[1] * d.ro_ost[1];
       im_out[l] = has_im ? cb_out[l] + (long long)d.half * d.ro_bst : -1;
     }
-    if (MID)
-      kbase[l] = (d.k_shared ? 0 : p) * d.k_pst + (long long)o[0] * d.k_ost[0] + (long long)o[1] * d.k_ost[1] + c;
+    if (MID) {
+      int mo[2] = {o[0], o[1]};
+      const bool mir = d.k_half && 2 * o[d.n_oth - 1] > d.oth_ext[d.n_oth - 1];
+      if (mir)
+        for (int a = 0; a < d.n_oth; ++a) mo[a] = (d.oth_ext[a] - o[a]) % d.oth_ext[a];
+      kbase[l] = (d.k_shared ? 0 : p) * d.k_pst + (long long)mo[0] * d.k_ost[0] + (long long)mo[1] * d.k_ost[1] + c;
+      pad[l] = mir ? 1 : 0;
+    }
   }
   __syncthreads();
 
@@ -643,10 +653,12 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
     if constexpr (MID) {
       if (cb_in[l] >= 0) {
         const long long kb = kbase[l];
+        const bool mir = pad[l] != 0;
 #pragma unroll
         for (int k2 = 0; k2 < R2; ++k2) {
-          float2 kv = __ldg(d.kin + kb + (long long)(k1 + R1 * k2) * d.k_tst);
-          if (MID == 2) kv.y = -kv.y;
+          const int kk = k1 + R1 * k2;
+          float2 kv = __ldg(d.kin + kb + (long long)(mir ? ((F - kk) & (F - 1)) : kk) * d.k_tst);
+          if (mir != (MID == 2)) kv.y = -kv.y;
           v[k2] = cmul(v[k2], kv);
         }
       }
@@ -696,7 +708,7 @@ __global__ void __launch_bounds__(kClWarps * 32) fft_lines_cl_kernel(const PassD
 template <int R1, int R2>
 __host__ __device__ constexpr size_t cl_bwd_smem_bytes() {
   return sizeof(float2) * (2 * (size_t)R1 * R2 * cl_lines_per_cta<R1 * R2>() + R1 * R2) +
-         5 * sizeof(long long) * cl_lines_per_cta<R1 * R2>();
+         6 * sizeof(long long) * cl_lines_per_cta<R1 * R2>();
 }
 
 template <int R1, int R2>
@@ -715,6 +727,7 @@ __global__ void __launch_bounds__(kClWarps * 32, 3) fft_lines_cl_bwd_kernel(cons
   long long* bdx = bdy + NL;
   long long* bdk = bdx + NL;
   long long* bkh = bdk + NL;
+  long long* bmir = bkh + NL;  // 1: the filter line is read mirrored and conjugated (k_half)
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long nl = fx.nlines / pl;
   const long long line0 = (long long)blockIdx.x * NL;
@@ -742,7 +755,12 @@ __global__ void __launch_bounds__(kClWarps * 32, 3) fft_lines_cl_bwd_kernel(cons
     bdy[l] = p * fdy.ci_pst + (long long)o[0] * fdy.ci_ost[0] + (long long)o[1] * fdy.ci_ost[1] + c;
     bdx[l] = p * idx.co_pst + (long long)o[0] * idx.co_ost[0] + (long long)o[1] * idx.co_ost[1] + c;
     bdk[l] = ks * idk.co_pst + (long long)o[0] * idk.co_ost[0] + (long long)o[1] * idk.co_ost[1] + c;
-    bkh[l] = ks * fx.k_pst + (long long)o[0] * fx.k_ost[0] + (long long)o[1] * fx.k_ost[1] + c;
+    int mo[2] = {o[0], o[1]};
+    const bool mir = fx.k_half && 2 * o[fx.n_oth - 1] > fx.oth_ext[fx.n_oth - 1];
+    if (mir)
+      for (int a = 0; a < fx.n_oth; ++a) mo[a] = (fx.oth_ext[a] - o[a]) % fx.oth_ext[a];
+    bkh[l] = ks * fx.k_pst + (long long)mo[0] * fx.k_ost[0] + (long long)mo[1] * fx.k_ost[1] + c;
+    bmir[l] = mir ? 1 : 0;
   }
   __syncthreads();
 
@@ -785,9 +803,12 @@ __global__ void __launch_bounds__(kClWarps * 32, 3) fft_lines_cl_bwd_kernel(cons
       dftR<R2>(v, -1.f);
       const long long kb = bkh[l];
       if (bx[l] >= 0) {
+        const bool mir = bmir[l] != 0;
 #pragma unroll
         for (int k2 = 0; k2 < R2; ++k2) {
-          const float2 kv = __ldg(fx.kin + kb + (long long)(k1 + R1 * k2) * fx.k_tst);
+          const int kk = k1 + R1 * k2;
+          float2 kv = __ldg(fx.kin + kb + (long long)(mir ? ((F - kk) & (F - 1)) : kk) * fx.k_tst);
+          if (mir) kv.y = -kv.y;
           const float2 dk = cmulc(v[k2], u[k2]);  // DY * conj(X)
           v[k2] = cmulc(v[k2], kv);               // DY * conj(Kh)
           u[k2] = dk;

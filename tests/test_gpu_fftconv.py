@@ -121,6 +121,14 @@ def test_unfused_backward_matches_oracle(case, monkeypatch):
     test_ops_vs_oracle_seeded(case)
 
 
+@pytest.mark.parametrize("case", [SHAPES[3], SHAPES[7]], ids=["2d-64", "3d-16"])
+def test_full_filter_spectrum_matches_oracle(case, monkeypatch):
+    """2D / 3D product passes normally read half of the (Hermitian) filter spectrum and mirror
+    the rest; the full-spectrum form of the same passes matches too."""
+    monkeypatch.setenv("HYFFT_FULL_KSPEC", "1")
+    test_ops_vs_oracle_seeded(case)
+
+
 def test_per_sample_kernel_and_odd_batch():
     g = torch.Generator().manual_seed(1)
     b2 = _b2()
