@@ -90,7 +90,7 @@ def decay_filter(C: int, K: tuple[int, ...], gen: torch.Generator, causal: bool)
 
 
 def make_inputs(cfg: dict, B: int, C: int, c_off: int, seed: int = 0):
-    """Seeded synthetic inputs (CPU, generated in the order of the survey's recipe)."""
+    """Seeded synthetic inputs on the CPU (activations, filter, D, short-conv weights, dy in that order)."""
     g = torch.Generator().manual_seed(seed)
     nd, S, K, dt = cfg["nd"], cfg["S"], cfg["K"], cfg["dtype"]
     if cfg.get("op_only"):
