@@ -2,7 +2,7 @@
 
 Run in the build container, where the read-only reference tree is mounted:
 
-    python tests/golden/make_golden.py [--ref /path/to/nvSubquadratic]
+    python tests/golden/make_golden.py --ref /path/to/nvSubquadratic
 
 It writes small ``*.pt`` fixtures next to this file. The fixtures are committed;
 the reference is NOT needed at test time (it does not exist on the GPU box).
@@ -280,7 +280,7 @@ def make_cp(ref_path: str) -> dict:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="root of the nvSubquadratic source tree (holds nvsubquadratic/)")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     _install_omegaconf_stub()
