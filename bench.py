@@ -6,12 +6,18 @@
 One "step" = forward + backward of the fused Hyena mixer (configs 1-3: short depthwise
 conv, gates, FFT long conv with D-skip) or of the op-level causal conv (config 0) on one
 batch of seeded synthetic input. Inputs are resident in HBM for ``value``; ``e2e`` runs
-the same step through the public API from pinned host buffers (H2D of the inputs and
-D2H of the output and all gradients inside the timed region).
+the same step through the public API from pinned host buffers: the H2D copy of every
+input and the D2H copy of the step's output y are inside the timed region, while the
+gradients stay on the device (where an optimizer step would read them).
 
-Multi-GPU (torchrun, one rank per GPU): config 1 runs one independent replica per rank
-(weak scaling); config 2 shards the batch and config 3 the channels across ranks
-(strong scaling). The time is the max over ranks of the device-timed region.
+Default workload: config 2 (B=8, C=256, 128x128, bf16). On one GPU the run also measures
+config 1 (the ViT grid) the same way and reports it under ``secondary``.
+
+Multi-GPU (torchrun, one rank per GPU): config 2 shards the batch (strong scaling: B=8
+split over the ranks), and every timed step ends with one NCCL all-reduce of the filter,
+D and short-conv gradients (partial sums over each rank's images); config 3 shards the
+channels (no collective); config 1 runs one independent replica per rank (weak
+scaling). The time is the max over ranks of the device-timed region.
 
 ``--impl reference`` times the reference's CPU path (the CPU oracle restating
 nvsubquadratic/ops/fftconv.py + hyena_nd.py on torch.fft) on the host cores, rank 0 only.
@@ -375,17 +381,27 @@ def run_gpu(args, cfg, rank, world, device):
     from nvsubquadratic_b200.fftconv import causal_fftconv1d_fp32_bhl
     from nvsubquadratic_b200.hyena import hyena_fused
 
+    from nvsubquadratic_b200.dp import GradBucket, batch_shard
+
     B, C = cfg["B"], cfg["C"]
     c_off = 0
     if world > 1 and cfg["shard"] == "batch":
-        assert B % world == 0
+        # the full batch's seeded inputs, this rank's slice of the activations
+        inp = make_inputs(cfg, B, C, 0, seed=0)
+        for key in ("qkv", "dy", "x"):
+            if key in inp:
+                inp[key] = batch_shard(inp[key], rank, world).contiguous()
         B //= world
-    elif world > 1 and cfg["shard"] == "channel":
-        assert C % world == 0
-        C //= world
-        c_off = rank * C
-    inp = make_inputs(cfg, B, C, c_off, seed=rank if cfg["shard"] == "replica" else 0)
+    else:
+        if world > 1 and cfg["shard"] == "channel":
+            assert C % world == 0
+            C //= world
+            c_off = rank * C
+        inp = make_inputs(cfg, B, C, c_off, seed=rank if cfg["shard"] == "replica" else 0)
     dev_inp = {k: (v.to(device) if v is not None else None) for k, v in inp.items()}
+    # batch shards: the parameter gradients are partial sums over the rank's batch slice;
+    # one NCCL all-reduce of a flat fp32 bucket (filter, D, short-conv) completes each step
+    dp_group = torch.distributed.group.WORLD if (world > 1 and cfg["shard"] == "batch") else None
 
     op_only = cfg.get("op_only", False)
     if op_only:
@@ -419,15 +435,23 @@ def run_gpu(args, cfg, rank, world, device):
         for p in params:
             p.grad = None
 
+    bucket = GradBucket([p for p in params if p is not (x if op_only else qkv)], device) if dp_group else None
+
+    def reduce_grads():
+        if bucket is not None:
+            bucket.reduce(dp_group)
+
     # eager warm-up (also counts kernel launches of one step)
     for _ in range(max(1, args.warmup)):
         zero_grads()
         step()
+        reduce_grads()
     torch.cuda.synchronize()
     if args.profile:
         for _ in range(args.steps):
             zero_grads()
             step()
+            reduce_grads()
         torch.cuda.synchronize()
         return None
     n0 = _lib.launch_count()
@@ -475,6 +499,7 @@ def run_gpu(args, cfg, rank, world, device):
             flush.zero_()  # evict L2 between timed steps (outside the events)
             starts[i].record()
             graph.replay()
+            reduce_grads()  # batch shards: gradient all-reduce inside the timed step
             ends[i].record()
         torch.cuda.synchronize()
     if world > 1:
@@ -496,7 +521,7 @@ def run_gpu(args, cfg, rank, world, device):
         pass_ms[nm] = t3.item()
 
     # e2e through the public API from pinned host buffers (eager, no graph)
-    e2e_ms, h2d, d2h, copy_ms = e2e_time(cfg, inp, device, op_only, max(3, min(args.steps, 10)))
+    e2e_ms, h2d, d2h, copy_ms = e2e_time(cfg, inp, device, op_only, max(3, min(args.steps, 10)), dp_group)
     t2 = torch.tensor([e2e_ms], device=device)
     if world > 1:
         torch.distributed.all_reduce(t2, op=torch.distributed.ReduceOp.MAX)
@@ -505,7 +530,8 @@ def run_gpu(args, cfg, rank, world, device):
                 B=B, C=C, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h, copy_ms=copy_ms)
 
 
-def e2e_time(cfg, inp, device, op_only, steps):
+def e2e_time(cfg, inp, device, op_only, steps, dp_group=None):
+    from nvsubquadratic_b200.dp import GradBucket
     from nvsubquadratic_b200.fftconv import causal_fftconv1d_fp32_bhl
     from nvsubquadratic_b200.hyena import hyena_fused
 
@@ -546,6 +572,8 @@ def e2e_time(cfg, inp, device, op_only, steps):
             q, k, v = qkv.chunk(3, dim=-1)
             y = hyena_fused(q, k, v, f, D, sw, None, causal=cfg["causal"], gate1=cfg["g1"], gate2=cfg["g2"])
             y.backward(dy)
+            if dp_group is not None:  # batch shards: full-batch parameter gradients
+                GradBucket([f, D, sw], device).reduce(dp_group)
             res = [y]  # the step's result; the gradients stay on the device for the optimizer
             ins = [host["qkv"], host["filt"], host["D"], host["dy"]] + ([host["sw"]] if sw is not None else [])
         if not outs:
@@ -562,14 +590,48 @@ def e2e_time(cfg, inp, device, op_only, steps):
     return statistics.median(times), h2d, d2h, statistics.median(copy_times[1:])
 
 
+def summarize(name: str, cfg: dict, res: dict, world: int, steps: int, peaks: dict) -> dict:
+    """Whole-job throughput (all ranks' elements / max-over-ranks time), the roofline of the
+    dominant library pass and the end-to-end throughput of one measured configuration."""
+    N = math.prod(cfg["S"])
+    elems_job = res["B"] * res["C"] * N * world
+    t_step = res["total_ms"] / steps / 1e3
+    peak = peaks.get("hbm_gbs", 6650.0)
+    step_achieved = alg_bytes(cfg, res["B"], res["C"]) / t_step / 1e9
+    pbytes = pass_bytes(cfg, res["B"], res["C"])
+    dom = max(res["pass_ms"], key=res["pass_ms"].get)
+    achieved = pbytes[dom] / (res["pass_ms"][dom] / 1e3) / 1e9
+    traffic = None
+    if world == 1:  # the captures are of the single-GPU workload
+        try:
+            with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+                traffic = json.load(f).get(name, {}).get(dom)
+        except (OSError, ValueError):
+            pass
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "kernel": dom, "pass_ms": {k: round(v, 4) for k, v in res["pass_ms"].items()},
+                "pass_bytes": pbytes,
+                "scope": "dominant library pass: its algorithmic bytes / its mean CUDA-event time "
+                         "(L2 flushed before each timed call); traffic = ncu dram read+write bytes "
+                         "per call from profiles/ncu_traffic.json",
+                "step_achieved": round(step_achieved, 1), "step_frac": round(step_achieved / peak, 4),
+                "peak_source": ("MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks
+                                else "fallback 6650 GB/s (of fallback)")}
+    return {"value": elems_job / t_step / 1e9, "t_step": t_step, "roofline": roofline,
+            "e2e_value": elems_job / (res["e2e_ms"] / 1e3) / 1e9}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="cfg1", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--secondary", default="cfg1",
+                    help="on one GPU, also measure this configuration and report it under 'secondary' ('' for none)")
     ap.add_argument("--profile", action="store_true",
                     help="run warmup + steps eager fwd+bwd steps and exit (for ncu captures)")
     ap.add_argument("--channels", type=int, default=None,
@@ -592,6 +654,10 @@ def main():
     dtname = {torch.float32: "f32", torch.bfloat16: "bf16"}[cfg["dtype"]]
     config = {"workload": args.config + ": " + cfg["desc"], "batch": B, "channels": C, "spatial": list(cfg["S"]),
               "filter": list(cfg["K"]), "sharding": cfg["shard"], "l2": "flushed between timed steps (256 MB write)"}
+    if cfg["shard"] == "batch":
+        config["parallelism"] = (f"dp{world}: batch shards of {B // world if B % world == 0 else '?'} images per "
+                                 "rank, filter/D/short-conv gradients summed by one NCCL all-reduce of a flat fp32 "
+                                 "bucket inside every timed step" if world > 1 else "dp1")
     if cfg["shard"] == "cp":
         config["l2"] = "inputs (GBs per rank) far larger than L2; no flush"
         config["parallelism"] = f"cp{world}"
@@ -632,30 +698,14 @@ def main():
             torch.distributed.destroy_process_group()
         return
 
-    # whole-job throughput: all ranks' elements / max-over-ranks time
-    elems_rank = res["B"] * res["C"] * N
-    elems_job = elems_rank * world
-    t_step = res["total_ms"] / args.steps / 1e3
-    value = elems_job / t_step / 1e9
-    bytes_rank = alg_bytes(cfg, res["B"], res["C"])
     peaks = {}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peaks = json.load(f)
     except OSError:
         pass
-    peak = peaks.get("hbm_gbs", 6650.0)
-    step_achieved = bytes_rank / t_step / 1e9
-    pbytes = pass_bytes(cfg, res["B"], res["C"])
-    dom = max(res["pass_ms"], key=res["pass_ms"].get)
-    achieved = pbytes[dom] / (res["pass_ms"][dom] / 1e3) / 1e9
-    traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
-            traffic = json.load(f).get(args.config, {}).get(dom)
-    except (OSError, ValueError):
-        pass
-    e2e_val = elems_job / (res["e2e_ms"] / 1e3) / 1e9
+    summ = summarize(args.config, cfg, res, world, args.steps, peaks)
+    value, t_step, e2e_val = summ["value"], summ["t_step"], summ["e2e_value"]
 
     if rank == 0:
         out = {
@@ -663,16 +713,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(t_step * 1e3, 4), "higher_is_better": True,
             "scaling": "weak" if cfg["shard"] == "replica" else "strong", "vs_baseline": None, "dtype": dtname,
             "data": "synthetic (seeded N(0,1) activations, random-init filters)", "config": config,
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": traffic,
-                         "kernel": dom, "pass_ms": {k: round(v, 4) for k, v in res["pass_ms"].items()},
-                         "pass_bytes": pbytes,
-                         "scope": "dominant library pass: its algorithmic bytes / its mean CUDA-event time "
-                                  "(L2 flushed before each timed call); traffic = ncu dram read+write bytes "
-                                  "per call from profiles/ncu_traffic.json",
-                         "step_achieved": round(step_achieved, 1), "step_frac": round(step_achieved / peak, 4),
-                         "peak_source": ("MEASURED_PEAKS.json hbm_gbs (of measured)" if "hbm_gbs" in peaks
-                                         else "fallback 6650 GB/s (of fallback)")},
+            "roofline": summ["roofline"],
             "e2e": {"value": round(e2e_val, 4), "unit": "GElem/s", "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"], "ms_per_step": round(res["e2e_ms"], 4),
                     "h2d_copy_ms": round(res["copy_ms"], 4) if res.get("copy_ms") is not None else None,
@@ -684,6 +725,18 @@ def main():
             gel, threads, sample, _ = cpu_reference_time(cfg)
             out["cpu_baseline"] = {"value": round(gel, 6), "unit": "GElem/s", "cores": threads, "kind": "port",
                                    "sample": sample}
+        if world == 1 and args.secondary and args.secondary != args.config:
+            # a second configuration measured the same way in the same run (single GPU only)
+            cfg2 = CONFIGS[args.secondary]
+            res2 = run_gpu(args, cfg2, rank, world, device)
+            s2 = summarize(args.secondary, cfg2, res2, world, args.steps, peaks)
+            out["secondary"] = {"workload": args.secondary + ": " + cfg2["desc"], "value": round(s2["value"], 4),
+                                "unit": "GElem/s", "ms_per_step": round(s2["t_step"] * 1e3, 4),
+                                "roofline": s2["roofline"],
+                                "e2e": {"value": round(s2["e2e_value"], 4), "unit": "GElem/s",
+                                        "ms_per_step": round(res2["e2e_ms"], 4), "h2d_bytes_per_step": res2["h2d"],
+                                        "d2h_bytes_per_step": res2["d2h"]},
+                                "gpu_launches": res2["launches"] * args.steps, "clocks": res2["clocks"]}
         print(json.dumps(out))
     if world > 1:
         torch.distributed.barrier()

@@ -99,8 +99,13 @@ HYFFT_API int hyfft_conv_forward(const hyfft_conv_desc* d, const void* x, const 
  * device image, one per device; channels are processed in chunks that fit it.
  *
  * - The first call on a device looks up that array's address for the device (with
- *   the device that owns x current); make that first call before any stream
- *   capture on the device.
+ *   the device that owns x current) and keeps it for the life of the process; make
+ *   that first call before any stream capture on the device. A device reset
+ *   (cudaDeviceReset, or tearing down and re-creating the primary context) can move
+ *   the array, so this entry point does not support calls after a reset.
+ * - It always runs the chunked pass chain, also for the 2D shapes that
+ *   hyfft_conv_forward sends to its large-grid kernels; results agree within the
+ *   tolerance of the dtype, not bit for bit.
  * - Problems whose single-channel spectra (plus the [H] float shortcut vector) do
  *   not fit in HYFFT_CONV_SCRATCH_MAX_BYTES are rejected with HYFFT_ERR_WORKSPACE
  *   before anything is launched; use hyfft_conv_forward with a workspace for them.

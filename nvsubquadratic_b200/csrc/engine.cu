@@ -595,7 +595,9 @@ static size_t ws_budget() {
   return (size_t)mb << 20;
 }
 
-static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p) {
+// allow_big2d = false plans the pass chain even for shapes the large-grid 2D kernels
+// would take (the static-scratch forward runs only the chunked pass chain).
+static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p, bool allow_big2d = true) {
   if (!d) return fail(HYFFT_ERR_INVALID, "null descriptor");
   HY_TRY(make_geo(d->ndim, d->n, d->k, d->causal, p.g));
   if (d->batch < 1 || d->channels < 1) return fail(HYFFT_ERR_INVALID, "batch and channels must be positive");
@@ -617,7 +619,7 @@ static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p) {
   const long long per_ch = 2 * (p.spec_x_bytes_per_ch + p.spec_k_bytes_per_ch);
   long long cc = (long long)(ws_budget() / (size_t)std::max<long long>(per_ch, 1));
   p.Cc = (int)std::max<long long>(1, std::min<long long>(cc, p.C));
-  p.big2d = p.g.D == 2 && !d->causal && p.g.F[0] == kB2F && p.g.F[1] == kB2F && p.g.N[0] <= kB2MaxN &&
+  p.big2d = allow_big2d && p.g.D == 2 && !d->causal && p.g.F[0] == kB2F && p.g.F[1] == kB2F && p.g.N[0] <= kB2MaxN &&
             p.g.N[1] <= kB2MaxN && p.kB == 1 && !getenv("HYFFT_DISABLE_BIG2D");
   const int F0 = p.g.F[0];
   p.khalf = p.g.D >= 2 && !p.g.four && !p.big2d && (F0 == 32 || F0 == 64 || F0 == 128 || F0 == 256) &&
@@ -1069,7 +1071,7 @@ extern "C" {
 int hyfft_conv_forward_static_scratch(const hyfft_conv_desc* d, const void* x, const float* kernel,
                                       const void* shortcut, void* y, void* stream) {
   ConvPlan p;
-  HY_TRY(make_conv_plan(d, p));
+  HY_TRY(make_conv_plan(d, p, /*allow_big2d=*/false));
   if (!x || !kernel || !y) return fail(HYFFT_ERR_INVALID, "null tensor pointer");
   // Chunk the channels so that one chunk's spectra, the float shortcut vector and the
   // 256-byte alignment padding of the two spectrum buffers fit the scratch.

@@ -5,8 +5,8 @@
   against the plain-torch restatement of the same permutations.
 * On 2+ GPUs (NCCL, one process per GPU): the CP fused Hyena mixer (sequence-sharded
   zigzag input -> all-to-all -> fused kernels on the local channel block -> all-to-all)
-  matches the single-device fused mixer on the gathered tensors, forward and backward,
-  for the 1D causal long-context configuration and a 2D grid.
+  matches the single-device fused mixer and the CPU oracle on the gathered tensors,
+  forward and backward, for the 1D causal long-context configuration and a 2D grid.
 """
 
 import os
@@ -126,6 +126,20 @@ def _cp_worker(rank, world, port, case, result_dir):
     dist.all_reduce(dD)
     got = [y, dq, dk, dv, dfilt, dD]
     errs = [rel_l2(a, b) for a, b in zip(ref, got)]
+    if rank == 0:
+        # and against the CPU oracle composition (hyena_nd.py:497-583 restated) on the
+        # gathered tensors with the module's own parameters
+        from oracle.hyena import hyena_forward
+
+        qr, kr, vr = (t.clone().requires_grad_(True) for t in (q, k, v))
+        fr = filt.clone().requires_grad_(True)
+        Dr = mod.shortcut.detach().cpu().to(dt).requires_grad_(True)
+        swr = mod.short_weight.detach().cpu() if mod.short_weight is not None else None
+        yr = hyena_forward(qr, kr, vr, fr, Dr, swr, None, causal=causal, short_causal=mod.short_causal,
+                           gate1=g1, gate2=g2)
+        yr.backward(dy)
+        oracle = [yr, qr.grad, kr.grad, vr.grad, fr.grad, Dr.grad]
+        errs += [rel_l2(a, b) for a, b in zip(oracle, got)]
     torch.save(errs, os.path.join(result_dir, f"rank{rank}.pt"))
     dist.barrier()
     dist.destroy_process_group()

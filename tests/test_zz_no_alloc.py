@@ -3,8 +3,9 @@ library's fixed device scratch instead of a caller workspace.
 
 Each case calls it twice in a row through the C ABI and compares both outputs with
 hyfft_conv_forward (caller workspace) on the same inputs, then once more on fresh
-inputs; one case is large enough to be split into several channel chunks, and one is
-too large for the scratch and must be refused before anything runs. The file is
+inputs; some cases are large enough to be split into several channel chunks (one of
+them a 128 x 128 grid that the workspace entry point runs on its large-grid kernels),
+and one is too large for the scratch and must be refused before anything runs. The file is
 collected last and also passes alone in a fresh process.
 """
 
@@ -29,6 +30,11 @@ CASES = [
     (2, 8, (8, 8, 8), (15, 15, 15), 2, False, torch.float32, BLH, False),
     # 2 MiB of spectra per channel: 24 channels run as chunks of 15 and 9
     (2, 24, (65536,), (65536,), 1, False, torch.float32, BHL, True),
+    # shapes the workspace entry point sends to its large-grid 2D kernels (F = 256 x 256,
+    # N <= 128, shared kernel); here they run the pass chain: 1 MiB of spectra per
+    # channel, so 4 channels fit one chunk and 64 channels run as chunks of 31, 31, 2
+    (2, 4, (128, 128), (128, 128), 1, False, torch.bfloat16, BLH, True),
+    (2, 64, (128, 128), (128, 128), 1, False, torch.float32, BHL, True),
 ]
 
 
