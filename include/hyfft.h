@@ -211,6 +211,20 @@ HYFFT_API int hyfft_cp_permute_cl(const void* src, void* dst, int32_t op, int64_
                                   int64_t G, int64_t C, int32_t P, int32_t zigzag, int32_t elem_bytes,
                                   void* stream);
 
+/* The full-C side of the channels-last exchange for a window of every rank's channel
+ * block, so that a caller can move the channels in groups and overlap each group's
+ * all-to-all with the computation on another group (the reference moves the whole
+ * tensor in one all_to_all_single, a2a_comms.py:194 and :277).
+ *   PACK_SEQ_TO_CHAN    [B, l, rest, G, C] -> send [P, B, l, rest, G, c_cnt]: for every
+ *                       destination rank j, channels [j*C/P + c_off, j*C/P + c_off + c_cnt)
+ *   UNPACK_CHAN_TO_SEQ  recv [P, B, l, rest, G, c_cnt] -> those channels of [B, l, rest, G, C]
+ *                       (the other channels of dst are left as they are)
+ * 0 <= c_off, c_off + c_cnt <= C/P. The channel-block side of the same exchange is
+ * hyfft_cp_permute_cl with C = c_cnt * P.                                           */
+HYFFT_API int hyfft_cp_permute_cl_window(const void* src, void* dst, int32_t op, int64_t B, int64_t l_rows,
+                                         int64_t rest, int64_t G, int64_t C, int32_t P, int64_t c_off,
+                                         int64_t c_cnt, int32_t elem_bytes, void* stream);
+
 /* ---------------------------------------------------------------- misc */
 /* Message of the most recent error on this thread ("" if none). */
 HYFFT_API const char* hyfft_last_error(void);

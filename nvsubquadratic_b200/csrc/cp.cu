@@ -30,6 +30,9 @@ struct CpDesc {
   int P, zigzag;
   long long rows, run;                // rows of `run` contiguous elements
   long long G;                        // channel groups (channels-last modes)
+  // channels-last pack (seq -> chan) / unpack (chan -> seq) on the full-C side: rank j's
+  // channels start at j * cblk + coff of the C channels (cblk = d, coff = 0 for the whole block)
+  long long cblk, coff;
 };
 
 __device__ __forceinline__ void cp_row(const CpDesc& c, long long row, long long& so, long long& dof) {
@@ -75,7 +78,7 @@ __device__ __forceinline__ void cp_row(const CpDesc& c, long long row, long long
     }
     case CL_PACK_S2F: {  // row = (j, b, t, g): dst[j,b,t,g,:] = src[b,t,g, j*d : (j+1)*d]
       const long long g = row % c.G, r1 = row / c.G, t = r1 % c.l, r2 = r1 / c.l, b = r2 % c.B, j = r2 / c.B;
-      so = ((b * c.l + t) * c.G + g) * c.C + j * c.d;
+      so = ((b * c.l + t) * c.G + g) * c.C + j * c.cblk + c.coff;
       dof = (((j * c.B + b) * c.l + t) * c.G + g) * c.d;
       break;
     }
@@ -108,7 +111,7 @@ __device__ __forceinline__ void cp_row(const CpDesc& c, long long row, long long
     default: {  // CL_UNPACK_F2S: row = (r, b, t, g): dst[b,t,g, r*d : (r+1)*d] = src[r,b,t,g,:]
       const long long g = row % c.G, r1 = row / c.G, t = r1 % c.l, r2 = r1 / c.l, b = r2 % c.B, r = r2 / c.B;
       so = (((r * c.B + b) * c.l + t) * c.G + g) * c.d;
-      dof = ((b * c.l + t) * c.G + g) * c.C + r * c.d;
+      dof = ((b * c.l + t) * c.G + g) * c.C + r * c.cblk + c.coff;
       break;
     }
   }
@@ -148,8 +151,9 @@ static int cp_launch(CpDesc c, const void* src, void* dst, int eb, cudaStream_t 
   const bool aligned = ((uintptr_t)src % 16 == 0) && ((uintptr_t)dst % 16 == 0);
   // every row offset is a multiple of `run` or of h*rest; require those to be 16-byte multiples
   int vec_ok;
-  if (c.mode >= CL_PACK_S2F) {  // every offset is a multiple of d or C elements
-    vec_ok = aligned && ((c.d * eb) % 16 == 0) && ((c.C * eb) % 16 == 0) && ((c.run * eb) % 16 == 0);
+  if (c.mode >= CL_PACK_S2F) {  // every offset is a multiple of d, C or cblk elements (plus coff)
+    vec_ok = aligned && ((c.d * eb) % 16 == 0) && ((c.C * eb) % 16 == 0) && ((c.run * eb) % 16 == 0) &&
+             ((c.cblk * eb) % 16 == 0) && ((c.coff * eb) % 16 == 0);
   } else {
     const long long unit = c.zigzag && (c.mode == UNPACK_S2F || c.mode == PACK_F2S) ? c.h * c.rest : c.run;
     vec_ok = aligned && ((c.run * eb) % 16 == 0) && ((unit * eb) % 16 == 0) && ((c.l * c.rest * eb) % 16 == 0) &&
@@ -224,6 +228,7 @@ int hyfft_cp_permute_cl(const void* src, void* dst, int32_t op, int64_t B, int64
   if (bind_device_of(src) != HYFFT_OK) return HYFFT_ERR_CUDA;
   CpDesc c{};
   c.B = B; c.C = C; c.d = C / P; c.G = G; c.P = P; c.zigzag = zigzag ? 1 : 0; c.rest = 1;
+  c.cblk = c.d; c.coff = 0;
   c.l = l_rows * rest;                        // positions per rank
   c.L = c.l * P;                              // positions of the full sequence
   c.h = zigzag ? (l_rows / 2) * rest : c.l;   // positions per zigzag chunk
@@ -242,6 +247,27 @@ int hyfft_cp_permute_cl(const void* src, void* dst, int32_t op, int64_t B, int64
     case HYFFT_CP_UNPACK_CHAN_TO_SEQ: c.mode = CL_UNPACK_F2S; c.rows = (long long)P * B * c.l * G; c.run = c.d; break;
     default: return HYFFT_ERR_INVALID;
   }
+  return cp_launch(c, src, dst, elem_bytes, (cudaStream_t)stream);
+}
+
+int hyfft_cp_permute_cl_window(const void* src, void* dst, int32_t op, int64_t B, int64_t l_rows, int64_t rest,
+                               int64_t G, int64_t C, int32_t P, int64_t c_off, int64_t c_cnt, int32_t elem_bytes,
+                               void* stream) {
+  if (P < 1 || !src || !dst || B < 1 || l_rows < 1 || rest < 1 || G < 1 || C < 1 || C % P != 0)
+    return HYFFT_ERR_INVALID;
+  const long long d = C / P;
+  if (c_off < 0 || c_cnt < 1 || c_off + c_cnt > d) return HYFFT_ERR_INVALID;
+  if (op != HYFFT_CP_PACK_SEQ_TO_CHAN && op != HYFFT_CP_UNPACK_CHAN_TO_SEQ) return HYFFT_ERR_INVALID;
+  if (bind_device_of(src) != HYFFT_OK) return HYFFT_ERR_CUDA;
+  CpDesc c{};
+  c.B = B; c.C = C; c.d = c_cnt; c.G = G; c.P = P; c.zigzag = 0; c.rest = 1;
+  c.cblk = d; c.coff = c_off;
+  c.l = l_rows * rest;
+  c.L = c.l * P;
+  c.h = c.l;
+  c.mode = op == HYFFT_CP_PACK_SEQ_TO_CHAN ? CL_PACK_S2F : CL_UNPACK_F2S;
+  c.rows = (long long)P * B * c.l * G;
+  c.run = c_cnt;
   return cp_launch(c, src, dst, elem_bytes, (cudaStream_t)stream);
 }
 

@@ -143,6 +143,78 @@ def _chunks(qkv):
     return qkv[..., :C], qkv[..., C:2 * C], qkv[..., 2 * C:]
 
 
+def _params32(filt, D, short_w, short_b, C):
+    """float32 contiguous copies of the parameters the library reads (no copy when they
+    already are); short_w flattened to [3C, taps]."""
+    filt32 = filt.detach().to(torch.float32).contiguous()
+    D32 = D.detach().to(torch.float32).contiguous()
+    sw32 = short_w.detach().to(torch.float32).reshape(3 * C, -1).contiguous() if short_w is not None else None
+    sb32 = short_b.detach().to(torch.float32).contiguous() if short_b is not None else None
+    return filt32, D32, sw32, sb32
+
+
+def forward_call(q, k, v, filt32, D32, sw32, sb32, cfg):
+    """One ``hyfft_hyena_forward`` on q, k, v ``[B, *S, C]`` (contiguous, or the three
+    channel chunks of one packed ``[B, *S, 3C]`` tensor). Returns ``(y, state)``; the
+    state (descriptor, saved buffer, backward workspace size) feeds ``backward_call``."""
+    dev = q.device
+    causal, short_k, short_causal, g1, g2 = cfg
+    B, C = q.shape[0], q.shape[-1]
+    y = torch.empty(q.shape, dtype=q.dtype, device=dev)
+    desc, (wf, wb, sv) = _plan(B, C, tuple(q.shape[1:-1]), tuple(filt32.shape[2:]), causal, short_k, short_causal,
+                               sb32 is not None, g1, g2, q.dtype, _pos_strides(q), _pos_strides(y))
+    ws = _lib.workspace(wf, dev)
+    saved = _lib.workspace(sv, dev)
+    rc = _lib.load().hyfft_hyena_forward(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                         filt32.data_ptr(), D32.data_ptr(), _lib.ptr(sw32), _lib.ptr(sb32),
+                                         y.data_ptr(), saved.data_ptr(), ws.data_ptr(), ws.numel(),
+                                         _lib.stream_ptr(dev))
+    _lib.check(rc, "hyfft_hyena_forward")
+    return y, (desc, saved, wb)
+
+
+def backward_call(q, k, v, filt32, D32, sw32, sb32, state, dy, dq, dk, dv):
+    """One ``hyfft_hyena_backward``: dq, dk, dv are written with q's strides (one packed
+    buffer for packed views); returns float32 (dfilt, dD, dshort_w [3C, taps], dshort_b)."""
+    desc, saved, wb = state
+    dev = q.device
+    ws = _lib.workspace(wb, dev)
+    dfilt = torch.empty_like(filt32)
+    dD = torch.empty_like(D32)
+    dsw = torch.empty_like(sw32) if sw32 is not None else None
+    dsb = torch.empty_like(sb32) if sb32 is not None else None
+    rc = _lib.load().hyfft_hyena_backward(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                          filt32.data_ptr(), D32.data_ptr(), _lib.ptr(sw32), _lib.ptr(sb32),
+                                          dy.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                                          dfilt.data_ptr(), dD.data_ptr(), _lib.ptr(dsw), _lib.ptr(dsb),
+                                          saved.data_ptr(), ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
+    _lib.check(rc, "hyfft_hyena_backward")
+    return dfilt, dD, dsw, dsb
+
+
+def _in_place_views(q, k, v):
+    """q, k, v as the library reads them: in place when contiguous or the three chunks of
+    one packed projection (their gradients then share that layout); else contiguous copies."""
+    strides = _pos_strides(q)
+    dense = (math.prod(q.shape[1:]), q.shape[-1])
+    if strides is None or _pos_strides(k) != strides or _pos_strides(v) != strides or (
+            strides != dense and not _packed_views(q, k, v)):
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    return q, k, v
+
+
+def _grad_buffers(q):
+    """dq, dk, dv with q's layout: separate tensors for contiguous q, else three chunks of
+    one packed [B, *S, 3C] buffer (returned as the fourth value)."""
+    shape, C, dev = q.shape, q.shape[-1], q.device
+    if q.is_contiguous():
+        dq, dk, dv = (torch.empty(shape, dtype=q.dtype, device=dev) for _ in range(3))
+        return dq, dk, dv, None
+    dqkv = torch.empty(tuple(shape[:-1]) + (3 * C,), dtype=q.dtype, device=dev)
+    dq, dk, dv = _chunks(dqkv)
+    return dq, dk, dv, dqkv
+
+
 class _HyenaFunction(torch.autograd.Function):
     """Fused Hyena on q, k, v (PACKED False) or on their packed [B, *S, 3C] projection
     (PACKED True: one input, one gradient)."""
@@ -154,38 +226,13 @@ class _HyenaFunction(torch.autograd.Function):
             q, k, v = _chunks(qkv)
         else:
             q, k, v, filt, D, short_w, short_b, cfg = args
-        causal, short_k, short_causal, g1, g2 = cfg
-        dev = _lib.require_cuda(q, k, v, filt, D, short_w, short_b)
-        lib = _lib.load()
-        # q, k, v are used in place when contiguous or the three chunks of one packed
-        # projection (their gradients then share that layout); anything else is copied
-        strides = _pos_strides(q)
-        dense = (math.prod(q.shape[1:]), q.shape[-1])
-        if strides is None or _pos_strides(k) != strides or _pos_strides(v) != strides or (
-                strides != dense and not _packed_views(q, k, v)):
-            q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-            strides = _pos_strides(q)
+        _lib.require_cuda(q, k, v, filt, D, short_w, short_b)
+        q, k, v = _in_place_views(q, k, v)
         ctx.packed = packed
-        B, C = q.shape[0], q.shape[-1]
-        spatial = tuple(q.shape[1:-1])
-        kshape = tuple(filt.shape[2:])
-        y = torch.empty(q.shape, dtype=q.dtype, device=dev)
-        out_strides = _pos_strides(y)
-        filt32 = filt.detach().to(torch.float32).contiguous()
-        D32 = D.detach().to(torch.float32).contiguous()
-        sw32 = short_w.detach().to(torch.float32).reshape(3 * C, -1).contiguous() if short_w is not None else None
-        sb32 = short_b.detach().to(torch.float32).contiguous() if short_b is not None else None
-        desc, (wf, wb, sv) = _plan(B, C, spatial, kshape, causal, short_k, short_causal, short_b is not None, g1,
-                                   g2, q.dtype, strides, out_strides)
-        ctx.wb = wb
-        ws = _lib.workspace(wf, dev)
-        saved = _lib.workspace(sv, dev)
-        rc = lib.hyfft_hyena_forward(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), filt32.data_ptr(),
-                                     D32.data_ptr(), _lib.ptr(sw32), _lib.ptr(sb32), y.data_ptr(), saved.data_ptr(),
-                                     ws.data_ptr(), ws.numel(), _lib.stream_ptr(dev))
-        _lib.check(rc, "hyfft_hyena_forward")
-        ctx.save_for_backward(q, k, v, filt32, D32, sw32, sb32, saved)
-        ctx.desc = desc
+        filt32, D32, sw32, sb32 = _params32(filt, D, short_w, short_b, q.shape[-1])
+        y, state = forward_call(q, k, v, filt32, D32, sw32, sb32, cfg)
+        ctx.save_for_backward(q, k, v, filt32, D32, sw32, sb32, state[1])
+        ctx.state = (state[0], state[2])
         ctx.dtypes = (filt.dtype, D.dtype, short_w.dtype if short_w is not None else None,
                       short_b.dtype if short_b is not None else None)
         ctx.sw_shape = short_w.shape if short_w is not None else None
@@ -194,31 +241,10 @@ class _HyenaFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         q, k, v, filt32, D32, sw32, sb32, saved = ctx.saved_tensors
-        dev = q.device
-        lib = _lib.load()
-        desc = ctx.desc
-        B, C = q.shape[0], q.shape[-1]
+        desc, wb = ctx.state
         dyc = dy.to(q.dtype).contiguous()
-        wb = ctx.wb
-        ws = _lib.workspace(wb, dev)
-        shape = q.shape
-        # dq, dk, dv are written with q's strides: one packed buffer for packed views
-        if q.is_contiguous():
-            dq, dk, dv = (torch.empty(shape, dtype=q.dtype, device=dev) for _ in range(3))
-            dqkv = None
-        else:
-            dqkv = torch.empty(tuple(shape[:-1]) + (3 * C,), dtype=q.dtype, device=dev)
-            dq, dk, dv = _chunks(dqkv)
-        dfilt = torch.empty_like(filt32)
-        dD = torch.empty_like(D32)
-        dsw = torch.empty_like(sw32) if sw32 is not None else None
-        dsb = torch.empty_like(sb32) if sb32 is not None else None
-        rc = lib.hyfft_hyena_backward(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(), filt32.data_ptr(),
-                                      D32.data_ptr(), _lib.ptr(sw32), _lib.ptr(sb32), dyc.data_ptr(), dq.data_ptr(),
-                                      dk.data_ptr(), dv.data_ptr(), dfilt.data_ptr(), dD.data_ptr(), _lib.ptr(dsw),
-                                      _lib.ptr(dsb), saved.data_ptr(), ws.data_ptr(), ws.numel(),
-                                      _lib.stream_ptr(dev))
-        _lib.check(rc, "hyfft_hyena_backward")
+        dq, dk, dv, dqkv = _grad_buffers(q)
+        dfilt, dD, dsw, dsb = backward_call(q, k, v, filt32, D32, sw32, sb32, (desc, saved, wb), dyc, dq, dk, dv)
         fdt, Ddt, swdt, sbdt = ctx.dtypes
         dfilt = dfilt.to(fdt)
         dD = dD.to(Ddt)

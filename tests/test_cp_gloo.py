@@ -45,6 +45,20 @@ def cpu_permute(x, op, B, l_rows, rest, G, C, P, zigzag, out):
     return out
 
 
+def cpu_permute_window(x, op, B, l_rows, rest, G, C, P, c_off, c_cnt, out):
+    """Plain-torch restatement of hyfft_cp_permute_cl_window (the full-C side of the
+    exchange for channels [j*C/P + c_off, j*C/P + c_off + c_cnt) of every rank block j)."""
+    d = C // P
+    if op == 0:  # [B, l, *rest, G, C] -> [P, B, l, *rest, G, c_cnt]
+        out.copy_(torch.stack([x[..., j * d + c_off:j * d + c_off + c_cnt] for j in range(P)], dim=0))
+    elif op == 3:  # [P, B, l, *rest, G, c_cnt] -> those channels of [B, l, *rest, G, C]
+        for r in range(P):
+            out[..., r * d + c_off:r * d + c_off + c_cnt] = x[r]
+    else:
+        raise ValueError(op)
+    return out
+
+
 def _worker(rank, world, port, result_dir):
     import sys
 
@@ -151,11 +165,26 @@ def _failing_worker(rank, world, port):
     cp.all_to_all_single_fn(dist.group.WORLD, "split_to_full", x, True)  # times out -> raises
 
 
-def _oracle_local(q, k, v, filt, D, sw, sb, *, causal, short_causal, gate1, gate2):
+def _oracle_local_forward(q, k, v, filt, D, sw, sb, cfg):
+    """CPU stand-in for the fused mixer on one channel group (the oracle with autograd)."""
     from oracle.hyena import hyena_forward
 
-    return hyena_forward(q, k, v, filt, D, sw, sb, causal=causal, short_causal=short_causal, gate1=gate1,
-                         gate2=gate2)
+    causal, short_k, short_causal, g1, g2 = cfg
+    ins = [None if t is None else t.detach().clone().requires_grad_(True) for t in (q, k, v, filt, D, sw, sb)]
+    with torch.enable_grad():
+        y = hyena_forward(*ins, causal=causal, short_causal=short_causal, gate1=g1, gate2=g2)
+    return y.detach(), (ins, y)
+
+
+def _oracle_local_backward(state, dy, dq, dk, dv):
+    ins, y = state
+    grads = iter(torch.autograd.grad(y, [t for t in ins if t is not None], dy))
+    g = [None if t is None else next(grads) for t in ins]
+    dq.copy_(g[0])
+    dk.copy_(g[1])
+    dv.copy_(g[2])
+    dsw = g[5].reshape(g[5].shape[0], -1) if g[5] is not None else None
+    return g[3], g[4], dsw, g[6]
 
 
 CP_MIXER_CASES = [
@@ -180,7 +209,9 @@ def _mixer_worker(rank, world, port, result_dir):
 
     dist.init_process_group("gloo", rank=rank, world_size=world)
     cp._permute_impl = cpu_permute
-    cp._local_mixer = _oracle_local
+    cp._permute_window_impl = cpu_permute_window
+    cp._local_forward = _oracle_local_forward
+    cp._local_backward = _oracle_local_backward
     group = dist.group.WORLD
     out = []
     for nd, B, C, S, causal, sk, g1, g2 in CP_MIXER_CASES:
@@ -216,10 +247,11 @@ def _mixer_worker(rank, world, port, result_dir):
 
 @pytest.mark.parametrize("world", [2, 4])
 def test_cp_mixer_choreography_matches_single_device(world, tmp_path):
-    """hyena_context_parallel (zigzag split -> seq->chan all-to-all -> local mixer on the
-    channel block -> chan->seq all-to-all, and the autograd duals) reproduces the
+    """hyena_context_parallel (zigzag split -> per channel group: seq->chan all-to-all ->
+    local mixer -> chan->seq all-to-all, pipelined; and the backward duals) reproduces the
     single-device mixer and its gradients; the local mixer and the permutations are the
-    CPU restatements here, the CUDA ones are covered by the GPU tests."""
+    CPU restatements here, the CUDA ones are covered by the GPU tests. With C = 8 every
+    rank's block (4 or 2 channels) is exchanged in several groups."""
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_mixer_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]

@@ -17,7 +17,7 @@ import torch
 import torch.multiprocessing as mp
 
 from tests.conftest import ROOT, rel_l2
-from tests.test_cp_gloo import cpu_permute
+from tests.test_cp_gloo import cpu_permute, cpu_permute_window
 
 pytestmark = pytest.mark.gpu
 
@@ -69,6 +69,30 @@ def test_permute_kernels_bit_exact(P, zigzag, dtype):
     for a, b, x in zip(ref2, got2, xs):
         assert torch.equal(a, b.cpu())
         assert torch.equal(a, x)  # seq -> chan -> seq is the identity
+
+
+@pytest.mark.parametrize("P,dtype,c_off,c_cnt", [(2, torch.bfloat16, 8, 8), (4, torch.float32, 0, 4),
+                                                  (4, torch.bfloat16, 3, 5), (8, torch.bfloat16, 8, 8)])
+def test_permute_window_kernels_bit_exact(P, dtype, c_off, c_cnt):
+    """The channel-window pack / unpack of the pipelined exchange (16-byte and scalar paths)."""
+    from nvsubquadratic_b200 import cp
+
+    g = torch.Generator().manual_seed(10 + P)
+    B, l, rest_shape, G = 2, 6, (3,), 3
+    d = 16
+    C = d * P
+    x = torch.randn((B, l) + rest_shape + (G, C), generator=g).to(dtype)
+    send_ref = torch.empty((P, B, l) + rest_shape + (G, c_cnt), dtype=dtype)
+    cpu_permute_window(x, 0, B, l, 3, G, C, P, c_off, c_cnt, send_ref)
+    send = torch.empty(send_ref.shape, dtype=dtype, device="cuda")
+    cp._permute_window_cuda(x.cuda(), 0, B, l, 3, G, C, P, c_off, c_cnt, send)
+    assert torch.equal(send.cpu(), send_ref)
+    base = torch.randn(x.shape, generator=g).to(dtype)
+    ref = base.clone()
+    cpu_permute_window(send_ref, 3, B, l, 3, G, C, P, c_off, c_cnt, ref)
+    got = base.cuda()
+    cp._permute_window_cuda(send, 3, B, l, 3, G, C, P, c_off, c_cnt, got)
+    assert torch.equal(got.cpu(), ref)  # the window is written, every other channel kept
 
 
 def _free_port():

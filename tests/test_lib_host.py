@@ -130,3 +130,22 @@ def test_packed_projection_detection():
     wide = torch.randn(2, 5, 6, 12)  # chunks of a 4C tensor are not a packed projection
     q, k, v = wide[..., :3], wide[..., 3:6], wide[..., 6:9]
     assert not _packed_views(q, k, v)
+
+
+def test_cp_window_permute_validation():
+    """hyfft_cp_permute_cl_window rejects windows outside a rank's channel block and the
+    two ops it does not cover before touching any memory (host-side checks)."""
+    lib = _lib.load()
+    buf = ctypes.c_void_p(16)  # never dereferenced: every call below fails validation first
+    args = dict(B=1, l=4, rest=1, G=3, C=16, P=2, elem=2)
+
+    def call(op, c_off, c_cnt):
+        a = args
+        return lib.hyfft_cp_permute_cl_window(buf, buf, op, a["B"], a["l"], a["rest"], a["G"], a["C"], a["P"],
+                                              c_off, c_cnt, a["elem"], None)
+
+    assert call(0, 6, 4) == _lib.HYFFT_ERR_INVALID   # 6 + 4 > C / P = 8
+    assert call(0, -1, 2) == _lib.HYFFT_ERR_INVALID
+    assert call(3, 0, 0) == _lib.HYFFT_ERR_INVALID
+    assert call(1, 0, 4) == _lib.HYFFT_ERR_INVALID   # unpack seq->chan has no window form
+    assert call(2, 0, 4) == _lib.HYFFT_ERR_INVALID   # pack chan->seq has no window form
