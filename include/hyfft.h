@@ -225,6 +225,24 @@ HYFFT_API int hyfft_cp_permute_cl_window(const void* src, void* dst, int32_t op,
                                          int64_t rest, int64_t G, int64_t C, int32_t P, int64_t c_off,
                                          int64_t c_cnt, int32_t elem_bytes, void* stream);
 
+/* ---------------------------------------------------------------- direct causal conv */
+/* Depthwise causal 1D convolution computed directly (no FFT), for short and medium
+ * filters (K <= 1024), channel-major [B, C, L] activations of `dtype`:
+ *   y = act(round(conv)),  conv[b, c, t] = sum_{k < K} w[c, k] x[b, c, t - (K - 1) + k] + bias[c]
+ * (x = 0 before t = 0), act = identity (activation 0) or SiLU (activation 1).
+ * Replaces the external kernel the reference binds in
+ *   causal_conv1d        nvsubquadratic/ops/causal_conv1d_custom.py:81-98
+ *   SubqOpsCausalConv1d  nvsubquadratic/modules/subq_ops_causal_conv1d.py:36-83
+ * weight: float32 [C, K]; bias: float32 [C] or NULL.                                  */
+HYFFT_API int hyfft_causal_conv1d_forward(const void* x, const float* weight, const float* bias, void* y,
+                                          int64_t B, int64_t C, int64_t L, int32_t K, int32_t activation,
+                                          int32_t dtype, void* stream);
+/* Gradients for upstream dy: dx ([B, C, L] of dtype), dweight (float32 [C, K]) and dbias
+ * (float32 [C], NULL to skip); dweight and dbias are overwritten.                      */
+HYFFT_API int hyfft_causal_conv1d_backward(const void* x, const float* weight, const float* bias, const void* dy,
+                                           void* dx, float* dweight, float* dbias, int64_t B, int64_t C, int64_t L,
+                                           int32_t K, int32_t activation, int32_t dtype, void* stream);
+
 /* ---------------------------------------------------------------- misc */
 /* Message of the most recent error on this thread ("" if none). */
 HYFFT_API const char* hyfft_last_error(void);

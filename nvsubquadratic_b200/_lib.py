@@ -88,6 +88,8 @@ SIGNATURES = {
     "hyfft_cp_unpack_full_to_split": [_vp, _vp, _i64, _i64, _i64, _i64, _i32, _i32, _vp],
     "hyfft_cp_permute_cl": [_vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _i32, _vp],
     "hyfft_cp_permute_cl_window": [_vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _i64, _i32, _vp],
+    "hyfft_causal_conv1d_forward": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp],
+    "hyfft_causal_conv1d_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp],
     "hyfft_last_error": [],
     "hyfft_version": [],
     "hyfft_launch_count": [],

@@ -201,14 +201,38 @@ __global__ void __launch_bounds__(kThreads) b2_kspec_cols(const Big2DParams p) {
 }
 
 // ---------------------------------------------------------------- row pass helpers
+// Lane l's points of rows [2 pr, 2 pr + 1] of image (b, c): v[m] = x[r0][l + 16 m] +
+// i x[r1][l + 16 m] for m < 8 (positions >= 128 >= N1 are zero), zeros for a pair past N0.
+template <typename T>
+__device__ __forceinline__ void rows_load(const Big2DView& in, int b, int c, int N0, int N1, int pr, int l,
+                                          float2 (&v)[8]) {
+  const int npairs = (N0 + 1) >> 1;
+  const bool act = pr < npairs;
+  const int r0 = 2 * pr, r1 = r0 + 1;
+  const bool has1 = act && r1 < N0;
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const int n = l + 16 * m;
+    v[m] = make_float2(0.f, 0.f);
+    if (act && n < N1) {
+      v[m].x = ldv<T>(in, b, c, r0, n);
+      if (has1) v[m].y = ldv<T>(in, b, c, r1, n);
+    }
+  }
+}
+
 // Forward row transforms of rows [2 pr, 2 pr + 1] of input view `in` for image (b, c):
 // bins j in [jlo, jlo + jn) go to dst[r * ld + j - jlo]. All threads of the CTA call it.
+// The next round's rows are loaded before this round's transform, so their global-memory
+// latency overlaps the arithmetic.
 template <typename T>
 __device__ __forceinline__ void rows_forward(const Big2DView& in, int b, int c, int N0, int N1, float2* dst, int ld,
                                              int jlo, int jn, float2* sc, const float2* tw) {
   const int g = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int npairs = (N0 + 1) >> 1;
   const int rounds = (npairs + kBigGroups - 1) / kBigGroups;
+  float2 nxt[8];
+  rows_load<T>(in, b, c, N0, N1, g, l, nxt);
   for (int rb = 0; rb < rounds; ++rb) {
     const int pr = rb * kBigGroups + g;
     const bool act = pr < npairs;
@@ -216,14 +240,11 @@ __device__ __forceinline__ void rows_forward(const Big2DView& in, int b, int c, 
     const bool has1 = act && r1 < N0;
     float2 v[16];
 #pragma unroll
-    for (int m = 0; m < 16; ++m) {
-      const int n = l + 16 * m;
-      v[m] = make_float2(0.f, 0.f);
-      if (act && n < N1) {
-        v[m].x = ldv<T>(in, b, c, r0, n);
-        if (has1) v[m].y = ldv<T>(in, b, c, r1, n);
-      }
+    for (int m = 0; m < 8; ++m) {
+      v[m] = nxt[m];
+      v[m + 8] = make_float2(0.f, 0.f);
     }
+    if (rb + 1 < rounds) rows_load<T>(in, b, c, N0, N1, pr + kBigGroups, l, nxt);
     fft256<true, false>(v, sc, tw, l, -1.f);
     float2 A[9], Bv[9];
     split_pair(v, l, A, Bv);
@@ -260,12 +281,16 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
   rows_forward<T>(p.x, b, c, N0, N1, A, kB2H, 0, kB2H, mysc, tw);
   __syncthreads();
 
-  // columns: transform, * Kh (or conj), inverse, keep rows [0, N0)
+  // columns: transform, * Kh (or conj), inverse, keep rows [0, N0); the filter-spectrum
+  // column (an L2 read) is loaded before the forward transform that it waits for
   const float2* kh = p.Kh + (long long)c * kB2H * kB2F;
   const float cj = p.conj ? -1.f : 1.f;
   for (int rb = 0; rb < (kB2H + kBigGroups - 1) / kBigGroups; ++rb) {
     const int j = rb * kBigGroups + g;
     const bool act = j < kB2H;
+    float2 kv[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) kv[m] = act ? __ldg(kh + (long long)j * kB2F + l + 16 * m) : make_float2(0.f, 0.f);
     float2 v[16];
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
@@ -275,7 +300,7 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
     fft256<true, false>(v, mysc, tw, l, -1.f);
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
-      float2 k = act ? __ldg(kh + (long long)j * kB2F + l + 16 * m) : make_float2(0.f, 0.f);
+      float2 k = kv[m];
       k.y *= cj;
       v[m] = cmul(v[m], k);
     }
@@ -320,6 +345,9 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
       }
       v[m] = make_float2(a.x - bb.y, a.y + bb.x);  // a + i b
     }
+    // the D-skip inputs of these two rows, loaded before the transform
+    float2 xs[8];
+    if (p.D) rows_load<T>(p.x, b, c, N0, N1, pr, l, xs);
     fft256<false, true>(v, mysc, tw, l, 1.f);
     if (act) {
 #pragma unroll
@@ -328,8 +356,8 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
         if (n < N1) {
           float o0 = DT<T>::round(v[m].x * scale), o1 = DT<T>::round(v[m].y * scale);
           if (p.D) {
-            o0 = DT<T>::round(o0 + DT<T>::round(Dc * ldv<T>(p.x, b, c, r0, n)));
-            if (has1) o1 = DT<T>::round(o1 + DT<T>::round(Dc * ldv<T>(p.x, b, c, r1, n)));
+            o0 = DT<T>::round(o0 + DT<T>::round(Dc * xs[m].x));
+            if (has1) o1 = DT<T>::round(o1 + DT<T>::round(Dc * xs[m].y));
           }
           DT<T>::store(yo + (long long)r0 * p.y.s0 + (long long)n * p.y.s1, o0);
           if (has1) DT<T>::store(yo + (long long)r1 * p.y.s0 + (long long)n * p.y.s1, o1);

@@ -145,8 +145,9 @@ struct Geo {
 // d = b - (N0 - 1):  forward  T1_d[m = c_out][k = c_in]  = k'[d + K0/2][c_out - c_in + K1/2]
 //                    adjoint  U_d[m = c_in][k = c_out]   = k'[K0/2 - d][c_out - c_in + K1/2]
 // with k' = k + D at the centre tap; stored K-major [m/8][k/8][m%8][k%8] (bf16).
+// f: the channel's K0 x K1 taps (shared memory).
 template <int N0, int N1, bool ADJ>
-__device__ __forceinline__ void gen_blocks(unsigned char* dst, const float* __restrict__ f, int K0, int K1, float Dc) {
+__device__ __forceinline__ void gen_blocks(unsigned char* dst, const float* f, int K0, int K1, float Dc) {
   constexpr int NBLK = Geo<N0>::NBLK;
   const int ck0 = K0 / 2, ck1 = K1 / 2;
   for (int it = threadIdx.x; it < NBLK * 32; it += blockDim.x) {
@@ -165,7 +166,7 @@ __device__ __forceinline__ void gen_blocks(unsigned char* dst, const float* __re
         const int col = co - ci + ck1;
         float val = 0.f;
         if (row_ok && k < N1 && col >= 0 && col < K1) {
-          val = __ldg(f + row * K1 + col);
+          val = f[row * K1 + col];
           if (row == ck0 && col == ck1) val += Dc;
         }
         v2[u] = val;
@@ -234,19 +235,56 @@ struct VS<8> {
   }
 };
 
+// cp.async copy of one position's CG channels (8 or 16 bytes) from global to shared
+// memory, left in flight; !valid zero-fills and reads nothing.
+template <int CG>
+__device__ __forceinline__ void cp_async_vec(void* sdst, const void* gsrc, bool valid) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(sdst);
+  if constexpr (CG * 2 == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(gsrc), "r"(valid ? 16 : 0)
+                 : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(d), "l"(gsrc), "r"(valid ? 8 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_f32(float* sdst, const float* gsrc) {
+  const unsigned d = (unsigned)__cvta_generic_to_shared(sdst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+// Up to four channels-last bf16 sources with their batch / position strides (channel
+// offset already applied).
+struct TileSrc {
+  const bf16* p[4];
+  long long bst[4], pst[4];
+};
+
 // Stage CG channels of NT_ tensors x HB images x NP positions (channels-last global, one
-// vector per position) into shared memory [tensor][image][position][CG]; zeros past B.
+// vector per position) into shared memory [tensor][image][position][CG] with cp.async:
+// every copy of the stage is in flight at once (one commit group; the caller waits);
+// zeros past B.
 template <int NP, int CG, int HB, int NT_>
-__device__ __forceinline__ void stage_tiles(bf16* R, const bf16* const* srcs, const long long* bst,
-                                            const long long* pst, int b_first, int B) {
-  using Raw = typename VS<CG>::Raw;
-  for (int i = threadIdx.x; i < NT_ * HB * NP; i += blockDim.x) {
-    const int t = i / (HB * NP), rem = i - t * (HB * NP), j = rem / NP, pos = rem - j * NP;
-    const int b = b_first + j;
-    Raw v = {};
-    if (b < B) v = __ldg(reinterpret_cast<const Raw*>(srcs[t] + (long long)b * bst[t] + (long long)pos * pst[t]));
-    *reinterpret_cast<Raw*>(R + ((long long)(t * HB + j) * NP + pos) * CG) = v;
+__device__ __forceinline__ void stage_async(bf16* R, const TileSrc& s, int b_first, int B) {
+#pragma unroll
+  for (int t = 0; t < NT_; ++t) {
+    for (int i = threadIdx.x; i < HB * NP; i += blockDim.x) {
+      const int j = i / NP, pos = i - j * NP;
+      const int b = b_first + j;
+      const bool ok = b < B;
+      const bf16* src = s.p[t] + (ok ? (long long)b * s.bst[t] + (long long)pos * s.pst[t] : 0LL);
+      cp_async_vec<CG>(R + ((long long)(t * HB + j) * NP + pos) * CG, src, ok);
+    }
   }
+  cp_async_commit();
+}
+
+// The CTA's CG channels of the filter, [CG][K0 * K1] float, into shared memory (cp.async,
+// committed with the next stage).
+__device__ __forceinline__ void stage_filter_async(float* fsm, const float* filt, int c0, int CG, int KK) {
+  const float* src = filt + (long long)c0 * KK;
+  for (int i = threadIdx.x; i < CG * KK; i += blockDim.x) cp_async_f32(fsm + i, src + i);
 }
 
 // Depthwise SKxSK "same" cross-correlation of CG channels at (n0, n1) of a staged
@@ -285,15 +323,26 @@ struct FwdLayout {
   static constexpr int RB = 32 * NB, HB = 8, NP = N0 * N1;
   static constexpr size_t z = 0;
   static constexpr size_t r = z + (size_t)CG * G::NR * RB;                     // [3][HB][NP][CG] bf16
-  static constexpr size_t t = r + ((size_t)3 * HB * NP * CG * 2 + 127) / 128 * 128;
-  static constexpr size_t w = t + 2 * (size_t)G::NBLK * G::BLKB;
-  static constexpr size_t bar = w + ((4 * (3 * CG * NT + 3 * CG) + 15) / 16) * 16;
-  static constexpr size_t total = bar + 32;
+  static constexpr size_t rsz = ((size_t)3 * HB * NP * CG * 2 + 127) / 128 * 128;
+  static constexpr size_t tsz = 2 * (size_t)G::NBLK * G::BLKB;                // block tables (alias r)
+  static constexpr size_t t = r;
+  static constexpr size_t w = r + (rsz > tsz ? rsz : tsz);
+  static constexpr size_t bar = w + ((4 * (3 * CG * NT + 3 * CG + CG) + 15) / 16) * 16;
+  static constexpr size_t fk = bar + 32;  // [CG][K0 * K1] filter taps (size set at launch)
   static constexpr uint32_t tcols = tmem_cols_for(CG * G::MT * NB);
+  static size_t bytes(int K0, int K1) { return fk + ((size_t)CG * K0 * K1 * 4 + 15) / 16 * 16; }
 };
 
+// Forward, per CTA CG channels x NB images (two CTAs per SM):
+//  1. cp.async: the CTA's filter taps and q, k of the first 8 images; while they fly, the
+//     z operand is cleared and the short-conv weights loaded;
+//  2. per 8 images: short conv + gate 1 -> z (operand layout), v' (bf16) kept in v_s for
+//     the epilogue... computed there from the staged v instead (re-staged by cp.async);
+//  3. per channel: Toeplitz blocks from the shared-memory filter (double-buffered tables,
+//     aliasing the staging area) and tcgen05 MMAs into TMEM;
+//  4. epilogue per 8 images: v staged by cp.async, y = round(h) * round(g2(v')).
 template <int N0, int N1, int SK, int CG, int NB>
-__global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
+__global__ void __launch_bounds__(256, 2) tp2d_fwd_kernel(const Fused2DParams p) {
   using G = Geo<N0>;
   using L = FwdLayout<N0, N1, SK, CG, NB>;
   constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = L::NP, HB = L::HB;
@@ -306,10 +355,27 @@ __global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
   unsigned char* Tb = smem + L::t;
   float* wts = reinterpret_cast<float*>(smem + L::w);
   float* bsm = wts + 3 * CG * NT;
+  float* Dsm = bsm + 3 * CG;
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + L::bar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + L::bar + 16);
+  float* fsm = reinterpret_cast<float*>(smem + L::fk);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c0 = blockIdx.x * CG, b0 = blockIdx.y * NB;
+  const int KK = p.K0 * p.K1;
+
+  TileSrc src;
+  src.p[0] = reinterpret_cast<const bf16*>(p.q) + c0;
+  src.p[1] = reinterpret_cast<const bf16*>(p.k) + c0;
+  src.p[2] = reinterpret_cast<const bf16*>(p.v) + c0;
+  src.p[3] = src.p[0];
+  for (int i = 0; i < 4; ++i) {
+    src.bst[i] = p.in_bst;
+    src.pst[i] = p.in_pst;
+  }
+  TileSrc vsrc = src;
+  vsrc.p[0] = src.p[2];
+  stage_filter_async(fsm, p.filt, c0, CG, KK);
+  stage_async<NP, CG, HB, 2>(R, src, b0, p.B);  // q, k of the first images (with the filter)
 
   if (warp == 0) umma::tmem_alloc(tslot, L::tcols);
   if (tid == 0) {
@@ -322,19 +388,20 @@ __global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
     wts[i] = SK > 0 ? p.w[((long long)t * p.C + c0 + cc) * NT + tap] : 1.f;
   }
   for (int i = tid; i < 3 * CG; i += blockDim.x) bsm[i] = p.bias ? p.bias[(i / CG) * p.C + c0 + i % CG] : 0.f;
+  for (int i = tid; i < CG; i += blockDim.x) Dsm[i] = p.D[c0 + i];
   for (int i = tid; i < CG * NR * RB / 16; i += blockDim.x) reinterpret_cast<uint4*>(Zt)[i] = make_uint4(0, 0, 0, 0);
 
-  const bf16* srcs[3] = {reinterpret_cast<const bf16*>(p.q) + c0, reinterpret_cast<const bf16*>(p.k) + c0,
-                         reinterpret_cast<const bf16*>(p.v) + c0};
-  const long long bst[3] = {p.in_bst, p.in_bst, p.in_bst}, pst[3] = {p.in_pst, p.in_pst, p.in_pst};
   const float* bq = p.bias ? bsm : nullptr;
   const float* bk = p.bias ? bsm + CG : nullptr;
   const float* bv = p.bias ? bsm + 2 * CG : nullptr;
 
   // ---- z = q' * g1(k') into the operand layout, 8 staged images at a time
   for (int h0 = 0; h0 < NB; h0 += HB) {
-    __syncthreads();
-    stage_tiles<NP, CG, HB, 2>(R, srcs, bst, pst, b0 + h0, p.B);
+    if (h0 > 0) {
+      __syncthreads();  // the previous images' stencils are done with R
+      stage_async<NP, CG, HB, 2>(R, src, b0 + h0, p.B);
+    }
+    cp_async_wait_all();
     __syncthreads();
     for (int it = tid; it < HB * NP; it += blockDim.x) {
       const int j = it / NP, pos = it - j * NP, r = pos / N1, c = pos - r * N1;
@@ -355,14 +422,13 @@ __global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
   umma::fence_after_sync();
   const uint32_t tmem = *tslot;
 
-  // ---- per channel: Toeplitz blocks + MMAs (double-buffered block tables)
+  // ---- per channel: Toeplitz blocks + MMAs (double-buffered block tables over the staging area)
   bool ok = true;
   for (int ch = 0; ch < CG; ++ch) {
     const int buf = ch & 1;
     if (ch >= 2) ok &= umma::mbar_wait(&mbar[buf], ((ch - 2) >> 1) & 1);
     unsigned char* tb = Tb + buf * G::NBLK * G::BLKB;
-    const int cg = c0 + ch;
-    gen_blocks<N0, N1, false>(tb, p.filt + (long long)cg * p.K0 * p.K1, p.K0, p.K1, p.D[cg]);
+    gen_blocks<N0, N1, false>(tb, fsm + ch * KK, p.K0, p.K1, Dsm[ch]);
     umma::fence_async_smem();
     __syncthreads();
     if (tid == 0) {
@@ -378,26 +444,28 @@ __global__ void __launch_bounds__(256) tp2d_fwd_kernel(const Fused2DParams p) {
       umma::commit(&mbar[buf]);
     }
   }
+  // the staging area holds the block tables until every MMA has read them
+  if (CG >= 2) ok &= umma::mbar_wait(&mbar[(CG - 2) & 1], ((CG - 2) >> 1) & 1);
+  ok &= umma::mbar_wait(&mbar[(CG - 1) & 1], ((CG - 1) >> 1) & 1);
+  umma::fence_after_sync();
 
   // ---- epilogue: y = round(h) * round(g2(v')), v staged 8 images at a time
   const int mt = warp >> 2, q4 = warp & 3;
   const int m = q4 * 32 + lane, r = mt * 8 + (m >> 4), c = m & 15;
   bf16* y = reinterpret_cast<bf16*>(p.y) + c0;
   const uint32_t lane_base = tmem + ((uint32_t)(q4 * 32) << 16);
-  const bf16* vsrc[1] = {srcs[2]};
   for (int h0 = 0; h0 < NB; h0 += HB) {
     __syncthreads();
-    stage_tiles<NP, CG, HB, 1>(R, vsrc, bst, pst, b0 + h0, p.B);
-    if (h0 == 0) ok &= umma::mbar_wait(&mbar[(CG - 1) & 1], ((CG - 1) >> 1) & 1);
+    stage_async<NP, CG, HB, 1>(R, vsrc, b0 + h0, p.B);
+    cp_async_wait_all();
     __syncthreads();
-    umma::fence_after_sync();
     if (mt < MT) {
       const bool valid = ok && r < N0 && c < N1;
       float h[CG][8];
 #pragma unroll
       for (int ch = 0; ch < CG; ++ch) umma::tmem_ld8(lane_base + (uint32_t)((ch * MT + mt) * NB + h0), h[ch]);
       if (valid) {
-#pragma unroll 2
+#pragma unroll
         for (int j = 0; j < HB; ++j) {
           const int b = b0 + h0 + j;
           if (b >= p.B) break;
@@ -422,25 +490,27 @@ struct BwdLayout {
   using G = Geo<N0>;
   static constexpr int NT = SK > 0 ? SK * SK : 1;
   static constexpr int RB = 32 * NB, HB = 8, NP = N0 * N1;
-  static constexpr int KR = 31, KP = 48;  // dK accumulator rows / padded row pitch (bank spread)
   static constexpr size_t z = 0;
   static constexpr size_t dh = z + (size_t)CG * G::NR * RB;
   static constexpr size_t rsz = ((size_t)4 * HB * NP * CG * 2 + 127) / 128 * 128;
   static constexpr size_t tsz = 2 * (size_t)G::NBLK * G::BLKB;  // forward + adjoint tables (aliased with R)
   static constexpr size_t r = dh + (size_t)CG * G::NR * RB;      // [4][HB][NP][CG] bf16
   static constexpr size_t ds = r + (rsz > tsz ? rsz : tsz);       // [3][HB][NP][CG] bf16
-  static constexpr size_t dk = ds + ((size_t)3 * HB * NP * CG * 2 + 15) / 16 * 16;
-  static constexpr size_t w = dk + (size_t)CG * KR * KP * 4;
-  static constexpr size_t dw = w + ((4 * (3 * CG * NT + 3 * CG) + 15) / 16) * 16;  // [3][CG][NT+1]
+  static constexpr size_t w = ds + ((size_t)3 * HB * NP * CG * 2 + 15) / 16 * 16;
+  static constexpr size_t dw = w + ((4 * (3 * CG * NT + 3 * CG + CG) + 15) / 16) * 16;  // [3][CG][NT+1]
   static constexpr size_t bar = dw + ((4 * 3 * CG * (NT + 1) + 15) / 16) * 16;
-  static constexpr size_t total = bar + 48;
+  static constexpr size_t dk = bar + 48;  // [CG][K0][kpitch(K1)] dK accumulators, then [CG][K0*K1] filter
+  // dK row pitch: 16 or 48 floats, so the two grid rows a warp covers land in disjoint banks
+  static __host__ __device__ int kpitch(int K1) { return K1 <= 16 ? 16 : 48; }
+  static __host__ __device__ size_t fk(int K0, int K1) { return dk + (size_t)CG * K0 * kpitch(K1) * 4; }
+  static size_t bytes(int K0, int K1) { return fk(K0, K1) + ((size_t)CG * K0 * K1 * 4 + 15) / 16 * 16; }
 };
 
 template <int N0, int N1, int SK, int CG, int NB>
 __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   using G = Geo<N0>;
   using L = BwdLayout<N0, N1, SK, CG, NB>;
-  constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = L::NP, HB = L::HB, KP = L::KP;
+  constexpr int MT = G::MT, NR = G::NR, RB = L::RB, NT = L::NT, NP = L::NP, HB = L::HB;
   constexpr uint32_t IDESC = umma::idesc_bf16(128, NB, 0, 0);
   constexpr uint32_t IDESC_G = umma::idesc_bf16(128, 16 * N0, 1, 1);
   constexpr uint32_t TCOLS = 512;
@@ -457,12 +527,27 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   float* dkacc = reinterpret_cast<float*>(smem + L::dk);
   float* wts = reinterpret_cast<float*>(smem + L::w);
   float* bsm = wts + 3 * CG * NT;
+  float* Dsm = bsm + 3 * CG;
   float* dwacc = reinterpret_cast<float*>(smem + L::dw);
   uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + L::bar);
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + L::bar + 32);
+  float* fsm = reinterpret_cast<float*>(smem + L::fk(p.K0, p.K1));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int c0 = blockIdx.x * CG, b0 = blockIdx.y * NB;
   const int ck0 = p.K0 / 2, ck1 = p.K1 / 2;
+  const int KK = p.K0 * p.K1, KP = L::kpitch(p.K1);
+
+  TileSrc src;
+  src.p[0] = reinterpret_cast<const bf16*>(p.q) + c0;
+  src.p[1] = reinterpret_cast<const bf16*>(p.k) + c0;
+  src.p[2] = reinterpret_cast<const bf16*>(p.v) + c0;
+  src.p[3] = reinterpret_cast<const bf16*>(p.dy) + c0;
+  src.bst[0] = src.bst[1] = src.bst[2] = p.in_bst;
+  src.pst[0] = src.pst[1] = src.pst[2] = p.in_pst;
+  src.bst[3] = p.out_bst;
+  src.pst[3] = p.out_pst;
+  stage_filter_async(fsm, p.filt, c0, CG, KK);
+  stage_async<NP, CG, HB, 4>(R, src, b0, p.B);  // q, k, v, dy of the first images (with the filter)
 
   if (warp == 0) umma::tmem_alloc(tslot, TCOLS);
   if (tid == 0) {
@@ -475,20 +560,20 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
     wts[i] = SK > 0 ? p.w[((long long)t * p.C + c0 + cc) * NT + tap] : 1.f;
   }
   for (int i = tid; i < 3 * CG; i += blockDim.x) bsm[i] = p.bias ? p.bias[(i / CG) * p.C + c0 + i % CG] : 0.f;
+  for (int i = tid; i < CG; i += blockDim.x) Dsm[i] = p.D[c0 + i];
   for (int i = tid; i < 2 * CG * NR * RB / 16; i += blockDim.x) reinterpret_cast<uint4*>(Zt)[i] = make_uint4(0, 0, 0, 0);
-  for (int i = tid; i < CG * L::KR * KP; i += blockDim.x) dkacc[i] = 0.f;
+  for (int i = tid; i < CG * p.K0 * KP; i += blockDim.x) dkacc[i] = 0.f;
   for (int i = tid; i < 3 * CG * (NT + 1); i += blockDim.x) dwacc[i] = 0.f;
 
-  const bf16* srcs[4] = {reinterpret_cast<const bf16*>(p.q) + c0, reinterpret_cast<const bf16*>(p.k) + c0,
-                         reinterpret_cast<const bf16*>(p.v) + c0, reinterpret_cast<const bf16*>(p.dy) + c0};
-  const long long bst[4] = {p.in_bst, p.in_bst, p.in_bst, p.out_bst};
-  const long long pst[4] = {p.in_pst, p.in_pst, p.in_pst, p.out_pst};
   const float* bias3[3] = {p.bias ? bsm : nullptr, p.bias ? bsm + CG : nullptr, p.bias ? bsm + 2 * CG : nullptr};
 
   // ---- z and dh into the operand layouts, 8 staged images at a time
   for (int h0 = 0; h0 < NB; h0 += HB) {
-    __syncthreads();
-    stage_tiles<NP, CG, HB, 4>(R, srcs, bst, pst, b0 + h0, p.B);
+    if (h0 > 0) {
+      __syncthreads();  // the previous images' stencils are done with R
+      stage_async<NP, CG, HB, 4>(R, src, b0 + h0, p.B);
+    }
+    cp_async_wait_all();
     __syncthreads();
     for (int it = tid; it < HB * NP; it += blockDim.x) {
       const int j = it / NP, pos = it - j * NP, r = pos / N1, c = pos - r * N1;
@@ -516,10 +601,9 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   bool ok = true;
   for (int ch = 0; ch < CG; ++ch) {
     if (ch >= 1) ok &= umma::mbar_wait(&mbar[0], (ch - 1) & 1);
-    const int cg = c0 + ch;
-    const float* fch = p.filt + (long long)cg * p.K0 * p.K1;
-    gen_blocks<N0, N1, false>(Tf, fch, p.K0, p.K1, p.D[cg]);
-    gen_blocks<N0, N1, true>(Tt, fch, p.K0, p.K1, p.D[cg]);
+    const float* fch = fsm + ch * KK;
+    gen_blocks<N0, N1, false>(Tf, fch, p.K0, p.K1, Dsm[ch]);
+    gen_blocks<N0, N1, true>(Tt, fch, p.K0, p.K1, Dsm[ch]);
     umma::fence_async_smem();
     __syncthreads();
     if (tid == 0) {
@@ -550,7 +634,8 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   constexpr int OFF = SK > 0 ? (SK - 1) / 2 : 0;
   for (int h0 = 0; h0 < NB; h0 += HB) {
     __syncthreads();
-    stage_tiles<NP, CG, HB, 4>(R, srcs, bst, pst, b0 + h0, p.B);
+    stage_async<NP, CG, HB, 4>(R, src, b0 + h0, p.B);
+    cp_async_wait_all();
     __syncthreads();
     umma::fence_after_sync();
     if (mt < MT) {
@@ -564,7 +649,7 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
         umma::tmem_ld8(lane_base + DZ0 + (uint32_t)((ch * MT + mt) * NB + h0), dacc[ch]);
       }
       if (valid) {
-#pragma unroll 1
+#pragma unroll
         for (int j = 0; j < HB; ++j) {
           if (b0 + h0 + j >= p.B) break;
           float qv[CG], kv[CG], vv[CG], g[CG], oq[CG], ok_[CG], ov[CG];
@@ -676,7 +761,7 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
     if (mt < MT) {
       const int m = q4 * 32 + lane, ro = mt * 8 + (m >> 4), co = m & 15;
       const bool valid = ok && ro < N0 && co < N1;
-      float* acc = dkacc + ch * L::KR * KP;
+      float* acc = dkacc + ch * p.K0 * KP;
 #pragma unroll 1
       for (int ri = 0; ri < N0; ++ri) {
         float gv[16];
@@ -706,7 +791,7 @@ __global__ void __launch_bounds__(256) tp2d_bwd_kernel(const Fused2DParams p) {
   // filter gradient (of k' = k + D*delta): dfilt = dk', dD = dk' at the centre tap
   for (int i = tid; i < CG * p.K0 * p.K1; i += blockDim.x) {
     const int ch = i / (p.K0 * p.K1), rr = i % (p.K0 * p.K1), a = rr / p.K1, bb = rr % p.K1;
-    const float v = dkacc[ch * L::KR * KP + a * KP + bb];
+    const float v = dkacc[(ch * p.K0 + a) * KP + bb];
     atomicAdd(p.dfilt + ((long long)(c0 + ch) * p.K0 + a) * p.K1 + bb, v);
     if (a == ck0 && bb == ck1) atomicAdd(p.dD + c0 + ch, v);
   }
@@ -722,20 +807,24 @@ template <int N0, int N1, int SK>
 static int tp_run(int op, const Fused2DParams* pp, cudaStream_t st) {
   using LF = FwdLayout<N0, N1, SK, kFwdCG, kNB>;
   using LB = BwdLayout<N0, N1, SK, kBwdCG, kNB>;
-  if (op == TP_PROBE) return (LF::total <= 227 * 1024 && LB::total <= 227 * 1024) ? HYFFT_OK : HYFFT_ERR_UNSUPPORTED;
+  // the largest filter the kernels take (31 x 31 taps) fixes the shared-memory bound
+  if (op == TP_PROBE)
+    return (LF::bytes(31, 31) <= 227 * 1024 && LB::bytes(31, 31) <= 227 * 1024) ? HYFFT_OK : HYFFT_ERR_UNSUPPORTED;
   const Fused2DParams& p = *pp;
   if (p.C % kFwdCG != 0 || p.C % kBwdCG != 0) return HYFFT_ERR_UNSUPPORTED;
   if (p.K0 > 2 * N0 - 1 + 1 || p.K1 > 2 * N1 - 1 + 1 || p.K0 > 31 || p.K1 > 31) return HYFFT_ERR_UNSUPPORTED;
   if (op == TP_FWD) {
     auto kern = tp2d_fwd_kernel<N0, N1, SK, kFwdCG, kNB>;
-    if (!kernel_smem_once((const void*)kern, LF::total)) return HYFFT_ERR_CUDA;
+    const size_t sm = LF::bytes(p.K0, p.K1);
+    if (!kernel_smem_once((const void*)kern, sm, true)) return HYFFT_ERR_CUDA;
     dim3 grid(p.C / kFwdCG, (p.B + kNB - 1) / kNB);
-    kern<<<grid, 256, LF::total, st>>>(p);
+    kern<<<grid, 256, sm, st>>>(p);
   } else {
     auto kern = tp2d_bwd_kernel<N0, N1, SK, kBwdCG, kNB>;
-    if (!kernel_smem_once((const void*)kern, LB::total)) return HYFFT_ERR_CUDA;
+    const size_t sm = LB::bytes(p.K0, p.K1);
+    if (!kernel_smem_once((const void*)kern, sm, true)) return HYFFT_ERR_CUDA;
     dim3 grid(p.C / kBwdCG, (p.B + kNB - 1) / kNB);
-    kern<<<grid, 256, LB::total, st>>>(p);
+    kern<<<grid, 256, sm, st>>>(p);
   }
   if (cudaGetLastError() != cudaSuccess) return HYFFT_ERR_CUDA;
   g_launches.fetch_add(1, std::memory_order_relaxed);
