@@ -76,6 +76,11 @@ typedef struct hyfft_conv_desc {
   int32_t causal;       /* 1: causal 1D conv (fftconv.py:546); 0: centred "same"    */
   int32_t dtype;        /* HYFFT_F32 / BF16 / F16: dtype of x, y, shortcut, dx, dy  */
   int32_t layout;       /* HYFFT_LAYOUT_BHL or HYFFT_LAYOUT_BLH for x, y, dx, dy    */
+  int32_t periodic;     /* bit d set: axis d is circular (FFT length n[d], a power   */
+                        /* of two, k[d] <= n[d], output aligned by (k[d] - 1) / 2):  */
+                        /* circular_fftconv{1,2,3}d_fp32_bhl ops/circular_fftconv.py */
+                        /* :310-583; mixed axes ops/mixed_fftconv.py:504-723. 0: all */
+                        /* axes zero-padded (the fftconv.py ops above)               */
 } hyfft_conv_desc;
 
 /* Workspace bytes for one forward / one backward call. */
@@ -145,6 +150,7 @@ typedef struct hyfft_hyena_desc {
                            /*   into one [B, *S, 3C] projection and its gradient       */
   int64_t out_batch_stride;/* element strides of y and dy (channel stride 1)          */
   int64_t out_pos_stride;
+  int32_t periodic;        /* circular axes of the long conv, as hyfft_conv_desc      */
 } hyfft_hyena_desc;
 
 /* Workspace bytes for forward / backward, and the bytes of the `saved` buffer the

@@ -42,6 +42,7 @@ class ConvDesc(ctypes.Structure):
         ("causal", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
         ("layout", ctypes.c_int32),
+        ("periodic", ctypes.c_int32),
     ]
 
 
@@ -63,6 +64,7 @@ class HyenaDesc(ctypes.Structure):
         ("in_pos_stride", ctypes.c_int64),
         ("out_batch_stride", ctypes.c_int64),
         ("out_pos_stride", ctypes.c_int64),
+        ("periodic", ctypes.c_int32),
     ]
 
 

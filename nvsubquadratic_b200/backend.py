@@ -7,7 +7,8 @@ restated as plain functions so that they can be called from ``CKConvND.__init__`
 * ``BACKENDS`` / ``check_fft_backend``: the allow-list assert of ckconv_nd.py:628-630,
   extended by ``"b200"``.
 * ``validate_ckconv_config``: the constructor constraints of ckconv_nd.py:640-724 for
-  this backend (zero padding only, causal is 1D only, data_dim 1..3).
+  this backend (zero, circular or per-axis mixed padding; causal is 1D and zero-padded;
+  data_dim 1..3).
 * ``select_fftconv_fns``: the binding of ``fftconv_fn`` (BLH) and
   ``fftconv_fn_bhl_input`` (BHL) of ckconv_nd.py:796-871.
 * ``apply_convolution``: ckconv_nd.py:1006-1062 (the kernel arrives channels-last and
@@ -34,6 +35,7 @@ __all__ = [
     "check_fft_backend",
     "validate_ckconv_config",
     "select_fftconv_fns",
+    "resolve_periodic",
     "apply_convolution",
     "ckconv_kernel",
     "fused_mixer_config",
@@ -53,7 +55,38 @@ FFT_FUNCTIONS = {
     "causal": {
         1: (_ops.causal_fftconv1d_fp32_bhl_w_reshape, _ops.causal_fftconv1d_fp32_bhl),
     },
+    "circular": {
+        1: (_ops.circular_fftconv1d_fp32_bhl_w_reshape, _ops.circular_fftconv1d_fp32_bhl),
+        2: (_ops.circular_fftconv2d_fp32_bhl_w_reshape, _ops.circular_fftconv2d_fp32_bhl),
+        3: (_ops.circular_fftconv3d_fp32_bhl_w_reshape, _ops.circular_fftconv3d_fp32_bhl),
+    },
 }
+# per-axis padding lists (ckconv_nd.py:832-850): the mixed ops with ``periodic`` bound
+MIXED_FFT_FUNCTIONS = {
+    1: (_ops.mixed_fftconv1d_fp32_bhl_w_reshape, _ops.mixed_fftconv1d_fp32_bhl),
+    2: (_ops.mixed_fftconv2d_fp32_bhl_w_reshape, _ops.mixed_fftconv2d_fp32_bhl),
+    3: (_ops.mixed_fftconv3d_fp32_bhl_w_reshape, _ops.mixed_fftconv3d_fp32_bhl),
+}
+
+
+def _is_tuple_mode(fft_padding) -> bool:
+    return isinstance(fft_padding, Sequence) and not isinstance(fft_padding, (str, bytes))
+
+
+def resolve_periodic(fft_padding, data_dim: int) -> tuple[bool, ...]:
+    """Per-axis periodic flags of a CKConvND ``fft_padding`` ("zero", "circular" or a
+    per-axis list of them)."""
+    if _is_tuple_mode(fft_padding):
+        modes = tuple(fft_padding)
+        if len(modes) != data_dim:
+            raise ValueError(f"fft_padding has {len(modes)} entries for data_dim={data_dim}.")
+        for m in modes:
+            if m not in ("zero", "circular"):
+                raise ValueError(f"Unknown fft_padding mode {m!r}: use 'zero' or 'circular'.")
+        return tuple(m == "circular" for m in modes)
+    if fft_padding not in ("zero", "circular"):
+        raise ValueError(f"Unknown fft_padding mode {fft_padding!r}: use 'zero' or 'circular'.")
+    return (fft_padding == "circular",) * data_dim
 
 
 def check_fft_backend(fft_backend: str) -> None:
@@ -95,24 +128,37 @@ def validate_ckconv_config(data_dim: int, fft_padding, grid_type, is_causal: boo
             "fft_padding='circular' requires grid_type='single' (kernel size equals input size).")
     if fft_backend != FFT_BACKEND:
         return
-    if tuple_mode:
-        raise ValueError(
-            "fft_backend='b200' does not support a per-axis fft_padding. The CUDA kernels implement "
-            "zero-padded conv only. Use fft_backend='torch_fft' for mixed boundary conditions.")
-    assert fft_padding == "zero", (
-        f"fft_backend='b200' only supports zero-padded convolutions. Got fft_padding='{fft_padding}'.")
     assert data_dim in (1, 2, 3), f"fft_backend='b200' only supports data_dim in (1, 2, 3). Got data_dim={data_dim}."
+    resolve_periodic(fft_padding, data_dim)  # zero / circular per axis (lengths checked per call)
     del use_chunked_fftconv
 
 
-def select_fftconv_fns(data_dim: int, is_causal: bool):
-    """(fftconv_fn, fftconv_fn_bhl_input) for this backend (ckconv_nd.py:796-871)."""
-    table = FFT_FUNCTIONS["causal" if is_causal else "zero"]
+def _bind_periodic(op_fn, periodic):
+    def _wrapped(x, kernel, shortcut):
+        return op_fn(x, kernel, periodic, shortcut)
+
+    return _wrapped
+
+
+def select_fftconv_fns(data_dim: int, is_causal: bool, fft_padding="zero"):
+    """(fftconv_fn, fftconv_fn_bhl_input) for this backend (ckconv_nd.py:796-871): causal,
+    zero-padded or circular ops for a single padding mode, the mixed ops with the per-axis
+    flags bound for a per-axis list."""
+    if _is_tuple_mode(fft_padding) and not is_causal:
+        per = resolve_periodic(fft_padding, data_dim)
+        try:
+            fn_blh, fn_bhl = MIXED_FFT_FUNCTIONS[data_dim]
+        except KeyError:
+            raise ValueError(f"Mixed-BC FFT conv not implemented for data_dim={data_dim}. "
+                             f"Valid: {sorted(MIXED_FFT_FUNCTIONS)}") from None
+        return _bind_periodic(fn_blh, per), _bind_periodic(fn_bhl, per)
+    mode = "causal" if is_causal else ("circular" if fft_padding == "circular" else "zero")
+    table = FFT_FUNCTIONS[mode]
     try:
         return table[data_dim]
     except KeyError:
         raise ValueError(
-            f"Unsupported configuration: fft_padding='{'causal' if is_causal else 'zero'}', data_dim={data_dim}. "
+            f"Unsupported configuration: fft_padding='{mode}', data_dim={data_dim}. "
             f"Valid dimensions: {sorted(table)}") from None
 
 
@@ -129,11 +175,14 @@ def ckconv_kernel(global_conv, spatial_dims, cp_group=None, **mixer_kwargs):
     """The BHL kernel ``[1|B, C, *K]`` and shortcut ``[C]`` a reference ``CKConvND``
     would hand to its op for inputs of ``spatial_dims`` (ckconv_nd.py:1143-1188).
 
-    ``global_conv`` is duck-typed: ``kernel``, ``mask``, ``is_causal``, ``shortcut`` and
-    ``grid_type`` as CKConvND defines them (zero padding, so every axis is double-grid
-    unless ``grid_type == "single"``)."""
-    single = getattr(global_conv, "grid_type", "double") == "single"
-    grid_lens = [(n + 1) // 2 if single else n for n in spatial_dims]
+    ``global_conv`` is duck-typed: ``kernel``, ``mask``, ``is_causal``, ``shortcut``,
+    ``grid_type`` and ``_periodic_per_axis`` as CKConvND defines them: a single grid on
+    every axis for ``grid_type == "single"``, per axis on the periodic axes when
+    ``grid_type`` is None (per-axis padding, ckconv_nd.py:406-440, :1143-1148)."""
+    grid_type = getattr(global_conv, "grid_type", "double")
+    per = getattr(global_conv, "_periodic_per_axis", None) or (False,) * len(spatial_dims)
+    single = tuple(per) if grid_type is None else (grid_type == "single",) * len(spatial_dims)
+    grid_lens = [(n + 1) // 2 if s else n for n, s in zip(spatial_dims, single)]
     conv_kernel, grid = global_conv.kernel(grid_lens, conditioning=mixer_kwargs.get("conditioning"))
     if not isinstance(global_conv.mask, torch.nn.Identity):
         conv_kernel = global_conv.mask(grid=grid, x=conv_kernel)
@@ -214,8 +263,9 @@ def fused_mixer_config(mixer) -> dict | None:
         g2 = gate_name(mixer.gate_nonlinear_2)
     except NotImplementedError:
         return None
+    per = tuple(getattr(gc, "_periodic_per_axis", None) or ())
     cfg = dict(gate1=g1, gate2=g2, causal=bool(gc.is_causal), short_k=None, short_causal=bool(gc.is_causal),
-               short_weight=lambda: None, short_bias=lambda: None)
+               short_weight=lambda: None, short_bias=lambda: None, periodic=per if any(per) else None)
     sc = mixer.short_conv
     if isinstance(sc, torch.nn.Identity):
         return cfg
@@ -242,6 +292,7 @@ class FusedHyena(torch.nn.Module):
         self._cfg = cfg
         self.gate1, self.gate2 = cfg["gate1"], cfg["gate2"]
         self.causal, self.short_causal = cfg["causal"], cfg["short_causal"]
+        self.periodic = cfg["periodic"]
 
     @property
     def shortcut(self):
@@ -269,4 +320,4 @@ class FusedHyena(torch.nn.Module):
             return hyena_context_parallel(self, query, key, value, filt, cp_group)
         return hyena_fused(query, key, value, filt, self.shortcut.to(query.dtype), self.short_weight,
                            self.short_bias, causal=self.causal, short_causal=self.short_causal,
-                           gate1=self.gate1, gate2=self.gate2)
+                           gate1=self.gate1, gate2=self.gate2, periodic=self.periodic)

@@ -387,6 +387,9 @@ def hyena_context_parallel(module, query, key, value, filt, group, zigzag: bool 
     else:
         x5 = torch.stack([query, key, value], dim=-2)
     short_k = tuple(module.short_weight.shape[2:]) if module.short_weight is not None else ()
+    per = getattr(module, "periodic", None)
+    if per is not None and any(per):
+        raise NotImplementedError("context parallelism with periodic (circular) axes is not supported")
     cfg = (bool(module.causal), short_k, bool(module.short_causal), module.gate1, module.gate2)
     return _ContextParallelMixer.apply(x5, filt, module.shortcut, module.short_weight, module.short_bias,
                                        (group, zigzag, cfg))

@@ -281,16 +281,19 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
   rows_forward<T>(p.x, b, c, N0, N1, A, kB2H, 0, kB2H, mysc, tw);
   __syncthreads();
 
-  // columns: transform, * Kh (or conj), inverse, keep rows [0, N0); the filter-spectrum
-  // column (an L2 read) is loaded before the forward transform that it waits for
+  // columns: transform, * Kh (or conj), inverse, keep rows [0, N0); each round's
+  // filter-spectrum column (an L2 read) is loaded one round ahead, right after the
+  // previous column has consumed its own, so the load overlaps an inverse and a forward
+  // transform
   const float2* kh = p.Kh + (long long)c * kB2H * kB2F;
   const float cj = p.conj ? -1.f : 1.f;
-  for (int rb = 0; rb < (kB2H + kBigGroups - 1) / kBigGroups; ++rb) {
+  constexpr int kColRounds = (kB2H + kBigGroups - 1) / kBigGroups;
+  float2 kv[16];
+#pragma unroll
+  for (int m = 0; m < 16; ++m) kv[m] = g < kB2H ? __ldg(kh + (long long)g * kB2F + l + 16 * m) : make_float2(0.f, 0.f);
+  for (int rb = 0; rb < kColRounds; ++rb) {
     const int j = rb * kBigGroups + g;
     const bool act = j < kB2H;
-    float2 kv[16];
-#pragma unroll
-    for (int m = 0; m < 16; ++m) kv[m] = act ? __ldg(kh + (long long)j * kB2F + l + 16 * m) : make_float2(0.f, 0.f);
     float2 v[16];
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
@@ -303,6 +306,11 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
       float2 k = kv[m];
       k.y *= cj;
       v[m] = cmul(v[m], k);
+    }
+    const int jn = j + kBigGroups;
+    if (rb + 1 < kColRounds) {
+#pragma unroll
+      for (int m = 0; m < 16; ++m) kv[m] = jn < kB2H ? __ldg(kh + (long long)jn * kB2F + l + 16 * m) : make_float2(0.f, 0.f);
     }
     fft256<false, true>(v, mysc, tw, l, 1.f);
     if (act) {

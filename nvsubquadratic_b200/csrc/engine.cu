@@ -80,18 +80,37 @@ struct Geo {
   bool four = false;        // 1D four-step decomposition F = Fa * Fb
   int Fa = 1, Fb = 1;
   long long vol_F = 1;      // prod F
+  // circular (periodic) axes: bit d set = axis d has FFT length N[d] (no padding) and its
+  // "same" alignment is a roll by rshift[d] = (K[d] - 1) / 2, applied as a phase ramp on
+  // the filter spectrum (ops/circular_fftconv.py:310-404, ops/mixed_fftconv.py:295-342)
+  int periodic = 0;
+  int rshift[3] = {0, 0, 0};
 };
 
-static int make_geo(int nd, const int* n, const int* k, int causal, Geo& g) {
+static int make_geo(int nd, const int* n, const int* k, int causal, int periodic, Geo& g) {
   if (nd < 1 || nd > 3) return fail(HYFFT_ERR_INVALID, "ndim must be 1..3 (got %d)", nd);
   if (causal && nd != 1) return fail(HYFFT_ERR_INVALID, "causal convolution is 1D only");
+  if (periodic & ~((1 << nd) - 1)) return fail(HYFFT_ERR_INVALID, "periodic mask 0x%x names axes beyond %d", periodic, nd);
+  if (periodic && causal) return fail(HYFFT_ERR_INVALID, "causal convolution has no periodic axis");
   g.D = nd;
   g.vol_F = 1;
+  g.periodic = periodic;
   for (int d = 0; d < nd; ++d) {
     if (n[d] < 1 || k[d] < 1) return fail(HYFFT_ERR_INVALID, "extents must be positive");
     if (k[d] > 2 * n[d]) return fail(HYFFT_ERR_INVALID, "kernel extent %d > 2 * input extent %d", k[d], n[d]);
     g.N[d] = n[d];
     g.K[d] = k[d];
+    if (periodic & (1 << d)) {
+      if (k[d] > n[d]) return fail(HYFFT_ERR_INVALID, "kernel extent %d > input extent %d on periodic axis %d", k[d], n[d], d);
+      if (next_pow2(n[d]) != n[d])
+        return fail(HYFFT_ERR_UNSUPPORTED, "periodic axis %d of length %d: circular FFT lengths must be powers of two", d, n[d]);
+      g.F[d] = n[d];
+      g.crop[d] = 0;
+      g.rshift[d] = (k[d] - 1) / 2;
+      if (nd > 1 && g.F[d] > kPassPoints) return fail(HYFFT_ERR_UNSUPPORTED, "multi-D axis FFT length %d > %d", g.F[d], kPassPoints);
+      g.vol_F *= g.F[d];
+      continue;
+    }
     long long need;
     if (causal) {
       if (k[d] > n[d] + 1)
@@ -599,7 +618,7 @@ static size_t ws_budget() {
 // would take (the static-scratch forward runs only the chunked pass chain).
 static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p, bool allow_big2d = true) {
   if (!d) return fail(HYFFT_ERR_INVALID, "null descriptor");
-  HY_TRY(make_geo(d->ndim, d->n, d->k, d->causal, p.g));
+  HY_TRY(make_geo(d->ndim, d->n, d->k, d->causal, d->periodic, p.g));
   if (d->batch < 1 || d->channels < 1) return fail(HYFFT_ERR_INVALID, "batch and channels must be positive");
   if (d->kernel_batch != 1 && d->kernel_batch != d->batch)
     return fail(HYFFT_ERR_INVALID, "kernel_batch must be 1 or batch (%d), got %d", d->batch, d->kernel_batch);
@@ -619,7 +638,7 @@ static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p, bool allow_big2
   const long long per_ch = 2 * (p.spec_x_bytes_per_ch + p.spec_k_bytes_per_ch);
   long long cc = (long long)(ws_budget() / (size_t)std::max<long long>(per_ch, 1));
   p.Cc = (int)std::max<long long>(1, std::min<long long>(cc, p.C));
-  p.big2d = allow_big2d && p.g.D == 2 && !d->causal && p.g.F[0] == kB2F && p.g.F[1] == kB2F && p.g.N[0] <= kB2MaxN &&
+  p.big2d = allow_big2d && !p.g.periodic && p.g.D == 2 && !d->causal && p.g.F[0] == kB2F && p.g.F[1] == kB2F && p.g.N[0] <= kB2MaxN &&
             p.g.N[1] <= kB2MaxN && p.kB == 1 && !getenv("HYFFT_DISABLE_BIG2D");
   const int F0 = p.g.F[0];
   p.khalf = p.g.D >= 2 && !p.g.four && !p.big2d && (F0 == 32 || F0 == 64 || F0 == 128 || F0 == 256) &&
@@ -726,6 +745,72 @@ static int fused_conv_chain(const Geo& g, int Cc, const RealView& xc, int tin, c
 }
 
 // One forward convolution over channels [c0, c0 + Cc) of already-prepared views.
+// Phase ramp of the periodic axes on a filter spectrum stored [pair][F...][C] (last axis
+// F/2 + 1 bins when half; 1D four-step layout [pair][k_a][k_b][C], k = k_a + Fa k_b):
+// S *= prod_d exp(sign * 2 pi i k_d rshift[d] / F[d]). sign +1 aligns the convolution
+// output like the reference's roll by -rshift; sign -1 (the conjugate) maps the gradient
+// of the rolled filter back to the filter's own taps.
+struct RampDesc {
+  int D, half, four, Fa, Fb;
+  int F[3], r[3];
+  long long C;
+  float sign;
+};
+
+__global__ void spec_ramp_kernel(float2* __restrict__ S, const RampDesc d, long long total) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total;
+       i += (long long)gridDim.x * blockDim.x) {
+    long long rest = i / d.C;
+    float2 w = make_float2(1.f, 0.f);
+    if (d.four) {
+      const long long kb = rest % d.Fb;
+      const long long ka = (rest / d.Fb) % d.Fa;
+      const long long F = (long long)d.Fa * d.Fb;
+      const long long m = ((ka + (long long)d.Fa * kb) % F) * d.r[0] % F;
+      float sn, cs;
+      sincospif(2.0f * (float)m / (float)F, &sn, &cs);
+      w = make_float2(cs, d.sign * sn);
+    } else {
+      for (int ax = d.D - 1; ax >= 0; --ax) {
+        const int ext = (d.half && ax == d.D - 1) ? d.F[ax] / 2 + 1 : d.F[ax];
+        const long long k = rest % ext;
+        rest /= ext;
+        if (d.r[ax] == 0) continue;
+        const long long m = k * d.r[ax] % d.F[ax];
+        float sn, cs;
+        sincospif(2.0f * (float)m / (float)d.F[ax], &sn, &cs);
+        w = cmul(w, make_float2(cs, d.sign * sn));
+      }
+    }
+    S[i] = cmul(S[i], w);
+  }
+}
+
+// Apply the periodic axes' phase ramp to a filter(-gradient) spectrum of Cc channels.
+static int apply_ramp(const ConvPlan& p, float2* S, int Cc, bool half, float sign, cudaStream_t st) {
+  if (!p.g.periodic) return HYFFT_OK;
+  RampDesc d;
+  d.D = p.g.D;
+  d.half = half ? 1 : 0;
+  d.four = p.g.four ? 1 : 0;
+  d.Fa = p.g.Fa;
+  d.Fb = p.g.Fb;
+  bool any = false;
+  long long vol = 1;
+  for (int a = 0; a < 3; ++a) {
+    d.F[a] = p.g.F[a];
+    d.r[a] = (p.g.periodic & (1 << a)) ? p.g.rshift[a] : 0;
+    any = any || d.r[a] != 0;
+  }
+  if (!any) return HYFFT_OK;
+  for (int a = 0; a < p.g.D; ++a) vol *= (half && a == p.g.D - 1) ? p.g.F[a] / 2 + 1 : p.g.F[a];
+  d.C = Cc;
+  d.sign = sign;
+  const long long total = (long long)p.pk.P * vol * Cc;
+  spec_ramp_kernel<<<grid_for(total), 256, 0, st>>>(S, d, total);
+  return check_launch("spec_ramp_kernel");
+}
+
 static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView& xv, const RealView& kv,
                               const float* Dfull, const RealView& yv, float2* S, float2* Kh, cudaStream_t st) {
   const int eb = dtype_bytes(p.dt);
@@ -734,6 +819,7 @@ static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView&
   const RealView yc = offset_channels(yv, c0, eb);
   const int zero[3] = {0, 0, 0};
   HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st, nullptr, p.khalf));
+  HY_TRY(apply_ramp(p, Kh, Cc, p.khalf, 1.f, st));
   Epilogue ep;
   if (Dfull) {
     ep.mode = OUT_REAL_SKIP;
@@ -746,7 +832,10 @@ static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView&
                                         p.g.N, ep, st, p.khalf);
   if (rc != HYFFT_ERR_UNSUPPORTED) return rc;
   // the elementwise product below reads the full filter spectrum
-  if (p.khalf) HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+  if (p.khalf) {
+    HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+    HY_TRY(apply_ramp(p, Kh, Cc, false, 1.f, st));
+  }
   HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S, st));
   const long long per_pair = p.g.vol_F * Cc;
   spec_mul_kernel<<<grid_for(per_pair * p.px.P), 256, 0, st>>>(S, Kh, per_pair, p.px.P, p.shared ? 1 : 0);
@@ -811,8 +900,13 @@ static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView
   const RealView kc = offset_channels(kv, c0, 4);
   const RealView dyc = offset_channels(dyv, c0, eb);
   const int zero[3] = {0, 0, 0};
-  if (!kh_ready) HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st, nullptr, p.khalf));
-  if (dxv.ptr && dkv.ptr) {
+  if (!kh_ready) {
+    HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st, nullptr, p.khalf));
+    HY_TRY(apply_ramp(p, Kh, Cc, p.khalf, 1.f, st));
+  }
+  // (periodic axes: the filter gradient needs the conjugate ramp before its inverse, so
+  // the merged backward pass, which inverts it in place, is not used)
+  if (dxv.ptr && dkv.ptr && !p.g.periodic) {
     Epilogue ep;
     if (Dfull) {
       ep.mode = OUT_REAL_SKIP;
@@ -824,12 +918,16 @@ static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView
     if (rc != HYFFT_ERR_UNSUPPORTED) return rc;
   }
   // the elementwise backward below reads the full filter spectrum
-  if (p.khalf) HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+  if (p.khalf) {
+    HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st));
+    HY_TRY(apply_ramp(p, Kh, Cc, false, 1.f, st));
+  }
   HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S1, st));
   HY_TRY(fwd_chain(p.g, Cc, dyc, p.dt, p.px, p.g.N, p.g.crop, S2, st));
   const long long per_pair = p.g.vol_F * Cc;
   spec_bwd_kernel<<<grid_for(per_pair), 256, 0, st>>>(S2, S1, Kh, dKh, per_pair, p.px.P, p.shared ? 1 : 0);
   HY_TRY(check_launch("spec_bwd_kernel"));
+  HY_TRY(apply_ramp(p, dKh, Cc, false, -1.f, st));
   if (dxv.ptr) {
     const RealView dxc = offset_channels(dxv, c0, eb);
     Epilogue ep;
@@ -1159,6 +1257,7 @@ static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
   cd.causal = d->causal;
   cd.dtype = d->dtype;
   cd.layout = HYFFT_LAYOUT_BLH;
+  cd.periodic = d->periodic;
   HY_TRY(make_conv_plan(&cd, h.cp));
   if (d->gate1 < 0 || d->gate1 > 2 || d->gate2 < 0 || d->gate2 > 2) return fail(HYFFT_ERR_INVALID, "bad gate");
   StencilGeom& g = h.sg;
@@ -1189,7 +1288,7 @@ static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
   // fused single-pass path: 2D, "same" 3x3 (or no) short conv, 8-channel vectors
   const bool sq3 = g.has_conv && g.k[0] == 3 && g.k[1] == 3 && !d->short_causal;
   h.SK = sq3 ? 3 : 0;
-  if (!getenv("HYFFT_DISABLE_FUSED") && d->ndim == 2 && !d->causal && (sq3 || !g.has_conv) &&
+  if (!getenv("HYFFT_DISABLE_FUSED") && !d->periodic && d->ndim == 2 && !d->causal && (sq3 || !g.has_conv) &&
       (d->dtype == HYFFT_BF16 || d->dtype == HYFFT_F32) && d->channels % 8 == 0 && d->in_pos_stride % 8 == 0 &&
       d->in_batch_stride % 8 == 0 && d->out_pos_stride % 8 == 0 && d->out_batch_stride % 8 == 0) {
     // the shortest compiled transform first (e.g. 24 = 3 * 8 for a 14-point axis and a 14-tap

@@ -45,11 +45,25 @@ __all__ = [
     "fftconv3d_fp32_bhl_w_reshape",
     "fftconv3d_fp32_blh",
     "fftconv_nd",
+    "mixed_fftconv_nd",
+    "circular_fftconv1d_fp32_bhl",
+    "circular_fftconv2d_fp32_bhl",
+    "circular_fftconv3d_fp32_bhl",
+    "circular_fftconv1d_fp32_bhl_w_reshape",
+    "circular_fftconv2d_fp32_bhl_w_reshape",
+    "circular_fftconv3d_fp32_bhl_w_reshape",
+    "mixed_fftconv1d_fp32_bhl",
+    "mixed_fftconv2d_fp32_bhl",
+    "mixed_fftconv3d_fp32_bhl",
+    "mixed_fftconv1d_fp32_bhl_w_reshape",
+    "mixed_fftconv2d_fp32_bhl_w_reshape",
+    "mixed_fftconv3d_fp32_bhl_w_reshape",
 ]
 
 
-def _conv_desc(B, H, spatial, kshape, kB, causal, dtype, layout) -> _lib.ConvDesc:
+def _conv_desc(B, H, spatial, kshape, kB, causal, dtype, layout, periodic=0) -> _lib.ConvDesc:
     d = _lib.ConvDesc()
+    d.periodic = periodic
     d.ndim = len(spatial)
     d.batch = B
     d.channels = H
@@ -92,7 +106,7 @@ def _plan(*args):
 
 class _FFTConvFunction(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, kernel, shortcut, causal, layout):
+    def forward(ctx, x, kernel, shortcut, causal, layout, periodic=0):
         dev = _lib.require_cuda(x, kernel, shortcut)
         lib = _lib.load()
         nd = x.ndim - 2
@@ -108,7 +122,7 @@ class _FFTConvFunction(torch.autograd.Function):
         xc = x.contiguous()
         kf = kernel.detach().to(torch.float32).contiguous()
         sc = shortcut.detach().contiguous() if shortcut is not None else None
-        desc, (wf, wb) = _plan(B, H, spatial, kshape, kB, causal, x.dtype, layout)
+        desc, (wf, wb) = _plan(B, H, spatial, kshape, kB, causal, x.dtype, layout, periodic)
         ctx.wb = wb
         ws = _lib.workspace(wf, dev)
         y = torch.empty_like(xc)
@@ -143,10 +157,10 @@ class _FFTConvFunction(torch.autograd.Function):
             dk = dk.to(ctx.kernel_dtype)
         if ds is not None and ctx.shortcut_dtype != torch.float32:
             ds = ds.to(ctx.shortcut_dtype)
-        return dx, dk, ds, None, None
+        return dx, dk, ds, None, None, None
 
 
-def _check_common(x, kernel, shortcut, nd, layout):
+def _check_common(x, kernel, shortcut, nd, layout, periodic=()):
     assert x.ndim == nd + 2, f"Unexpected input shape: {tuple(x.shape)}."
     assert kernel.ndim == nd + 2, f"Unexpected kernel shape: {kernel.shape}."
     B = x.shape[0]
@@ -157,8 +171,11 @@ def _check_common(x, kernel, shortcut, nd, layout):
         H, spatial, kshape, kH = x.shape[1], x.shape[2:], kernel.shape[2:], kernel.shape[1]
     else:
         H, spatial, kshape, kH = x.shape[-1], x.shape[1:-1], kernel.shape[1:-1], kernel.shape[-1]
-    for n, k in zip(spatial, kshape):
-        assert k <= 2 * n, f"Kernel size must be less than or equal to 2 * input size. Got {k} for size {n}."
+    for d, (n, k) in enumerate(zip(spatial, kshape)):
+        if d < len(periodic) and periodic[d]:
+            assert k <= n, f"K must be <= N on periodic axis {d}: K={k}, N={n}."
+        else:
+            assert k <= 2 * n, f"Kernel size must be less than or equal to 2 * input size. Got {k} for size {n}."
     assert kH == H, "Input and kernel must have the same number of channels (H)."
     if shortcut is not None:
         assert shortcut.dtype == x.dtype, f"shortcut.dtype ({shortcut.dtype}) must match x.dtype ({x.dtype})"
@@ -196,7 +213,7 @@ def fftconv_nd(x, kernel, shortcut=None, *, causal: bool = False, layout: int = 
         if K >= L + 2:
             kernel = _causal_alias_kernel(kernel, L, layout)
             causal = False
-    return _FFTConvFunction.apply(x, kernel, shortcut, causal, layout)
+    return _FFTConvFunction.apply(x, kernel, shortcut, causal, layout, 0)
 
 
 # ---------------------------------------------------------------- BHL
@@ -248,3 +265,71 @@ causal_fftconv1d_fp32_bhl_w_reshape = causal_fftconv1d_fp32_blh
 fftconv1d_fp32_bhl_w_reshape = fftconv1d_fp32_blh
 fftconv2d_fp32_bhl_w_reshape = fftconv2d_fp32_blh
 fftconv3d_fp32_bhl_w_reshape = fftconv3d_fp32_blh
+
+
+# ---------------------------------------------------------------- circular and mixed boundaries
+def _normalize_periodic(periodic, data_dim: int) -> tuple[bool, ...]:
+    """Per-axis periodic flags as a tuple of bools of length data_dim (mixed_fftconv.py:420-442)."""
+    t = tuple(bool(p) for p in periodic)
+    assert len(t) == data_dim, f"periodic must have length {data_dim} (data_dim), got length {len(t)}"
+    return t
+
+
+def _mask(periodic: tuple[bool, ...]) -> int:
+    return sum(1 << d for d, p in enumerate(periodic) if p)
+
+
+def mixed_fftconv_nd(x, kernel, periodic, shortcut=None, *, layout: int = _lib.LAYOUT_BHL):
+    """Per-axis boundary conditions: periodic axes are circular (FFT length N, output
+    aligned by (K - 1) // 2, K <= N), the others zero-padded "same" (crop at K // 2);
+    ops/mixed_fftconv.py:504-623. Periodic axis lengths must be powers of two here."""
+    nd = x.ndim - 2
+    per = _normalize_periodic(periodic, nd)
+    _check_common(x, kernel, shortcut, nd, layout, per)
+    return _FFTConvFunction.apply(x, kernel, shortcut, False, layout, _mask(per))
+
+
+def _circular(nd):
+    def fn(x, kernel, shortcut=None, use_phase_shift: bool = True):
+        # use_phase_shift picks how the reference applies the alignment (phase ramp or roll);
+        # both give the same result, and the library always uses the phase ramp
+        return mixed_fftconv_nd(x, kernel, (True,) * nd, shortcut, layout=_lib.LAYOUT_BHL)
+
+    return fn
+
+
+def _circular_blh(nd):
+    def fn(x, kernel, shortcut=None, use_phase_shift: bool = True):
+        return mixed_fftconv_nd(x, kernel, (True,) * nd, shortcut, layout=_lib.LAYOUT_BLH)
+
+    return fn
+
+
+circular_fftconv1d_fp32_bhl = _circular(1)
+circular_fftconv1d_fp32_bhl.__doc__ = "Circular 1D conv, x [B, H, L], kernel [1|B, H, K<=L] (circular_fftconv.py:310-403)."
+circular_fftconv2d_fp32_bhl = _circular(2)
+circular_fftconv2d_fp32_bhl.__doc__ = "Circular 2D conv (circular_fftconv.py:406-483)."
+circular_fftconv3d_fp32_bhl = _circular(3)
+circular_fftconv3d_fp32_bhl.__doc__ = "Circular 3D conv (circular_fftconv.py:486-582)."
+# channels-last forms (the reference transposes to BHL, circular_fftconv.py:585-660; read in place here)
+circular_fftconv1d_fp32_bhl_w_reshape = _circular_blh(1)
+circular_fftconv2d_fp32_bhl_w_reshape = _circular_blh(2)
+circular_fftconv3d_fp32_bhl_w_reshape = _circular_blh(3)
+
+
+def _mixed(nd, layout):
+    def fn(x, kernel, periodic, shortcut=None, use_phase_shift: bool = True):
+        return mixed_fftconv_nd(x, kernel, periodic, shortcut, layout=layout)
+
+    return fn
+
+
+mixed_fftconv1d_fp32_bhl = _mixed(1, _lib.LAYOUT_BHL)
+mixed_fftconv2d_fp32_bhl = _mixed(2, _lib.LAYOUT_BHL)
+mixed_fftconv3d_fp32_bhl = _mixed(3, _lib.LAYOUT_BHL)
+mixed_fftconv1d_fp32_bhl_w_reshape = _mixed(1, _lib.LAYOUT_BLH)
+mixed_fftconv2d_fp32_bhl_w_reshape = _mixed(2, _lib.LAYOUT_BLH)
+mixed_fftconv3d_fp32_bhl_w_reshape = _mixed(3, _lib.LAYOUT_BLH)
+for _f, _n in ((mixed_fftconv1d_fp32_bhl, "mixed_fftconv.py:631-660"), (mixed_fftconv2d_fp32_bhl, "mixed_fftconv.py:663-697"),
+               (mixed_fftconv3d_fp32_bhl, "mixed_fftconv.py:700-723")):
+    _f.__doc__ = f"Mixed boundary conditions, periodic = per-axis flags ({_n})."

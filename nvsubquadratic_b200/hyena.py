@@ -61,8 +61,9 @@ def _pos_strides(t: torch.Tensor) -> tuple[int, int] | None:
 
 
 def _hyena_desc(B, C, spatial, kshape, causal, short_k, short_causal, short_bias, g1, g2, dtype,
-                in_strides, out_strides) -> _lib.HyenaDesc:
+                in_strides, out_strides, periodic=0) -> _lib.HyenaDesc:
     d = _lib.HyenaDesc()
+    d.periodic = periodic
     d.ndim = len(spatial)
     d.batch = B
     d.channels = C
@@ -158,11 +159,12 @@ def forward_call(q, k, v, filt32, D32, sw32, sb32, cfg):
     channel chunks of one packed ``[B, *S, 3C]`` tensor). Returns ``(y, state)``; the
     state (descriptor, saved buffer, backward workspace size) feeds ``backward_call``."""
     dev = q.device
-    causal, short_k, short_causal, g1, g2 = cfg
+    causal, short_k, short_causal, g1, g2 = cfg[:5]
+    periodic = cfg[5] if len(cfg) > 5 else 0  # bit mask of circular axes
     B, C = q.shape[0], q.shape[-1]
     y = torch.empty(q.shape, dtype=q.dtype, device=dev)
     desc, (wf, wb, sv) = _plan(B, C, tuple(q.shape[1:-1]), tuple(filt32.shape[2:]), causal, short_k, short_causal,
-                               sb32 is not None, g1, g2, q.dtype, _pos_strides(q), _pos_strides(y))
+                               sb32 is not None, g1, g2, q.dtype, _pos_strides(q), _pos_strides(y), periodic)
     ws = _lib.workspace(wf, dev)
     saved = _lib.workspace(sv, dev)
     rc = _lib.load().hyfft_hyena_forward(ctypes.byref(desc), q.data_ptr(), k.data_ptr(), v.data_ptr(),
@@ -260,10 +262,12 @@ class _HyenaFunction(torch.autograd.Function):
 
 
 def hyena_fused(q, k, v, filt, D, short_w=None, short_b=None, *, causal=False, short_causal=None,
-                gate1="identity", gate2=None):
+                gate1="identity", gate2=None, periodic=None):
     """Functional fused Hyena. q, k, v ``[B, *S, C]``; filt ``[1, C, *K]`` (BHL, any float
     dtype, computed in float32); D ``[C]``; short_w ``[3C, 1, *k]`` or ``[3C, *k]``; short_b
-    ``[3C]`` or None. Returns ``[B, *S, C]`` in q's dtype."""
+    ``[3C]`` or None; periodic: per-axis circular flags of the long conv (CKConvND's
+    fft_padding "circular" / per-axis list) or None (zero padding). Returns ``[B, *S, C]``
+    in q's dtype."""
     nd = q.ndim - 2
     assert nd in (1, 2, 3), f"unsupported rank {q.ndim}"
     assert q.shape == k.shape == v.shape, "query, key and value must have the same shape"
@@ -271,8 +275,13 @@ def hyena_fused(q, k, v, filt, D, short_w=None, short_b=None, *, causal=False, s
     assert filt.ndim == nd + 2 and filt.shape[0] == 1 and filt.shape[1] == C, (
         f"filter must be [1, C, *K]; got {tuple(filt.shape)}")
     assert tuple(D.shape) == (C,)
-    for n, kk in zip(q.shape[1:-1], filt.shape[2:]):
-        assert kk <= 2 * n, f"Kernel size must be less than or equal to 2 * input size. Got {kk} for size {n}."
+    per = tuple(bool(x) for x in periodic) if periodic is not None else (False,) * nd
+    assert len(per) == nd, f"periodic must have length {nd} (data_dim), got length {len(per)}"
+    for ax, (n, kk) in enumerate(zip(q.shape[1:-1], filt.shape[2:])):
+        if per[ax]:
+            assert kk <= n, f"K must be <= N on periodic axis {ax}: K={kk}, N={n}."
+        else:
+            assert kk <= 2 * n, f"Kernel size must be less than or equal to 2 * input size. Got {kk} for size {n}."
     g1 = gate_name(gate1)
     g2 = gate_name(gate2) if gate2 is not None else g1
     short_k = ()
@@ -285,7 +294,7 @@ def hyena_fused(q, k, v, filt, D, short_w=None, short_b=None, *, causal=False, s
         L, K = q.shape[1], filt.shape[2]
         assert nd == 1, "causal Hyena is 1D only"
         assert K <= L + 1, "causal filter longer than L+1 is not supported by the fused path"
-    cfg = (bool(causal), short_k, bool(short_causal), g1, g2)
+    cfg = (bool(causal), short_k, bool(short_causal), g1, g2, sum(1 << ax for ax, p_ in enumerate(per) if p_))
     base = _packed_base(q, k, v) if torch.is_grad_enabled() else None
     if base is not None:
         return _HyenaFunction.apply(True, base, filt, D, short_w, short_b, cfg)
@@ -317,13 +326,15 @@ class HyenaB200(torch.nn.Module):
             defaults to gate1 (hyena_nd.py:274-278).
         causal: causal 1D global conv (short conv is causal too unless short_causal=False).
         short_bias: learnable bias on the short conv.
+        periodic: per-axis circular flags of the global conv (None: zero padding on every axis).
     """
 
     def __init__(self, hidden_dim: int, data_dim: int, kernel_fn: Callable, *, short_kernel_size: int | None = 3,
                  gate1="identity", gate2=None, causal: bool = False, short_causal: bool | None = None,
-                 short_bias: bool = False, dtype=torch.float32, device=None):
+                 short_bias: bool = False, periodic=None, dtype=torch.float32, device=None):
         super().__init__()
         self.hidden_dim = hidden_dim
+        self.periodic = tuple(bool(x) for x in periodic) if periodic is not None else None
         self.data_dim = data_dim
         self.kernel_fn = kernel_fn
         self.gate1 = gate_name(gate1)
@@ -355,4 +366,4 @@ class HyenaB200(torch.nn.Module):
             return hyena_context_parallel(self, query, key, value, filt, cp_group)
         return hyena_fused(query, key, value, filt, self.shortcut.to(query.dtype), self.short_weight,
                            self.short_bias, causal=self.causal, short_causal=self.short_causal,
-                           gate1=self.gate1, gate2=self.gate2)
+                           gate1=self.gate1, gate2=self.gate2, periodic=self.periodic)

@@ -61,8 +61,11 @@ def fftconv_bhl(
     kernel: torch.Tensor,
     shortcut: torch.Tensor | None = None,
     causal: bool = False,
+    periodic: tuple[bool, ...] | None = None,
 ) -> torch.Tensor:
-    """Generic N-D (N = x.ndim - 2) zero-padded linear FFT conv, BHL layout.
+    """Generic N-D (N = x.ndim - 2) FFT conv, BHL layout: zero-padded linear on every axis,
+    or per-axis circular where ``periodic[d]`` is set (mixed_fftconv.py:295-342 recipe: FFT
+    length N_d, no crop, output rolled by -((K_d - 1) // 2); circular_fftconv.py:374-396).
 
     x: ``[B, H, *S]`` any float dtype; kernel: ``[1|B, H, *K]``;
     shortcut: ``[H]`` of ``x.dtype`` or None. Returns ``[B, H, *S]`` in ``x.dtype``.
@@ -76,18 +79,29 @@ def fftconv_bhl(
     )
     spatial = tuple(x.shape[2:])
     kshape = tuple(kernel.shape[2:])
-    for n, k in zip(spatial, kshape):
-        assert k <= 2 * n, f"Kernel size must be at most 2 * input size. Got {k} for size {n}."
+    per = tuple(bool(p) for p in periodic) if periodic is not None else (False,) * nd
+    assert len(per) == nd, f"periodic must have length {nd}"
+    for d, (n, k) in enumerate(zip(spatial, kshape)):
+        if per[d]:
+            assert not causal and k <= n, f"K must be <= N on periodic axis {d}: K={k}, N={n}."
+        else:
+            assert k <= 2 * n, f"Kernel size must be at most 2 * input size. Got {k} for size {n}."
     if nd > 1:
         assert kernel.shape[1] == H, "Input and kernel must have the same number of channels (H)."
 
-    sizes = fft_sizes(spatial, kshape, causal)
-    starts = crop_starts(kshape, causal)
+    sizes = list(fft_sizes(spatial, kshape, causal))
+    starts = list(crop_starts(kshape, causal))
+    shifts = [0] * nd
+    for d in range(nd):
+        if per[d]:
+            sizes[d], starts[d], shifts[d] = spatial[d], 0, -((kshape[d] - 1) // 2)
     dims = tuple(range(2, 2 + nd))
 
     xs = torch.fft.rfftn(x.to(torch.float32), s=sizes, dim=dims)
     ks = torch.fft.rfftn(kernel.to(torch.float32), s=sizes, dim=dims)
     full = torch.fft.irfftn(xs * ks, s=sizes, dim=dims)
+    if any(shifts):
+        full = torch.roll(full, shifts=tuple(shifts), dims=dims)
     window = tuple(slice(c, c + n) for c, n in zip(starts, spatial))
     y = full[(slice(None), slice(None)) + window].to(x.dtype)
 

@@ -82,6 +82,7 @@ def hyena_forward(
     short_causal: bool | None = None,
     gate1: str = "identity",
     gate2: str | None = None,
+    periodic: tuple[bool, ...] | None = None,
 ) -> torch.Tensor:
     """q, k, v: ``[B, *S, C]``; filt: ``[1|B, C, *K]`` (the BHL kernel CKConvND hands to
     the op, ckconv_nd.py:1055-1062); D: ``[C]`` in the activation dtype or None;
@@ -97,6 +98,6 @@ def hyena_forward(
         x = depthwise_short_conv(x, short_w, short_b, short_causal)
         qb, kb, vb = (t.contiguous() for t in x.split(C, dim=1))
     z = qb * gate_fn(gate1, kb)
-    h = fftconv_bhl(z, filt, D, causal=causal)
+    h = fftconv_bhl(z, filt, D, causal=causal, periodic=periodic)
     y = h * gate_fn(gate2, vb)
     return y.movedim(1, -1)

@@ -124,6 +124,43 @@ def make_ops(ref) -> dict:
     return {"cases": cases}
 
 
+def make_boundary(circ, mixed) -> dict:
+    """Circular (periodic) and mixed-boundary ops of the reference
+    (nvsubquadratic/ops/circular_fftconv.py, nvsubquadratic/ops/mixed_fftconv.py)."""
+    cases = []
+    # (name, fn_name, periodic or None, x_shape, k_shape, dtype, with_shortcut)
+    specs = [
+        ("circ1d_a", "circular_fftconv1d_fp32_bhl", None, (2, 8, 64), (1, 8, 15), torch.float32, True),
+        ("circ1d_even", "circular_fftconv1d_fp32_bhl", None, (2, 4, 32), (1, 4, 8), torch.float32, True),
+        ("circ1d_KeqL", "circular_fftconv1d_fp32_bhl", None, (1, 4, 16), (1, 4, 16), torch.float32, False),
+        ("circ2d_a", "circular_fftconv2d_fp32_bhl", None, (2, 4, 16, 32), (1, 4, 5, 7), torch.float32, True),
+        ("circ2d_full", "circular_fftconv2d_fp32_bhl", None, (2, 3, 32, 32), (1, 3, 32, 32), torch.float32, True),
+        ("circ2d_bf16", "circular_fftconv2d_fp32_bhl", None, (2, 4, 16, 16), (1, 4, 16, 16), torch.bfloat16, True),
+        ("circ2d_persample", "circular_fftconv2d_fp32_bhl", None, (2, 3, 8, 8), (2, 3, 4, 6), torch.float32, True),
+        ("circ3d_a", "circular_fftconv3d_fp32_bhl", None, (1, 2, 8, 16, 8), (1, 2, 3, 6, 8), torch.float32, True),
+        ("mixed2d_xy", "mixed_fftconv2d_fp32_bhl", (True, False), (2, 4, 32, 20), (1, 4, 9, 39), torch.float32, True),
+        ("mixed2d_yx", "mixed_fftconv2d_fp32_bhl", (False, True), (2, 4, 12, 32), (1, 4, 23, 32), torch.float32, True),
+        ("mixed3d", "mixed_fftconv3d_fp32_bhl", (True, True, False), (1, 2, 16, 8, 6), (1, 2, 5, 8, 11),
+         torch.float32, True),
+        ("mixed3d_bf16", "mixed_fftconv3d_fp32_bhl", (False, True, True), (2, 2, 6, 16, 16), (1, 2, 11, 3, 16),
+         torch.bfloat16, True),
+    ]
+    g = torch.Generator().manual_seed(5)
+    for name, fn_name, per, xs, ks, dt, with_sc in specs:
+        mod = mixed if fn_name.startswith("mixed") else circ
+        base = getattr(mod, fn_name)
+        fn = (lambda x, k, sc, _b=base, _p=per: _b(x, k, _p, sc)) if per is not None else base
+        x = torch.randn(xs, generator=g).to(dt)
+        k = (torch.randn(ks, generator=g) / (torch.tensor(ks[2:]).prod() ** 0.5)).to(dt)
+        sc = torch.randn(xs[1], generator=g).to(dt) if with_sc else None
+        dy = torch.randn(xs, generator=g).to(dt)
+        res = _grad_case(fn, x, k, sc, dy)
+        case = {"name": name, "fn": fn_name, "periodic": per, "x": x, "k": k, "shortcut": sc, "dy": dy}
+        case.update(res)
+        cases.append(case)
+    return {"cases": cases}
+
+
 class _FixedKernel(torch.nn.Module):
     """Stands in for SIRENKernelND: returns a stored channels-last kernel [1, *K, C]."""
 
@@ -281,6 +318,7 @@ def make_cp(ref_path: str) -> dict:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="root of the nvSubquadratic source tree (holds nvsubquadratic/)")
+    ap.add_argument("--only", default="", help="comma-separated subset of ops,hyena,cp,boundary to regenerate")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     _install_omegaconf_stub()
@@ -289,10 +327,19 @@ def main() -> None:
     from nvsubquadratic.modules.ckconv_nd import CKConvND
     from nvsubquadratic.modules.hyena_nd import Hyena
 
-    torch.save(make_ops(ref_fftconv), HERE / "ops.pt")
-    torch.save(make_hyena(Hyena, CKConvND, ref_fftconv), HERE / "hyena.pt")
-    torch.save(make_cp(args.ref), HERE / "cp.pt")
-    for f in ("ops.pt", "hyena.pt", "cp.pt"):
+    from nvsubquadratic.ops import circular_fftconv as ref_circ
+    from nvsubquadratic.ops import mixed_fftconv as ref_mixed
+
+    only = set(args.only.split(",")) if args.only else {"ops", "hyena", "cp", "boundary"}
+    if "ops" in only:
+        torch.save(make_ops(ref_fftconv), HERE / "ops.pt")
+    if "hyena" in only:
+        torch.save(make_hyena(Hyena, CKConvND, ref_fftconv), HERE / "hyena.pt")
+    if "cp" in only:
+        torch.save(make_cp(args.ref), HERE / "cp.pt")
+    if "boundary" in only:
+        torch.save(make_boundary(ref_circ, ref_mixed), HERE / "boundary.pt")
+    for f in sorted(n + ".pt" for n in only):
         print(f, (HERE / f).stat().st_size, "bytes")
 
 

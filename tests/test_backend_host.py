@@ -24,9 +24,17 @@ def test_rejects_invalid_backend():
         backend.validate_ckconv_config(2, "zero", "double", fft_backend="not_a_backend")
 
 
-def test_rejects_circular_padding():
-    with pytest.raises(AssertionError, match="only supports zero-padded"):
-        backend.validate_ckconv_config(2, "circular", "single")
+def test_accepts_circular_and_per_axis_padding():
+    backend.validate_ckconv_config(2, "circular", "single")
+    backend.validate_ckconv_config(3, ["circular", "circular", "zero"], None)
+    assert backend.resolve_periodic(["zero", "circular"], 2) == (False, True)
+    assert backend.resolve_periodic("circular", 3) == (True, True, True)
+    with pytest.raises(ValueError, match="Unknown fft_padding"):
+        backend.validate_ckconv_config(2, ["zero", "reflect"], None)
+    with pytest.raises(AssertionError, match="requires grid_type='single'"):
+        backend.validate_ckconv_config(2, "circular", "double")
+    with pytest.raises(ValueError, match="incompatible with periodic"):
+        backend.validate_ckconv_config(1, "circular", "single", is_causal=True)
 
 
 def test_rejects_causal_with_2d():
@@ -34,9 +42,9 @@ def test_rejects_causal_with_2d():
         backend.validate_ckconv_config(2, "zero", "double", is_causal=True)
 
 
-def test_rejects_per_axis_padding():
-    with pytest.raises(ValueError, match="does not support a per-axis fft_padding"):
-        backend.validate_ckconv_config(2, ["zero", "zero"], None)
+def test_rejects_per_axis_padding_misuse():
+    with pytest.raises(ValueError, match="not supported with a per-axis"):
+        backend.validate_ckconv_config(1, ["zero"], None, is_causal=True)
     with pytest.raises(ValueError, match="grid_type must be None"):
         backend.validate_ckconv_config(2, ["zero", "circular"], "double")
 
@@ -57,6 +65,11 @@ def test_function_binding():
         assert blh is getattr(fftconv, f"fftconv{nd}d_fp32_bhl_w_reshape")
     with pytest.raises(ValueError, match="Valid dimensions"):
         backend.select_fftconv_fns(2, True)
+    for nd in (1, 2, 3):
+        blh, bhl = backend.select_fftconv_fns(nd, False, "circular")
+        assert bhl is getattr(fftconv, f"circular_fftconv{nd}d_fp32_bhl")
+    blh, bhl = backend.select_fftconv_fns(2, False, ["circular", "zero"])
+    assert callable(blh) and callable(bhl)
 
 
 class _GlobalConv(torch.nn.Module):

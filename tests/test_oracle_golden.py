@@ -145,3 +145,41 @@ def test_oracle_cp_matches_reference(golden, world):
         d = C // world
         for r in range(world):
             assert torch.equal(s2f[r], full[:, r * d:(r + 1) * d])
+
+
+@pytest.mark.parametrize("idx", range(12))
+def test_oracle_boundary_ops_match_reference(golden, idx):
+    """Circular and mixed boundary conditions (ops/circular_fftconv.py, ops/mixed_fftconv.py)."""
+    cases = golden["boundary"]["cases"]
+    if idx >= len(cases):
+        pytest.skip("no such case")
+    c = cases[idx]
+    nd = c["x"].ndim - 2
+    per = c["periodic"] if c["periodic"] is not None else (True,) * nd
+    x = c["x"].clone().requires_grad_(True)
+    k = c["k"].clone().requires_grad_(True)
+    sc = c["shortcut"].clone().requires_grad_(True) if c["shortcut"] is not None else None
+    y = ofc.fftconv_bhl(x, k, sc, periodic=per)
+    y.backward(c["dy"])
+    tol = _tol(c["x"].dtype)
+    assert rel_l2(c["y"], y) <= tol, c["name"]
+    assert rel_l2(c["dx"], x.grad) <= tol, c["name"]
+    assert rel_l2(c["dk"], k.grad) <= tol, c["name"]
+    if sc is not None:
+        assert rel_l2(c["dshortcut"], sc.grad) <= tol, c["name"]
+
+
+def test_oracle_circular_matches_direct_periodic_convolution():
+    """Independent check of the circular restatement: float64 periodic spatial convolution
+    with the "same" alignment (output t takes taps x[(t + (K - 1) // 2 - j) mod N])."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(1, 2, 8, 12, generator=g, dtype=torch.float64)
+    k = torch.randn(1, 2, 4, 5, generator=g, dtype=torch.float64)
+    y = ofc.fftconv_bhl(x, k, periodic=(True, True))
+    ref = torch.zeros_like(x)
+    N0, N1, K0, K1 = 8, 12, 4, 5
+    s0, s1 = (K0 - 1) // 2, (K1 - 1) // 2
+    for a in range(K0):
+        for b in range(K1):
+            ref += k[:, :, a, b, None, None] * torch.roll(x, shifts=(a - s0, b - s1), dims=(2, 3))
+    assert rel_l2(ref, y) <= 1e-6
