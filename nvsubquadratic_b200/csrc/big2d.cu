@@ -301,6 +301,21 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
       v[m] = (m < 8 && act && r < N0) ? A[r * kB2H + j] : make_float2(0.f, 0.f);
     }
     fft256<true, false>(v, mysc, tw, l, -1.f);
+    if (p.zs_mode != 0 && act) {
+      float2* zc = p.Zs + (((long long)b * p.C + c) * kB2H + j) * kB2F + l;
+      if (p.zs_mode == 1) {
+#pragma unroll
+        for (int m = 0; m < 16; ++m) zc[16 * m] = v[m];
+      } else {
+        // G[c][j][i] += conj(Z[b][c][j][i]) * DY[j][i] (the per-image term of the filter gradient)
+        float2* gc = p.G + ((long long)c * kB2H + j) * kB2F + l;
+        float2 z[16];
+#pragma unroll
+        for (int m = 0; m < 16; ++m) z[m] = __ldcs(zc + 16 * m);
+#pragma unroll
+        for (int m = 0; m < 16; ++m) atomicAdd(gc + 16 * m, cmulc(v[m], z[m]));
+      }
+    }
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
       float2 k = kv[m];

@@ -28,6 +28,12 @@ struct Big2DParams {
   float2* G;          // [C][129][256] filter-gradient spectrum accumulator (zeroed by the host)
   int B, C, N0, N1, K0, K1;
   int conj;           // 1: multiply by conj(Kh) (the adjoint, dx = corr(dy, k))
+  // Column spectra of the conv input, [B][C][129][256]: with zs_mode 1 the conv kernel
+  // stores each column's forward transform there (the mixer's forward keeps z's); with
+  // zs_mode 2 the adjoint conv kernel adds conj(Zs) * (its own input's column spectrum)
+  // into G, the filter-gradient spectrum, so no separate dK kernel recomputes both.
+  float2* Zs;
+  int zs_mode;
 };
 
 enum Big2DOp { B2_KSPEC = 0, B2_CONV = 1, B2_DK = 2, B2_DFILT = 3 };

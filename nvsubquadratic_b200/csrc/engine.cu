@@ -989,27 +989,54 @@ static void big2d_params(const ConvPlan& p, const RealView& kv, const float* D, 
   b.K1 = p.g.K[1];
 }
 
+// [B][C][129][256] column spectra of a conv input (the mixer keeps z's for its backward).
+static size_t big2d_zs_bytes(const ConvPlan& p) {
+  return align_up((size_t)p.B * p.C * kB2H * kB2F * sizeof(float2));
+}
+
+// zs_out: if set, the conv stores its input's column spectra there (zs_mode 1).
 static int big2d_forward(const ConvPlan& p, const RealView& xv, const RealView& kv, const float* D, const RealView& yv,
-                         char* ws, cudaStream_t st) {
+                         char* ws, cudaStream_t st, float2* zs_out = nullptr) {
   Big2DParams b;
   big2d_params(p, kv, D, ws, b);
   b.x = b2view(xv);
   b.y = b2view(yv);
+  if (zs_out) {
+    b.Zs = zs_out;
+    b.zs_mode = 1;
+  }
   if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
   if (big2d_dispatch(B2_CONV, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d conv launch failed");
   return HYFFT_OK;
 }
 
+// zs_in: the forward input's column spectra (kept by big2d_forward); with them the
+// adjoint conv also accumulates the filter-gradient spectrum and the dK kernel is skipped.
 static int big2d_backward(const ConvPlan& p, const RealView& xv, const RealView& kv, const float* D,
-                          const RealView& dyv, const RealView& dxv, const RealView& dkv, char* ws, cudaStream_t st) {
+                          const RealView& dyv, const RealView& dxv, const RealView& dkv, char* ws, cudaStream_t st,
+                          float2* zs_in = nullptr) {
   Big2DParams b;
   big2d_params(p, kv, D, ws, b);
   if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
+  const bool fused_dk = zs_in && dxv.ptr && dkv.ptr;
+  if (fused_dk && cudaMemsetAsync(b.G, 0, big2d_spec_bytes(p), st) != cudaSuccess)
+    return fail(HYFFT_ERR_CUDA, "memset G");
   if (dxv.ptr) {  // dx = corr(dy, k) + D * dy
     b.x = b2view(dyv);
     b.y = b2view(dxv);
     b.conj = 1;
+    if (fused_dk) {
+      b.Zs = zs_in;
+      b.zs_mode = 2;
+    }
     if (big2d_dispatch(B2_CONV, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d adjoint launch failed");
+    b.Zs = nullptr;
+    b.zs_mode = 0;
+  }
+  if (fused_dk) {
+    b.dfilt = b2view(dkv);
+    if (big2d_dispatch(B2_DFILT, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d dfilt launch failed");
+    return HYFFT_OK;
   }
   if (dkv.ptr) {
     if (cudaMemsetAsync(b.G, 0, big2d_spec_bytes(p), st) != cudaSuccess) return fail(HYFFT_ERR_CUDA, "memset G");
@@ -1336,6 +1363,7 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
   const size_t act = align_up((size_t)h.E * h.eb);
   saved = 5 * act;                 // q', k', v', z, h
   if (h.cache_kh) saved += align_up((size_t)h.cp.spec_k_bytes_per_ch * h.cp.C);  // filter spectrum
+  if (h.cp.big2d) saved += big2d_zs_bytes(h.cp);  // z's column spectra (the backward's dK)
   fwd = cf + align_up((size_t)h.d.channels * 4);
   bwd = cb + 5 * act + align_up((size_t)h.d.channels * 4);  // dh, dz, dv', dq', dk'
   if (h.cp.big2d) {  // channel-major copies around the large-grid kernels: z, h | z, dh, dz
@@ -1437,6 +1465,13 @@ static bool elem_pairs_ok(const HyenaPlan& h, std::initializer_list<const void*>
   return true;
 }
 
+// dD[c] = dfilt[c][K0 / 2][K1 / 2]: for a centred filter the D-skip acts at the tap whose
+// gradient is sum_n dh[n] z[n], so the two gradients coincide.
+__global__ void centre_tap_kernel(const float* __restrict__ dfilt, float* __restrict__ dD, int C, int K0, int K1) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < C) dD[c] = dfilt[((long long)c * K0 + K0 / 2) * K1 + K1 / 2];
+}
+
 template <typename T>
 static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt, const float* D,
                            const float* sw, const float* sb, T* y, char* saved, char* ws, cudaStream_t st) {
@@ -1501,7 +1536,8 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
     T* hc = (T*)((char*)zc + align_up((size_t)h.E * h.eb));
     HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
     HY_TRY(big2d_forward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
-                         real_view(hc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), ws, st));
+                         real_view(hc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), ws, st,
+                         (float2*)(saved + 5 * act)));
     HY_TRY(cl_cm<T>(hc, hb, d.batch, h.Ntot, d.channels, false, st));
   } else {
     for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
@@ -1569,23 +1605,32 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     const RealView dhv = real_view(dh, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
     const RealView dzv = real_view(dz, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
     const RealView dkv = real_view(dfilt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
+    // large grid with a filter gradient: the adjoint conv accumulates it from z's column
+    // spectra kept by the forward, so z itself is not transformed again, and dD is the
+    // gradient's centre tap (the rolled filter's tap (0, 0) is where the D-skip acts)
+    const bool zs = p.big2d && dfilt != nullptr;
     if (p.big2d) {  // channel-major z, dh, dz around the large-grid kernels
       T* zc = (T*)(ws + cb + 5 * act + align_up((size_t)d.channels * 4));
       T* dhc = (T*)((char*)zc + act);
       T* dzc = (T*)((char*)dhc + act);
-      HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
+      if (!zs) HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
       HY_TRY(cl_cm<T>(dh, dhc, d.batch, h.Ntot, d.channels, true, st));
       HY_TRY(big2d_backward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
                             real_view(dhc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D),
-                            real_view(dzc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), dkv, ws, st));
+                            real_view(dzc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), dkv, ws, st,
+                            zs ? (float2*)const_cast<char*>(saved + 5 * act) : nullptr));
       HY_TRY(cl_cm<T>(dzc, dz, d.batch, h.Ntot, d.channels, false, st));
+      if (zs && dD) {
+        centre_tap_kernel<<<(d.channels + 255) / 256, 256, 0, st>>>(dfilt, dD, d.channels, p.g.K[0], p.g.K[1]);
+        HY_TRY(check_launch("centre_tap_kernel"));
+      }
     } else {
       for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
         const int cc = std::min(p.Cc, p.C - c0);
         HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, Kh, dKh, st, h.cache_kh));
       }
     }
-    if (dD) {
+    if (dD && !zs) {
       if (cudaMemsetAsync(dD, 0, sizeof(float) * (size_t)d.channels, st) != cudaSuccess)
         return fail(HYFFT_ERR_CUDA, "memset dD");
       const dim3 rg(eg.x, (unsigned)red_rows((int)eg.x), 1);
