@@ -995,8 +995,9 @@ static size_t big2d_zs_bytes(const ConvPlan& p) {
 }
 
 // zs_out: if set, the conv stores its input's column spectra there (zs_mode 1).
+// kh: if set, the filter spectrum goes there (the mixer keeps it for its backward).
 static int big2d_forward(const ConvPlan& p, const RealView& xv, const RealView& kv, const float* D, const RealView& yv,
-                         char* ws, cudaStream_t st, float2* zs_out = nullptr) {
+                         char* ws, cudaStream_t st, float2* zs_out = nullptr, float2* kh = nullptr) {
   Big2DParams b;
   big2d_params(p, kv, D, ws, b);
   b.x = b2view(xv);
@@ -1005,6 +1006,7 @@ static int big2d_forward(const ConvPlan& p, const RealView& xv, const RealView& 
     b.Zs = zs_out;
     b.zs_mode = 1;
   }
+  if (kh) b.Kh = kh;
   if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
   if (big2d_dispatch(B2_CONV, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d conv launch failed");
   return HYFFT_OK;
@@ -1012,12 +1014,15 @@ static int big2d_forward(const ConvPlan& p, const RealView& xv, const RealView& 
 
 // zs_in: the forward input's column spectra (kept by big2d_forward); with them the
 // adjoint conv also accumulates the filter-gradient spectrum and the dK kernel is skipped.
+// kh_in: the filter spectrum the forward kept (else it is recomputed).
 static int big2d_backward(const ConvPlan& p, const RealView& xv, const RealView& kv, const float* D,
                           const RealView& dyv, const RealView& dxv, const RealView& dkv, char* ws, cudaStream_t st,
-                          float2* zs_in = nullptr) {
+                          float2* zs_in = nullptr, float2* kh_in = nullptr) {
   Big2DParams b;
   big2d_params(p, kv, D, ws, b);
-  if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
+  if (kh_in) b.Kh = kh_in;
+  else if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK)
+    return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
   const bool fused_dk = zs_in && dxv.ptr && dkv.ptr;
   if (fused_dk && cudaMemsetAsync(b.G, 0, big2d_spec_bytes(p), st) != cudaSuccess)
     return fail(HYFFT_ERR_CUDA, "memset G");
@@ -1363,7 +1368,7 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
   const size_t act = align_up((size_t)h.E * h.eb);
   saved = 5 * act;                 // q', k', v', z, h
   if (h.cache_kh) saved += align_up((size_t)h.cp.spec_k_bytes_per_ch * h.cp.C);  // filter spectrum
-  if (h.cp.big2d) saved += big2d_zs_bytes(h.cp);  // z's column spectra (the backward's dK)
+  if (h.cp.big2d) saved += big2d_zs_bytes(h.cp) + big2d_spec_bytes(h.cp);  // z's column spectra, filter spectrum
   fwd = cf + align_up((size_t)h.d.channels * 4);
   bwd = cb + 5 * act + align_up((size_t)h.d.channels * 4);  // dh, dz, dv', dq', dk'
   if (h.cp.big2d) {  // channel-major copies around the large-grid kernels: z, h | z, dh, dz
@@ -1531,13 +1536,16 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
   const RealView zv = real_view(z, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
   const RealView kv = real_view(filt, HYFFT_LAYOUT_BHL, 1, p.C, p.g.K, p.g.D);
   const RealView hv = real_view(hb, HYFFT_LAYOUT_BLH, p.B, p.C, p.g.N, p.g.D);
-  if (p.big2d) {  // channel-major z and h around the large-grid kernels (unit-stride rows)
+  if (p.big2d) {
+    float2* zs = (float2*)(saved + 5 * act);
+    float2* khs = (float2*)(saved + 5 * act + big2d_zs_bytes(p));
+    // channel-major z and h around the large-grid kernels (unit-stride rows; reading the
+    // channels-last tensors in place with 2-byte strided accesses measured 1.5x slower)
     T* zc = (T*)(ws + cf + align_up((size_t)d.channels * 4));
     T* hc = (T*)((char*)zc + align_up((size_t)h.E * h.eb));
     HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
     HY_TRY(big2d_forward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
-                         real_view(hc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), ws, st,
-                         (float2*)(saved + 5 * act)));
+                         real_view(hc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), ws, st, zs, khs));
     HY_TRY(cl_cm<T>(hc, hb, d.batch, h.Ntot, d.channels, false, st));
   } else {
     for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
@@ -1609,7 +1617,10 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     // spectra kept by the forward, so z itself is not transformed again, and dD is the
     // gradient's centre tap (the rolled filter's tap (0, 0) is where the D-skip acts)
     const bool zs = p.big2d && dfilt != nullptr;
-    if (p.big2d) {  // channel-major z, dh, dz around the large-grid kernels
+    if (p.big2d) {
+      float2* zsp = zs ? (float2*)const_cast<char*>(saved + 5 * act) : nullptr;
+      float2* khs = (float2*)const_cast<char*>(saved + 5 * act + big2d_zs_bytes(p));
+      // channel-major z, dh, dz around the large-grid kernels
       T* zc = (T*)(ws + cb + 5 * act + align_up((size_t)d.channels * 4));
       T* dhc = (T*)((char*)zc + act);
       T* dzc = (T*)((char*)dhc + act);
@@ -1617,8 +1628,7 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
       HY_TRY(cl_cm<T>(dh, dhc, d.batch, h.Ntot, d.channels, true, st));
       HY_TRY(big2d_backward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
                             real_view(dhc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D),
-                            real_view(dzc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), dkv, ws, st,
-                            zs ? (float2*)const_cast<char*>(saved + 5 * act) : nullptr));
+                            real_view(dzc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), dkv, ws, st, zsp, khs));
       HY_TRY(cl_cm<T>(dzc, dz, d.batch, h.Ntot, d.channels, false, st));
       if (zs && dD) {
         centre_tap_kernel<<<(d.channels + 255) / 256, 256, 0, st>>>(dfilt, dD, d.channels, p.g.K[0], p.g.K[1]);
