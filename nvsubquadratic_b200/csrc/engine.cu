@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "fft_pass.cuh"
+#include "fft_long.h"
 #include "big2d.h"
 #include "hyena_elem.cuh"
 #include "stencil3d.cuh"
@@ -130,8 +131,10 @@ static int make_geo(int nd, const int* n, const int* k, int causal, int periodic
   g.four = (nd == 1 && g.F[0] > kPassPoints);
   if (g.four) {
     const int lf = ilog2(g.F[0]);
-    g.Fa = 1 << ((lf + 1) / 2);
-    g.Fb = g.F[0] / g.Fa;
+    // the second axis takes the larger factor: the first axis carries the real activation
+    // side, whose channel runs (lines per CTA of the long passes) are then the longer ones
+    g.Fb = 1 << ((lf + 1) / 2);
+    g.Fa = g.F[0] / g.Fb;
   }
   return HYFFT_OK;
 }
@@ -297,7 +300,13 @@ static int launch_cl_bwd(const PassDesc& fx, const PassDesc& fdy, const PassDesc
   }
 }
 
+// Long-line channel-innermost passes (fft_long.cu) take the four-step passes and every pass
+// longer than the two-level kernel's 256 points.
 static int launch_pass(const PassDesc& d, int im, int om, int tin, int tout, cudaStream_t st) {
+  if ((d.tw_logF != 0 || d.F > 256) && long_pass_applies(d, im, om, tin, tout)) {
+    const int rc = launch_long_pass(d, im, om, tin, tout, st);
+    if (rc != HYFFT_ERR_UNSUPPORTED) return rc == HYFFT_OK ? rc : fail(rc, "fft_long_cl_kernel launch failed");
+  }
   if (cl_pass_applies(d, im, om, tin, tout)) return launch_cl(d, im, om, tin, tout, st);
   if (im == IN_REAL && om == OUT_CPLX) return launch_pass_dt<IN_REAL, OUT_CPLX>(d, tin, tout, st);
   if (im == IN_REAL && om == OUT_REAL) return launch_pass_dt<IN_REAL, OUT_REAL>(d, tin, tout, st);
@@ -811,13 +820,38 @@ static int apply_ramp(const ConvPlan& p, float2* S, int Cc, bool half, float sig
   return check_launch("spec_ramp_kernel");
 }
 
+template <typename T>
+static int cl_cm(const T* src, T* dst, int B, long long N, int C, bool to_cm, cudaStream_t st);
+
+// The long 1D (four-step) passes read and write channels-last real tensors with coalesced
+// runs of channels. A channel-major filter chunk [kB][C][K] (float32) is therefore
+// transposed to [kB][K][Cc] in a free spectrum buffer before its transform, and its
+// gradient is written channels-last there and transposed back after the inverse.
+static bool four_step_cl_filter(const ConvPlan& p, const RealView& kv) {
+  return p.g.four && kv.cst != 1 && !getenv("HYFFT_DISABLE_LONG_PASS") && p.g.Fa >= 128 && p.g.Fa <= 4096;
+}
+static int filter_to_cl(const ConvPlan& p, const RealView& kc, int Cc, float* T, RealView& out, cudaStream_t st) {
+  const long long K = p.g.K[0];
+  for (int b = 0; b < p.kB; ++b)
+    HY_TRY(cl_cm<float>((const float*)kc.ptr + b * kc.bst, T + (size_t)b * K * Cc, 1, K, Cc, false, st));
+  out = real_view(T, HYFFT_LAYOUT_BLH, p.kB, Cc, p.g.K, 1);
+  return HYFFT_OK;
+}
+static int filter_from_cl(const ConvPlan& p, const float* T, int Cc, const RealView& dkc, cudaStream_t st) {
+  const long long K = p.g.K[0];
+  for (int b = 0; b < p.kB; ++b)
+    HY_TRY(cl_cm<float>(T + (size_t)b * K * Cc, (float*)const_cast<void*>(dkc.ptr) + b * dkc.bst, 1, K, Cc, true, st));
+  return HYFFT_OK;
+}
+
 static int conv_forward_chunk(const ConvPlan& p, int c0, int Cc, const RealView& xv, const RealView& kv,
                               const float* Dfull, const RealView& yv, float2* S, float2* Kh, cudaStream_t st) {
   const int eb = dtype_bytes(p.dt);
   const RealView xc = offset_channels(xv, c0, eb);
-  const RealView kc = offset_channels(kv, c0, 4);
+  RealView kc = offset_channels(kv, c0, 4);
   const RealView yc = offset_channels(yv, c0, eb);
   const int zero[3] = {0, 0, 0};
+  if (four_step_cl_filter(p, kv)) HY_TRY(filter_to_cl(p, kc, Cc, (float*)S, kc, st));  // S is free until z's pass
   HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st, nullptr, p.khalf));
   HY_TRY(apply_ramp(p, Kh, Cc, p.khalf, 1.f, st));
   Epilogue ep;
@@ -891,16 +925,64 @@ static int fused_bwd_chain(const ConvPlan& p, int Cc, const RealView& xc, const 
   return HYFFT_OK;
 }
 
+// Backward of a long 1D (four-step) convolution with the second-axis forward passes of x and
+// dy, the spectral products and the second-axis inverse passes of dx and dK merged into one
+// backward product pass (fft_long_bwd_kernel). fcl: the filter gradient is written
+// channels-last into S1 (free once the merged pass has read it) and transposed into dkc.
+// Returns HYFFT_ERR_UNSUPPORTED (nothing launched) when the lengths have no such pass.
+static int long_bwd_chain(const ConvPlan& p, int Cc, const RealView& xc, const RealView& dyc, const RealView& dxc,
+                          const RealView& dkc, const Epilogue& ep, float2* S1, float2* S2, const float2* Kh,
+                          float2* dKh, bool fcl, cudaStream_t st) {
+  const int zero[3] = {0, 0, 0};
+  if (!p.g.four || p.g.periodic || p.g.Fb < 128 || p.g.Fb > 2048 || getenv("HYFFT_DISABLE_LONG_PASS") ||
+      getenv("HYFFT_DISABLE_BWD_PASS"))
+    return HYFFT_ERR_UNSUPPORTED;
+  PassList fx, fy, ix, ik;
+  HY_TRY(fwd_chain(p.g, Cc, xc, p.dt, p.px, p.g.N, zero, S1, st, &fx));
+  HY_TRY(fwd_chain(p.g, Cc, dyc, p.dt, p.px, p.g.N, p.g.crop, S2, st, &fy));
+  HY_TRY(inv_chain(p.g, Cc, S2, dxc, p.dt, p.px, zero, p.g.N, ep, st, &ix));
+  Epilogue none;
+  const RealView dk_dst = fcl ? real_view(S1, HYFFT_LAYOUT_BLH, p.kB, Cc, p.g.K, 1) : dkc;
+  HY_TRY(inv_chain(p.g, Cc, dKh, dk_dst, HYFFT_F32, p.pk, zero, p.g.K, none, st, &ik));
+  if (fx.n != 2 || fy.n != 2 || ix.n != 2 || ik.n != 2) return HYFFT_ERR_UNSUPPORTED;
+  const PassDesc& b = fx.r[1].d;  // x's second-axis pass: lines (pair, k_a, c) along n_b
+  LongBwdDesc d;
+  d.sx = S1;
+  d.sdy = S2;
+  d.kh = Kh;
+  d.dkh = dKh;
+  d.pst = b.ci_pst;
+  d.tst = b.ci_tst;
+  d.ost = b.ci_ost[0];
+  d.k_pst = p.shared ? 0 : b.ci_pst;
+  d.pl = p.shared ? p.px.P : 1;
+  d.nlines = (long long)(p.px.P / d.pl) * p.g.Fa * Cc;
+  d.C = Cc;
+  d.Fa = p.g.Fa;
+  d.tw_logF = ix.r[0].d.tw_logF;
+  d.scale = ix.r[0].d.scale;
+  HY_TRY(launch_pass(fx.r[0].d, fx.r[0].im, fx.r[0].om, fx.r[0].tin, fx.r[0].tout, st));
+  HY_TRY(launch_pass(fy.r[0].d, fy.r[0].im, fy.r[0].om, fy.r[0].tin, fy.r[0].tout, st));
+  const int rc = launch_long_bwd(d, p.g.Fb, st);
+  if (rc != HYFFT_OK) return fail(rc == HYFFT_ERR_UNSUPPORTED ? HYFFT_ERR_CUDA : rc, "fft_long_bwd_kernel launch failed");
+  HY_TRY(launch_pass(ix.r[1].d, ix.r[1].im, ix.r[1].om, ix.r[1].tin, ix.r[1].tout, st));
+  HY_TRY(launch_pass(ik.r[1].d, ik.r[1].im, ik.r[1].om, ik.r[1].tin, ik.r[1].tout, st));
+  if (fcl) HY_TRY(filter_from_cl(p, (const float*)S1, Cc, dkc, st));
+  return HYFFT_OK;
+}
+
 static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView& xv, const RealView& kv,
                                const float* Dfull, const RealView& dyv, const RealView& dxv, const RealView& dkv,
                                float2* S1, float2* S2, float2* Kh, float2* dKh, cudaStream_t st,
                                bool kh_ready = false) {
   const int eb = dtype_bytes(p.dt);
   const RealView xc = offset_channels(xv, c0, eb);
-  const RealView kc = offset_channels(kv, c0, 4);
+  RealView kc = offset_channels(kv, c0, 4);
   const RealView dyc = offset_channels(dyv, c0, eb);
   const int zero[3] = {0, 0, 0};
+  const bool fcl = four_step_cl_filter(p, kv);
   if (!kh_ready) {
+    if (fcl) HY_TRY(filter_to_cl(p, kc, Cc, (float*)S1, kc, st));  // S1 is free until x's pass
     HY_TRY(fwd_chain(p.g, Cc, kc, HYFFT_F32, p.pk, p.g.K, zero, Kh, st, nullptr, p.khalf));
     HY_TRY(apply_ramp(p, Kh, Cc, p.khalf, 1.f, st));
   }
@@ -913,8 +995,10 @@ static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView
       ep.skip = dyc.ptr;
       ep.Dv = Dfull + c0;
     }
-    const int rc = fused_bwd_chain(p, Cc, xc, dyc, offset_channels(dxv, c0, eb), offset_channels(dkv, c0, 4), ep, S1,
-                                   S2, Kh, dKh, st);
+    const int rc = p.g.four ? long_bwd_chain(p, Cc, xc, dyc, offset_channels(dxv, c0, eb), offset_channels(dkv, c0, 4),
+                                             ep, S1, S2, Kh, dKh, fcl, st)
+                            : fused_bwd_chain(p, Cc, xc, dyc, offset_channels(dxv, c0, eb),
+                                              offset_channels(dkv, c0, 4), ep, S1, S2, Kh, dKh, st);
     if (rc != HYFFT_ERR_UNSUPPORTED) return rc;
   }
   // the elementwise backward below reads the full filter spectrum
@@ -941,6 +1025,11 @@ static int conv_backward_chunk(const ConvPlan& p, int c0, int Cc, const RealView
   if (dkv.ptr) {
     const RealView dkc = offset_channels(dkv, c0, 4);
     Epilogue ep;
+    if (fcl) {  // channels-last into S1 (free since the spectral products), then transposed
+      HY_TRY(inv_chain(p.g, Cc, dKh, real_view(S1, HYFFT_LAYOUT_BLH, p.kB, Cc, p.g.K, 1), HYFFT_F32, p.pk, zero,
+                       p.g.K, ep, st));
+      return filter_from_cl(p, (const float*)S1, Cc, dkc, st);
+    }
     HY_TRY(inv_chain(p.g, Cc, dKh, dkc, HYFFT_F32, p.pk, zero, p.g.K, ep, st));
   }
   return HYFFT_OK;
@@ -1378,8 +1467,15 @@ static void hyena_sizes(const HyenaPlan& h, size_t& fwd, size_t& bwd, size_t& sa
 }
 
 // channels-last [B][N][C] <-> channel-major [B][C][N] (contiguous)
+int cl_cm_tma(const void* src, void* dst, int B, long long N, int C, bool to_cm, int* status, cudaStream_t st);
+
 template <typename T>
 static int cl_cm(const T* src, T* dst, int B, long long N, int C, bool to_cm, cudaStream_t st) {
+  if (sizeof(T) == 2) {  // 64 x 64 tiles moved by TMA (transpose_tma.cu) where the shape allows
+    const int rc = cl_cm_tma(src, dst, B, N, C, to_cm, nullptr, st);
+    if (rc == HYFFT_OK) return HYFFT_OK;
+    if (rc != HYFFT_ERR_UNSUPPORTED) return fail(rc, "cl_cm_tma_kernel launch failed");
+  }
   const dim3 grid((unsigned)((N + 31) / 32), (unsigned)((C + 31) / 32), (unsigned)B);
   if (to_cm) cl_cm_transpose_kernel<T, true><<<grid, 256, 0, st>>>(src, dst, N, C);
   else cl_cm_transpose_kernel<T, false><<<grid, 256, 0, st>>>(src, dst, N, C);

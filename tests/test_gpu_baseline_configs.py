@@ -163,3 +163,26 @@ def test_channel_chunked_mixer_vs_oracle(B, C, S, K, sk, causal, monkeypatch):
     recomputes each chunk's filter spectrum instead of reading the saved one)."""
     monkeypatch.setenv("HYFFT_WS_BUDGET_MB", "64")
     _check_mixer(B, C, S, K, sk, torch.bfloat16, causal=causal, g1="silu", g2="sigmoid")
+
+
+def test_cfg2_grid_tma_transposes_vs_oracle_and_fallback(monkeypatch):
+    """cfg2's grid at 64 channels, where the channels-last <-> channel-major transposes
+    around the large-grid kernels run on TMA (64 x 64 tiles): against the oracle, and
+    against the shared-memory transpose kernel (pure data movement: y and the activation
+    gradients agree bit for bit; the filter gradient is summed by atomics)."""
+    from nvsubquadratic_b200.hyena import hyena_fused
+
+    _check_mixer(2, 64, (128, 128), (128, 128), 3, torch.bfloat16)
+    qkv, filt, D, sw, dy = _mixer_inputs(2, 64, (128, 128), (128, 128), 3, torch.bfloat16, False)
+    outs = []
+    for env in (None, "1"):
+        if env:
+            monkeypatch.setenv("HYFFT_DISABLE_TMA", env)
+        x = qkv.cuda().requires_grad_(True)
+        pd = [t.cuda().requires_grad_(True) for t in (filt, D, sw)]
+        y = hyena_fused(*x.chunk(3, dim=-1), *pd, None)
+        y.backward(dy.cuda())
+        torch.cuda.synchronize()
+        outs.append((y.detach(), x.grad, pd[0].grad))
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert rel_l2(outs[1][2], outs[0][2]) <= 1e-6
