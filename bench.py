@@ -661,7 +661,8 @@ def main():
     if cfg["shard"] == "cp":
         config["l2"] = "inputs (GBs per rank) far larger than L2; no flush"
         config["parallelism"] = f"cp{world}"
-        # keep the engine's spectrum workspace small next to the 1M-long activations
+        # keep the engine's spectrum workspace (and the filter-spectrum cache, kept only where
+        # it fits this budget: P >= 4) small next to the 1M-long activations
         os.environ.setdefault("HYFFT_WS_BUDGET_MB", "4096")
         # GB-sized activations of varying shapes: avoid caching-allocator fragmentation
         os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")

@@ -1343,8 +1343,9 @@ struct HyenaPlan {
   bool tp = false;      // tensor-core Toeplitz kernels (toeplitz.cu) apply (takes precedence)
   int SK = 0;
   int fF[2] = {0, 0};   // FFT sizes of the fused kernels (2^m or 3 * 2^m per axis)
-  bool cache_kh = false;  // general engine, one channel chunk: the forward keeps the filter
-                          // spectrum in the saved state and the backward reuses it
+  bool cache_kh = false;  // general engine: the forward keeps the filter spectrum of every channel
+                          // chunk in the saved state (chunk c0's block at c0 * spec_k_bytes_per_ch)
+                          // and the backward reuses it
 };
 
 // Smallest FFT length of the fused kernels (2^m or 3 * 2^m, at most 64) for an axis of
@@ -1434,7 +1435,9 @@ static int make_hyena_plan(const hyfft_hyena_desc* d, HyenaPlan& h) {
            K1 <= 2 * N1 && tp2d_dispatch(TP_PROBE, N0, N1, h.SK, nullptr, nullptr) == HYFFT_OK;
     if (h.tp) h.fused = false;
   }
-  h.cache_kh = !h.fused && !h.tp && !h.cp.big2d && h.cp.Cc == h.cp.C && !getenv("HYFFT_NO_KH_CACHE");
+  // (kept when it fits the workspace budget: the backward then skips one filter transform per chunk)
+  h.cache_kh = !h.fused && !h.tp && !h.cp.big2d && !getenv("HYFFT_NO_KH_CACHE") &&
+               (size_t)h.cp.spec_k_bytes_per_ch * h.cp.C <= ws_budget();
   return HYFFT_OK;
 }
 
@@ -1646,7 +1649,8 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
   } else {
     for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
       const int cc = std::min(p.Cc, p.C - c0);
-      HY_TRY(conv_forward_chunk(p, c0, cc, zv, kv, D, hv, S, Kh, st));
+      float2* khc = h.cache_kh ? Kh + (size_t)c0 * (p.spec_k_bytes_per_ch / sizeof(float2)) : Kh;
+      HY_TRY(conv_forward_chunk(p, c0, cc, zv, kv, D, hv, S, khc, st));
     }
   }
   if (pair)
@@ -1733,7 +1737,8 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     } else {
       for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
         const int cc = std::min(p.Cc, p.C - c0);
-        HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, Kh, dKh, st, h.cache_kh));
+        float2* khc = h.cache_kh ? Kh + (size_t)c0 * (p.spec_k_bytes_per_ch / sizeof(float2)) : Kh;
+        HY_TRY(conv_backward_chunk(p, c0, cc, zv, kv, D, dhv, dzv, dkv, S1, S2, khc, dKh, st, h.cache_kh));
       }
     }
     if (dD && !zs) {

@@ -81,8 +81,8 @@ __host__ __device__ constexpr int long_twn() { return R1 * R2 * R3 + R2 * R3; }
 template <int R1, int R2, int R3, int NSETS = 1>
 __host__ __device__ constexpr size_t long_smem_bytes() {
   constexpr int F = R1 * R2 * R3, NL = NSETS == 1 ? long_lines<F>() : long_bwd_lines<F>();
-  return sizeof(float2) * ((size_t)NSETS * (F + F / R3) * NL + long_twn<R1, R2, R3>()) + 5 * sizeof(long long) * NL +
-         3 * sizeof(int) * NL;
+  return sizeof(float2) * ((size_t)NSETS * (F + F / R3) * NL + long_twn<R1, R2, R3>() + F) +
+         5 * sizeof(long long) * NL + 3 * sizeof(int) * NL;
 }
 
 template <int R1, int R2, int R3>
@@ -127,6 +127,28 @@ __device__ __forceinline__ TwRun tw_run(int m, int t0, int S, int tw_logF, float
   return r;
 }
 
+// Store-side twiddle table of a CTA whose lines share one four-step multiplier m (the channel
+// count is a multiple of the lines per CTA): T4[e] = scale e^{dir 2 pi i m t(e) / 2^tw_logF}
+// for the F output points, in the order the storing level walks them, so that an item's
+// points sit at compile-time offsets and neighbouring lanes read neighbouring entries:
+//   level-3 store (k1, k2; k3):  e = (k1 R3 + k3) R2 + k2,  t = k1 + R1 k2 + R1 R2 k3
+//   adjoint level-1 store (j; r): e = r M + j,              t = j + M r
+template <int R1, int R2, int R3, bool L1ORDER>
+__device__ __forceinline__ void long_fill_store_twiddles(float2* t4, int m, int tw_logF, float scale, float dir) {
+  constexpr int F = R1 * R2 * R3, M = R2 * R3;
+  const unsigned mask = (1u << tw_logF) - 1u;
+  for (int e = threadIdx.x; e < F; e += kLongThreads) {
+    int t;
+    if constexpr (L1ORDER) {
+      t = e % M + M * (e / M);
+    } else {
+      const int k2 = e % R2, k3 = (e / R2) % R3, k1 = e / (R2 * R3);
+      t = k1 + R1 * k2 + R1 * R2 * k3;
+    }
+    t4[e] = cscale(four_step_twiddle(((unsigned)m * (unsigned)t) & mask, tw_logF, dir), scale);
+  }
+}
+
 // Per-line bookkeeping of a CTA's lines in shared memory.
 struct LongLines {
   long long *cb_in, *cb_out, *im_in, *im_out, *kbase;
@@ -149,25 +171,46 @@ __device__ __forceinline__ LongLines long_lines_at(void* p) {
 // The R points of a run t0 + S q of line l, forward-ordered, scaled, twiddled and stored
 // with the output window, dtype rounding and D-skip of the pass (fft_pass_kernel semantics).
 // full: every point of the run lies inside the output window (complex output).
-template <int R, int OM, typename TO>
+// D * skip of the real item of a run (rounded to the activation dtype), loaded ahead
+template <int R, typename TO>
+__device__ __forceinline__ void long_skip_run(const PassDesc& d, const LongLines& L, int l, int t0, int S,
+                                              float (&sre)[R]) {
+  const int pb = t0 * d.pos_mul + L.pos0[l] - d.out_lo, ps = S * d.pos_mul;
+  const long long step = (long long)ps * d.ro_tst;
+  const TO* sk = reinterpret_cast<const TO*>(d.skip) + L.cb_out[l] + (long long)pb * d.ro_tst;
+  const float Dc = reinterpret_cast<const float*>(d.Dv)[L.chan[l]];
+#pragma unroll
+  for (int q = 0; q < R; ++q) {
+    const int pos = pb + ps * q;
+    sre[q] = (pos >= 0 && pos < d.n_out) ? DT<TO>::round(Dc * DT<TO>::load(sk + q * step)) : 0.f;
+  }
+}
+
+// pre: D * skip of the real item from long_skip_run (OUT_REAL_SKIP)
+// tt: this run's entries of the store twiddle table (stride TS), or null (factors from tw_run)
+template <int R, int TS, int OM, typename TO>
 __device__ __forceinline__ void long_store_run(const PassDesc& d, const LongLines& L, int l, int t0, int S, float sd,
-                                               bool full, float2 (&v)[R]) {
-  TwRun tr = tw_run(L.twm[l], t0, S, d.tw_logF, d.scale, sd);
+                                               bool full, float2 (&v)[R], const float (&pre)[R], const float2* tt) {
+  TwRun tr;
+  if (!tt) tr = tw_run(L.twm[l], t0, S, d.tw_logF, d.scale, sd);
+  auto wq = [&](int q) {
+    if (tt) return tt[q * TS];
+    const float2 w = tr.w;
+    tr.w = cmul(tr.w, tr.s);
+    return w;
+  };
   if constexpr (OM == OUT_CPLX) {
     float2* dst = d.cout + L.cb_out[l] + (long long)(t0 - d.out_lo) * d.co_tst;
     const long long step = (long long)S * d.co_tst;
     if (full) {
 #pragma unroll
-      for (int q = 0; q < R; ++q) {
-        dst[q * step] = cmul(v[q], tr.w);
-        tr.w = cmul(tr.w, tr.s);
-      }
+      for (int q = 0; q < R; ++q) dst[q * step] = cmul(v[q], wq(q));
     } else {
 #pragma unroll
       for (int q = 0; q < R; ++q) {
         const int bo = t0 + S * q - d.out_lo;
-        if (bo >= 0 && bo < d.n_out) dst[q * step] = cmul(v[q], tr.w);
-        tr.w = cmul(tr.w, tr.s);
+        const float2 w = wq(q);
+        if (bo >= 0 && bo < d.n_out) dst[q * step] = cmul(v[q], w);
       }
     }
   } else {
@@ -176,28 +219,24 @@ __device__ __forceinline__ void long_store_run(const PassDesc& d, const LongLine
     TO* dst = reinterpret_cast<TO*>(d.rout) + L.cb_out[l] + off0;
     const long long ri = L.im_out[l];
     TO* dsti = reinterpret_cast<TO*>(d.rout) + ri + off0;
-    float sre[R], sim[R];  // D * skip, loaded ahead of the stores (which may alias the skip tensor)
+    float sim[R];  // D * skip of the imaginary item, loaded ahead of the stores (which may alias it)
     if constexpr (OM == OUT_REAL_SKIP) {
-      const TO* sk = reinterpret_cast<const TO*>(d.skip) + L.cb_out[l] + off0;
       const TO* ski = reinterpret_cast<const TO*>(d.skip) + ri + off0;
       const float Dc = reinterpret_cast<const float*>(d.Dv)[L.chan[l]];
 #pragma unroll
       for (int q = 0; q < R; ++q) {
         const int pos = pb + ps * q;
-        const bool ok = pos >= 0 && pos < d.n_out;
-        sre[q] = ok ? DT<TO>::round(Dc * DT<TO>::load(sk + q * step)) : 0.f;
-        sim[q] = (ok && ri >= 0) ? DT<TO>::round(Dc * DT<TO>::load(ski + q * step)) : 0.f;
+        sim[q] = (ri >= 0 && pos >= 0 && pos < d.n_out) ? DT<TO>::round(Dc * DT<TO>::load(ski + q * step)) : 0.f;
       }
     }
 #pragma unroll
     for (int q = 0; q < R; ++q) {
       const int pos = pb + ps * q;
-      const float2 val = cmul(v[q], tr.w);
-      tr.w = cmul(tr.w, tr.s);
+      const float2 val = cmul(v[q], wq(q));
       if (pos < 0 || pos >= d.n_out) continue;
       float re = DT<TO>::round(val.x), im = DT<TO>::round(val.y);
       if constexpr (OM == OUT_REAL_SKIP) {
-        re = re + sre[q];
+        re = re + pre[q];
         im = im + sim[q];
       }
       DT<TO>::store(dst + q * step, re);
@@ -211,8 +250,8 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
   constexpr int F = R1 * R2 * R3, M = R2 * R3, S3 = R1 * R2;
   constexpr int NL = long_lines<F>();
   constexpr int T = kLongThreads;
-  constexpr int IT1 = NL * M / T, IT2 = NL * R1 * R3 / T, IT3 = NL * R1 * R2 / T;
-  static_assert(IT1 * T == NL * M && IT2 * T == NL * R1 * R3 && IT3 * T == NL * R1 * R2, "items fill the threads");
+  constexpr int N1 = NL * M, N2 = NL * R1 * R3, N3 = NL * R1 * R2;  // items per level
+  constexpr int IT1 = (N1 + T - 1) / T, IT2 = (N2 + T - 1) / T, IT3 = (N3 + T - 1) / T;
   using X = LongIdx<R1, R2, R3, NL>;
   constexpr float D1 = MID ? -1.f : (float)DIR;  // direction of the forward levels
   constexpr float SD = MID ? 1.f : (float)DIR;   // direction of the store-side twiddle
@@ -221,7 +260,8 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
   float2* tw = sm + (size_t)(F + F / R3) * NL;       // T1 then T2
   const float2* T1 = tw;
   const float2* T2 = tw + F;
-  const LongLines L = long_lines_at<NL>(tw + long_twn<R1, R2, R3>());
+  float2* T4 = tw + long_twn<R1, R2, R3>();  // [F] store twiddles (uniform multiplier)
+  const LongLines L = long_lines_at<NL>(T4 + F);
   const long long line0 = (long long)blockIdx.x * NL;
   long_fill_twiddles<R1, R2, R3>(tw);
   for (int l = threadIdx.x; l < NL; l += T) {
@@ -258,6 +298,8 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
   }
   __syncthreads();
   const bool full_out = OM == OUT_CPLX && d.out_lo == 0 && d.n_out >= F;
+  // the CTA's lines share one four-step multiplier when the channel count is a multiple of NL
+  const float2* t4 = (d.tw_logF > 0 && d.C % NL == 0) ? T4 : nullptr;
 
   // level 1: R1-point transforms over r of x[j + M r], twiddle W_F^(j k1) -> A[k1 M + j];
   // the loads of all of a thread's items are issued before the first transform
@@ -266,6 +308,7 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
 #pragma unroll
     for (int u = 0; u < IT1; ++u) {
       const int it = threadIdx.x + u * T, l = it % NL, j = it / NL;
+      if (N1 % T != 0 && it >= N1) continue;
       const long long base = L.cb_in[l];
       if constexpr (IM == IN_CPLX) {
         const int b0 = j - d.in_off;
@@ -287,18 +330,28 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
         const long long off0 = (long long)p0 * d.ri_tst, step = (long long)ps * d.ri_tst;
         const TI* s0 = reinterpret_cast<const TI*>(d.rin) + base + off0;
         const TI* s1 = reinterpret_cast<const TI*>(d.rin) + ri + off0;
+        if (ri < 0) {  // no second item packed into the imaginary part
 #pragma unroll
-        for (int r = 0; r < R1; ++r) {
-          const int pos = p0 + ps * r;
-          const bool ok = base >= 0 && pos >= 0 && pos < d.n_in;
-          v[u][r] = make_float2(ok ? DT<TI>::load(s0 + r * step) : 0.f,
-                                (ok && ri >= 0) ? DT<TI>::load(s1 + r * step) : 0.f);
+          for (int r = 0; r < R1; ++r) {
+            const int pos = p0 + ps * r;
+            v[u][r] = make_float2((base >= 0 && pos >= 0 && pos < d.n_in) ? DT<TI>::load(s0 + r * step) : 0.f, 0.f);
+          }
+        } else {
+#pragma unroll
+          for (int r = 0; r < R1; ++r) {
+            const int pos = p0 + ps * r;
+            const bool ok = pos >= 0 && pos < d.n_in;
+            v[u][r] = make_float2(ok ? DT<TI>::load(s0 + r * step) : 0.f, ok ? DT<TI>::load(s1 + r * step) : 0.f);
+          }
         }
       }
     }
+    // (while the loads are in flight) the store twiddle table, read after two barriers
+    if (t4) long_fill_store_twiddles<R1, R2, R3, MID != 0>(T4, L.twm[0], d.tw_logF, d.scale, SD);
 #pragma unroll
     for (int u = 0; u < IT1; ++u) {
       const int it = threadIdx.x + u * T, l = it % NL, j = it / NL;
+      if (N1 % T != 0 && it >= N1) continue;
       dftR<R1>(v[u], D1);
       float2* o = sm + X::b1(l, j);
       const float2* t1 = T1 + j;
@@ -315,6 +368,7 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
 #pragma unroll
     for (int u = 0; u < IT3; ++u) {
       const int it = threadIdx.x + u * T, l = it % NL, k2 = (it / NL) % R2, k1 = it / (NL * R2);
+      if (N3 % T != 0 && it >= N3) continue;
       const bool ok = L.cb_in[l] >= 0;
       const float2* kp = d.kin + (ok ? L.kbase[l] : 0) + (long long)(k1 + R1 * k2) * d.k_tst;
       const long long ks = (long long)S3 * d.k_tst;
@@ -323,11 +377,24 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
     }
   }
 
+  // D * skip of every level-3 item's points (inverse passes with the skip epilogue), likewise
+  constexpr bool PRE = !MID && OM == OUT_REAL_SKIP;
+  float pre[PRE ? IT3 : 1][PRE ? R3 : 1];
+  if constexpr (PRE) {
+#pragma unroll
+    for (int u = 0; u < IT3; ++u) {
+      const int it = threadIdx.x + u * T, l = it % NL, k2 = (it / NL) % R2, k1 = it / (NL * R2);
+      if (N3 % T != 0 && it >= N3) continue;
+      if (L.cb_in[l] >= 0) long_skip_run<R3, TO>(d, L, l, k1 + R1 * k2, S3, pre[u]);
+    }
+  }
+
   // level 2 (in place per item): R2-point transforms over s of A[k1 M + i + R3 s], twiddle
   // W_M^(i k2) -> B[k1 M + k2 R3 + i]
 #pragma unroll
   for (int u = 0; u < IT2; ++u) {
     const int it = threadIdx.x + u * T, l = it % NL, i = (it / NL) % R3, k1 = it / (NL * R3);
+    if (N2 % T != 0 && it >= N2) continue;
     float2* o = sm + X::b2(l, i, k1);
     const float2* t2 = T2 + i;
     float2 v[R2];
@@ -344,6 +411,7 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
 #pragma unroll
   for (int u = 0; u < IT3; ++u) {
     const int it = threadIdx.x + u * T, l = it % NL, k2 = (it / NL) % R2, k1 = it / (NL * R2);
+    if (N3 % T != 0 && it >= N3) continue;
     float2* o = sm + X::b3(l, k1, k2);
     float2 v[R3];
 #pragma unroll
@@ -360,7 +428,13 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
 #pragma unroll
       for (int i = 0; i < R3; ++i) o[i * NL] = v[i];
     } else {
-      if (L.cb_in[l] >= 0) long_store_run<R3, OM, TO>(d, L, l, k1 + R1 * k2, S3, SD, full_out, v);
+      const float2* tt = t4 ? t4 + k1 * R3 * R2 + k2 : nullptr;
+      if constexpr (PRE) {
+        if (L.cb_in[l] >= 0) long_store_run<R3, R2, OM, TO>(d, L, l, k1 + R1 * k2, S3, SD, full_out, v, pre[u], tt);
+      } else {
+        const float none[R3] = {};
+        if (L.cb_in[l] >= 0) long_store_run<R3, R2, OM, TO>(d, L, l, k1 + R1 * k2, S3, SD, full_out, v, none, tt);
+      }
     }
   }
   if constexpr (MID) {
@@ -369,6 +443,7 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
 #pragma unroll
     for (int u = 0; u < IT2; ++u) {
       const int it = threadIdx.x + u * T, l = it % NL, i = (it / NL) % R3, k1 = it / (NL * R3);
+      if (N2 % T != 0 && it >= N2) continue;
       float2* o = sm + X::b2(l, i, k1);
       const float2* t2 = T2 + i;
       float2 v[R2];
@@ -384,6 +459,7 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
 #pragma unroll
     for (int u = 0; u < IT1; ++u) {
       const int it = threadIdx.x + u * T, l = it % NL, j = it / NL;
+      if (N1 % T != 0 && it >= N1) continue;
       const float2* o = sm + X::b1(l, j);
       const float2* t1 = T1 + j;
       float2 v[R1];
@@ -391,7 +467,8 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_cl_kern
 #pragma unroll
       for (int k1 = 1; k1 < R1; ++k1) v[k1] = cmul(o[k1 * X::C1], conj_if(t1[k1 * M], 1.f));
       dftR<R1>(v, 1.f);
-      if (L.cb_in[l] >= 0) long_store_run<R1, OM, TO>(d, L, l, j, M, SD, full_out, v);
+      const float none[R1] = {};
+      if (L.cb_in[l] >= 0) long_store_run<R1, M, OM, TO>(d, L, l, j, M, SD, full_out, v, none, t4 ? t4 + j : nullptr);
     }
   }
 }
@@ -419,7 +496,8 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_bwd_ker
   float2* tw = smy + (size_t)(F + F / R3) * NL;        // T1 then T2
   const float2* T1 = tw;
   const float2* T2 = tw + F;
-  long long* sb = reinterpret_cast<long long*>(tw + long_twn<R1, R2, R3>());  // [NL] spectrum base (-1: past the end)
+  float2* T4 = tw + long_twn<R1, R2, R3>();  // [F] store twiddles (uniform multiplier)
+  long long* sb = reinterpret_cast<long long*>(T4 + F);  // [NL] spectrum base (-1: past the end)
   long long* kb = sb + NL;                                                    // [NL] filter base
   int* twm = reinterpret_cast<int*>(kb + NL);                                 // [NL] k_a
   const long long line0 = (long long)blockIdx.x * NL;
@@ -439,6 +517,8 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_bwd_ker
     twm[l] = ka;
   }
   __syncthreads();
+  const float2* t4 = d.C % NL == 0 ? T4 : nullptr;
+  if (t4) long_fill_store_twiddles<R1, R2, R3, true>(T4, twm[0], d.tw_logF, d.scale, 1.f);
 
   // forward level 1 of one line set (g: partial spectrum, pair offset qoff) into sm
   auto forward1 = [&](const float2* g, float2* sm, long long qoff) {
@@ -506,11 +586,18 @@ __global__ void __launch_bounds__(kLongThreads, kLongMinBlocks) fft_long_bwd_ker
       if (sb[l] < 0) continue;
       float2* gl = g + gb[l] + qoff + (long long)j * d.tst;
       const long long step = (long long)M * d.tst;
-      TwRun tr = tw_run(twm[l], j, M, d.tw_logF, d.scale, 1.f);
+      TwRun tr;
+      if (!t4) tr = tw_run(twm[l], j, M, d.tw_logF, d.scale, 1.f);
 #pragma unroll
       for (int r = 0; r < R1; ++r) {
-        float2 val = cmul(v[r], tr.w);
-        tr.w = cmul(tr.w, tr.s);
+        float2 w;
+        if (t4) {
+          w = t4[r * M + j];
+        } else {
+          w = tr.w;
+          tr.w = cmul(tr.w, tr.s);
+        }
+        float2 val = cmul(v[r], w);
         if (add) val = cadd(val, gl[r * step]);
         gl[r * step] = val;
       }

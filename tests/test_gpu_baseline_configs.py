@@ -121,6 +121,31 @@ def test_cfg4_length_causal_op_vs_oracle(dt):
         assert e <= tol, (name, e)
 
 
+@pytest.mark.parametrize("C,L", [(16, 1 << 20), (64, 1 << 16), (24, 1 << 13)])
+def test_long_passes_channel_runs_vs_oracle(C, L):
+    """The long 1D passes with channel counts that fill every CTA's run of lines (one
+    four-step multiplier per CTA: the store twiddles come from a per-CTA table) and with a
+    ragged count (24: runs straddle rows, per-run twiddle factors), op and mixer."""
+    from nvsubquadratic_b200.fftconv import causal_fftconv1d_fp32_bhl
+
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(1, C, L, generator=g)
+    t = torch.arange(L, dtype=torch.float32)
+    k = torch.randn(1, C, L, generator=g) * torch.exp(-(torch.rand(C, 1, generator=g) * 4.5 + 0.5) / L * t) / 32
+    sc = torch.randn(C, generator=g)
+    dy = torch.randn(1, C, L, generator=g)
+    xr, kr, sr = (u.clone().requires_grad_(True) for u in (x, k, sc))
+    yr = ofc.fftconv_bhl(xr, kr, sr, causal=True)
+    yr.backward(dy)
+    xd, kd, sd = (u.cuda().requires_grad_(True) for u in (x, k, sc))
+    y = causal_fftconv1d_fp32_bhl(xd, kd, sd)
+    y.backward(dy.cuda())
+    torch.cuda.synchronize()
+    for name, a, b in (("y", yr, y), ("dx", xr.grad, xd.grad), ("dk", kr.grad, kd.grad), ("dD", sr.grad, sd.grad)):
+        assert rel_l2(a, b) <= 1e-5, (name, rel_l2(a, b))
+    _check_mixer(1, C, (L,), (L,), 7, torch.bfloat16, causal=True, g1="silu")
+
+
 @pytest.mark.parametrize("causal,xs,ks,dt", [
     # 1 MiB spectra per channel at F = 2^17: a 64 MiB budget holds 16 channels -> 16, 16, 8
     (True, (2, 40, 1 << 16), (1, 40, 1 << 16), torch.float32),
@@ -152,16 +177,19 @@ def test_channel_chunked_op_vs_oracle(causal, xs, ks, dt, monkeypatch):
         assert e <= tol, (name, e)
 
 
+@pytest.mark.parametrize("kh_cache", [True, False])
 @pytest.mark.parametrize("B,C,S,K,sk,causal", [
     # F = 2^17, one pair: 4 MiB per channel -> chunks of 16 at a 64 MiB budget
     (1, 48, (1 << 16,), (1 << 16,), 7, True),
     # F = 64^3: 8 MiB per channel -> chunks of 8
     (2, 24, (32, 32, 32), (32, 32, 32), 3, False),
 ])
-def test_channel_chunked_mixer_vs_oracle(B, C, S, K, sk, causal, monkeypatch):
-    """hyfft_hyena_* on the general engine with several channel chunks (the backward then
-    recomputes each chunk's filter spectrum instead of reading the saved one)."""
+def test_channel_chunked_mixer_vs_oracle(B, C, S, K, sk, causal, kh_cache, monkeypatch):
+    """hyfft_hyena_* on the general engine with several channel chunks: the backward reads
+    each chunk's filter spectrum from the saved state, or (HYFFT_NO_KH_CACHE) recomputes it."""
     monkeypatch.setenv("HYFFT_WS_BUDGET_MB", "64")
+    if not kh_cache:
+        monkeypatch.setenv("HYFFT_NO_KH_CACHE", "1")
     _check_mixer(B, C, S, K, sk, torch.bfloat16, causal=causal, g1="silu", g2="sigmoid")
 
 
