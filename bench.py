@@ -687,10 +687,15 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
-    if cfg["shard"] == "cp":
+    if cfg["shard"] == "cp" and world == 1 and args.profile:
+        # one GPU, --profile: the mixer on one channel block at full length (what every rank
+        # runs between the exchanges), for kernel captures
+        res = run_gpu(args, dict(cfg, shard="replica"), rank, world, device)
+    elif cfg["shard"] == "cp":
         if world < 2:
             raise SystemExit("cfg4 (context parallel, 12.9 GB of q/k/v per copy) runs on 2 or more GPUs "
-                             "(python -m torch.distributed.run ... bench.py --config cfg4 --gpus N)")
+                             "(python -m torch.distributed.run ... bench.py --config cfg4 --gpus N); "
+                             "on one GPU only as --profile --channels C (the local channel block)")
         res = run_cp(args, cfg, rank, world, device)
     else:
         res = run_gpu(args, cfg, rank, world, device)

@@ -249,6 +249,46 @@ HYFFT_API int hyfft_causal_conv1d_backward(const void* x, const float* weight, c
                                            void* dx, float* dweight, float* dbias, int64_t B, int64_t C, int64_t L,
                                            int32_t K, int32_t activation, int32_t dtype, void* stream);
 
+/* ---------------------------------------------------------------- implicit filter (SIREN)
+ * The filter generator of the Hyena long convolution: a SIREN network evaluated on the
+ * coordinate grid, then the exponential window, in float32 (replaces
+ * nvsubquadratic/modules/kernels_nd.py SIRENKernelND.forward :1149-1199 with its positional
+ * embedding :818-874, no FiLM, and masks_nd.py ExponentialModulationND.forward :229-255).
+ *
+ *   h0 = sin(pe_w x + pe_b); h_l = sin(W_l h_{l-1} + b_l), l = 1..num_hidden;
+ *   k[p, c] = (out_w h + out_b)[c] * prod_d exp(-|x_d(p)| |mask_w[d, c]|)
+ *
+ * coords: the per-axis coordinate vectors concatenated (n[0] + .. + n[ndim-1] floats, the
+ * reference's sliced linspace grid); points are row-major over the axes (G = prod n).
+ * Weights: pe_w [E, ndim], pe_b [E] | NULL, hid_w the hidden layers' weights concatenated
+ * ([H, E] then num_hidden - 1 times [H, H]), hid_b [num_hidden, H] | NULL, out_w [C, H],
+ * out_b [C] | NULL, mask_w [ndim, C] | NULL (no window). kernel: [G, C] (layout BLH, the
+ * reference's [1, *S, C]) or [C, G] (layout BHL, the mixer's [1, C, *S]). saved: G * H
+ * floats written by the forward and read by the backward; workspace: G * H floats.
+ * The backward overwrites every gradient it is given; mask_w gets none (fixed window).
+ * E, H <= 128 (HYFFT_ERR_UNSUPPORTED above, or when the backward's shared memory would
+ * exceed a CTA's). */
+typedef struct hyfft_siren_desc {
+  int32_t ndim;        /* 1..3 */
+  int32_t n[3];        /* grid points per axis (2 * seq_len - 1 in the reference) */
+  int32_t embedding;   /* E */
+  int32_t hidden;      /* H */
+  int32_t num_hidden;  /* hidden linear layers (the reference's num_layers - 1), >= 1 */
+  int32_t channels;    /* C */
+  int32_t layout;      /* HYFFT_LAYOUT_BLH: kernel [G, C]; HYFFT_LAYOUT_BHL: [C, G] */
+} hyfft_siren_desc;
+
+HYFFT_API int hyfft_siren_sizes(const hyfft_siren_desc* d, size_t* saved_bytes, size_t* workspace_bytes);
+HYFFT_API int hyfft_siren_forward(const hyfft_siren_desc* d, const float* coords, const float* pe_w,
+                                  const float* pe_b, const float* hid_w, const float* hid_b, const float* out_w,
+                                  const float* out_b, const float* mask_w, float* kernel, void* saved,
+                                  size_t saved_bytes, void* stream);
+HYFFT_API int hyfft_siren_backward(const hyfft_siren_desc* d, const float* coords, const float* pe_w,
+                                   const float* pe_b, const float* hid_w, const float* hid_b, const float* out_w,
+                                   const float* mask_w, const float* dkernel, const void* saved, float* d_pe_w,
+                                   float* d_pe_b, float* d_hid_w, float* d_hid_b, float* d_out_w, float* d_out_b,
+                                   void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- misc */
 /* Message of the most recent error on this thread ("" if none). */
 HYFFT_API const char* hyfft_last_error(void);

@@ -74,6 +74,18 @@ _i64 = ctypes.c_int64
 _i32 = ctypes.c_int32
 
 # name -> argtypes (restype is int unless listed in _STR_FUNCS)
+class SirenDesc(ctypes.Structure):
+    _fields_ = [
+        ("ndim", ctypes.c_int32),
+        ("n", ctypes.c_int32 * 3),
+        ("embedding", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+        ("num_hidden", ctypes.c_int32),
+        ("channels", ctypes.c_int32),
+        ("layout", ctypes.c_int32),
+    ]
+
+
 SIGNATURES = {
     "hyfft_conv_workspace_size": [ctypes.POINTER(ConvDesc), ctypes.POINTER(_sz), ctypes.POINTER(_sz)],
     "hyfft_conv_forward": [ctypes.POINTER(ConvDesc), _vp, _vp, _vp, _vp, _vp, _sz, _vp],
@@ -92,6 +104,9 @@ SIGNATURES = {
     "hyfft_cp_permute_cl_window": [_vp, _vp, _i32, _i64, _i64, _i64, _i64, _i64, _i32, _i64, _i64, _i32, _vp],
     "hyfft_causal_conv1d_forward": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp],
     "hyfft_causal_conv1d_backward": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _i32, _vp],
+    "hyfft_siren_sizes": [ctypes.POINTER(SirenDesc), ctypes.POINTER(_sz), ctypes.POINTER(_sz)],
+    "hyfft_siren_forward": [ctypes.POINTER(SirenDesc)] + [_vp] * 10 + [_sz, _vp],
+    "hyfft_siren_backward": [ctypes.POINTER(SirenDesc)] + [_vp] * 16 + [_sz, _vp],
     "hyfft_last_error": [],
     "hyfft_version": [],
     "hyfft_launch_count": [],

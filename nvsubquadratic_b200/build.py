@@ -24,7 +24,7 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libhyfft.so"
 STAMP = PKG / ".libhyfft.stamp"
 
-SOURCES = ["engine.cu", "cp.cu", "fused.cu", "toeplitz.cu", "big2d.cu", "shortconv.cu", "transpose_tma.cu", "fft_long.cu"]
+SOURCES = ["engine.cu", "cp.cu", "fused.cu", "toeplitz.cu", "big2d.cu", "shortconv.cu", "transpose_tma.cu", "fft_long.cu", "siren.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -37,5 +37,5 @@ def golden():
     here = os.path.join(ROOT, "tests", "golden")
     return {
         name: torch.load(os.path.join(here, f"{name}.pt"), weights_only=False)
-        for name in ("ops", "hyena", "cp", "boundary")
+        for name in ("ops", "hyena", "cp", "boundary", "siren")
     }

@@ -315,10 +315,47 @@ def make_cp(ref_path: str) -> dict:
     return out
 
 
+def make_siren(SIRENKernelND, ExponentialModulationND) -> dict:
+    """The reference's implicit filter (nvsubquadratic/modules/kernels_nd.py SIRENKernelND, no
+    FiLM) and exponential window (modules/masks_nd.py ExponentialModulationND) on seeded
+    weights: kernel, masked kernel and the gradients of every SIREN parameter for a random
+    upstream gradient of the masked kernel. Cases cover 1D / 2D / 3D grids, with and without
+    biases, a grid extended past L_cache, and widths up to 64."""
+    cases = []
+    # (name, out_dim, data_dim, hidden, num_layers, emb, omega_0, L_cache, use_bias, seq_lens)
+    specs = [
+        ("siren1d", 16, 1, 32, 3, 16, 10.0, 64, True, (64,)),
+        ("siren1d_ext", 8, 1, 16, 2, 8, 5.0, 32, True, (48,)),
+        ("siren2d", 24, 2, 32, 3, 32, 10.0, 14, True, (14, 14)),
+        ("siren2d_nobias", 12, 2, 64, 2, 32, 30.0, 8, False, (8, 6)),
+        ("siren3d", 8, 3, 32, 3, 16, 10.0, 6, True, (6, 5, 4)),
+    ]
+    for i, (name, C, D, H, NL, E, w0, L, bias, seq) in enumerate(specs):
+        torch.manual_seed(100 + i)
+        m = SIRENKernelND(out_dim=C, data_dim=D, mlp_hidden_dim=H, num_layers=NL, embedding_dim=E, omega_0=w0,
+                          L_cache=L, use_bias=bias)
+        if bias:  # non-zero biases, so that they are exercised
+            with torch.no_grad():
+                for mod in [m.positional_embedding.linear, *m.hidden_linears, m.out_linear]:
+                    mod.bias.uniform_(-0.5, 0.5)
+        mask = ExponentialModulationND(data_dim=D, num_channels=C)
+        k, grid = m(seq)
+        km = mask(grid=grid, x=k)
+        dk = torch.randn(km.shape, generator=torch.Generator().manual_seed(200 + i))
+        km.backward(dk)
+        cases.append(dict(
+            name=name, cfg=dict(out_dim=C, data_dim=D, mlp_hidden_dim=H, num_layers=NL, embedding_dim=E,
+                                omega_0=w0, L_cache=L, use_bias=bias), seq_lens=seq,
+            state={kk: v.detach().clone() for kk, v in m.state_dict().items()},
+            mask_weight=mask.weight.detach().clone(), kernel=k.detach(), masked=km.detach(), grid=grid.detach(),
+            dk=dk, grads={kk: v.grad.detach().clone() for kk, v in m.named_parameters()}))
+    return {"cases": cases}
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="root of the nvSubquadratic source tree (holds nvsubquadratic/)")
-    ap.add_argument("--only", default="", help="comma-separated subset of ops,hyena,cp,boundary to regenerate")
+    ap.add_argument("--only", default="", help="comma-separated subset of ops,hyena,cp,boundary,siren to regenerate")
     args = ap.parse_args()
     sys.path.insert(0, args.ref)
     _install_omegaconf_stub()
@@ -330,7 +367,10 @@ def main() -> None:
     from nvsubquadratic.ops import circular_fftconv as ref_circ
     from nvsubquadratic.ops import mixed_fftconv as ref_mixed
 
-    only = set(args.only.split(",")) if args.only else {"ops", "hyena", "cp", "boundary"}
+    from nvsubquadratic.modules.kernels_nd import SIRENKernelND
+    from nvsubquadratic.modules.masks_nd import ExponentialModulationND
+
+    only = set(args.only.split(",")) if args.only else {"ops", "hyena", "cp", "boundary", "siren"}
     if "ops" in only:
         torch.save(make_ops(ref_fftconv), HERE / "ops.pt")
     if "hyena" in only:
@@ -339,6 +379,8 @@ def main() -> None:
         torch.save(make_cp(args.ref), HERE / "cp.pt")
     if "boundary" in only:
         torch.save(make_boundary(ref_circ, ref_mixed), HERE / "boundary.pt")
+    if "siren" in only:
+        torch.save(make_siren(SIRENKernelND, ExponentialModulationND), HERE / "siren.pt")
     for f in sorted(n + ".pt" for n in only):
         print(f, (HERE / f).stat().st_size, "bytes")
 
