@@ -590,6 +590,55 @@ def e2e_time(cfg, inp, device, op_only, steps, dp_group=None):
     return statistics.median(times), h2d, d2h, statistics.median(copy_times[1:])
 
 
+def measure_filter_gen(device, steps: int, warmup: int) -> dict:
+    """The implicit filter generator (SIREN network + exponential window, forward and backward:
+    nvsubquadratic_b200.siren.ckconv_filter) on the reference's double grid of cfg1 (27x27
+    points, 768 channels) and of cfg2 (255x255 points, 256 channels), 3 SIREN layers of width
+    64, embedding 32: device time per fwd+bwd (CUDA events, median), filter values per second,
+    and the CPU oracle (torch, all host threads) on the cfg1 case."""
+    from nvsubquadratic_b200.siren import SIRENKernelB200, ckconv_filter
+    from oracle import siren as osr
+
+    res = {"layers": 3, "hidden": 64, "embedding": 32, "stat": "median of the timed fwd+bwd calls"}
+    for name, C, seq in (("cfg1", 768, (14, 14)), ("cfg2", 256, (128, 128))):
+        torch.manual_seed(0)
+        m = SIRENKernelB200(out_dim=C, data_dim=2, mlp_hidden_dim=64, num_layers=3, embedding_dim=32, omega_0=10.0,
+                            L_cache=seq[0], use_bias=True).to(device)
+        mw = osr.mask_init(2, C).to(device)
+        G = (2 * seq[0] - 1) * (2 * seq[1] - 1)
+        dk = torch.randn(1, C, 2 * seq[0] - 1, 2 * seq[1] - 1, device=device)
+        times = []
+        for i in range(warmup + steps):
+            m.zero_grad(set_to_none=True)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            ckconv_filter(m, mw, seq, layout="bhl").backward(dk)
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= warmup:
+                times.append(e0.elapsed_time(e1))
+        ms = statistics.median(times)
+        res[name] = {"grid": [2 * seq[0] - 1, 2 * seq[1] - 1], "channels": C, "ms_fwd_bwd": round(ms, 4),
+                     "gvalues_per_s": round(G * C / (ms * 1e-3) / 1e9, 3)}
+        if name == "cfg1":
+            cpu = {k: v.detach().cpu() for k, v in m.state_dict().items()}
+            p = {"pe.weight": cpu["positional_embedding.linear.weight"], "pe.bias": cpu["positional_embedding.linear.bias"],
+                 "out.weight": cpu["out_linear.weight"], "out.bias": cpu["out_linear.bias"]}
+            for i in range(2):
+                p[f"hidden.{i}.weight"] = cpu[f"hidden_linears.{i}.weight"]
+                p[f"hidden.{i}.bias"] = cpu[f"hidden_linears.{i}.bias"]
+            p = {k: v.requires_grad_(True) for k, v in p.items()}
+            mwc, dkc = mw.cpu(), dk.cpu().permute(0, 2, 3, 1)
+            ct = []
+            for _ in range(3):
+                t0 = time.perf_counter()
+                osr.siren_filter(p, seq, seq[0], mwc)[0].backward(dkc)
+                ct.append(time.perf_counter() - t0)
+            res[name]["cpu_oracle_ms"] = round(statistics.median(ct) * 1e3, 3)
+            res[name]["cpu_threads"] = torch.get_num_threads()
+    return res
+
+
 def summarize(name: str, cfg: dict, res: dict, world: int, steps: int, peaks: dict) -> dict:
     """Whole-job throughput (all ranks' elements / max-over-ranks time), the roofline of the
     dominant library pass and the end-to-end throughput of one measured configuration."""
@@ -632,6 +681,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--secondary", default="cfg1",
                     help="on one GPU, also measure this configuration and report it under 'secondary' ('' for none)")
+    ap.add_argument("--filter-gen", default=True, action=argparse.BooleanOptionalAction,
+                    help="on one GPU, also time the implicit filter generator (SIREN + window, fwd+bwd)")
     ap.add_argument("--profile", action="store_true",
                     help="run warmup + steps eager fwd+bwd steps and exit (for ncu captures)")
     ap.add_argument("--channels", type=int, default=None,
@@ -743,6 +794,8 @@ def main():
                                         "ms_per_step": round(res2["e2e_ms"], 4), "h2d_bytes_per_step": res2["h2d"],
                                         "d2h_bytes_per_step": res2["d2h"]},
                                 "gpu_launches": res2["launches"] * args.steps, "clocks": res2["clocks"]}
+        if world == 1 and args.filter_gen:
+            out["filter_gen"] = measure_filter_gen(device, args.steps, args.warmup)
         print(json.dumps(out))
     if world > 1:
         torch.distributed.barrier()

@@ -197,3 +197,29 @@ def ckconv_filter(kernel: SIRENKernelB200, mask_weight: torch.Tensor | None, gri
     k = siren_generate(kernel, ax, mask_weight, layout)
     S = tuple(a.numel() for a in ax)
     return k.view((1, kernel.out_dim) + S) if layout == "bhl" else k.view((1,) + S + (kernel.out_dim,))
+
+
+class SirenFilter(torch.nn.Module):
+    """The implicit filter of a CKConvND (ckconv_nd.py:1133-1164) as the ``kernel_fn`` of
+    ``HyenaB200``: ``spatial_dims -> [1, C, *K]`` from the SIREN network on the double grid
+    (K = 2 N - 1 per axis), the exponential window (``mask.weight`` [D, C], the reference's
+    ``ExponentialModulationND`` default decay ramp unless given) and, causal, the second half of
+    the grid (K = N)."""
+
+    def __init__(self, kernel: SIRENKernelB200, causal: bool = False, mask_weight: torch.Tensor | None = None,
+                 use_mask: bool = True):
+        super().__init__()
+        self.kernel = kernel
+        self.causal = causal
+        if use_mask:
+            if mask_weight is None:  # masks_nd.py:197-201: linspace(2.3, 13.81, C) / D on every axis
+                ramp = torch.linspace(2.3, 13.81, kernel.out_dim) / kernel.data_dim
+                mask_weight = torch.stack([ramp] * kernel.data_dim, dim=0)
+            self.mask = torch.nn.Module()
+            self.mask.register_buffer("weight", mask_weight.to(torch.float32).clone())
+        else:
+            self.mask = None
+
+    def forward(self, spatial_dims, **_):
+        mw = self.mask.weight if self.mask is not None else None
+        return ckconv_filter(self.kernel, mw, tuple(int(s) for s in spatial_dims), causal=self.causal, layout="bhl")
