@@ -49,6 +49,9 @@ static int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+// for the other translation units: record msg as this thread's last error, return code
+int set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 std::atomic<long long> g_launches{0};
 
 static int check_launch(const char* what) {

@@ -12,14 +12,14 @@
 // reference's layout) or channel-major [C, G] (what the mixer's long convolution reads),
 // so no copy or transpose sits between the generator and the filter transform.
 //
-// Kernels: the per-point network (one thread per point, activations in shared memory laid
-// out [unit][point], weights broadcast from L1) writes h_NH [G, H]; the readout is a tiled
-// SGEMM (64 x 64 tile, 4 x 4 per thread) whose epilogue adds the bias, applies the mask and
-// stores in the requested layout. The backward forms dh = (dk * mask) W_out and
+// Kernels: the network on tiles of 16 points (256 threads over (point, unit) pairs, each
+// layer's weights staged in shared memory) writes h_NH [G, H]; the readout is a tiled SGEMM
+// (64 x 64 tile, 4 x 4 per thread) whose epilogue adds the bias, applies the mask and stores
+// in the requested layout. The backward forms dh = (dk * mask) W_out and
 // dW_out = (dk * mask)^T h, db_out as tiled SGEMMs (the latter split over point chunks,
-// float atomics), then walks the network backwards per point (recomputing the
-// pre-activations) with each CTA's weight-gradient sums kept in shared memory across a
-// grid-stride loop and added once per CTA. The mask's decay rates get no gradient: the
+// float atomics), then walks the network backwards tile by tile (recomputing the
+// pre-activations), with each CTA's weight-gradient sums kept in shared memory across a
+// grid-stride loop and added once per CTA (per tile when they do not fit). The mask's decay rates get no gradient: the
 // reference describes them as fixed (masks_nd.py:150-156).
 #include <cuda_runtime.h>
 
@@ -32,10 +32,10 @@
 namespace hyfft {
 
 extern std::atomic<long long> g_launches;
+int set_error(int code, const char* msg);  // engine.cu: the message hyfft_last_error returns
 
 namespace {
 
-constexpr int kPtT = 64;     // points per CTA of the per-point kernels
 constexpr int kMaxWidth = 128;  // embedding / hidden widths the kernels take
 
 struct Net {
@@ -65,55 +65,84 @@ __device__ __forceinline__ void point_coords(const Coords& co, long long p, floa
   }
 }
 
-// Pre-activations and activations of every layer of one point (thread t of the CTA):
-// pre[(l * W + u) * kPtT + t], act = sin(pre) likewise; l = 0 is the embedding, W the
-// wider of E and H.
-__device__ __forceinline__ void net_forward_point(const Net& net, const float (&x)[3], float* pre, float* act, int W,
-                                                  int t) {
-  for (int e = 0; e < net.E; ++e) {
-    float acc = net.pe_b ? __ldg(net.pe_b + e) : 0.f;
-    for (int d = 0; d < net.D; ++d) acc = fmaf(__ldg(net.pe_w + e * net.D + d), x[d], acc);
-    pre[e * kPtT + t] = acc;
-    act[e * kPtT + t] = sinf(acc);
-  }
-  int in = net.E;
-  for (int l = 0; l < net.NH; ++l) {
-    const float* w = layer_w(net, l);
-    const float* src = act + (size_t)l * W * kPtT;
-    float* dp = pre + (size_t)(l + 1) * W * kPtT;
-    float* da = act + (size_t)(l + 1) * W * kPtT;
-    for (int j = 0; j < net.H; ++j) {
-      float acc = net.hb ? __ldg(net.hb + l * net.H + j) : 0.f;
-      const float* wr = w + (size_t)j * in;
-      for (int i = 0; i < in; ++i) acc = fmaf(__ldg(wr + i), src[i * kPtT + t], acc);
-      dp[j * kPtT + t] = acc;
-      da[j * kPtT + t] = sinf(acc);
-    }
-    in = net.H;
+// The network on a tile of kNetP points, by all kNetThreads threads of the CTA over
+// (point, unit) pairs: pre-activations pre[(l * kNetP + p) * W + u] and activations
+// act = sin(pre) likewise (l = 0: the embedding; W the wider of E and H). Each hidden layer's
+// weights are staged in shared memory first (rows padded by one, so that the lanes of a
+// warp, on neighbouring units of one point, read different banks). xs: [kNetP][3] coordinates.
+constexpr int kNetThreads = 256;
+constexpr int kNetP = 16;
+
+__device__ __forceinline__ void stage_layer(const Net& net, int l, float* wsm) {
+  const int in = l == 0 ? net.E : net.H;
+  const float* w = layer_w(net, l);
+  for (int q = threadIdx.x; q < net.H * in; q += kNetThreads) {
+    const int j = q / in, i = q - j * in;
+    wsm[j * (in + 1) + i] = __ldg(w + q);
   }
 }
 
-__host__ __device__ inline size_t net_smem_bytes(int NH, int W) { return sizeof(float) * 2 * (size_t)(NH + 1) * W * kPtT; }
+__device__ __forceinline__ void net_forward_tile(const Net& net, const float* xs, float* pre, float* act, float* wsm,
+                                                 int W) {
+  for (int q = threadIdx.x; q < kNetP * net.E; q += kNetThreads) {
+    const int p = q / net.E, e = q - p * net.E;
+    float acc = net.pe_b ? __ldg(net.pe_b + e) : 0.f;
+    for (int d = 0; d < net.D; ++d) acc = fmaf(__ldg(net.pe_w + e * net.D + d), xs[p * 3 + d], acc);
+    pre[p * W + e] = acc;
+    act[p * W + e] = sinf(acc);
+  }
+  int in = net.E;
+  for (int l = 0; l < net.NH; ++l) {
+    __syncthreads();  // the previous layer's activations, and wsm free again
+    stage_layer(net, l, wsm);
+    __syncthreads();
+    const float* src = act + (size_t)l * kNetP * W;
+    float* dp = pre + (size_t)(l + 1) * kNetP * W;
+    float* da = act + (size_t)(l + 1) * kNetP * W;
+    for (int q = threadIdx.x; q < kNetP * net.H; q += kNetThreads) {
+      const int p = q / net.H, j = q - p * net.H;
+      float acc = net.hb ? __ldg(net.hb + l * net.H + j) : 0.f;
+      const float* wr = wsm + j * (in + 1);
+      const float* ar = src + p * W;
+      for (int i = 0; i < in; ++i) acc = fmaf(wr[i], ar[i], acc);
+      dp[p * W + j] = acc;
+      da[p * W + j] = sinf(acc);
+    }
+    in = net.H;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ void tile_coords(const Coords& co, long long p0, long long G, float* xs) {
+  if (threadIdx.x < kNetP) {
+    float x[3];
+    point_coords(co, p0 + threadIdx.x < G ? p0 + threadIdx.x : G - 1, x);
+    for (int d = 0; d < 3; ++d) xs[threadIdx.x * 3 + d] = x[d];
+  }
+  __syncthreads();
+}
+
+__host__ __device__ inline size_t net_smem_bytes(int NH, int E, int H) {
+  const int W = E > H ? E : H, in = W;
+  return sizeof(float) * (2 * (size_t)(NH + 1) * kNetP * W + (size_t)H * (in + 1) + 3 * kNetP);
+}
 
 // h_NH of every point: [G][H]
-__global__ void __launch_bounds__(kPtT) siren_hidden_kernel(const Net net, const Coords co, long long G,
-                                                            float* __restrict__ hout) {
+__global__ void __launch_bounds__(kNetThreads) siren_hidden_kernel(const Net net, const Coords co, long long G,
+                                                                   float* __restrict__ hout) {
   extern __shared__ float smem[];
   const int W = max(net.E, net.H);
-  float* pre = smem;                                  // [NH + 1][W][kPtT]
-  float* act = smem + (size_t)(net.NH + 1) * W * kPtT;  // sin(pre)
-  const int t = threadIdx.x;
-  for (long long p0 = (long long)blockIdx.x * kPtT; p0 < G; p0 += (long long)gridDim.x * kPtT) {
-    const long long p = p0 + t;
-    float x[3];
-    point_coords(co, p < G ? p : G - 1, x);
-    net_forward_point(net, x, pre, act, W, t);
-    __syncthreads();
-    // stored row-major: consecutive threads, consecutive units
-    const float* last = act + (size_t)net.NH * W * kPtT;
-    for (int q = t; q < kPtT * net.H; q += kPtT) {
-      const int pt = q / net.H, j = q - pt * net.H;
-      if (p0 + pt < G) hout[(p0 + pt) * net.H + j] = last[j * kPtT + pt];
+  float* pre = smem;                                 // [NH + 1][kNetP][W]
+  float* act = pre + (size_t)(net.NH + 1) * kNetP * W;  // sin(pre)
+  float* wsm = act + (size_t)(net.NH + 1) * kNetP * W;  // one layer's weights, rows padded
+  float* xs = wsm + (size_t)net.H * (W + 1);          // [kNetP][3]
+  for (long long p0 = (long long)blockIdx.x * kNetP; p0 < G; p0 += (long long)gridDim.x * kNetP) {
+    tile_coords(co, p0, G, xs);
+    net_forward_tile(net, xs, pre, act, wsm, W);
+    const float* last = act + (size_t)net.NH * kNetP * W;
+    for (int q = threadIdx.x; q < kNetP * net.H; q += kNetThreads) {
+      const int p = q / net.H, j = q - p * net.H;
+      if (p0 + p < G) hout[(p0 + p) * net.H + j] = last[p * W + j];
     }
     __syncthreads();
   }
@@ -312,79 +341,89 @@ __host__ __device__ inline size_t grad_floats(int D, int E, int H, int NH) {
   return (size_t)E * D + E + (size_t)H * E + (size_t)(NH - 1) * H * H + (size_t)NH * H;
 }
 
-__global__ void __launch_bounds__(kPtT) siren_hidden_bwd_kernel(const Net net, const Coords co, long long G,
-                                                                const float* __restrict__ dh, NetGrad g) {
+__global__ void __launch_bounds__(kNetThreads) siren_hidden_bwd_kernel(const Net net, const Coords co, long long G,
+                                                                       const float* __restrict__ dh, NetGrad g,
+                                                                       int acc_smem) {
   extern __shared__ float smem[];
   const int W = max(net.E, net.H);
-  const int t = threadIdx.x;
-  float* pre = smem;                                     // [NH + 1][W][kPtT]
-  float* act = pre + (size_t)(net.NH + 1) * W * kPtT;    // sin(pre)
-  float* gA = act + (size_t)(net.NH + 1) * W * kPtT;     // dL/dpre of the current layer [W][kPtT]
-  float* gB = gA + (size_t)W * kPtT;                     // dL/dact of the layer below
-  float* xs = gB + (size_t)W * kPtT;                     // [3][kPtT]
-  float* acc = xs + 3 * kPtT;                            // the CTA's gradient sums (grad_floats)
+  float* pre = smem;                                    // [NH + 1][kNetP][W]
+  float* act = pre + (size_t)(net.NH + 1) * kNetP * W;  // sin(pre)
+  float* wsm = act + (size_t)(net.NH + 1) * kNetP * W;  // one layer's weights, rows padded
+  float* xs = wsm + (size_t)net.H * (W + 1);            // [kNetP][3]
+  float* gA = xs + 3 * kNetP;                           // dL/dpre of the current layer [kNetP][W]
+  float* gB = gA + (size_t)kNetP * W;                   // dL/dact of the layer below
+  float* acc = gB + (size_t)kNetP * W;                  // the CTA's gradient sums (grad_floats)
   // accumulator offsets: pe_w, pe_b, then per hidden layer its weight, then the hidden biases
   const size_t o_pe_b = (size_t)net.E * net.D, o_hw = o_pe_b + net.E;
   const size_t o_hb = o_hw + (size_t)net.H * net.E + (size_t)(net.NH - 1) * net.H * net.H;
   const size_t nacc = grad_floats(net.D, net.E, net.H, net.NH);
-  for (size_t i = t; i < nacc; i += kPtT) acc[i] = 0.f;
-  for (long long p0 = (long long)blockIdx.x * kPtT; p0 < G; p0 += (long long)gridDim.x * kPtT) {
-    const long long p = p0 + t;
-    const bool ok = p < G;
-    float x[3];
-    point_coords(co, ok ? p : G - 1, x);
-    for (int d = 0; d < 3; ++d) xs[d * kPtT + t] = ok ? x[d] : 0.f;
-    net_forward_point(net, x, pre, act, W, t);
+  auto dst_of = [&](size_t i) -> float* {
+    if (i < o_pe_b) return g.pe_w + i;
+    if (i < o_hw) return g.pe_b ? g.pe_b + (i - o_pe_b) : nullptr;
+    if (i < o_hb) return g.hw + (i - o_hw);
+    return g.hb ? g.hb + (i - o_hb) : nullptr;
+  };
+  // the CTA's sums in shared memory when they fit, else added to the outputs per tile
+  auto add = [&](size_t i, float v) {
+    if (acc_smem) {
+      acc[i] += v;
+    } else if (float* d = dst_of(i)) {
+      atomicAdd(d, v);
+    }
+  };
+  if (acc_smem)
+    for (size_t i = threadIdx.x; i < nacc; i += kNetThreads) acc[i] = 0.f;
+  for (long long p0 = (long long)blockIdx.x * kNetP; p0 < G; p0 += (long long)gridDim.x * kNetP) {
+    tile_coords(co, p0, G, xs);
+    net_forward_tile(net, xs, pre, act, wsm, W);
     // dL/dact of the last layer (zero for points past the end)
-    for (int q = t; q < kPtT * net.H; q += kPtT) {
-      const int pt = q / net.H, j = q - pt * net.H;
-      gB[j * kPtT + pt] = (p0 + pt < G) ? __ldg(dh + (p0 + pt) * net.H + j) : 0.f;
+    for (int q = threadIdx.x; q < kNetP * net.H; q += kNetThreads) {
+      const int p = q / net.H, j = q - p * net.H;
+      gB[p * W + j] = (p0 + p < G) ? __ldg(dh + (p0 + p) * net.H + j) : 0.f;
     }
     __syncthreads();
     for (int l = net.NH; l >= 0; --l) {
       const int width = l == 0 ? net.E : net.H;
-      const float* pl = pre + (size_t)l * W * kPtT;
-      for (int u = 0; u < width; ++u) gA[u * kPtT + t] = gB[u * kPtT + t] * cosf(pl[u * kPtT + t]);
+      const float* pl = pre + (size_t)l * kNetP * W;
+      for (int q = threadIdx.x; q < kNetP * width; q += kNetThreads) {
+        const int p = q / width, u = q - p * width;
+        gA[p * W + u] = gB[p * W + u] * cosf(pl[p * W + u]);
+      }
+      if (l > 0) stage_layer(net, l - 1, wsm);  // the weights of hidden layer l (index l - 1)
       __syncthreads();
-      if (l == 0) {  // embedding: dW_pe[e][d] += sum_t gA[e][t] x_d[t], db_pe[e] += sum_t gA[e][t]
-        for (int q = t; q < net.E * (net.D + 1); q += kPtT) {
+      if (l == 0) {  // embedding: dW_pe[e][d] += sum_p gA[p][e] x_d[p], db_pe[e] += sum_p gA[p][e]
+        for (int q = threadIdx.x; q < net.E * (net.D + 1); q += kNetThreads) {
           const int e = q / (net.D + 1), d = q - e * (net.D + 1);
-          float s = 0.f;
-          for (int tt = 0; tt < kPtT; ++tt) s = fmaf(gA[e * kPtT + tt], d < net.D ? xs[d * kPtT + tt] : 1.f, s);
-          if (d < net.D) acc[e * net.D + d] += s;
-          else acc[o_pe_b + e] += s;
+          float sacc = 0.f;
+          for (int p = 0; p < kNetP; ++p) sacc = fmaf(gA[p * W + e], d < net.D ? xs[p * 3 + d] : 1.f, sacc);
+          add(d < net.D ? (size_t)e * net.D + d : o_pe_b + e, sacc);
         }
-      } else {  // hidden layer l (weights index l - 1): input act[l - 1]
+      } else {  // hidden layer l: input act[l - 1]
         const int in = l == 1 ? net.E : net.H;
-        const float* a_in = act + (size_t)(l - 1) * W * kPtT;
-        const float* w = layer_w(net, l - 1);
-        float* aw = acc + o_hw + (l == 1 ? 0 : (size_t)net.H * net.E + (size_t)(l - 2) * net.H * net.H);
-        for (int q = t; q < net.H * (in + 1); q += kPtT) {
+        const float* a_in = act + (size_t)(l - 1) * kNetP * W;
+        const size_t o_w = o_hw + (l == 1 ? 0 : (size_t)net.H * net.E + (size_t)(l - 2) * net.H * net.H);
+        // neighbouring threads on neighbouring inputs i of one unit j
+        for (int q = threadIdx.x; q < net.H * (in + 1); q += kNetThreads) {
           const int j = q / (in + 1), i = q - j * (in + 1);
-          float s = 0.f;
-          for (int tt = 0; tt < kPtT; ++tt) s = fmaf(gA[j * kPtT + tt], i < in ? a_in[i * kPtT + tt] : 1.f, s);
-          if (i < in) aw[(size_t)j * in + i] += s;
-          else acc[o_hb + (size_t)(l - 1) * net.H + j] += s;
+          float sacc = 0.f;
+          for (int p = 0; p < kNetP; ++p) sacc = fmaf(gA[p * W + j], i < in ? a_in[p * W + i] : 1.f, sacc);
+          add(i < in ? o_w + (size_t)j * in + i : o_hb + (size_t)(l - 1) * net.H + j, sacc);
         }
-        // dL/dact of the layer below for this thread's point
-        for (int i = 0; i < in; ++i) {
-          float s = 0.f;
-          for (int j = 0; j < net.H; ++j) s = fmaf(__ldg(w + (size_t)j * in + i), gA[j * kPtT + t], s);
-          gB[i * kPtT + t] = s;
+        // dL/dact of the layer below: gB[p][i] = sum_j W[j][i] gA[p][j]
+        for (int q = threadIdx.x; q < kNetP * in; q += kNetThreads) {
+          const int p = q / in, i = q - p * in;
+          float sacc = 0.f;
+          for (int j = 0; j < net.H; ++j) sacc = fmaf(wsm[j * (in + 1) + i], gA[p * W + j], sacc);
+          gB[p * W + i] = sacc;
         }
       }
       __syncthreads();
     }
   }
+  if (!acc_smem) return;
   __syncthreads();
-  for (size_t i = t; i < nacc; i += kPtT) {
-    float* dst;
-    if (i < o_pe_b) dst = g.pe_w + i;
-    else if (i < o_hw) dst = g.pe_b ? g.pe_b + (i - o_pe_b) : nullptr;
-    else if (i < o_hb) dst = g.hw + (i - o_hw);
-    else dst = g.hb ? g.hb + (i - o_hb) : nullptr;
-    if (dst) atomicAdd(dst, acc[i]);
-  }
+  for (size_t i = threadIdx.x; i < nacc; i += kNetThreads)
+    if (float* d = dst_of(i)) atomicAdd(d, acc[i]);
 }
 
 }  // namespace
@@ -398,21 +437,25 @@ struct SirenPlan {
   Coords co;
   Net net;
   int C = 0, cl = 1, W = 0;
+  int acc_smem = 1;  // backward sums in shared memory
   size_t smem_fwd = 0, smem_bwd = 0;
 };
 
+constexpr size_t kSmemMax = 227 * 1024;
+
 int siren_plan(const hyfft_siren_desc* d, const float* coords, const float* pe_w, const float* pe_b, const float* hw,
                const float* hb, SirenPlan& s) {
-  if (!d || !coords || !pe_w || !hw) return HYFFT_ERR_INVALID;
+  if (!d || !coords || !pe_w || !hw) return set_error(HYFFT_ERR_INVALID, "siren: null descriptor or parameter");
   if (d->ndim < 1 || d->ndim > 3 || d->embedding < 1 || d->hidden < 1 || d->num_hidden < 1 || d->channels < 1)
-    return HYFFT_ERR_INVALID;
-  if (d->layout != HYFFT_LAYOUT_BHL && d->layout != HYFFT_LAYOUT_BLH) return HYFFT_ERR_INVALID;
-  if (d->embedding > kMaxWidth || d->hidden > kMaxWidth) return HYFFT_ERR_UNSUPPORTED;
+    return set_error(HYFFT_ERR_INVALID, "siren: ndim must be 1..3 and every width positive");
+  if (d->layout != HYFFT_LAYOUT_BHL && d->layout != HYFFT_LAYOUT_BLH) return set_error(HYFFT_ERR_INVALID, "siren: bad layout");
+  if (d->embedding > kMaxWidth || d->hidden > kMaxWidth)
+    return set_error(HYFFT_ERR_UNSUPPORTED, "siren: embedding and hidden widths above 128 are not covered");
   s.co.D = d->ndim;
   long long off = 0;
   for (int a = 0; a < 3; ++a) {
     s.co.n[a] = a < d->ndim ? d->n[a] : 1;
-    if (s.co.n[a] < 1) return HYFFT_ERR_INVALID;
+    if (s.co.n[a] < 1) return set_error(HYFFT_ERR_INVALID, "siren: grid extents must be positive");
     s.co.c[a] = coords + off;
     if (a < d->ndim) off += s.co.n[a];
     s.G *= s.co.n[a];
@@ -421,17 +464,23 @@ int siren_plan(const hyfft_siren_desc* d, const float* coords, const float* pe_w
   s.C = d->channels;
   s.cl = d->layout == HYFFT_LAYOUT_BLH ? 1 : 0;
   s.W = std::max(d->embedding, d->hidden);
-  s.smem_fwd = net_smem_bytes(d->num_hidden, s.W);
-  s.smem_bwd = s.smem_fwd + sizeof(float) * (2 * (size_t)s.W * kPtT + 3 * kPtT +
-                                             grad_floats(d->ndim, d->embedding, d->hidden, d->num_hidden));
-  if (s.smem_bwd > 227 * 1024) return HYFFT_ERR_UNSUPPORTED;
+  // the backward keeps its gradient sums in shared memory when they fit beside the tile
+  const size_t nacc = grad_floats(d->ndim, d->embedding, d->hidden, d->num_hidden);
+  s.smem_fwd = net_smem_bytes(d->num_hidden, d->embedding, d->hidden);
+  const size_t bwd_base = s.smem_fwd + sizeof(float) * 2 * (size_t)kNetP * s.W;
+  s.acc_smem = bwd_base + sizeof(float) * nacc <= kSmemMax ? 1 : 0;
+  s.smem_bwd = bwd_base + (s.acc_smem ? sizeof(float) * nacc : 0);
+  if (s.smem_fwd > kSmemMax || s.smem_bwd > kSmemMax)
+    return set_error(HYFFT_ERR_UNSUPPORTED, "siren: the network's activations do not fit a CTA's shared memory");
   return HYFFT_OK;
 }
 
-int grid_stride_ctas(long long G) { return (int)std::max<long long>(1, std::min<long long>((G + kPtT - 1) / kPtT, 4 * 148)); }
+int grid_stride_ctas(long long G) {
+  return (int)std::max<long long>(1, std::min<long long>((G + kNetP - 1) / kNetP, 4 * 148));
+}
 
 int launched() {
-  if (cudaGetLastError() != cudaSuccess) return HYFFT_ERR_CUDA;
+  if (cudaGetLastError() != cudaSuccess) return set_error(HYFFT_ERR_CUDA, "siren: kernel launch failed");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return HYFFT_OK;
 }
@@ -444,10 +493,10 @@ using namespace hyfft;
 extern "C" {
 
 int hyfft_siren_sizes(const hyfft_siren_desc* d, size_t* saved_bytes, size_t* workspace_bytes) {
-  if (!d || d->ndim < 1 || d->ndim > 3 || d->hidden < 1) return HYFFT_ERR_INVALID;
+  if (!d || d->ndim < 1 || d->ndim > 3 || d->hidden < 1) return set_error(HYFFT_ERR_INVALID, "siren: bad descriptor");
   long long G = 1;
   for (int a = 0; a < d->ndim; ++a) {
-    if (d->n[a] < 1) return HYFFT_ERR_INVALID;
+    if (d->n[a] < 1) return set_error(HYFFT_ERR_INVALID, "siren: grid extents must be positive");
     G *= d->n[a];
   }
   if (saved_bytes) *saved_bytes = sizeof(float) * (size_t)G * d->hidden;      // h of the last hidden layer
@@ -461,13 +510,13 @@ int hyfft_siren_forward(const hyfft_siren_desc* d, const float* coords, const fl
   SirenPlan s;
   int rc = siren_plan(d, coords, pe_w, pe_b, hid_w, hid_b, s);
   if (rc != HYFFT_OK) return rc;
-  if (!out_w || !kernel || !saved) return HYFFT_ERR_INVALID;
-  if (saved_bytes < sizeof(float) * (size_t)s.G * s.net.H) return HYFFT_ERR_WORKSPACE;
+  if (!out_w || !kernel || !saved) return set_error(HYFFT_ERR_INVALID, "siren: null output or saved buffer");
+  if (saved_bytes < sizeof(float) * (size_t)s.G * s.net.H) return set_error(HYFFT_ERR_WORKSPACE, "siren: saved buffer too small");
   if (bind_device_of(kernel) != HYFFT_OK) return HYFFT_ERR_CUDA;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   float* h = static_cast<float*>(saved);
   if (!kernel_smem_once((const void*)siren_hidden_kernel, s.smem_fwd)) return HYFFT_ERR_CUDA;
-  siren_hidden_kernel<<<grid_stride_ctas(s.G), kPtT, s.smem_fwd, st>>>(s.net, s.co, s.G, h);
+  siren_hidden_kernel<<<grid_stride_ctas(s.G), kNetThreads, s.smem_fwd, st>>>(s.net, s.co, s.G, h);
   if ((rc = launched()) != HYFFT_OK) return rc;
   const dim3 og((unsigned)((s.G + 63) / 64), (unsigned)((s.C + 63) / 64));
   siren_out_kernel<<<og, 256, 0, st>>>(h, out_w, out_b, mask_w, s.co, s.G, s.C, s.net.H, s.cl, kernel);
@@ -482,9 +531,11 @@ int hyfft_siren_backward(const hyfft_siren_desc* d, const float* coords, const f
   SirenPlan s;
   int rc = siren_plan(d, coords, pe_w, pe_b, hid_w, hid_b, s);
   if (rc != HYFFT_OK) return rc;
-  if (!out_w || !dkernel || !saved || !d_pe_w || !d_hid_w || !d_out_w || !workspace) return HYFFT_ERR_INVALID;
-  if ((pe_b != nullptr) != (d_pe_b != nullptr) || (hid_b != nullptr) != (d_hid_b != nullptr)) return HYFFT_ERR_INVALID;
-  if (workspace_bytes < sizeof(float) * (size_t)s.G * s.net.H) return HYFFT_ERR_WORKSPACE;
+  if (!out_w || !dkernel || !saved || !d_pe_w || !d_hid_w || !d_out_w || !workspace)
+    return set_error(HYFFT_ERR_INVALID, "siren: null tensor in the backward");
+  if ((pe_b != nullptr) != (d_pe_b != nullptr) || (hid_b != nullptr) != (d_hid_b != nullptr))
+    return set_error(HYFFT_ERR_INVALID, "siren: bias gradients must match the biases given");
+  if (workspace_bytes < sizeof(float) * (size_t)s.G * s.net.H) return set_error(HYFFT_ERR_WORKSPACE, "siren: workspace too small");
   if (bind_device_of(dkernel) != HYFFT_OK) return HYFFT_ERR_CUDA;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int D = s.net.D, E = s.net.E, H = s.net.H, NH = s.net.NH;
@@ -510,8 +561,8 @@ int hyfft_siren_backward(const hyfft_siren_desc* d, const float* coords, const f
   siren_dwo_kernel<<<wg, 256, 0, st>>>(dkernel, h, mask_w, s.co, s.G, s.C, H, s.cl, chunk, d_out_w, d_out_b);
   if ((rc = launched()) != HYFFT_OK) return rc;
   if (!kernel_smem_once((const void*)siren_hidden_bwd_kernel, s.smem_bwd)) return HYFFT_ERR_CUDA;
-  siren_hidden_bwd_kernel<<<grid_stride_ctas(s.G), kPtT, s.smem_bwd, st>>>(s.net, s.co, s.G, dh,
-                                                                            NetGrad{d_pe_w, d_pe_b, d_hid_w, d_hid_b});
+  siren_hidden_bwd_kernel<<<grid_stride_ctas(s.G), kNetThreads, s.smem_bwd, st>>>(
+      s.net, s.co, s.G, dh, NetGrad{d_pe_w, d_pe_b, d_hid_w, d_hid_b}, s.acc_smem);
   return launched();
 }
 
