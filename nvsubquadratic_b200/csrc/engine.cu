@@ -615,6 +615,7 @@ struct ConvPlan {
   int Cc = 0;  // channels per chunk
   long long spec_x_bytes_per_ch = 0, spec_k_bytes_per_ch = 0;
   bool big2d = false;  // fused large-grid 2D kernels (big2d.cu) instead of the pass chain
+  int b2F = 0;         // their FFT length per axis (192 or 256)
   bool khalf = false;  // the filter spectrum keeps bins [0, F/2] of the last axis only (product passes
                        // of 2D / 3D convolutions read the other half mirrored and conjugated)
 };
@@ -652,6 +653,15 @@ static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p, bool allow_big2
   p.Cc = (int)std::max<long long>(1, std::min<long long>(cc, p.C));
   p.big2d = allow_big2d && !p.g.periodic && p.g.D == 2 && !d->causal && p.g.F[0] == kB2F && p.g.F[1] == kB2F && p.g.N[0] <= kB2MaxN &&
             p.g.N[1] <= kB2MaxN && p.kB == 1 && !getenv("HYFFT_DISABLE_BIG2D");
+  if (p.big2d) {
+    // the circular convolution of length F equals the linear one on the output window
+    // [0, N) while F >= N + ceil(K/2) - 1 (no tap offset of another output wraps onto a
+    // tap): 192 covers the 128 x 128 grid with a 128 x 128 filter
+    bool short_ok = !getenv("HYFFT_B2_F256");
+    for (int a = 0; a < 2; ++a)
+      short_ok = short_ok && p.g.N[a] + (p.g.K[a] + 1) / 2 - 1 <= kB2FShort && p.g.K[a] <= kB2FShort;
+    p.b2F = short_ok ? kB2FShort : kB2F;
+  }
   const int F0 = p.g.F[0];
   p.khalf = p.g.D >= 2 && !p.g.four && !p.big2d && (F0 == 32 || F0 == 64 || F0 == 128 || F0 == 256) &&
             p.g.F[p.g.D - 1] % 2 == 0 && !getenv("HYFFT_DISABLE_CL_PASS") && !getenv("HYFFT_DISABLE_PRODUCT_PASS") &&
@@ -661,8 +671,10 @@ static int make_conv_plan(const hyfft_conv_desc* d, ConvPlan& p, bool allow_big2
 
 static size_t align_up(size_t v) { return (v + 255) & ~(size_t)255; }
 
-// One [C][129][256] complex spectrum of the large-grid 2D kernels.
-static size_t big2d_spec_bytes(const ConvPlan& p) { return align_up((size_t)p.C * kB2H * kB2F * sizeof(float2)); }
+// One [C][F/2+1][F] complex spectrum of the large-grid 2D kernels.
+static size_t big2d_spec_bytes(const ConvPlan& p) {
+  return align_up((size_t)p.C * (p.b2F / 2 + 1) * p.b2F * sizeof(float2));
+}
 
 static void conv_ws_sizes(const ConvPlan& p, size_t& fwd, size_t& bwd) {
   if (p.big2d) {  // Kh, T (+ G for the backward), then the float shortcut vector
@@ -1054,7 +1066,7 @@ static int run_dshortcut(int dt, int layout, const void* dy, const void* x, floa
   return check_launch("dshortcut_kernel");
 }
 
-// ---- large-grid 2D path: workspace = [Kh | T | G], all [C][129][256]-sized
+// ---- large-grid 2D path: workspace = [Kh | T | G], all [C][F/2+1][F]-sized
 static Big2DView b2view(const RealView& v) {
   Big2DView o;
   o.ptr = v.ptr;
@@ -1073,6 +1085,7 @@ static void big2d_params(const ConvPlan& p, const RealView& kv, const float* D, 
   b.Kh = (float2*)ws;
   b.T = (float2*)(ws + spec);
   b.G = (float2*)(ws + 2 * spec);
+  b.F = p.b2F;
   b.B = p.B;
   b.C = p.C;
   b.N0 = p.g.N[0];
@@ -1081,9 +1094,9 @@ static void big2d_params(const ConvPlan& p, const RealView& kv, const float* D, 
   b.K1 = p.g.K[1];
 }
 
-// [B][C][129][256] column spectra of a conv input (the mixer keeps z's for its backward).
+// [B][C][F/2+1][F] column spectra of a conv input (the mixer keeps z's for its backward).
 static size_t big2d_zs_bytes(const ConvPlan& p) {
-  return align_up((size_t)p.B * p.C * kB2H * kB2F * sizeof(float2));
+  return align_up((size_t)p.B * p.C * (p.b2F / 2 + 1) * p.b2F * sizeof(float2));
 }
 
 // zs_out: if set, the conv stores its input's column spectra there (zs_mode 1).

@@ -87,7 +87,7 @@ def _workspace_sizes(desc: _lib.ConvDesc) -> tuple[int, int]:
 
 _PLANS: dict = {}
 # the library's switches that change the conv plan (and so its workspace sizes)
-_PLAN_SWITCHES = ("HYFFT_WS_BUDGET_MB", "HYFFT_DISABLE_BIG2D")
+_PLAN_SWITCHES = ("HYFFT_WS_BUDGET_MB", "HYFFT_DISABLE_BIG2D", "HYFFT_B2_F256")
 
 
 def _plan(*args):

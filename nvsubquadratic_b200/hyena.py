@@ -92,7 +92,7 @@ def _sizes(desc) -> tuple[int, int, int]:
 _PLANS: dict = {}
 # the library's switches that change which kernels (and so which workspace sizes) a plan uses
 _PLAN_SWITCHES = ("HYFFT_USE_TP", "HYFFT_DISABLE_TP", "HYFFT_DISABLE_FUSED", "HYFFT_FUSED_POW2", "HYFFT_NO_KH_CACHE",
-                  "HYFFT_WS_BUDGET_MB", "HYFFT_DISABLE_BIG2D")
+                  "HYFFT_WS_BUDGET_MB", "HYFFT_DISABLE_BIG2D", "HYFFT_B2_F256")
 
 
 def _plan(*args):

@@ -6,8 +6,8 @@ seconds), so every path a bench line times is also checked against the oracle:
 
 * cfg1 in full: B=32, C=768, 14x14 grid, 14x14 filter, 3x3 short conv, bf16 (the fused
   small-grid kernels, 24x24 transforms);
-* cfg2's 128x128 grid with a 128x128 filter (F = 256 x 256, the large-grid kernels) at
-  B=2, C=32;
+* cfg2's 128x128 grid with a 128x128 filter (the large-grid kernels, on the 192-point
+  transforms they use for it and on 256-point ones) at B=2, C=32, mixer and op;
 * cfg3's 64^3 volume with a full-extent 64^3 filter (F = 128^3, the channel-innermost
   passes and the 3x3x3 plane stencils) at B=2, C=8;
 * cfg4's length: the causal op at L = 2^20 (F = 2^21, four-step passes) and the causal
@@ -79,9 +79,38 @@ def test_cfg1_full_size_vs_oracle():
     _check_mixer(32, 768, (14, 14), (14, 14), 3, torch.bfloat16)
 
 
-def test_cfg2_grid_vs_oracle():
-    """cfg2's 128x128 grid and 128x128 filter (large-grid kernels) at B=2, C=32."""
+@pytest.mark.parametrize("f256", [False, True], ids=["F192", "F256"])
+def test_cfg2_grid_vs_oracle(f256, monkeypatch):
+    """cfg2's 128x128 grid and 128x128 filter (large-grid kernels) at B=2, C=32, on the
+    192-point transforms the library picks for it and on the 256-point ones."""
+    if f256:
+        monkeypatch.setenv("HYFFT_B2_F256", "1")
     _check_mixer(2, 32, (128, 128), (128, 128), 3, torch.bfloat16)
+
+
+@pytest.mark.parametrize("f256", [False, True], ids=["F192", "F256"])
+@pytest.mark.parametrize("dt", [torch.float32, torch.bfloat16])
+def test_cfg2_grid_op_vs_oracle(dt, f256, monkeypatch):
+    """The op-level 2D conv at cfg2's grid (forward, dx, dk, dshortcut) on both large-grid
+    FFT lengths, odd batch and channel counts."""
+    from nvsubquadratic_b200 import fftconv as b2
+
+    if f256:
+        monkeypatch.setenv("HYFFT_B2_F256", "1")
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(3, 5, 128, 128, generator=g).to(dt)
+    k = torch.randn(1, 5, 128, 128, generator=g) / 128
+    sc = torch.randn(5, generator=g).to(dt)
+    dy = torch.randn(3, 5, 128, 128, generator=g).to(dt)
+    xr, kr, sr = (t.clone().requires_grad_(True) for t in (x, k, sc))
+    yr = ofc.fftconv_bhl(xr, kr, sr, causal=False)
+    yr.backward(dy)
+    xd, kd, sd = (t.cuda().requires_grad_(True) for t in (x, k, sc))
+    y = b2.fftconv2d_fp32_bhl(xd, kd, sd)
+    y.backward(dy.cuda())
+    torch.cuda.synchronize()
+    for name, a, b in (("y", yr, y), ("dx", xr.grad, xd.grad), ("dk", kr.grad, kd.grad), ("ds", sr.grad, sd.grad)):
+        assert rel_l2(a, b) <= TOL[dt], (name, rel_l2(a, b))
 
 
 def test_cfg3_volume_vs_oracle():
