@@ -86,6 +86,20 @@ __device__ __forceinline__ float2 csub(float2 a, float2 b) {
 #endif
 }
 __device__ __forceinline__ float2 cscale(float2 a, float s) { return make_float2(a.x * s, a.y * s); }
+// (a.x * b.x + c.x, a.y * b.y + c.y), each lane one fused multiply-add rounded to nearest
+// (fma.rn.f32x2 on sm_100a: the results equal two fmaf calls)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
+  float2 r;
+  asm("{\n.reg .b64 ra, rb, rc, rd;\nmov.b64 ra, {%2, %3};\nmov.b64 rb, {%4, %5};\nmov.b64 rc, {%6, %7};\n"
+      "fma.rn.f32x2 rd, ra, rb, rc;\nmov.b64 {%0, %1}, rd;\n}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+#else
+  return make_float2(fmaf(a.x, b.x, c.x), fmaf(a.y, b.y, c.y));
+#endif
+}
 
 // e^{i*pi*x}
 __device__ __forceinline__ float2 expipi(float x) {

@@ -1537,12 +1537,29 @@ static bool plane_stencil_ok(const HyenaPlan& h, std::initializer_list<const voi
 struct PlaneLaunch {
   dim3 grid;
   int xchunk;
-  StencilGeom g;  // 3D geometry of the kernels (a 2D grid is one x plane)
+  StencilGeom g;  // 3D geometry of the kernels
 };
-// x runs per CTA such that the grid fills about two waves of two CTAs per SM.
+// A 2D grid whose last axis has at least 96 positions marches along its first axis (as x)
+// with one-row planes of up to 128 positions; a smaller one runs as one x plane of 4 x 32
+// tiles.
+static bool plane_march2d(const HyenaPlan& h) { return h.d.ndim == 2 && h.sg.n[1] >= 96; }
+// x runs per CTA such that the grid fills about two waves of two CTAs per SM (3D), or one
+// wave of three CTAs per SM (2D march: the halo rows re-read per run stay few).
 static PlaneLaunch plane_launch(const HyenaPlan& h) {
   StencilGeom g = h.sg;
-  if (h.d.ndim == 2) {
+  const bool march = plane_march2d(h);
+  int TY = kS3TY, TZ = kS3TZ;
+  if (march) {  // (n0, n1) -> (x = n0, y = 1, z = n1)
+    g.nd = 3;
+    g.n[2] = g.n[1];
+    g.n[1] = 1;
+    g.k[2] = g.k[1];
+    g.k[1] = 1;
+    g.off[2] = g.off[1];
+    g.off[1] = 0;
+    TY = 1;
+    TZ = kS2TZ;
+  } else if (h.d.ndim == 2) {  // (n0, n1) -> (x = 1, y = n0, z = n1)
     g.nd = 3;
     g.n[2] = g.n[1];
     g.n[1] = g.n[0];
@@ -1554,14 +1571,16 @@ static PlaneLaunch plane_launch(const HyenaPlan& h) {
     g.off[1] = g.off[0];
     g.off[0] = 0;
   }
-  const long long base = (long long)((h.d.channels + kElemCG - 1) / kElemCG) * ((g.n[1] + kS3TY - 1) / kS3TY) *
-                         ((g.n[2] + kS3TZ - 1) / kS3TZ) * h.d.batch;
-  const long long nxc = std::max<long long>(1, std::min<long long>(g.n[0], (4 * 148 + base - 1) / base));
+  const long long base = (long long)((h.d.channels + kElemCG - 1) / kElemCG) * ((g.n[1] + TY - 1) / TY) *
+                         ((g.n[2] + TZ - 1) / TZ) * h.d.batch;
+  const long long target = march ? 3 * 148 : 4 * 148;
+  const long long nxc = march ? std::max<long long>(1, std::min<long long>(g.n[0], target / base))
+                              : std::max<long long>(1, std::min<long long>(g.n[0], (target + base - 1) / base));
   PlaneLaunch pl;
   pl.xchunk = (int)((g.n[0] + nxc - 1) / nxc);
   const long long chunks = (g.n[0] + pl.xchunk - 1) / pl.xchunk;
   pl.grid = dim3((unsigned)((h.d.channels + kElemCG - 1) / kElemCG),
-                 (unsigned)(((g.n[1] + kS3TY - 1) / kS3TY) * ((g.n[2] + kS3TZ - 1) / kS3TZ)),
+                 (unsigned)(((g.n[1] + TY - 1) / TY) * ((g.n[2] + TZ - 1) / TZ)),
                  (unsigned)(h.d.batch * chunks));
   pl.g = g;
   return pl;
@@ -1614,8 +1633,19 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
         if constexpr ((ND == 3 || ND == 2) && P && sizeof(T) == 2 && KA == 3 && KI == 3 && (ND == 2 || KB == 3)) {
           constexpr int PX = ND == 3 ? 3 : 1;
           constexpr size_t sm = s3_smem_bytes<PX, 3, 3>();
+          if constexpr (ND == 2) {
+            constexpr size_t sm2 = s3_smem_bytes<3, 1, 3, 1, kS2TZ>();
+            if (plane_march2d(h) && plane_stencil_ok<T>(h, {q, k, v}) &&
+                kernel_smem_once((const void*)hyena_plane_stencil_kernel<T, 3, 1, 3, 0, 1, kS2TZ>, sm2)) {
+              const PlaneLaunch pl = plane_launch(h);
+              hyena_plane_stencil_kernel<T, 3, 1, 3, 0, 1, kS2TZ><<<pl.grid, kElemThreads, sm2, st>>>(
+                  q, k, v, d.in_batch_stride, d.in_pos_stride, qs, ks, vs, 0, 0, z, pl.g, d.channels, sw, sb,
+                  d.gate1, pl.xchunk);
+              return;
+            }
+          }
           // (the line kernels below take over if the shared-memory size cannot be granted)
-          if (plane_stencil_ok<T>(h, {q, k, v}) &&
+          if (!plane_march2d(h) && plane_stencil_ok<T>(h, {q, k, v}) &&
               kernel_smem_once((const void*)hyena_plane_stencil_kernel<T, PX, 3, 3, 0>, sm)) {
             const PlaneLaunch pl = plane_launch(h);
             hyena_plane_stencil_kernel<T, PX, 3, 3, 0><<<pl.grid, kElemThreads, sm, st>>>(
@@ -1779,7 +1809,18 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
         if constexpr ((ND == 3 || ND == 2) && P && sizeof(T) == 2 && KA == 3 && KI == 3 && (ND == 2 || KB == 3)) {
           constexpr int PX = ND == 3 ? 3 : 1;
           constexpr size_t sm = s3_smem_bytes<PX, 3, 3>();
-          if (plane_stencil_ok<T>(h, {dqp, dkp, dvp, dq, dk, dv}) &&
+          if constexpr (ND == 2) {
+            constexpr size_t sm2 = s3_smem_bytes<3, 1, 3, 1, kS2TZ>();
+            if (plane_march2d(h) && plane_stencil_ok<T>(h, {dqp, dkp, dvp, dq, dk, dv}) &&
+                kernel_smem_once((const void*)hyena_plane_stencil_kernel<T, 3, 1, 3, 1, 1, kS2TZ>, sm2)) {
+              const PlaneLaunch pl = plane_launch(h);
+              hyena_plane_stencil_kernel<T, 3, 1, 3, 1, 1, kS2TZ><<<pl.grid, kElemThreads, sm2, st>>>(
+                  dqp, dkp, dvp, 0, 0, dq, dk, dv, d.in_batch_stride, d.in_pos_stride, nullptr, pl.g, d.channels,
+                  sw, nullptr, 0, pl.xchunk);
+              return;
+            }
+          }
+          if (!plane_march2d(h) && plane_stencil_ok<T>(h, {dqp, dkp, dvp, dq, dk, dv}) &&
               kernel_smem_once((const void*)hyena_plane_stencil_kernel<T, PX, 3, 3, 1>, sm)) {
             const PlaneLaunch pl = plane_launch(h);
             hyena_plane_stencil_kernel<T, PX, 3, 3, 1><<<pl.grid, kElemThreads, sm, st>>>(
@@ -1827,7 +1868,18 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
           if constexpr ((ND == 3 || ND == 2) && P && sizeof(T) == 2 && KA == 3 && KI == 3 && (ND == 2 || KB == 3)) {
             constexpr int PX = ND == 3 ? 3 : 1;
             constexpr size_t sm = s3_wgrad_smem_bytes<PX, 3, 3>();
-            if (plane_stencil_ok<T>(h, {q, k, v, dqp, dkp, dvp}) &&
+            if constexpr (ND == 2) {
+              constexpr size_t sm2 = s3_wgrad_smem_bytes<3, 1, 3, 1, kS2TZ>();
+              if (plane_march2d(h) && plane_stencil_ok<T>(h, {q, k, v, dqp, dkp, dvp}) &&
+                  kernel_smem_once((const void*)hyena_plane_wgrad_kernel<T, 3, 1, 3, 1, kS2TZ>, sm2)) {
+                const PlaneLaunch pl = plane_launch(h);
+                hyena_plane_wgrad_kernel<T, 3, 1, 3, 1, kS2TZ><<<pl.grid, kElemThreads, sm2, st>>>(
+                    dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, pl.g, d.channels, dsw,
+                    h.sg.has_bias ? dsb : nullptr, pl.xchunk);
+                return;
+              }
+            }
+            if (!plane_march2d(h) && plane_stencil_ok<T>(h, {q, k, v, dqp, dkp, dvp}) &&
                 kernel_smem_once((const void*)hyena_plane_wgrad_kernel<T, PX, 3, 3>, sm)) {
               const PlaneLaunch pl = plane_launch(h);
               hyena_plane_wgrad_kernel<T, PX, 3, 3><<<pl.grid, kElemThreads, sm, st>>>(

@@ -12,6 +12,11 @@
 // the KZ taps of that row, so the KX * KY * KZ weights (or, for the weight gradient, the
 // accumulators) stay in registers.
 //
+// A 2D grid (Y, Z) with Z >= 96 runs the same kernels as a march along Y: each "plane" is
+// one row of up to 128 positions (tile 1 x 128, KY = 1), so a CTA streams a run of rows
+// through the four-slot ring, every input row is read from HBM once per run (plus two
+// halo rows), and the CTA's weight-gradient partial sums cover the whole run.
+//
 // Reference: the depthwise short conv applied to q, k, v before the long convolution,
 // nvsubquadratic Hyena mixer (hyena_nd.py:530-546); cross-correlation with left padding
 // off = (k - 1) / 2 ("same") or k - 1 (causal) per axis.
@@ -21,29 +26,32 @@
 
 namespace hyfft {
 
-constexpr int kS3TY = 4;    // output rows (y) per tile: two warps per row
+constexpr int kS3TY = 4;    // output rows (y) per tile of a 3D plane: two warps per row
 constexpr int kS3TZ = 32;   // output positions (z) per tile row: 16 per warp
 constexpr int kS3Buf = 4;   // ring of input planes
 constexpr int kS3ZU = 4;    // z positions a warp computes per step
+// A 2D grid marches along its first axis as x with one-row "planes" (y extent 1) of up to
+// 128 positions: tile 1 x 128, eight warps side by side along z.
+constexpr int kS2TZ = 128;
 
-template <int KY, int KZ>
+template <int KY, int KZ, int TY = kS3TY, int TZ = kS3TZ>
 __host__ __device__ constexpr int s3_plane_positions() {
-  return (kS3TY + KY - 1) * (kS3TZ + KZ - 1);
+  return (TY + KY - 1) * (TZ + KZ - 1);
 }
 // ring depth: four planes for a 3D stencil, one for a 2D stencil run as one x plane
 template <int KX>
 __host__ __device__ constexpr int s3_ring() {
   return KX == 1 ? 1 : kS3Buf;
 }
-template <int KX, int KY, int KZ>
+template <int KX, int KY, int KZ, int TY = kS3TY, int TZ = kS3TZ>
 __host__ __device__ constexpr size_t s3_smem_bytes() {
-  return (size_t)s3_ring<KX>() * s3_plane_positions<KY, KZ>() * kElemCG * 2;  // 16-bit elements
+  return (size_t)s3_ring<KX>() * s3_plane_positions<KY, KZ, TY, TZ>() * kElemCG * 2;  // 16-bit elements
 }
 // the weight-gradient kernel reuses its ring for the CTA reduction [8 warps][taps + 1][64]
-template <int KX, int KY, int KZ>
+template <int KX, int KY, int KZ, int TY = kS3TY, int TZ = kS3TZ>
 __host__ __device__ constexpr size_t s3_wgrad_smem_bytes() {
-  return s3_smem_bytes<KX, KY, KZ>() > (size_t)8 * (KX * KY * KZ + 1) * kElemCG * 4
-             ? s3_smem_bytes<KX, KY, KZ>()
+  return s3_smem_bytes<KX, KY, KZ, TY, TZ>() > (size_t)8 * (KX * KY * KZ + 1) * kElemCG * 4
+             ? s3_smem_bytes<KX, KY, KZ, TY, TZ>()
              : (size_t)8 * (KX * KY * KZ + 1) * kElemCG * 4;
 }
 
@@ -52,13 +60,14 @@ struct S3Tile {
 };
 
 // Tile of this CTA: grid (ceil(C / 64), y tiles * z tiles, B * x chunks).
+template <int TY, int TZ>
 __device__ __forceinline__ S3Tile s3_tile(const StencilGeom& g, int xchunk) {
   S3Tile t;
-  const int nzt = (g.n[2] + kS3TZ - 1) / kS3TZ;
+  const int nzt = (g.n[2] + TZ - 1) / TZ;
   const int nxc = (g.n[0] + xchunk - 1) / xchunk;
   t.c0 = blockIdx.x * kElemCG;
-  t.y0 = (blockIdx.y / nzt) * kS3TY;
-  t.z0 = (blockIdx.y % nzt) * kS3TZ;
+  t.y0 = (blockIdx.y / nzt) * TY;
+  t.z0 = (blockIdx.y % nzt) * TZ;
   t.b = blockIdx.z / nxc;
   t.xa = (blockIdx.z % nxc) * xchunk;
   t.xb = min(g.n[0], t.xa + xchunk);
@@ -66,11 +75,11 @@ __device__ __forceinline__ S3Tile s3_tile(const StencilGeom& g, int xchunk) {
 }
 
 // cp.async of input plane xin of the tile (positions y0 - oy .. , z0 - oz ..) into a ring slot.
-template <typename T, int KY, int KZ>
+template <typename T, int KY, int KZ, int TY, int TZ>
 __device__ __forceinline__ void s3_load_plane(T* slot, const T* src, long long bst, long long pst,
                                               const StencilGeom& g, const S3Tile& t, int C, int xin, int oy,
                                               int oz) {
-  constexpr int ZW = kS3TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ>();
+  constexpr int ZW = TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ, TY, TZ>();
   const bool xok = xin >= 0 && xin < g.n[0];
   for (int q = threadIdx.x; q < NPOS * 8; q += blockDim.x) {
     const int pos = q >> 3, part = q & 7;
@@ -96,18 +105,20 @@ __device__ __forceinline__ float2 s3_ld(const T* p) {
 // MODE 1: in = dq'/dk'/dv' contiguous, out = dq/dk/dv (out_bst, out_pst):
 //   out[p] = sum_tap w[tap] in[p - tap + off], a forward stencil with flipped taps and
 //   left padding k - 1 - off.
-template <typename T, int KX, int KY, int KZ, int MODE>
-__global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_stencil_kernel(
+template <typename T, int KX, int KY, int KZ, int MODE, int TY = kS3TY, int TZ = kS3TZ>
+__global__ void __launch_bounds__(kElemThreads, (KX == 1 || KY == 1) ? 3 : 2) hyena_plane_stencil_kernel(
     const T* __restrict__ in0, const T* __restrict__ in1, const T* __restrict__ in2, long long in_bst,
     long long in_pst, T* __restrict__ out0, T* __restrict__ out1, T* __restrict__ out2, long long out_bst,
     long long out_pst, T* __restrict__ z, StencilGeom g, int C, const float* __restrict__ w,
     const float* __restrict__ bias, int gate1, int xchunk) {
-  constexpr int NT = KX * KY * KZ, ZW = kS3TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ>(), NB = s3_ring<KX>();
+  constexpr int NT = KX * KY * KZ, ZW = TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ, TY, TZ>(), NB = s3_ring<KX>();
+  constexpr int WPR = TZ / 16;  // warps per tile row, 16 z positions each
+  static_assert(TY * WPR == kElemThreads / 32, "one warp per 16 positions of the tile");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
-  const S3Tile t = s3_tile(g, xchunk);
+  const S3Tile t = s3_tile<TY, TZ>(g, xchunk);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int yl = warp >> 1, zw = (warp & 1) * (kS3TZ / 2);
+  const int yl = warp / WPR, zw = (warp % WPR) * 16;
   const int c = t.c0 + 2 * lane;
   const bool cok = c < C;
   const int ox = MODE == 0 ? g.off[0] : KX - 1 - g.off[0];
@@ -117,8 +128,6 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
   const long long ps = MODE == 0 ? in_pst : (long long)C;
   const long long bs = MODE == 0 ? in_bst : N * C;
   const int gy = t.y0 + yl;
-  const T* ins[3] = {in0, in1, in2};
-  T* outs[3] = {out0, out1, out2};
 
 #pragma unroll 1
   for (int ti = 0; ti < 3; ++ti) {
@@ -138,12 +147,14 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
     const float2 bs2 = (MODE == 0 && g.has_bias && bias && cok)
                            ? make_float2(__ldg(bias + (long long)ti * C + c), __ldg(bias + (long long)ti * C + c + 1))
                            : make_float2(0.f, 0.f);
-    const T* src = ins[ti];
+    // (pointers picked by value: an array indexed by ti would live in local memory)
+    const T* src = ti == 0 ? in0 : (ti == 1 ? in1 : in2);
+    T* dst = ti == 0 ? out0 : (ti == 1 ? out1 : out2);
     // prologue: the KX planes of the first output plane
 #pragma unroll 1
     for (int a = 0; a < KX; ++a) {
       const int xin = t.xa - ox + a;
-      s3_load_plane<T, KY, KZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, bs, ps, g, t, C, xin, oy,
+      s3_load_plane<T, KY, KZ, TY, TZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, bs, ps, g, t, C, xin, oy,
                                oz);
     }
 #pragma unroll 1
@@ -151,7 +162,7 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
       const bool pre = x + 1 < t.xb;
       if (pre) {
         const int xin = x - ox + KX;
-        s3_load_plane<T, KY, KZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, bs, ps, g, t, C, xin,
+        s3_load_plane<T, KY, KZ, TY, TZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, bs, ps, g, t, C, xin,
                                  oy, oz);
         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
       } else {
@@ -160,7 +171,7 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
       __syncthreads();
       if (cok && gy < g.n[1]) {
 #pragma unroll 1
-        for (int zb = 0; zb < kS3TZ / 2; zb += kS3ZU) {
+        for (int zb = 0; zb < 16; zb += kS3ZU) {
           float2 acc[kS3ZU];
 #pragma unroll
           for (int i = 0; i < kS3ZU; ++i) acc[i] = bs2;
@@ -172,7 +183,7 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
             for (int i = 0; i < kS3ZU; ++i) {
               const int gz = t.z0 + zw + zb + i;
               const long long o = ((long long)t.b * N + ((long long)x * g.n[1] + gy) * g.n[2] + gz) * C + c;
-              qpre[i] = gz < g.n[2] ? V2<T>::load(outs[0] + o) : make_float2(0.f, 0.f);
+              qpre[i] = gz < g.n[2] ? V2<T>::load(out0 + o) : make_float2(0.f, 0.f);
             }
           }
 #pragma unroll
@@ -189,8 +200,7 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
 #pragma unroll
                 for (int e = 0; e < KZ; ++e) {
                   const float2 wv = wr[(a * KY + bq) * KZ + e];
-                  acc[i].x = fmaf(wv.x, v[i + e].x, acc[i].x);
-                  acc[i].y = fmaf(wv.y, v[i + e].y, acc[i].y);
+                  acc[i] = ffma2(wv, v[i + e], acc[i]);
                 }
             }
           }
@@ -202,14 +212,14 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
             if constexpr (MODE == 0) {
               const long long o = ((long long)t.b * N + pos) * C + c;
               const float2 r = V2<T>::round(acc[i]);
-              V2<T>::store(outs[ti] + o, r);
+              V2<T>::store(dst + o, r);
               if (ti == 1) {  // z = q' * g1(k')
                 const float2 qv = qpre[i];
                 const float2 g1 = V2<T>::round(make_float2(gate_f(gate1, r.x), gate_f(gate1, r.y)));
                 V2<T>::store(z + o, make_float2(qv.x * g1.x, qv.y * g1.y));
               }
             } else {
-              V2<T>::store(outs[ti] + (long long)t.b * out_bst + pos * out_pst + c, acc[i]);
+              V2<T>::store(dst + (long long)t.b * out_bst + pos * out_pst + c, acc[i]);
             }
           }
         }
@@ -225,26 +235,26 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_ste
 // with in = q/k/v (in_bst, in_pst) and dout = dq'/dk'/dv' contiguous; db[t][c] = sum dout.
 // Per-thread accumulators for all taps, a shared-memory reduction over the CTA's warps,
 // one atomic per channel and tap per CTA (dw, db zeroed by the host).
-template <typename T, int KX, int KY, int KZ>
-__global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_wgrad_kernel(
+template <typename T, int KX, int KY, int KZ, int TY = kS3TY, int TZ = kS3TZ>
+__global__ void __launch_bounds__(kElemThreads, (KX == 1 || KY == 1) ? 3 : 2) hyena_plane_wgrad_kernel(
     const T* __restrict__ d0, const T* __restrict__ d1, const T* __restrict__ d2, const T* __restrict__ in0,
     const T* __restrict__ in1, const T* __restrict__ in2, long long in_bst, long long in_pst, StencilGeom g, int C,
     float* __restrict__ dw, float* __restrict__ db, int xchunk) {
-  constexpr int NT = KX * KY * KZ, ZW = kS3TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ>(), NB = s3_ring<KX>();
+  constexpr int NT = KX * KY * KZ, ZW = TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ, TY, TZ>(), NB = s3_ring<KX>();
   constexpr int NW = kElemThreads / 32;
+  constexpr int WPR = TZ / 16;  // warps per tile row, 16 z positions each
+  static_assert(TY * WPR == NW, "one warp per 16 positions of the tile");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* ring = reinterpret_cast<T*>(smem_raw);
   float* red = reinterpret_cast<float*>(smem_raw);  // [NW][NT + 1][64] after the march
-  const S3Tile t = s3_tile(g, xchunk);
+  const S3Tile t = s3_tile<TY, TZ>(g, xchunk);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int yl = warp >> 1, zw = (warp & 1) * (kS3TZ / 2);
+  const int yl = warp / WPR, zw = (warp % WPR) * 16;
   const int c = t.c0 + 2 * lane;
   const bool cok = c < C;
   const int ox = g.off[0], oy = g.off[1], oz = g.off[2];
   const long long N = (long long)g.n[0] * g.n[1] * g.n[2];
   const int gy = t.y0 + yl;
-  const T* ds[3] = {d0, d1, d2};
-  const T* ins[3] = {in0, in1, in2};
 
 #pragma unroll 1
   for (int ti = 0; ti < 3; ++ti) {
@@ -252,12 +262,12 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_wgr
 #pragma unroll
     for (int j = 0; j < NT; ++j) acc[j] = make_float2(0.f, 0.f);
     float2 accb = make_float2(0.f, 0.f);
-    const T* src = ins[ti];
-    const T* dsrc = ds[ti];
+    const T* src = ti == 0 ? in0 : (ti == 1 ? in1 : in2);
+    const T* dsrc = ti == 0 ? d0 : (ti == 1 ? d1 : d2);
 #pragma unroll 1
     for (int a = 0; a < KX; ++a) {
       const int xin = t.xa - ox + a;
-      s3_load_plane<T, KY, KZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, in_bst, in_pst, g, t, C,
+      s3_load_plane<T, KY, KZ, TY, TZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, in_bst, in_pst, g, t, C,
                                xin, oy, oz);
     }
 #pragma unroll 1
@@ -265,7 +275,7 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_wgr
       const bool pre = x + 1 < t.xb;
       if (pre) {
         const int xin = x - ox + KX;
-        s3_load_plane<T, KY, KZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, in_bst, in_pst, g, t,
+        s3_load_plane<T, KY, KZ, TY, TZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, in_bst, in_pst, g, t,
                                  C, xin, oy, oz);
         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
       } else {
@@ -279,14 +289,14 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_wgr
           for (int i = 0; i < kS3ZU; ++i) {
             const int gz = t.z0 + zw + zb + i;
             const long long pos = ((long long)x * g.n[1] + gy) * g.n[2] + gz;
-            dv[i] = (zb < kS3TZ / 2 && gz < g.n[2]) ? V2<T>::load(dsrc + ((long long)t.b * N + pos) * C + c)
+            dv[i] = (zb < 16 && gz < g.n[2]) ? V2<T>::load(dsrc + ((long long)t.b * N + pos) * C + c)
                                                     : make_float2(0.f, 0.f);
           }
         };
         float2 dnext[kS3ZU];
         ld_dout(0, dnext);
 #pragma unroll 1
-        for (int zb = 0; zb < kS3TZ / 2; zb += kS3ZU) {
+        for (int zb = 0; zb < 16; zb += kS3ZU) {
           float2 dv[kS3ZU];
 #pragma unroll
           for (int i = 0; i < kS3ZU; ++i) {
@@ -309,8 +319,7 @@ __global__ void __launch_bounds__(kElemThreads, KX == 1 ? 3 : 2) hyena_plane_wgr
                 float2& ac = acc[(a * KY + bq) * KZ + e];
 #pragma unroll
                 for (int i = 0; i < kS3ZU; ++i) {
-                  ac.x = fmaf(dv[i].x, v[i + e].x, ac.x);
-                  ac.y = fmaf(dv[i].y, v[i + e].y, ac.y);
+                  ac = ffma2(dv[i], v[i + e], ac);
                 }
               }
             }
