@@ -7,8 +7,10 @@ One "step" = forward + backward of the fused Hyena mixer (configs 1-3: short dep
 conv, gates, FFT long conv with D-skip) or of the op-level causal conv (config 0) on one
 batch of seeded synthetic input. Inputs are resident in HBM for ``value``; ``e2e`` runs
 the same step through the public API from pinned host buffers: the H2D copy of every
-input and the D2H copy of the step's output y are inside the timed region, while the
-gradients stay on the device (where an optimizer step would read them).
+input and the D2H copy of the step's output y are inside the timed region (the next
+step's inputs are copied on a second stream while the current step computes, as a
+training loop prefetches its next batch), while the gradients stay on the device (where
+an optimizer step would read them).
 
 Default workload: config 2 (B=8, C=256, 128x128, bf16). On one GPU the run also measures
 config 1 (the ViT grid) the same way and reports it under ``secondary``.
@@ -531,63 +533,89 @@ def run_gpu(args, cfg, rank, world, device):
 
 
 def e2e_time(cfg, inp, device, op_only, steps, dp_group=None):
+    """End-to-end steps through the public API from pinned host buffers.
+
+    Every step copies all of its inputs (activations, upstream gradient and the parameters)
+    host -> device, runs forward + backward through hyena_fused / the op API, and copies its
+    result y device -> host. The copies of step i + 1 run on a copy stream while step i
+    computes (two device slots per input), the way a training loop prefetches its next
+    batch; the time is the device span from the first copy of the first timed step to the
+    last device -> host copy, divided by the number of steps. Returns (ms per step, H2D
+    bytes per step, D2H bytes per step, ms of one step's H2D copies alone)."""
     from nvsubquadratic_b200.dp import GradBucket
     from nvsubquadratic_b200.fftconv import causal_fftconv1d_fp32_bhl
     from nvsubquadratic_b200.hyena import hyena_fused
 
-    host = {k: (v.pin_memory() if v is not None else None) for k, v in inp.items()}
+    names = ["x", "filt", "D", "dy"] if op_only else ["qkv", "filt", "D", "sw", "dy"]
+    host = {k: inp[k].pin_memory() for k in names if inp.get(k) is not None}
     # the host->device copies alone (same pinned buffers), to separate link time from the rest
     copy_times = []
     for _ in range(5):
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record()
-        _tmp = [t.to(device, non_blocking=True) for t in host.values() if t is not None]
+        _tmp = [t.to(device, non_blocking=True) for t in host.values()]
         b.record()
         torch.cuda.synchronize()
         copy_times.append(a.elapsed_time(b))
         del _tmp
-    outs = {}
-    h2d = d2h = 0
-    times = []
-    for i in range(steps + 3):
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
+    main = torch.cuda.current_stream(device)
+    cs = torch.cuda.Stream(device)
+    slots = [{k: torch.empty(v.shape, dtype=v.dtype, device=device) for k, v in host.items()} for _ in range(2)]
+    copied = [torch.cuda.Event() for _ in range(2)]
+    freed = [torch.cuda.Event() for _ in range(2)]
+    for e in freed:
+        e.record(main)
+    out = None
+
+    def issue_copy(i):
+        s = i % 2
+        with torch.cuda.stream(cs):
+            cs.wait_event(freed[s])  # step i - 2 is done with this slot
+            for k, v in host.items():
+                slots[s][k].copy_(v, non_blocking=True)
+            copied[s].record(cs)
+
+    def run_step(i):
+        nonlocal out
+        s = i % 2
+        main.wait_event(copied[s])
+        d = {k: v.detach().requires_grad_(k != "dy") for k, v in slots[s].items()}
         if op_only:
-            x = host["x"].to(device, non_blocking=True).requires_grad_(True)
-            f = host["filt"].to(device, non_blocking=True).requires_grad_(True)
-            D = host["D"].to(device, non_blocking=True).requires_grad_(True)
-            dy = host["dy"].to(device, non_blocking=True)
-            y = causal_fftconv1d_fp32_bhl(x, f, D)
-            y.backward(dy)
-            res = [y]  # the step's result; the gradients stay on the device for the optimizer
-            ins = [host["x"], host["filt"], host["D"], host["dy"]]
+            y = causal_fftconv1d_fp32_bhl(d["x"], d["filt"], d["D"])
         else:
-            qkv = host["qkv"].to(device, non_blocking=True).requires_grad_(True)
-            f = host["filt"].to(device, non_blocking=True).requires_grad_(True)
-            D = host["D"].to(device, non_blocking=True).requires_grad_(True)
-            sw = host["sw"].to(device, non_blocking=True).requires_grad_(True) if host["sw"] is not None else None
-            dy = host["dy"].to(device, non_blocking=True)
-            q, k, v = qkv.chunk(3, dim=-1)
-            y = hyena_fused(q, k, v, f, D, sw, None, causal=cfg["causal"], gate1=cfg["g1"], gate2=cfg["g2"])
-            y.backward(dy)
-            if dp_group is not None:  # batch shards: full-batch parameter gradients
-                GradBucket([f, D, sw], device).reduce(dp_group)
-            res = [y]  # the step's result; the gradients stay on the device for the optimizer
-            ins = [host["qkv"], host["filt"], host["D"], host["dy"]] + ([host["sw"]] if sw is not None else [])
-        if not outs:
-            outs = [torch.empty(r.shape, dtype=r.dtype, pin_memory=True) for r in res]
-        for o, r in zip(outs, res):
-            o.copy_(r, non_blocking=True)
-        b.record()
-        torch.cuda.synchronize()
-        if i >= 3:
-            times.append(a.elapsed_time(b))
-        h2d = sum(t.numel() * t.element_size() for t in ins)
-        d2h = sum(r.numel() * r.element_size() for r in res)
-    # median step: one host-side stall (allocator, scheduler) must not stand for the path
-    return statistics.median(times), h2d, d2h, statistics.median(copy_times[1:])
+            q, k, v = d["qkv"].chunk(3, dim=-1)
+            y = hyena_fused(q, k, v, d["filt"], d["D"], d.get("sw"), None, causal=cfg["causal"], gate1=cfg["g1"],
+                            gate2=cfg["g2"])
+        y.backward(d["dy"])
+        if dp_group is not None:  # batch shards: full-batch parameter gradients
+            GradBucket([d["filt"], d["D"], d.get("sw")], device).reduce(dp_group)
+        if out is None:
+            out = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        out.copy_(y, non_blocking=True)  # the step's result; gradients stay on the device
+        freed[s].record(main)
+        return y
+
+    n_warm = 3
+    issue_copy(0)
+    for i in range(n_warm):
+        if i + 1 < n_warm:
+            issue_copy(i + 1)
+        run_step(i)
+    torch.cuda.synchronize()
+    # timed: exactly `steps` copies in, `steps` fwd+bwd, `steps` copies out
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(main)
+    issue_copy(n_warm)
+    for i in range(steps):
+        if i + 1 < steps:
+            issue_copy(n_warm + i + 1)
+        run_step(n_warm + i)
+    t1.record(main)
+    torch.cuda.synchronize()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out.numel() * out.element_size()
+    return t0.elapsed_time(t1) / steps, h2d, d2h, statistics.median(copy_times[1:])
 
 
 def measure_filter_gen(device, steps: int, warmup: int) -> dict:
@@ -774,7 +802,9 @@ def main():
             "e2e": {"value": round(e2e_val, 4), "unit": "GElem/s", "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"], "ms_per_step": round(res["e2e_ms"], 4),
                     "h2d_copy_ms": round(res["copy_ms"], 4) if res.get("copy_ms") is not None else None,
-                    "stat": "median step (eager, through hyena_fused / the op API)"},
+                    "stat": "mean over the timed steps (eager, through hyena_fused / the op API); every step's "
+                            "inputs copied H2D from pinned memory and y copied D2H, the next step's H2D overlapped "
+                            "with this step's compute on a copy stream"},
             "gpu_launches": res["launches"] * args.steps,
             "clocks": res["clocks"],
         }

@@ -349,22 +349,24 @@ __device__ __forceinline__ void rows_load(const Big2DView& in, int b, int c, int
   }
 }
 
-// Forward row transforms of rows [2 pr, 2 pr + 1] of input view `in` for image (b, c):
-// bins j in [jlo, jlo + jn) go to dst[r * ld + j - jlo]. All threads of the CTA call it.
-// The next round's rows are loaded before this round's transform, so their global-memory
-// latency overlaps the arithmetic.
-template <typename T, int F>
+// Forward row transforms of the row pairs pr0 .. pr0 + npr - 1 (rows 2 pr, 2 pr + 1) of
+// input view `in` for image (b, c), NG transform groups: bins j in [jlo, jlo + jn) of row
+// r go to dst[(r - 2 pr0) * ld + j - jlo]. All threads of the CTA call it. The next
+// round's rows are loaded before this round's transform, so their global-memory latency
+// overlaps the arithmetic.
+template <typename T, int F, int NG>
 __device__ __forceinline__ void rows_forward(const Big2DView& in, int b, int c, int N0, int N1, float2* dst, int ld,
-                                             int jlo, int jn, float2* sc, const float2* tw) {
+                                             int jlo, int jn, float2* sc, const float2* tw, int pr0 = 0,
+                                             int npr = kB2MaxN / 2) {
   using G = B2<F>;
   const int g = threadIdx.x >> 4, l = threadIdx.x & 15;
   const int npairs = (N0 + 1) >> 1;
-  const int rounds = (npairs + kBigGroups - 1) / kBigGroups;
+  const int rounds = (npr + NG - 1) / NG;
   float2 nxt[8];
-  rows_load<T>(in, b, c, N0, N1, g, l, nxt);
+  rows_load<T>(in, b, c, N0, N1, g < npr ? pr0 + g : npairs, l, nxt);
   for (int rb = 0; rb < rounds; ++rb) {
-    const int pr = rb * kBigGroups + g;
-    const bool act = pr < npairs;
+    const int pl = rb * NG + g, pr = pr0 + pl;
+    const bool act = pl < npr && pr < npairs;
     const int r0 = 2 * pr, r1 = r0 + 1;
     const bool has1 = act && r1 < N0;
     float2 v[16];
@@ -373,17 +375,18 @@ __device__ __forceinline__ void rows_forward(const Big2DView& in, int b, int c, 
       v[m] = nxt[m];
       v[m + 8] = make_float2(0.f, 0.f);
     }
-    if (rb + 1 < rounds) rows_load<T>(in, b, c, N0, N1, pr + kBigGroups, l, nxt);
+    if (rb + 1 < rounds) rows_load<T>(in, b, c, N0, N1, pl + NG < npr ? pr + NG : npairs, l, nxt);
     fwdT<F, true>(v, sc, tw, l, -1.f);
     float2 A[9], Bv[9];
     split_pair<G::R>(v, l, A, Bv);
     if (act && l < G::R) {
+      float2* d0 = dst + (r0 - 2 * pr0) * ld - jlo;
 #pragma unroll
       for (int m = 0; m <= 8; ++m) {
-        const int j = l + G::R * m - jlo;
-        if (j >= 0 && j < jn && j + jlo < G::H) {
-          dst[r0 * ld + j] = A[m];
-          if (has1) dst[r1 * ld + j] = Bv[m];
+        const int j = l + G::R * m;
+        if (j >= jlo && j < jlo + jn && j < G::H) {
+          d0[j] = A[m];
+          if (has1) d0[ld + j] = Bv[m];
         }
       }
     }
@@ -391,8 +394,8 @@ __device__ __forceinline__ void rows_forward(const Big2DView& in, int b, int c, 
 }
 
 // ---------------------------------------------------------------- convolution
-// Per-group transpose scratch of b2_conv (float2): the 16 x 13 tile of the 192-point
-// transforms, the 16 x 17 tile of the 256-point ones.
+// Per-group transpose scratch of the conv kernels (float2): the 16 x 13 tile of the
+// 192-point transforms, the 16 x 17 tile of the 256-point ones.
 template <int F>
 constexpr int conv_sc() {
   return F == 192 ? 16 * kSc12 : kScSize;
@@ -422,60 +425,61 @@ __device__ __forceinline__ void stage_col(float2* dst, const float2* src, int l)
   for (int i = l; i < F / 2; i += 16) cp16(dst + 2 * i, src + 2 * i);
 }
 
-template <typename T, int F>
-__global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
+// Shared-memory layout behind the row half-spectra of a conv CTA (NG groups):
+// sc [NG][conv_sc] | tw [F] | ext [3][F] | zb [NG][F] (zs_mode 2 staging, F = 192 only).
+// ext holds the packed task's extra operands: the filter-spectrum column F/2 and, with
+// zs_mode 2, the image's kept Zs columns 0 and F/2.
+template <int F, int NG>
+constexpr size_t conv_tail_floats2(bool zstage) {
+  return (size_t)NG * conv_sc<F>() + 4 * F + (zstage ? (size_t)NG * F : 0);
+}
+
+// Prologue copies (cp.async, one commit group): the packed task's extra operands when this
+// CTA runs task 0, and with zstage the kept Zs column of this group's first task.
+template <int F, int NT>
+__device__ __forceinline__ void conv_prologue(const Big2DParams& p, int b, int c, float2* ext, float2* myzb,
+                                              int first_task, bool has_packed, bool zstage) {
   using G = B2<F>;
-  constexpr int H = G::H, R = G::R, SCS = conv_sc<F>(), LD = conv_ld<F>();
-  extern __shared__ __align__(16) unsigned char smem[];
-  float2* A = reinterpret_cast<float2*>(smem);                  // [128][H]
-  float2* sc = A + kB2MaxN * H;                                  // [32][SCS]
-  float2* tw = sc + kBigGroups * SCS;                            // [F]
-  float2* ext = tw + F;        // [3][F]: Kh column F/2; zs_mode 2: the image's kept Zs columns 0 and F/2
-  float2* zb = ext + 3 * F;    // [32][F]: zs_mode 2, F = 192: each group's next kept Zs column
-  const int g = threadIdx.x >> 4, l = threadIdx.x & 15;
-  // channels-last inputs: neighbouring channels of one image run together (shared
-  // sectors); channel-major: the batch items of one channel do (shared filter spectrum)
-  const bool cfast = p.x.cst == 1;
-  const int c = cfast ? blockIdx.x : blockIdx.y, b = cfast ? blockIdx.y : blockIdx.x;
-  const int N0 = p.N0, N1 = p.N1;
-  const bool sl = l < R;  // lane holds spectral values
-  const bool zstage = conv_zstage<F>() && p.zs_mode == 2;
-  float2* mysc = sc + g * SCS;
-  float2* myzb = zb + g * F;
-  const float2* kh = p.Kh + (long long)c * H * F;
-  const float2* zimg = p.Zs + ((long long)b * p.C + c) * H * F;  // this image's kept column spectra
-  // the packed task's extra operands and round 0's kept Zs columns, copied while the
-  // rows are transformed
-  for (int i = threadIdx.x; i < F / 2; i += kBigThreads) cp16(ext + 2 * i, kh + (long long)(F / 2) * F + 2 * i);
-  if (p.zs_mode == 2) {
-    for (int i = threadIdx.x; i < F / 2; i += kBigThreads) {
-      cp16(ext + F + 2 * i, zimg + 2 * i);
-      cp16(ext + 2 * F + 2 * i, zimg + (long long)(F / 2) * F + 2 * i);
+  const float2* kh = p.Kh + (long long)c * G::H * F;
+  const float2* zimg = p.Zs + ((long long)b * p.C + c) * G::H * F;
+  if (has_packed) {
+    for (int i = threadIdx.x; i < F / 2; i += NT) cp16(ext + 2 * i, kh + (long long)(F / 2) * F + 2 * i);
+    if (p.zs_mode == 2) {
+      for (int i = threadIdx.x; i < F / 2; i += NT) {
+        cp16(ext + F + 2 * i, zimg + 2 * i);
+        cp16(ext + 2 * F + 2 * i, zimg + (long long)(F / 2) * F + 2 * i);
+      }
     }
-    if (zstage && g > 0) stage_col<F>(myzb, zimg + (long long)g * F, l);
   }
+  if (zstage && first_task > 0) stage_col<F>(myzb, zimg + (long long)first_task * F, threadIdx.x & 15);
   cp_commit();
-  init_tw<F>(tw);
-  __syncthreads();
+}
 
-  rows_forward<T, F>(p.x, b, c, N0, N1, A, H, 0, H, mysc, tw);
-  cp_wait_all();
-  __syncthreads();
-
-  // columns: transform, * Kh (or conj), inverse, keep rows [0, N0). Task t handles
-  // column t; task 0 handles columns 0 and F/2 together (both real along the rows).
-  // Each round's filter-spectrum column (an L2 read) is loaded one round ahead, right
-  // after the previous column has consumed its own, so the load overlaps an inverse and
-  // a forward transform; with zs_mode 2 the next round's kept Zs column is copied to
-  // shared memory at the same point.
+// Column phase: tasks t0 .. t0 + ntask - 1 (task t: column t; task 0: columns 0 and F/2,
+// both real along the rows, as one complex column) by NG groups, ntask / NG rounds.
+// Row r of the half-spectra is at (r < 64 ? Alo : Ahi)[(r & 63) * H + j]. Each column: transform, * Kh (or conj), inverse,
+// keep rows [0, N0). Each round's filter-spectrum column (an L2 read) is loaded one round
+// ahead, right after the previous column has consumed its own, so the load overlaps an
+// inverse and a forward transform; with zs_mode 2 the next round's kept Zs column is
+// copied to shared memory at the same point.
+template <int F, int NG>
+__device__ __forceinline__ void column_phase(const Big2DParams& p, float2* Alo, float2* Ahi, int t0, int ntask, int b,
+                                             int c, float2* mysc, float2* myzb, const float2* ext, const float2* tw,
+                                             bool zstage) {
+  using G = B2<F>;
+  constexpr int H = G::H, R = G::R, LD = conv_ld<F>();
+  const int g = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const bool sl = l < R;  // lane holds spectral values
+  const int N0 = p.N0;
+  const float2* kh = p.Kh + (long long)c * H * F;
+  const float2* zimg = p.Zs + ((long long)b * p.C + c) * H * F;
   const float cj = p.conj ? -1.f : 1.f;
-  constexpr int kColRounds = G::TASKS / kBigGroups;
-  static_assert(G::TASKS % kBigGroups == 0, "whole column rounds");
+  const int rounds = ntask / NG;
   float2 kv[16];
 #pragma unroll
-  for (int m = 0; m < 16; ++m) kv[m] = sl ? __ldg(kh + (long long)g * F + l + R * m) : make_float2(0.f, 0.f);
-  for (int rb = 0; rb < kColRounds; ++rb) {
-    const int j = rb * kBigGroups + g;
+  for (int m = 0; m < 16; ++m) kv[m] = sl ? __ldg(kh + (long long)(t0 + g) * F + l + R * m) : make_float2(0.f, 0.f);
+  for (int rb = 0; rb < rounds; ++rb) {
+    const int j = t0 + rb * NG + g;
     const bool packed = j == 0;
     float2 v[16];
 #pragma unroll
@@ -483,8 +487,9 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
       const int r = l + 16 * m;
       v[m] = make_float2(0.f, 0.f);
       if (m < 8 && r < N0) {
-        if (packed) v[m] = make_float2(A[r * H].x, A[r * H + F / 2].x);
-        else v[m] = A[r * H + j];
+        const float2* row = (m < 4 ? Alo : Ahi) + (r & 63) * H;
+        if (packed) v[m] = make_float2(row[0].x, row[F / 2].x);
+        else v[m] = row[j];
       }
     }
     fwdT<F, true>(v, mysc, tw, l, -1.f);
@@ -558,8 +563,8 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
         v[m] = make_float2(p0.x - pH.y, p0.y + pH.x);  // p0 + i pH
       }
     }
-    const int jn = j + kBigGroups;
-    if (rb + 1 < kColRounds) {
+    const int jn = j + NG;
+    if (rb + 1 < rounds) {
 #pragma unroll
       for (int m = 0; m < 16; ++m) kv[m] = sl ? __ldg(kh + (long long)jn * F + l + R * m) : make_float2(0.f, 0.f);
       if (zstage) {  // every lane of the group is done with this round's staged column
@@ -573,27 +578,39 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
     for (int m = 0; m < 8; ++m) {
       const int r = l + 16 * m;
       if (r < N0) {
+        float2* row = (m < 4 ? Alo : Ahi) + (r & 63) * H;
         if (packed) {
-          A[r * H] = make_float2(v[m].x, 0.f);
-          A[r * H + F / 2] = make_float2(v[m].y, 0.f);
+          row[0] = make_float2(v[m].x, 0.f);
+          row[F / 2] = make_float2(v[m].y, 0.f);
         } else {
-          A[r * H + j] = v[m];
+          row[j] = v[m];
         }
       }
     }
   }
-  __syncthreads();
+}
 
-  // inverse rows two at a time, epilogue
+// Inverse row transforms of the row pairs pr0 .. pr0 + npr - 1, two rows as one complex
+// line, and the epilogue (scale, D-skip, dtype rounding, store). Row r's half spectrum is
+// at A[(r - 2 pr0) * H].
+template <typename T, int F, int NG>
+__device__ __forceinline__ void rows_inverse(const Big2DParams& p, const float2* A, int b, int c, int pr0, int npr,
+                                             float2* mysc, const float2* tw) {
+  using G = B2<F>;
+  constexpr int H = G::H, R = G::R;
+  const int g = threadIdx.x >> 4, l = threadIdx.x & 15;
+  const bool sl = l < R;
+  const int N0 = p.N0, N1 = p.N1;
   const float scale = 1.0f / (float)(F * F);
   const int npairs = (N0 + 1) >> 1;
   const float Dc = p.D ? p.D[c] : 0.f;
   T* yo = reinterpret_cast<T*>(const_cast<void*>(p.y.ptr)) + (long long)b * p.y.bst + (long long)c * p.y.cst;
-  for (int rb = 0; rb < (npairs + kBigGroups - 1) / kBigGroups; ++rb) {
-    const int pr = rb * kBigGroups + g;
-    const bool act = pr < npairs;
+  for (int rb = 0; rb < (npr + NG - 1) / NG; ++rb) {
+    const int pl = rb * NG + g, pr = pr0 + pl;
+    const bool act = pl < npr && pr < npairs;
     const int r0 = 2 * pr, r1 = r0 + 1;
     const bool has1 = act && r1 < N0;
+    const float2* a0 = A + (r0 - 2 * pr0) * H;
     float2 v[16];
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
@@ -601,13 +618,13 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
       float2 a = make_float2(0.f, 0.f), bb = make_float2(0.f, 0.f);
       if (act && sl) {
         if (j < H) {
-          a = A[r0 * H + j];
-          if (has1) bb = A[r1 * H + j];
+          a = a0[j];
+          if (has1) bb = a0[H + j];
         } else {
-          a = A[r0 * H + (F - j)];
+          a = a0[F - j];
           a.y = -a.y;
           if (has1) {
-            bb = A[r1 * H + (F - j)];
+            bb = a0[H + F - j];
             bb.y = -bb.y;
           }
         }
@@ -616,7 +633,7 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
     }
     // the D-skip inputs of these two rows, loaded before the transform
     float2 xs[8];
-    if (p.D) rows_load<T>(p.x, b, c, N0, N1, pr, l, xs);
+    if (p.D) rows_load<T>(p.x, b, c, N0, N1, act ? pr : npairs, l, xs);
     invT<F, true>(v, mysc, tw, l, 1.f);
     if (act) {
 #pragma unroll
@@ -634,6 +651,36 @@ __global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
       }
     }
   }
+}
+
+// One CTA per image (b, c): all 128 rows of the half spectra in shared memory, 32 groups.
+template <typename T, int F>
+__global__ void __launch_bounds__(kBigThreads) b2_conv(const Big2DParams p) {
+  using G = B2<F>;
+  constexpr int H = G::H;
+  extern __shared__ __align__(16) unsigned char smem[];
+  float2* A = reinterpret_cast<float2*>(smem);                  // [128][H]
+  float2* sc = A + kB2MaxN * H;                                  // [32][conv_sc]
+  float2* tw = sc + kBigGroups * conv_sc<F>();                   // [F]
+  float2* ext = tw + F;                                          // [3][F]
+  float2* zb = ext + 3 * F;                                      // [32][F]
+  const int g = threadIdx.x >> 4;
+  // channels-last inputs: neighbouring channels of one image run together (shared
+  // sectors); channel-major: the batch items of one channel do (shared filter spectrum)
+  const bool cfast = p.x.cst == 1;
+  const int c = cfast ? blockIdx.x : blockIdx.y, b = cfast ? blockIdx.y : blockIdx.x;
+  const bool zstage = conv_zstage<F>() && p.zs_mode == 2;
+  float2* mysc = sc + g * conv_sc<F>();
+  float2* myzb = zb + g * F;
+  conv_prologue<F, kBigThreads>(p, b, c, ext, myzb, g, true, zstage);
+  init_tw<F>(tw);
+  __syncthreads();
+  rows_forward<T, F, kBigGroups>(p.x, b, c, p.N0, p.N1, A, H, 0, H, mysc, tw);
+  cp_wait_all();
+  __syncthreads();
+  column_phase<F, kBigGroups>(p, A, A + 64 * H, 0, G::TASKS, b, c, mysc, myzb, ext, tw, zstage);
+  __syncthreads();
+  rows_inverse<T, F, kBigGroups>(p, A, b, c, 0, kB2MaxN / 2, mysc, tw);
 }
 
 // ---------------------------------------------------------------- filter gradient
@@ -658,8 +705,8 @@ __global__ void __launch_bounds__(kBigThreads) b2_dk(const Big2DParams p) {
   float2* Gc = p.G + (long long)c * H * F;
   for (int h = 0; h < 2; ++h) {
     const int jlo = h ? HALF : 0, jn = h ? H - HALF : HALF;
-    rows_forward<T, F>(p.x, b, c, N0, N1, Ax, HALF, jlo, jn, mysc, tw);
-    rows_forward<T, F>(p.x2, b, c, N0, N1, Ay, HALF, jlo, jn, mysc, tw);
+    rows_forward<T, F, kBigGroups>(p.x, b, c, N0, N1, Ax, HALF, jlo, jn, mysc, tw);
+    rows_forward<T, F, kBigGroups>(p.x2, b, c, N0, N1, Ay, HALF, jlo, jn, mysc, tw);
     __syncthreads();
     for (int rb = 0; rb < (jn + kBigGroups - 1) / kBigGroups; ++rb) {
       const int jj = rb * kBigGroups + g;
@@ -757,8 +804,7 @@ __global__ void __launch_bounds__(kThreads) b2_dfilt_rows(const Big2DParams p) {
 
 template <int F>
 constexpr size_t conv_smem(bool zstage) {
-  return sizeof(float2) * ((size_t)kB2MaxN * B2<F>::H + kBigGroups * conv_sc<F>() + 4 * F +
-                           (zstage ? (size_t)kBigGroups * F : 0));
+  return sizeof(float2) * ((size_t)kB2MaxN * B2<F>::H + conv_tail_floats2<F, kBigGroups>(zstage));
 }
 template <int F>
 constexpr size_t dk_smem() {
