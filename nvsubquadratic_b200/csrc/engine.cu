@@ -1501,6 +1501,27 @@ static int cl_cm(const T* src, T* dst, int B, long long N, int C, bool to_cm, cu
   return check_launch("cl_cm_transpose_kernel");
 }
 
+// The gates fused with the layout change around the large-grid kernels (cl_cm_gate_kernel),
+// where the shape and the pointers allow: 16-bit activations, C and N multiples of 64,
+// every tensor contiguous and 16-byte aligned.
+static bool gate_x_ok(int eb, int C, long long N, std::initializer_list<const void*> ps) {
+  if (eb != 2 || C % 64 || N % 64 || getenv("HYFFT_DISABLE_GATE_FUSION")) return false;
+  for (const void* q : ps)
+    if (((uintptr_t)q % 16) != 0) return false;
+  return true;
+}
+template <typename T, int MODE>
+static int gate_x(const T* a, const T* b1, const T* b2, T* o1, T* o2, int gate, int B, long long N, int C,
+                  cudaStream_t st) {
+  if constexpr (sizeof(T) != 2) {
+    return fail(HYFFT_ERR_UNSUPPORTED, "cl_cm_gate_kernel: 16-bit activations only");
+  } else {
+    const dim3 grid((unsigned)(N / 64), (unsigned)(C / 64), (unsigned)B);
+    cl_cm_gate_kernel<T, MODE><<<grid, 256, 0, st>>>(a, b1, b2, o1, o2, gate, N, C);
+    return check_launch("cl_cm_gate_kernel");
+  }
+}
+
 // ---- launch helpers of the elementwise / stencil kernels (hyena_elem.cuh)
 template <int V> using IC = std::integral_constant<int, V>;
 
@@ -1691,6 +1712,10 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
     HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
     HY_TRY(big2d_forward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
                          real_view(hc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), ws, st, zs, khs));
+    // h back to channels-last and gate 2 in one pass where the output is contiguous
+    if (d.out_pos_stride == d.channels && d.out_batch_stride == h.Ntot * d.channels &&
+        gate_x_ok(sizeof(T), d.channels, h.Ntot, {hc, hb, vs, y}))
+      return gate_x<T, GATE_POST_FWD>(hc, vs, nullptr, hb, y, d.gate2, d.batch, h.Ntot, d.channels, st);
     HY_TRY(cl_cm<T>(hc, hb, d.batch, h.Ntot, d.channels, false, st));
   } else {
     for (int c0 = 0; c0 < p.C; c0 += p.Cc) {
@@ -1739,13 +1764,28 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
   auto red_rows = [&](int cols) {
     return std::max<long long>(1, std::min<long long>(65535, 1200 / std::max(1, cols)));
   };
-  if (pair)
-    hyena_bwd_gate2_kernel<T, true><<<eg, kElemThreads, 0, st>>>(dy, d.out_batch_stride, d.out_pos_stride, hb, vs,
-                                                                 d.gate2, h.Ntot, d.batch, d.channels, dh, dvp);
-  else
-    hyena_bwd_gate2_kernel<T, false><<<eg, kElemThreads, 0, st>>>(dy, d.out_batch_stride, d.out_pos_stride, hb, vs,
-                                                                  d.gate2, h.Ntot, d.batch, d.channels, dh, dvp);
-  HY_TRY(check_launch("hyena_bwd_gate2_kernel"));
+  // large grid: channel-major copies of z, dh, dz around the large-grid kernels; the gates
+  // on either side of them are fused with the layout changes where gate_x_ok allows (gate 2
+  // only when the adjoint also forms the filter gradient, the path that needs no
+  // channels-last dh)
+  T* zc = p.big2d ? (T*)(ws + cb + 5 * act + align_up((size_t)d.channels * 4)) : nullptr;
+  T* dhc = p.big2d ? (T*)((char*)zc + act) : nullptr;
+  T* dzc = p.big2d ? (T*)((char*)dhc + act) : nullptr;
+  const bool fuse2 = p.big2d && dfilt != nullptr && d.out_pos_stride == d.channels &&
+                     d.out_batch_stride == h.Ntot * d.channels &&
+                     gate_x_ok(sizeof(T), d.channels, h.Ntot, {dy, hb, vs, dvp, dhc});
+  const bool fuse1 = p.big2d && gate_x_ok(sizeof(T), d.channels, h.Ntot, {dzc, qs, ks, dqp, dkp});
+  if (fuse2) {
+    HY_TRY((gate_x<T, GATE_BWD2>(dy, hb, vs, dvp, dhc, d.gate2, d.batch, h.Ntot, d.channels, st)));
+  } else {
+    if (pair)
+      hyena_bwd_gate2_kernel<T, true><<<eg, kElemThreads, 0, st>>>(dy, d.out_batch_stride, d.out_pos_stride, hb,
+                                                                   vs, d.gate2, h.Ntot, d.batch, d.channels, dh, dvp);
+    else
+      hyena_bwd_gate2_kernel<T, false><<<eg, kElemThreads, 0, st>>>(dy, d.out_batch_stride, d.out_pos_stride, hb,
+                                                                    vs, d.gate2, h.Ntot, d.batch, d.channels, dh, dvp);
+    HY_TRY(check_launch("hyena_bwd_gate2_kernel"));
+  }
   // long conv backward: dz = convT(dh) + D*dh, dfilt, dD
   {
     const size_t sx = align_up((size_t)p.spec_x_bytes_per_ch * p.Cc);
@@ -1766,16 +1806,12 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     if (p.big2d) {
       float2* zsp = zs ? (float2*)const_cast<char*>(saved + 5 * act) : nullptr;
       float2* khs = (float2*)const_cast<char*>(saved + 5 * act + big2d_zs_bytes(p));
-      // channel-major z, dh, dz around the large-grid kernels
-      T* zc = (T*)(ws + cb + 5 * act + align_up((size_t)d.channels * 4));
-      T* dhc = (T*)((char*)zc + act);
-      T* dzc = (T*)((char*)dhc + act);
       if (!zs) HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
-      HY_TRY(cl_cm<T>(dh, dhc, d.batch, h.Ntot, d.channels, true, st));
+      if (!fuse2) HY_TRY(cl_cm<T>(dh, dhc, d.batch, h.Ntot, d.channels, true, st));
       HY_TRY(big2d_backward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
                             real_view(dhc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D),
                             real_view(dzc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), dkv, ws, st, zsp, khs));
-      HY_TRY(cl_cm<T>(dzc, dz, d.batch, h.Ntot, d.channels, false, st));
+      if (!fuse1) HY_TRY(cl_cm<T>(dzc, dz, d.batch, h.Ntot, d.channels, false, st));
       if (zs && dD) {
         centre_tap_kernel<<<(d.channels + 255) / 256, 256, 0, st>>>(dfilt, dD, d.channels, p.g.K[0], p.g.K[1]);
         HY_TRY(check_launch("centre_tap_kernel"));
@@ -1796,9 +1832,15 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
       HY_TRY(check_launch("hyena_dskip_kernel"));
     }
   }
-  if (pair) hyena_bwd_gate1_kernel<T, true><<<eg, kElemThreads, 0, st>>>(dz, qs, ks, d.gate1, rows, d.channels, dqp, dkp);
-  else hyena_bwd_gate1_kernel<T, false><<<eg, kElemThreads, 0, st>>>(dz, qs, ks, d.gate1, rows, d.channels, dqp, dkp);
-  HY_TRY(check_launch("hyena_bwd_gate1_kernel"));
+  if (fuse1) {  // dz back to channels-last and gate 1 in one pass
+    HY_TRY((gate_x<T, GATE_BWD1>(dzc, qs, ks, dqp, dkp, d.gate1, d.batch, h.Ntot, d.channels, st)));
+  } else {
+    if (pair)
+      hyena_bwd_gate1_kernel<T, true><<<eg, kElemThreads, 0, st>>>(dz, qs, ks, d.gate1, rows, d.channels, dqp, dkp);
+    else
+      hyena_bwd_gate1_kernel<T, false><<<eg, kElemThreads, 0, st>>>(dz, qs, ks, d.gate1, rows, d.channels, dqp, dkp);
+    HY_TRY(check_launch("hyena_bwd_gate1_kernel"));
+  }
   auto dgrad = [&](auto pr) {
     constexpr bool P = decltype(pr)::value;
     with_stencil<P>(h.sg, [&](auto a, auto b, auto c) {

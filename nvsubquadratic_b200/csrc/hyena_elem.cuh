@@ -786,4 +786,110 @@ __global__ void __launch_bounds__(256) cl_cm_transpose_kernel(const T* __restric
   }
 }
 
+// ---------------------------------------------------------------- transposes fused with the gates
+// The large-grid kernels read and write channel-major [B][C][N] tensors; the gates around
+// them are elementwise over channels-last [B][N][C] ones. These kernels do a gate and the
+// layout change in one pass over a 64-position x 64-channel tile (256 threads, 16-byte
+// chunks of 8 channels or 8 positions, the tile in shared memory with its 16-byte chunks
+// XOR-swizzled by (row / 8) so both the row-wise and the column-wise accesses are free of
+// bank conflicts), with the rounding of the separate kernels they replace:
+//   GATE_POST_FWD:  in hc (cm) -> hb = hc (cl), y = h * round(g2(v'))           (hyena_post_fwd_kernel)
+//   GATE_BWD2:      dy, hb, v' (cl) -> dv' = dy * h * g2'(v') (cl),
+//                                      dh = dy * round(g2(v')) written cm      (hyena_bwd_gate2_kernel)
+//   GATE_BWD1:      in dz (cm), q', k' (cl) -> dq' = dz * round(g1(k')),
+//                                             dk' = dz * q' * g1'(k') (cl)      (hyena_bwd_gate1_kernel)
+// All tensors contiguous; N and C multiples of 64; grid (N / 64, C / 64, B).
+enum GateXMode { GATE_POST_FWD = 0, GATE_BWD2 = 1, GATE_BWD1 = 2 };
+
+template <typename T>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = DT<T>::load(e + i);
+}
+template <typename T>
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) DT<T>::store(e + i, f[i]);
+  return u;
+}
+
+template <typename T, int MODE>
+__global__ void __launch_bounds__(256) cl_cm_gate_kernel(const T* __restrict__ a, const T* __restrict__ b1,
+                                                         const T* __restrict__ b2, T* __restrict__ o1,
+                                                         T* __restrict__ o2, int gate, long long N, int C) {
+  static_assert(sizeof(T) == 2, "16-bit activations");
+  __shared__ __align__(16) T tile[64 * 64];  // [channel][position], 16-byte chunks swizzled
+  const long long n0 = (long long)blockIdx.x * 64;
+  const int c0 = blockIdx.y * 64;
+  const long long base = (long long)blockIdx.z * N * C;
+  const int t = threadIdx.x;
+  // swizzled element offset of (channel row r, position p) in the tile
+  auto at = [](int r, int p) { return r * 64 + ((((p >> 3) ^ (r >> 3)) & 7) << 3) + (p & 7); };
+  if constexpr (MODE != GATE_BWD2) {
+    // channel-major input rows: chunk (row r, positions 8k..8k+7)
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int q = t + 256 * it, r = q >> 3, k = q & 7;
+      const uint4 u = *reinterpret_cast<const uint4*>(a + base + (long long)(c0 + r) * N + n0 + 8 * k);
+      *reinterpret_cast<uint4*>(tile + at(r, 8 * k)) = u;
+    }
+    __syncthreads();
+  }
+  // channels-last chunks: (position p, channels 8g..8g+7); a warp covers 4 positions x 64 channels
+#pragma unroll
+  for (int it = 0; it < 2; ++it) {
+    const int q = t + 256 * it, p = q >> 3, g8 = q & 7;
+    const long long off = base + (n0 + p) * C + c0 + 8 * g8;
+    if constexpr (MODE == GATE_POST_FWD) {
+      float h[8], v[8], y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) h[i] = DT<T>::load(tile + at(8 * g8 + i, p));
+      unpack8<T>(*reinterpret_cast<const uint4*>(b1 + off), v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = h[i] * DT<T>::round(gate_f(gate, v[i]));
+      *reinterpret_cast<uint4*>(o1 + off) = pack8<T>(h);  // hb: the same bits as hc
+      *reinterpret_cast<uint4*>(o2 + off) = pack8<T>(y);
+    } else if constexpr (MODE == GATE_BWD2) {
+      float dy[8], h[8], v[8], dv[8], dh[8];
+      unpack8<T>(*reinterpret_cast<const uint4*>(a + off), dy);
+      unpack8<T>(*reinterpret_cast<const uint4*>(b1 + off), h);
+      unpack8<T>(*reinterpret_cast<const uint4*>(b2 + off), v);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dh[i] = dy[i] * DT<T>::round(gate_f(gate, v[i]));
+        dv[i] = dy[i] * h[i] * gate_df(gate, v[i]);
+      }
+      *reinterpret_cast<uint4*>(o1 + off) = pack8<T>(dv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) DT<T>::store(tile + at(8 * g8 + i, p), dh[i]);
+    } else {
+      float dz[8], kk[8], qq[8], dq[8], dk[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) dz[i] = DT<T>::load(tile + at(8 * g8 + i, p));
+      unpack8<T>(*reinterpret_cast<const uint4*>(b1 + off), qq);
+      unpack8<T>(*reinterpret_cast<const uint4*>(b2 + off), kk);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        dq[i] = dz[i] * DT<T>::round(gate_f(gate, kk[i]));
+        dk[i] = dz[i] * qq[i] * gate_df(gate, kk[i]);
+      }
+      *reinterpret_cast<uint4*>(o1 + off) = pack8<T>(dq);
+      *reinterpret_cast<uint4*>(o2 + off) = pack8<T>(dk);
+    }
+  }
+  if constexpr (MODE == GATE_BWD2) {
+    __syncthreads();
+    // dh channel-major rows
+#pragma unroll
+    for (int it = 0; it < 2; ++it) {
+      const int q = t + 256 * it, r = q >> 3, k = q & 7;
+      *reinterpret_cast<uint4*>(o2 + base + (long long)(c0 + r) * N + n0 + 8 * k) =
+          *reinterpret_cast<const uint4*>(tile + at(r, 8 * k));
+    }
+  }
+}
+
 }  // namespace hyfft
