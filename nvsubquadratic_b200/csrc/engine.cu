@@ -1550,6 +1550,9 @@ static bool plane_stencil_ok(const HyenaPlan& h, std::initializer_list<const voi
   const bool s2 = d.ndim == 2 && h.sg.k[0] == 3 && h.sg.k[1] == 3;
   if (sizeof(T) != 2 || !h.sg.has_conv || !(s3 || s2) || getenv("HYFFT_DISABLE_PLANE_STENCIL")) return false;
   if (d.channels % 8 || d.in_batch_stride % 8 || d.in_pos_stride % 8) return false;
+  // one-row planes keep a thread's in-row chunk offsets as int
+  if ((long long)h.sg.n[d.ndim - 1] * std::max<long long>(d.in_pos_stride, d.channels) + d.channels >= (1LL << 31))
+    return false;
   for (const void* p : ps)
     if (p && ((uintptr_t)p % 16) != 0) return false;
   return true;

@@ -93,6 +93,46 @@ __device__ __forceinline__ void s3_load_plane(T* slot, const T* src, long long b
   asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 
+// One-row planes (the 2D march, KY = 1): a thread's 16-byte chunks sit at the same offsets
+// in every plane, so their in-plane offsets (int: the host keeps a row of positions times
+// the position stride below 2^31) and range checks are computed once per kernel.
+template <int KZ, int TZ>
+struct RowChunks {
+  static constexpr int NCH = (TZ + KZ - 1) * 8, IT = (NCH + kElemThreads - 1) / kElemThreads;
+  int off[IT];
+  unsigned okm;
+  __device__ __forceinline__ RowChunks(const StencilGeom& g, const S3Tile& t, int C, long long pst, int oz) {
+    okm = 0;
+#pragma unroll
+    for (int i = 0; i < IT; ++i) {
+      const int q = threadIdx.x + i * kElemThreads;
+      const int gz = t.z0 - oz + (q >> 3), c = t.c0 + (q & 7) * 8;
+      const bool ok = q < NCH && gz >= 0 && gz < g.n[2] && c < C;
+      off[i] = ok ? (int)((long long)gz * pst + c) : 0;
+      okm |= (ok ? 1u : 0u) << i;
+    }
+  }
+  // cp.async of row plane xin (one commit group)
+  template <typename T>
+  __device__ __forceinline__ void load(T* slot, const T* src, long long bst, long long pst, const StencilGeom& g,
+                                       const S3Tile& t, int xin) const {
+    const bool xok = xin >= 0 && xin < g.n[0];
+    const T* base = src + (long long)t.b * bst + (long long)xin * g.n[2] * pst;
+#pragma unroll
+    for (int i = 0; i < IT; ++i) {
+      const int q = threadIdx.x + i * kElemThreads;
+      if (q < NCH) {
+        const bool ok = xok && ((okm >> i) & 1u);
+        const T* sp = ok ? base + off[i] : src;
+        const unsigned d = (unsigned)__cvta_generic_to_shared(slot + q * 8);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(sp), "r"(ok ? 16 : 0)
+                     : "memory");
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  }
+};
+
 template <typename T>
 __device__ __forceinline__ float2 s3_ld(const T* p) {
   return V2<T>::load(p);
@@ -128,6 +168,11 @@ __global__ void __launch_bounds__(kElemThreads, (KX == 1 || KY == 1) ? 3 : 2) hy
   const long long ps = MODE == 0 ? in_pst : (long long)C;
   const long long bs = MODE == 0 ? in_bst : N * C;
   const int gy = t.y0 + yl;
+  const RowChunks<KZ, TZ> rows(g, t, C, ps, oz);  // used by one-row planes only
+  auto load_plane = [&](T* slot, const T* src, int xin) {
+    if constexpr (KY == 1 && TY == 1) rows.template load<T>(slot, src, bs, ps, g, t, xin);
+    else s3_load_plane<T, KY, KZ, TY, TZ>(slot, src, bs, ps, g, t, C, xin, oy, oz);
+  };
 
 #pragma unroll 1
   for (int ti = 0; ti < 3; ++ti) {
@@ -154,16 +199,14 @@ __global__ void __launch_bounds__(kElemThreads, (KX == 1 || KY == 1) ? 3 : 2) hy
 #pragma unroll 1
     for (int a = 0; a < KX; ++a) {
       const int xin = t.xa - ox + a;
-      s3_load_plane<T, KY, KZ, TY, TZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, bs, ps, g, t, C, xin, oy,
-                               oz);
+      load_plane(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, xin);
     }
 #pragma unroll 1
     for (int x = t.xa; x < t.xb; ++x) {
       const bool pre = x + 1 < t.xb;
       if (pre) {
         const int xin = x - ox + KX;
-        s3_load_plane<T, KY, KZ, TY, TZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, bs, ps, g, t, C, xin,
-                                 oy, oz);
+        load_plane(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, xin);
         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
       } else {
         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
@@ -255,6 +298,11 @@ __global__ void __launch_bounds__(kElemThreads, (KX == 1 || KY == 1) ? 3 : 2) hy
   const int ox = g.off[0], oy = g.off[1], oz = g.off[2];
   const long long N = (long long)g.n[0] * g.n[1] * g.n[2];
   const int gy = t.y0 + yl;
+  const RowChunks<KZ, TZ> rows(g, t, C, in_pst, oz);  // used by one-row planes only
+  auto load_plane = [&](T* slot, const T* src, int xin) {
+    if constexpr (KY == 1 && TY == 1) rows.template load<T>(slot, src, in_bst, in_pst, g, t, xin);
+    else s3_load_plane<T, KY, KZ, TY, TZ>(slot, src, in_bst, in_pst, g, t, C, xin, oy, oz);
+  };
 
 #pragma unroll 1
   for (int ti = 0; ti < 3; ++ti) {
@@ -267,16 +315,14 @@ __global__ void __launch_bounds__(kElemThreads, (KX == 1 || KY == 1) ? 3 : 2) hy
 #pragma unroll 1
     for (int a = 0; a < KX; ++a) {
       const int xin = t.xa - ox + a;
-      s3_load_plane<T, KY, KZ, TY, TZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, in_bst, in_pst, g, t, C,
-                               xin, oy, oz);
+      load_plane(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, xin);
     }
 #pragma unroll 1
     for (int x = t.xa; x < t.xb; ++x) {
       const bool pre = x + 1 < t.xb;
       if (pre) {
         const int xin = x - ox + KX;
-        s3_load_plane<T, KY, KZ, TY, TZ>(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, in_bst, in_pst, g, t,
-                                 C, xin, oy, oz);
+        load_plane(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, xin);
         asm volatile("cp.async.wait_group 1;\n" ::: "memory");
       } else {
         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
