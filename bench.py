@@ -320,9 +320,11 @@ def run_cp(args, cfg, rank, world, device):
     n0 = _lib.launch_count()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    torch.distributed.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(device.index if device.index is not None else 0) as clk:
+        # the timed steps start together on every rank (the sampler's start-up differs per rank)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        torch.cuda.synchronize()
         for i in range(args.steps):
             zero_grads()
             starts[i].record()
@@ -481,22 +483,27 @@ def run_gpu(args, cfg, rank, world, device):
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
     # estimate the step time to size an untimed, clock-sampled burn-in of ~0.5 s right before
-    # the timed steps (nvidia-smi samples every 50 ms; a short timed region alone gets 0-1 samples)
+    # the timed steps (nvidia-smi samples every 50 ms; a short timed region alone gets 0-1 samples);
+    # every rank runs the same number of burn-in steps (the slowest rank's estimate)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(3):
         graph.replay()
     e1.record()
     torch.cuda.synchronize()
-    est_ms = max(e0.elapsed_time(e1) / 3, 1e-3)
-    n_burn = int(min(20000, max(10, 500.0 / est_ms)))
+    est = torch.tensor([max(e0.elapsed_time(e1) / 3, 1e-3)], device=device)
+    if world > 1:
+        torch.distributed.all_reduce(est, op=torch.distributed.ReduceOp.MAX)
+    n_burn = int(min(20000, max(10, 500.0 / est.item())))
     with ClockSampler(device.index if device.index is not None else 0) as clk:
         for _ in range(n_burn):
             graph.replay()
+        # the timed steps start together on every rank: barrier + synchronize right before them
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
         for i in range(args.steps):
             flush.zero_()  # evict L2 between timed steps (outside the events)
             starts[i].record()
@@ -603,6 +610,9 @@ def e2e_time(cfg, inp, device, op_only, steps, dp_group=None):
             issue_copy(i + 1)
         run_step(i)
     torch.cuda.synchronize()
+    if dp_group is not None:  # the ranks start the timed steps together
+        torch.distributed.barrier(group=dp_group)
+        torch.cuda.synchronize()
     # timed: exactly `steps` copies in, `steps` fwd+bwd, `steps` copies out
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(main)
