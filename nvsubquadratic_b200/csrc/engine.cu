@@ -1099,10 +1099,67 @@ static size_t big2d_zs_bytes(const ConvPlan& p) {
   return align_up((size_t)p.B * p.C * (p.b2F / 2 + 1) * p.b2F * sizeof(float2));
 }
 
+// A second stream per device for work off the mixer's critical path (the large-grid
+// filter-spectrum and filter-gradient transforms, which depend only on the filter or on the
+// accumulated gradient spectrum): forked from the caller's stream and joined back into it
+// with events, so it overlaps the stencils and gates. Created on the first call on a device
+// (before any stream capture); the record/wait pairs are serialised per device, so calls
+// from several host threads stay ordered. HYFFT_NO_SIDE_STREAM keeps everything on the
+// caller's stream.
+struct SideStream {
+  cudaStream_t s = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  std::mutex mu;
+};
+static SideStream* side_stream() {
+  if (getenv("HYFFT_NO_SIDE_STREAM")) return nullptr;
+  static std::mutex mu;
+  static std::map<int, SideStream> m;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  SideStream& ss = m[dev];
+  if (!ss.s) {
+    if (cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      ss.s = nullptr;
+      return nullptr;
+    }
+  }
+  return &ss;
+}
+// the side stream waits for everything issued on st so far
+static int fork_side(SideStream* ss, cudaStream_t st) {
+  std::lock_guard<std::mutex> lock(ss->mu);
+  if (cudaEventRecord(ss->fork, st) != cudaSuccess || cudaStreamWaitEvent(ss->s, ss->fork, 0) != cudaSuccess)
+    return fail(HYFFT_ERR_CUDA, "fork to the side stream failed");
+  return HYFFT_OK;
+}
+// st waits for everything issued on the side stream so far
+static int join_side(SideStream* ss, cudaStream_t st) {
+  std::lock_guard<std::mutex> lock(ss->mu);
+  if (cudaEventRecord(ss->join, ss->s) != cudaSuccess || cudaStreamWaitEvent(st, ss->join, 0) != cudaSuccess)
+    return fail(HYFFT_ERR_CUDA, "join from the side stream failed");
+  return HYFFT_OK;
+}
+
+// The rolled filter's spectrum into kh (workspace T scratch as in big2d_forward).
+static int big2d_kspec(const ConvPlan& p, const RealView& kv, char* ws, float2* kh, cudaStream_t st) {
+  Big2DParams b;
+  big2d_params(p, kv, nullptr, ws, b);
+  b.Kh = kh;
+  if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
+  return HYFFT_OK;
+}
+
 // zs_out: if set, the conv stores its input's column spectra there (zs_mode 1).
 // kh: if set, the filter spectrum goes there (the mixer keeps it for its backward).
+// kspec_done: kh already holds the filter spectrum (computed on the side stream).
 static int big2d_forward(const ConvPlan& p, const RealView& xv, const RealView& kv, const float* D, const RealView& yv,
-                         char* ws, cudaStream_t st, float2* zs_out = nullptr, float2* kh = nullptr) {
+                         char* ws, cudaStream_t st, float2* zs_out = nullptr, float2* kh = nullptr,
+                         bool kspec_done = false) {
   Big2DParams b;
   big2d_params(p, kv, D, ws, b);
   b.x = b2view(xv);
@@ -1112,7 +1169,8 @@ static int big2d_forward(const ConvPlan& p, const RealView& xv, const RealView& 
     b.zs_mode = 1;
   }
   if (kh) b.Kh = kh;
-  if (big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
+  if (!kspec_done && big2d_dispatch(B2_KSPEC, p.dt, b, st) != HYFFT_OK)
+    return fail(HYFFT_ERR_CUDA, "big2d filter spectrum launch failed");
   if (big2d_dispatch(B2_CONV, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d conv launch failed");
   return HYFFT_OK;
 }
@@ -1120,9 +1178,11 @@ static int big2d_forward(const ConvPlan& p, const RealView& xv, const RealView& 
 // zs_in: the forward input's column spectra (kept by big2d_forward); with them the
 // adjoint conv also accumulates the filter-gradient spectrum and the dK kernel is skipped.
 // kh_in: the filter spectrum the forward kept (else it is recomputed).
+// side: with the fused filter gradient, its inverse transforms run there (forked after the
+// adjoint; the caller joins).
 static int big2d_backward(const ConvPlan& p, const RealView& xv, const RealView& kv, const float* D,
                           const RealView& dyv, const RealView& dxv, const RealView& dkv, char* ws, cudaStream_t st,
-                          float2* zs_in = nullptr, float2* kh_in = nullptr) {
+                          float2* zs_in = nullptr, float2* kh_in = nullptr, SideStream* side = nullptr) {
   Big2DParams b;
   big2d_params(p, kv, D, ws, b);
   if (kh_in) b.Kh = kh_in;
@@ -1145,7 +1205,9 @@ static int big2d_backward(const ConvPlan& p, const RealView& xv, const RealView&
   }
   if (fused_dk) {
     b.dfilt = b2view(dkv);
-    if (big2d_dispatch(B2_DFILT, p.dt, b, st) != HYFFT_OK) return fail(HYFFT_ERR_CUDA, "big2d dfilt launch failed");
+    if (side) HY_TRY(fork_side(side, st));
+    if (big2d_dispatch(B2_DFILT, p.dt, b, side ? side->s : st) != HYFFT_OK)
+      return fail(HYFFT_ERR_CUDA, "big2d dfilt launch failed");
     return HYFFT_OK;
   }
   if (dkv.ptr) {
@@ -1636,8 +1698,9 @@ __global__ void centre_tap_kernel(const float* __restrict__ dfilt, float* __rest
 }
 
 template <typename T>
-static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt, const float* D,
-                           const float* sw, const float* sb, T* y, char* saved, char* ws, cudaStream_t st) {
+static int hyena_forward_body(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt,
+                              const float* D, const float* sw, const float* sb, T* y, char* saved, char* ws,
+                              cudaStream_t st, SideStream* side) {
   const hyfft_hyena_desc& d = h.d;
   const size_t act = align_up((size_t)h.E * h.eb);
   T* qs = (T*)(saved);
@@ -1645,6 +1708,11 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
   T* vs = (T*)(saved + 2 * act);
   T* z = (T*)(saved + 3 * act);
   T* hb = (T*)(saved + 4 * act);
+  if (side) {  // large grid: the filter spectrum on the side stream, overlapping the short conv
+    HY_TRY(fork_side(side, st));
+    HY_TRY(big2d_kspec(h.cp, real_view(filt, HYFFT_LAYOUT_BHL, 1, h.cp.C, h.cp.g.K, h.cp.g.D), ws,
+                       (float2*)(saved + 5 * act + big2d_zs_bytes(h.cp)), side->s));
+  }
   const long long rows = (long long)d.batch * h.Ntot;
   const bool pair = elem_pairs_ok(h, {q, k, v, y});
   auto pre = [&](auto pr) {
@@ -1713,8 +1781,9 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
     T* zc = (T*)(ws + cf + align_up((size_t)d.channels * 4));
     T* hc = (T*)((char*)zc + align_up((size_t)h.E * h.eb));
     HY_TRY(cl_cm<T>(z, zc, d.batch, h.Ntot, d.channels, true, st));
+    if (side) HY_TRY(join_side(side, st));
     HY_TRY(big2d_forward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
-                         real_view(hc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), ws, st, zs, khs));
+                         real_view(hc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), ws, st, zs, khs, side != nullptr));
     // h back to channels-last and gate 2 in one pass where the output is contiguous
     if (d.out_pos_stride == d.channels && d.out_batch_stride == h.Ntot * d.channels &&
         gate_x_ok(sizeof(T), d.channels, h.Ntot, {hc, hb, vs, y}))
@@ -1737,9 +1806,10 @@ static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* 
 }
 
 template <typename T>
-static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt,
-                            const float* D, const float* sw, const T* dy, T* dq, T* dk, T* dv, float* dfilt,
-                            float* dD, float* dsw, float* dsb, const char* saved, char* ws, cudaStream_t st) {
+static int hyena_backward_body(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt,
+                               const float* D, const float* sw, const T* dy, T* dq, T* dk, T* dv, float* dfilt,
+                               float* dD, float* dsw, float* dsb, const char* saved, char* ws, cudaStream_t st,
+                               SideStream* side) {
   const hyfft_hyena_desc& d = h.d;
   const size_t act = align_up((size_t)h.E * h.eb);
     const T* qs = (const T*)(saved);
@@ -1813,10 +1883,13 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
       if (!fuse2) HY_TRY(cl_cm<T>(dh, dhc, d.batch, h.Ntot, d.channels, true, st));
       HY_TRY(big2d_backward(p, real_view(zc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), kv, D,
                             real_view(dhc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D),
-                            real_view(dzc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), dkv, ws, st, zsp, khs));
+                            real_view(dzc, HYFFT_LAYOUT_BHL, p.B, p.C, p.g.N, p.g.D), dkv, ws, st, zsp, khs,
+                            zs ? side : nullptr));
       if (!fuse1) HY_TRY(cl_cm<T>(dzc, dz, d.batch, h.Ntot, d.channels, false, st));
       if (zs && dD) {
-        centre_tap_kernel<<<(d.channels + 255) / 256, 256, 0, st>>>(dfilt, dD, d.channels, p.g.K[0], p.g.K[1]);
+        // after the filter gradient, on the stream that computes it
+        centre_tap_kernel<<<(d.channels + 255) / 256, 256, 0, side ? side->s : st>>>(dfilt, dD, d.channels,
+                                                                                       p.g.K[0], p.g.K[1]);
         HY_TRY(check_launch("centre_tap_kernel"));
       }
     } else {
@@ -1958,6 +2031,33 @@ static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T*
     HY_TRY(check_launch("hyena_short_wgrad_kernel"));
   }
   return HYFFT_OK;
+}
+
+// The mixer passes with the large-grid filter transforms on the side stream; every path
+// joins it back into the caller's stream before returning (also after a failure).
+template <typename T>
+static int hyena_forward_t(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt, const float* D,
+                           const float* sw, const float* sb, T* y, char* saved, char* ws, cudaStream_t st) {
+  SideStream* side = h.cp.big2d ? side_stream() : nullptr;
+  const int rc = hyena_forward_body<T>(h, q, k, v, filt, D, sw, sb, y, saved, ws, st, side);
+  if (side) {
+    const int jc = join_side(side, st);
+    if (rc == HYFFT_OK) return jc;
+  }
+  return rc;
+}
+template <typename T>
+static int hyena_backward_t(const HyenaPlan& h, const T* q, const T* k, const T* v, const float* filt,
+                            const float* D, const float* sw, const T* dy, T* dq, T* dk, T* dv, float* dfilt,
+                            float* dD, float* dsw, float* dsb, const char* saved, char* ws, cudaStream_t st) {
+  SideStream* side = h.cp.big2d ? side_stream() : nullptr;
+  const int rc = hyena_backward_body<T>(h, q, k, v, filt, D, sw, dy, dq, dk, dv, dfilt, dD, dsw, dsb, saved, ws, st,
+                                        side);
+  if (side) {
+    const int jc = join_side(side, st);
+    if (rc == HYFFT_OK) return jc;
+  }
+  return rc;
 }
 
 static bool aligned16(std::initializer_list<const void*> ps) {
