@@ -1631,7 +1631,7 @@ struct PlaneLaunch {
 static bool plane_march2d(const HyenaPlan& h) { return h.d.ndim == 2 && h.sg.n[1] >= 96; }
 // x runs per CTA such that the grid fills about two waves of two CTAs per SM (3D), or one
 // wave of three CTAs per SM (2D march: the halo rows re-read per run stay few).
-static PlaneLaunch plane_launch(const HyenaPlan& h) {
+static PlaneLaunch plane_launch(const HyenaPlan& h, int march_ctas_per_sm = 3) {
   StencilGeom g = h.sg;
   const bool march = plane_march2d(h);
   int TY = kS3TY, TZ = kS3TZ;
@@ -1659,7 +1659,7 @@ static PlaneLaunch plane_launch(const HyenaPlan& h) {
   }
   const long long base = (long long)((h.d.channels + kElemCG - 1) / kElemCG) * ((g.n[1] + TY - 1) / TY) *
                          ((g.n[2] + TZ - 1) / TZ) * h.d.batch;
-  const long long target = march ? 3 * 148 : 4 * 148;
+  const long long target = march ? (long long)march_ctas_per_sm * 148 : 4 * 148;
   const long long nxc = march ? std::max<long long>(1, std::min<long long>(g.n[0], target / base))
                               : std::max<long long>(1, std::min<long long>(g.n[0], (target + base - 1) / base));
   PlaneLaunch pl;
@@ -1917,6 +1917,11 @@ static int hyena_backward_body(const HyenaPlan& h, const T* q, const T* k, const
       hyena_bwd_gate1_kernel<T, false><<<eg, kElemThreads, 0, st>>>(dz, qs, ks, d.gate1, rows, d.channels, dqp, dkp);
     HY_TRY(check_launch("hyena_bwd_gate1_kernel"));
   }
+  // 2D march with short-conv weight gradients: the weight gradient runs inside the
+  // transposed-stencil kernel (HYFFT_DISABLE_FUSED_WGRAD keeps the two kernels)
+  const bool fuse_wgrad = h.sg.has_conv && dsw != nullptr && !getenv("HYFFT_DISABLE_FUSED_WGRAD");
+  bool wgrad_done = false;
+  int launch_rc = HYFFT_OK;
   auto dgrad = [&](auto pr) {
     constexpr bool P = decltype(pr)::value;
     with_stencil<P>(h.sg, [&](auto a, auto b, auto c) {
@@ -1928,6 +1933,23 @@ static int hyena_backward_body(const HyenaPlan& h, const T* q, const T* k, const
           constexpr int PX = ND == 3 ? 3 : 1;
           constexpr size_t sm = s3_smem_bytes<PX, 3, 3>();
           if constexpr (ND == 2) {
+            // transposed stencil and weight / bias gradients in one march (two CTAs per SM)
+            constexpr size_t smb = s3_wgrad_smem_bytes<3, 1, 3, 1, kS2TZ>();
+            if (fuse_wgrad && plane_march2d(h) && plane_stencil_ok<T>(h, {q, k, v, dqp, dkp, dvp, dq, dk, dv}) &&
+                kernel_smem_once((const void*)hyena_plane_bwd_kernel<T, 3, 1, 3, 1, kS2TZ>, smb)) {
+              if (cudaMemsetAsync(dsw, 0, sizeof(float) * 3 * (size_t)d.channels * h.sg.ntaps, st) != cudaSuccess ||
+                  (dsb && h.sg.has_bias &&
+                   cudaMemsetAsync(dsb, 0, sizeof(float) * 3 * (size_t)d.channels, st) != cudaSuccess)) {
+                launch_rc = fail(HYFFT_ERR_CUDA, "memset short-conv gradients");
+                return;
+              }
+              const PlaneLaunch pl = plane_launch(h, 2);
+              hyena_plane_bwd_kernel<T, 3, 1, 3, 1, kS2TZ><<<pl.grid, kElemThreads, smb, st>>>(
+                  dqp, dkp, dvp, q, k, v, d.in_batch_stride, d.in_pos_stride, dq, dk, dv, pl.g, d.channels, sw, dsw,
+                  h.sg.has_bias ? dsb : nullptr, pl.xchunk);
+              wgrad_done = true;
+              return;
+            }
             constexpr size_t sm2 = s3_smem_bytes<3, 1, 3, 1, kS2TZ>();
             if (plane_march2d(h) && plane_stencil_ok<T>(h, {dqp, dkp, dvp, dq, dk, dv}) &&
                 kernel_smem_once((const void*)hyena_plane_stencil_kernel<T, 3, 1, 3, 1, 1, kS2TZ>, sm2)) {
@@ -1965,7 +1987,8 @@ static int hyena_backward_body(const HyenaPlan& h, const T* q, const T* k, const
   if (pair) dgrad(std::true_type{});
   else dgrad(std::false_type{});
   HY_TRY(check_launch("hyena_short_dgrad_kernel"));
-  if (h.sg.has_conv && dsw) {
+  HY_TRY(launch_rc);
+  if (h.sg.has_conv && dsw && !wgrad_done) {
     if (cudaMemsetAsync(dsw, 0, sizeof(float) * 3 * (size_t)d.channels * h.sg.ntaps, st) != cudaSuccess)
       return fail(HYFFT_ERR_CUDA, "memset dshort_w");
     if (dsb && h.sg.has_bias && cudaMemsetAsync(dsb, 0, sizeof(float) * 3 * (size_t)d.channels, st) != cudaSuccess)

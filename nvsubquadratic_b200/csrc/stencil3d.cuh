@@ -274,6 +274,169 @@ __global__ void __launch_bounds__(kElemThreads, (KX == 1 || KY == 1) ? 3 : 2) hy
   }
 }
 
+// Transposed stencil and weight / bias gradients in one march over the same ring of dout
+// planes (dq'/dk'/dv', contiguous): for output position p the ring holds the neighbourhood
+// dout[p - tap + off] of every tap, so
+//   dq[p]     = sum_tap w[tap] dout[p - tap + off]                (as MODE 1 above)
+//   dW[tap]  += in[p] dout[p - tap + off]  (= sum_p' dout[p'] in[p' + tap - off])
+//   db       += dout[p]                     (the centre tap's neighbour)
+// with in = q/k/v read at p only (in_bst, in_pst): the gradient pass needs no ring of its
+// own, and every ring value is unpacked once for both products. Per-thread accumulators, a
+// shared-memory reduction over the CTA's warps and one atomic per channel and tap per CTA
+// (dw, db zeroed by the host).
+template <typename T, int KX, int KY, int KZ, int TY, int TZ>
+__global__ void __launch_bounds__(kElemThreads, 2) hyena_plane_bwd_kernel(
+    const T* __restrict__ d0, const T* __restrict__ d1, const T* __restrict__ d2, const T* __restrict__ in0,
+    const T* __restrict__ in1, const T* __restrict__ in2, long long in_bst, long long in_pst, T* __restrict__ out0,
+    T* __restrict__ out1, T* __restrict__ out2, StencilGeom g, int C, const float* __restrict__ w,
+    float* __restrict__ dw, float* __restrict__ db, int xchunk) {
+  constexpr int NT = KX * KY * KZ, ZW = TZ + KZ - 1, NPOS = s3_plane_positions<KY, KZ, TY, TZ>(), NB = s3_ring<KX>();
+  constexpr int NW = kElemThreads / 32;
+  constexpr int WPR = TZ / 16;  // warps per tile row, 16 z positions each
+  static_assert(TY * WPR == NW, "one warp per 16 positions of the tile");
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* ring = reinterpret_cast<T*>(smem_raw);
+  float* red = reinterpret_cast<float*>(smem_raw);  // [NW][NT + 1][64] after the march
+  const S3Tile t = s3_tile<TY, TZ>(g, xchunk);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int yl = warp / WPR, zw = (warp % WPR) * 16;
+  const int c = t.c0 + 2 * lane;
+  const bool cok = c < C;
+  // ring offsets of the transposed stencil (flipped taps, left padding k - 1 - off)
+  const int ox = KX - 1 - g.off[0], oy = KY - 1 - g.off[1], oz = KZ - 1 - g.off[2];
+  // neighbourhood index of the centre tap (tap == off on every axis)
+  const int ac = KX - 1 - g.off[0], bc = KY - 1 - g.off[1], ec = KZ - 1 - g.off[2];
+  const long long N = (long long)g.n[0] * g.n[1] * g.n[2];
+  const long long ps = C, bs = N * C;
+  const int gy = t.y0 + yl;
+  const RowChunks<KZ, TZ> rows(g, t, C, ps, oz);  // used by one-row planes only
+  auto load_plane = [&](T* slot, const T* src, int xin) {
+    if constexpr (KY == 1 && TY == 1) rows.template load<T>(slot, src, bs, ps, g, t, xin);
+    else s3_load_plane<T, KY, KZ, TY, TZ>(slot, src, bs, ps, g, t, C, xin, oy, oz);
+  };
+
+#pragma unroll 1
+  for (int ti = 0; ti < 3; ++ti) {
+    float2 wr[NT], dacc[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int a = j / (KY * KZ), bq = (j / KZ) % KY, e = j % KZ;
+      const int tap = ((KX - 1 - a) * KY + (KY - 1 - bq)) * KZ + (KZ - 1 - e);
+      const long long wi = ((long long)ti * C + c) * NT + tap;
+      wr[j] = cok ? make_float2(__ldg(w + wi), __ldg(w + wi + NT)) : make_float2(0.f, 0.f);
+      dacc[j] = make_float2(0.f, 0.f);
+    }
+    float2 accb = make_float2(0.f, 0.f);
+    const T* src = ti == 0 ? d0 : (ti == 1 ? d1 : d2);
+    const T* xin_t = ti == 0 ? in0 : (ti == 1 ? in1 : in2);
+    T* dst = ti == 0 ? out0 : (ti == 1 ? out1 : out2);
+#pragma unroll 1
+    for (int a = 0; a < KX; ++a) {
+      const int xin = t.xa - ox + a;
+      load_plane(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, xin);
+    }
+#pragma unroll 1
+    for (int x = t.xa; x < t.xb; ++x) {
+      const bool pre = x + 1 < t.xb;
+      if (pre) {
+        const int xin = x - ox + KX;
+        load_plane(ring + ((xin + 256) % NB) * NPOS * kElemCG, src, xin);
+        asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      }
+      __syncthreads();
+      if (cok && gy < g.n[1]) {
+        // in[p] of the next step loaded one step ahead, behind the current step's taps
+        auto ld_in = [&](int zb, float2 (&iv)[kS3ZU]) {
+#pragma unroll
+          for (int i = 0; i < kS3ZU; ++i) {
+            const int gz = t.z0 + zw + zb + i;
+            const long long pos = ((long long)x * g.n[1] + gy) * g.n[2] + gz;
+            iv[i] = (zb < 16 && gz < g.n[2]) ? V2<T>::load(xin_t + (long long)t.b * in_bst + pos * in_pst + c)
+                                             : make_float2(0.f, 0.f);
+          }
+        };
+        float2 inext[kS3ZU];
+        ld_in(0, inext);
+#pragma unroll 1
+        for (int zb = 0; zb < 16; zb += kS3ZU) {
+          float2 iv[kS3ZU], acc[kS3ZU];
+#pragma unroll
+          for (int i = 0; i < kS3ZU; ++i) {
+            iv[i] = inext[i];
+            acc[i] = make_float2(0.f, 0.f);
+          }
+          ld_in(zb + kS3ZU, inext);
+#pragma unroll
+          for (int a = 0; a < KX; ++a) {
+            const T* sl = ring + ((x - ox + a + 256) % NB) * NPOS * kElemCG;
+#pragma unroll
+            for (int bq = 0; bq < KY; ++bq) {
+              const T* row = sl + ((yl + bq) * ZW + zw + zb) * kElemCG + 2 * lane;
+              float2 v[kS3ZU + KZ - 1];
+#pragma unroll
+              for (int m = 0; m < kS3ZU + KZ - 1; ++m) v[m] = s3_ld<T>(row + m * kElemCG);
+#pragma unroll
+              for (int e = 0; e < KZ; ++e) {
+                const int j = (a * KY + bq) * KZ + e;
+                const bool centre = a == ac && bq == bc && e == ec;  // (v indexed statically only)
+#pragma unroll
+                for (int i = 0; i < kS3ZU; ++i) {
+                  acc[i] = ffma2(wr[j], v[i + e], acc[i]);
+                  dacc[j] = ffma2(iv[i], v[i + e], dacc[j]);
+                  if (centre) {
+                    accb.x += v[i + e].x;
+                    accb.y += v[i + e].y;
+                  }
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < kS3ZU; ++i) {
+            const int gz = t.z0 + zw + zb + i;
+            if (gz >= g.n[2]) {  // positions past the grid add nothing to the gradients either
+              break;
+            }
+            const long long pos = ((long long)x * g.n[1] + gy) * g.n[2] + gz;
+            V2<T>::store(dst + (long long)t.b * in_bst + pos * in_pst + c, acc[i]);
+          }
+        }
+      }
+      __syncthreads();  // the next prefetch overwrites the oldest plane read here
+    }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    __syncthreads();
+    // CTA reduction over the warps through the (now idle) ring; dacc[j] belongs to tap
+    // flip(j), the bias sum to the last slot
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      red[(warp * (NT + 1) + j) * kElemCG + 2 * lane] = dacc[j].x;
+      red[(warp * (NT + 1) + j) * kElemCG + 2 * lane + 1] = dacc[j].y;
+    }
+    red[(warp * (NT + 1) + NT) * kElemCG + 2 * lane] = accb.x;
+    red[(warp * (NT + 1) + NT) * kElemCG + 2 * lane + 1] = accb.y;
+    __syncthreads();
+    for (int i = threadIdx.x; i < (NT + 1) * kElemCG; i += blockDim.x) {
+      const int j = i / kElemCG, cc = i - j * kElemCG, ch = t.c0 + cc;
+      float sum = 0.f;
+#pragma unroll
+      for (int q = 0; q < NW; ++q) sum += red[(q * (NT + 1) + j) * kElemCG + cc];
+      if (ch < C) {
+        if (j < NT) {
+          const int a = j / (KY * KZ), bq = (j / KZ) % KY, e = j % KZ;
+          const int tap = ((KX - 1 - a) * KY + (KY - 1 - bq)) * KZ + (KZ - 1 - e);
+          atomicAdd(dw + ((long long)ti * C + ch) * NT + tap, sum);
+        } else if (db) {
+          atomicAdd(db + (long long)ti * C + ch, sum);
+        }
+      }
+    }
+    __syncthreads();  // the ring is refilled for the next tensor
+  }
+}
+
 // Weight and bias gradients: dW[t][c][tap] = sum_{b, p} dout[b, p, c] * in[b, p + tap - off, c]
 // with in = q/k/v (in_bst, in_pst) and dout = dq'/dk'/dv' contiguous; db[t][c] = sum dout.
 // Per-thread accumulators for all taps, a shared-memory reduction over the CTA's warps,

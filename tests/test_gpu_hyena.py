@@ -76,9 +76,14 @@ CASES = [
     # 2D 3x3 short conv on the same kernels as one x plane (ragged y / z tiles, channel tail)
     (2, 3, 72, (37, 45), (37, 45), 3, False, "sigmoid", "silu", torch.bfloat16, True, True),
     (2, 3, 8, (12, 10), (23, 19), 0, False, "identity", "sigmoid", torch.float32, False, False),
-    # large-grid 2D kernels (F = 256 x 256)
+    # large-grid 2D kernels (F = 192 or 256 per axis)
     (2, 2, 8, (128, 128), (128, 128), 3, False, "silu", "sigmoid", torch.bfloat16, False, True),
     (2, 1, 4, (100, 90), (129, 120), 3, False, "identity", "sigmoid", torch.float32, True, False),
+    # 2D grids whose rows march through the plane kernels (last axis >= 96): the transposed
+    # stencil with the weight and bias gradients in one kernel, a channel tail block, a
+    # ragged first axis, bias, strided q/k/v views
+    (2, 2, 72, (45, 100), (45, 100), 3, False, "silu", "identity", torch.bfloat16, True, True),
+    (2, 3, 16, (112, 128), (63, 63), 3, False, "sigmoid", "silu", torch.bfloat16, True, False),
 ]
 
 
