@@ -255,12 +255,6 @@ __device__ __forceinline__ void split_pair(const float2 (&v)[16], int l, float2 
   }
 }
 
-template <typename T>
-__device__ __forceinline__ float ldv(const Big2DView& v, int b, int c, int i0, int i1) {
-  return DT<T>::load(reinterpret_cast<const T*>(v.ptr) + (long long)b * v.bst + (long long)c * v.cst +
-                     (long long)i0 * v.s0 + (long long)i1 * v.s1);
-}
-
 // ---------------------------------------------------------------- filter spectrum
 // Row transforms of the rolled filter: T[c][r][j], r < F, j <= F/2. grid (C, F/2/16).
 template <int F>
@@ -338,13 +332,28 @@ __device__ __forceinline__ void rows_load(const Big2DView& in, int b, int c, int
   const bool act = pr < npairs;
   const int r0 = 2 * pr, r1 = r0 + 1;
   const bool has1 = act && r1 < N0;
+  const T* row0 = reinterpret_cast<const T*>(in.ptr) + (long long)b * in.bst + (long long)c * in.cst +
+                  (long long)r0 * in.s0;
+  const T* row1 = row0 + in.s0;
+  if (in.s1 == 1) {  // unit-stride rows (channel-major activations): constant offsets from one base
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
-    const int n = l + 16 * m;
-    v[m] = make_float2(0.f, 0.f);
-    if (act && n < N1) {
-      v[m].x = ldv<T>(in, b, c, r0, n);
-      if (has1) v[m].y = ldv<T>(in, b, c, r1, n);
+    for (int m = 0; m < 8; ++m) {
+      const int n = l + 16 * m;
+      v[m] = make_float2(0.f, 0.f);
+      if (act && n < N1) {
+        v[m].x = DT<T>::load(row0 + n);
+        if (has1) v[m].y = DT<T>::load(row1 + n);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      const int n = l + 16 * m;
+      v[m] = make_float2(0.f, 0.f);
+      if (act && n < N1) {
+        v[m].x = DT<T>::load(row0 + (long long)n * in.s1);
+        if (has1) v[m].y = DT<T>::load(row1 + (long long)n * in.s1);
+      }
     }
   }
 }
@@ -611,6 +620,7 @@ __device__ __forceinline__ void rows_inverse(const Big2DParams& p, const float2*
     const int r0 = 2 * pr, r1 = r0 + 1;
     const bool has1 = act && r1 < N0;
     const float2* a0 = A + (r0 - 2 * pr0) * H;
+    T* y0 = yo + (long long)r0 * p.y.s0;
     float2 v[16];
 #pragma unroll
     for (int m = 0; m < 16; ++m) {
@@ -645,8 +655,9 @@ __device__ __forceinline__ void rows_inverse(const Big2DParams& p, const float2*
             o0 = DT<T>::round(o0 + DT<T>::round(Dc * xs[m].x));
             if (has1) o1 = DT<T>::round(o1 + DT<T>::round(Dc * xs[m].y));
           }
-          DT<T>::store(yo + (long long)r0 * p.y.s0 + (long long)n * p.y.s1, o0);
-          if (has1) DT<T>::store(yo + (long long)r1 * p.y.s0 + (long long)n * p.y.s1, o1);
+          const long long on = p.y.s1 == 1 ? n : (long long)n * p.y.s1;
+          DT<T>::store(y0 + on, o0);
+          if (has1) DT<T>::store(y0 + p.y.s0 + on, o1);
         }
       }
     }
