@@ -546,8 +546,9 @@ def e2e_time(cfg, inp, device, op_only, steps, dp_group=None):
     host -> device, runs forward + backward through hyena_fused / the op API, and copies its
     result y device -> host. The copies of step i + 1 run on a copy stream while step i
     computes (two device slots per input), the way a training loop prefetches its next
-    batch; the time is the device span from the first copy of the first timed step to the
-    last device -> host copy, divided by the number of steps. Returns (ms per step, H2D
+    batch; the time of a block of steps is the device span from its first copy to its last
+    device -> host copy, divided by the number of steps, and the median of three blocks is
+    reported. Returns (ms per step, H2D
     bytes per step, D2H bytes per step, ms of one step's H2D copies alone)."""
     from nvsubquadratic_b200.dp import GradBucket
     from nvsubquadratic_b200.fftconv import causal_fftconv1d_fp32_bhl
@@ -610,22 +611,29 @@ def e2e_time(cfg, inp, device, op_only, steps, dp_group=None):
             issue_copy(i + 1)
         run_step(i)
     torch.cuda.synchronize()
-    if dp_group is not None:  # the ranks start the timed steps together
-        torch.distributed.barrier(group=dp_group)
+    # timed: blocks of exactly `steps` copies in, `steps` fwd+bwd, `steps` copies out; three
+    # blocks, the median block reported (one host-side stall of the eager path, an allocator
+    # or scheduler hiccup, must not stand for the path)
+    blocks = []
+    base = n_warm
+    for _ in range(3):
+        if dp_group is not None:  # the ranks start each timed block together
+            torch.distributed.barrier(group=dp_group)
+            torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(main)
+        issue_copy(base)
+        for i in range(steps):
+            if i + 1 < steps:
+                issue_copy(base + i + 1)
+            run_step(base + i)
+        t1.record(main)
         torch.cuda.synchronize()
-    # timed: exactly `steps` copies in, `steps` fwd+bwd, `steps` copies out
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record(main)
-    issue_copy(n_warm)
-    for i in range(steps):
-        if i + 1 < steps:
-            issue_copy(n_warm + i + 1)
-        run_step(n_warm + i)
-    t1.record(main)
-    torch.cuda.synchronize()
+        blocks.append(t0.elapsed_time(t1) / steps)
+        base += steps
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = out.numel() * out.element_size()
-    return t0.elapsed_time(t1) / steps, h2d, d2h, statistics.median(copy_times[1:])
+    return statistics.median(blocks), h2d, d2h, statistics.median(copy_times[1:])
 
 
 def measure_filter_gen(device, steps: int, warmup: int) -> dict:
@@ -812,9 +820,9 @@ def main():
             "e2e": {"value": round(e2e_val, 4), "unit": "GElem/s", "h2d_bytes_per_step": res["h2d"],
                     "d2h_bytes_per_step": res["d2h"], "ms_per_step": round(res["e2e_ms"], 4),
                     "h2d_copy_ms": round(res["copy_ms"], 4) if res.get("copy_ms") is not None else None,
-                    "stat": "mean over the timed steps (eager, through hyena_fused / the op API); every step's "
-                            "inputs copied H2D from pinned memory and y copied D2H, the next step's H2D overlapped "
-                            "with this step's compute on a copy stream"},
+                    "stat": "median of three blocks of timed steps, each block's mean per step (eager, through "
+                            "hyena_fused / the op API); every step's inputs copied H2D from pinned memory and y "
+                            "copied D2H, the next step's H2D overlapped with this step's compute on a copy stream"},
             "gpu_launches": res["launches"] * args.steps,
             "clocks": res["clocks"],
         }
