@@ -149,3 +149,30 @@ def test_cp_window_permute_validation():
     assert call(3, 0, 0) == _lib.HYFFT_ERR_INVALID
     assert call(1, 0, 4) == _lib.HYFFT_ERR_INVALID   # unpack seq->chan has no window form
     assert call(2, 0, 4) == _lib.HYFFT_ERR_INVALID   # pack chan->seq has no window form
+
+
+def _large_grid_ws(C, F):
+    """Forward / backward workspace of the large-grid 2D kernels: two / three
+    [C][F/2+1][F] complex spectra (256-byte aligned) and the float shortcut vector."""
+    spec = (C * (F // 2 + 1) * F * 8 + 255) // 256 * 256
+    dvec = (C * 4 + 255) // 256 * 256
+    return 2 * spec + dvec, 3 * spec + dvec
+
+
+@pytest.mark.parametrize("N,K,F", [
+    ((128, 128), (128, 128), 192),   # cfg2's grid: N + ceil(K/2) - 1 = 191 on both axes
+    ((112, 128), (127, 101), 192),
+    ((100, 120), (129, 150), 256),   # 120 + 75 - 1 = 194 > 192 on the second axis
+    ((128, 97), (255, 193), 256),
+])
+def test_large_grid_fft_length_choice(N, K, F, monkeypatch):
+    """The large-grid plan takes the 192-point transforms exactly where the circular
+    convolution of that length is alias-free on the output window (F >= N + ceil(K/2) - 1
+    on both axes), else 256 points; HYFFT_B2_F256 forces 256. Read from the workspace sizes
+    the library reports (host-only planning)."""
+    C = 64
+    d = b2._conv_desc(2, C, N, K, 1, False, torch.bfloat16, 0)
+    assert b2._workspace_sizes(d) == _large_grid_ws(C, F)
+    monkeypatch.setenv("HYFFT_B2_F256", "1")
+    d = b2._conv_desc(2, C, N, K, 1, False, torch.bfloat16, 0)
+    assert b2._workspace_sizes(d) == _large_grid_ws(C, 256)
