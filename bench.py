@@ -54,7 +54,7 @@ CONFIGS = {
                  desc="2D HyenaND ViT-B grid 14x14, SIREN-style 14x14 filter, F=24x24 (linear-conv length 21 padded to 3*2^3), 3x3 short conv"),
     "cfg2": dict(nd=2, B=8, C=256, S=(128, 128), K=(128, 128), short=3, g1="identity", g2="identity",
                  dtype=torch.bfloat16, causal=False, shard="batch",
-                 desc="2D HyenaND 128x128, exp-radial 128x128 filter, F=256x256, batch-sharded"),
+                 desc="2D HyenaND 128x128, exp-radial 128x128 filter, F=192x192 (alias-free for N=128, K=128), batch-sharded"),
     "cfg3": dict(nd=3, B=2, C=192, S=(64, 64, 64), K=(64, 64, 64), short=3, g1="identity", g2="identity",
                  dtype=torch.bfloat16, causal=False, shard="channel",
                  desc="3D HyenaND 64^3, full-extent exp-radial filter, F=128^3, channel-sharded"),
